@@ -1,0 +1,442 @@
+#!/usr/bin/env python
+"""Benchmark of the chunkwise gated fast-weight scan, fwd+bwd (one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
+
+A step is one forward + backward of the mixer core (phases 1-3 of
+train_ablation.py:142-187, i.e. the B200 op ``chunk_fast_weight``) over one
+batch of the workload, default config 1 of the baseline: B8 H16 T4096 dh128,
+chunk 64, delta rule, bf16 activations with fp32 state.  Inputs are seeded
+synthetic tensors with the distributions the baseline names (no dataset).
+
+  value     whole-job tokens/s (B*T per rank per step, summed over ranks) with
+            the inputs resident in HBM, timed by CUDA events, max over ranks.
+  e2e       the same metric through the public API from pinned host buffers,
+            host->device copy of the inputs and device->host copy of o and all
+            gradients inside the timed region.
+  roofline  the dominant kernel: algorithmic work per launch / its average
+            launch time (CUDA events on its own stream, over the timed region).
+  cpu_baseline  the CPU oracle (a port of the reference's eager path) on a
+            bounded sample of the same workload, rank 0, N=1 only.
+
+Multi-GPU (torchrun, one process per GPU): every rank runs its own config-1
+batch (weak scaling, no data-path collective); the timing barrier and the
+max-over-ranks reduction are the only NCCL traffic.
+
+``--impl reference`` times the reference algorithm on the host cores instead
+(the oracle port; the reference itself is Python and is not present on the
+GPU box), rank 0 only, on a bounded sample scaled to the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+PKG_NAME = "gmdn-gated-muon-deltanet_b200"
+METRIC = "scan tokens/s fwd+bwd B8·H16·T4096·d128 bf16 at 1/2/4/8 GPU; % roofline"
+
+CONFIGS = {
+    "config1_delta": dict(B=8, H=16, T=4096, dh=128, chunk=64, rule=0, ns=5),
+    "config2_muon": dict(B=8, H=16, T=4096, dh=128, chunk=64, rule=1, ns=5),
+    "config3_adam": dict(B=8, H=16, T=4096, dh=128, chunk=64, rule=2, ns=5),
+    "config3_adam_long": dict(B=1, H=16, T=65536, dh=128, chunk=64, rule=2, ns=5),
+}
+RULE_NAMES = {0: "delta", 1: "muon", 2: "adam"}
+
+
+# ---------------------------------------------------------------------------
+# algorithmic work per kernel launch (units: flops or bytes for one launch)
+# ---------------------------------------------------------------------------
+
+def kernel_work(name: str, cfg: dict) -> tuple[str, float]:
+    """(bound, algorithmic work per launch) of a library kernel.
+
+    Per chunk-head (C tokens, head dim d): phase-1 products Kw, Uv are
+    2 * 2*C*d^2 flops; A, Qt, Ov, o are 2*C^2*d + 2*C^2*d + 2*C^2*d + 2*C*d^2;
+    the scan step S K is 2*d^3 (muon adds 3 products per NS step).  The
+    backward kernels count the products they must evaluate.
+    """
+    B, H, T, d, C = cfg["B"], cfg["H"], cfg["T"], cfg["dh"], cfg["chunk"]
+    N = T // C
+    units = B * H * N
+    ns = cfg["ns"] if cfg["rule"] == 1 else 0
+    mm = 2.0 * d ** 3
+    table = {
+        "chunk_prep": 4.0 * C * d * d,
+        "chunk_out": 6.0 * C * C * d + 2.0 * C * d * d,
+        "chunk_state_grad": 4.0 * C * C * d + 2.0 * C * d * d,
+        "chunk_token_grad": 14.0 * C * C * d + 10.0 * C * d * d,
+        "scan_fwd_ieee": mm * (1 + 3 * ns),
+        "scan_bwd_ieee": mm * (3 + 8 * ns),
+        "scan_fwd_fast": mm * (1 + 3 * ns),
+        "scan_bwd_fast": mm * (3 + 8 * ns),
+    }
+    if name not in table:
+        return "tensor", float("nan")
+    return "tensor", table[name] * units
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def load_traffic() -> dict:
+    """dram bytes per launch by kernel, from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.proc = None
+        self.out = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.target = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        except Exception:
+            self.target = None
+
+    def __enter__(self):
+        try:
+            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                   "-lms", "100"]
+            if self.target:
+                cmd += ["-i", self.target]
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                self.out = ""
+
+    def summary(self) -> dict | None:
+        if not self.out:
+            return None
+        rows = []
+        for line in self.out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[0]), max=float(parts[1]),
+                                 power=float(parts[2]) if parts[2] not in ("[N/A]", "") else 0.0,
+                                 hw=parts[4], hwt=parts[5], swt=parts[6], pcap=parts[7]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        loaded = [r for r in rows if r["power"] > 0.3 * max(x["power"] for x in rows)] or rows
+        reasons = set()
+        for r in loaded:
+            for key, label in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                               ("swt", "sw_thermal_slowdown"), ("pcap", "sw_power_cap")):
+                if r[key].lower() == "active":
+                    reasons.add(label)
+        return {"sm_mhz": statistics.median(r["sm"] for r in loaded),
+                "sm_max_mhz": max(r["max"] for r in loaded),
+                "samples": len(loaded), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (oracle port of the reference's eager path)
+# ---------------------------------------------------------------------------
+
+def cpu_sample_cfg(cfg: dict) -> dict:
+    s = dict(cfg)
+    s["B"] = 1
+    s["H"] = min(cfg["H"], 4 if cfg["rule"] != 0 else 16)
+    return s
+
+
+def cpu_oracle_step(pkg, oracle_mod, scfg: dict, inp) -> float:
+    t0 = time.perf_counter()
+    names = ["q", "k", "v", "alpha", "beta", "mu", "nu"]
+    ins = [None if getattr(inp, n) is None else getattr(inp, n).clone().requires_grad_(True)
+           for n in names]
+    o = oracle_mod.mixer_core_forward(*ins, scfg["rule"], scfg["ns"], scfg["chunk"])
+    o.backward(inp.dO)
+    return time.perf_counter() - t0
+
+
+def cpu_tokens(cfg: dict, scfg: dict) -> float:
+    """Config-equivalent tokens of one sample step: B_s*T scaled by the share of
+    heads the sample covers (heads are independent)."""
+    return scfg["B"] * scfg["T"] * scfg["H"] / cfg["H"]
+
+
+def cpu_baseline(pkg, cfg: dict, reps: int = 3) -> dict:
+    import oracle as oracle_mod
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    scfg = cpu_sample_cfg(cfg)
+    inp = pkg.workloads.mixer_inputs(scfg["B"], scfg["H"], scfg["T"], scfg["dh"], scfg["rule"],
+                                     scfg["chunk"], seed=0)
+    cpu_oracle_step(pkg, oracle_mod, scfg, inp)  # warm-up
+    times = [cpu_oracle_step(pkg, oracle_mod, scfg, inp) for _ in range(reps)]
+    t = statistics.median(times)
+    return {"value": cpu_tokens(cfg, scfg) / t, "unit": "tokens/s", "cores": threads,
+            "kind": "port",
+            "sample": (f"oracle mixer core fwd+bwd fp32 on B{scfg['B']} H{scfg['H']} "
+                       f"T{scfg['T']} dh{scfg['dh']} ({RULE_NAMES[cfg['rule']]}), "
+                       f"median of {reps} after 1 warm-up, {t:.2f} s/step; tokens scaled by "
+                       f"heads covered ({scfg['H']}/{cfg['H']})")}
+
+
+def run_reference_arm(args, cfg: dict) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    pkg = importlib.import_module(PKG_NAME + ".workloads")
+    import oracle as oracle_mod
+
+    class _P:
+        workloads = pkg
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    scfg = cpu_sample_cfg(cfg)
+    inp = pkg.mixer_inputs(scfg["B"], scfg["H"], scfg["T"], scfg["dh"], scfg["rule"],
+                           scfg["chunk"], seed=0)
+    for _ in range(args.warmup):
+        cpu_oracle_step(_P, oracle_mod, scfg, inp)
+    times = [cpu_oracle_step(_P, oracle_mod, scfg, inp) for _ in range(args.steps)]
+    total = sum(times)
+    value = cpu_tokens(cfg, scfg) * args.steps / total
+    sample = (f"oracle port of the reference eager path (fast_scan.py:72-95 + "
+              f"train_ablation.py:142-187), fp32 autograd, B{scfg['B']} H{scfg['H']} "
+              f"T{scfg['T']} dh{scfg['dh']} per step; tokens scaled by heads covered")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.config, **cfg, "rule": RULE_NAMES[cfg["rule"]]},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="config1_delta", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--precision", default="fast", choices=["fast", "ieee"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+
+    if args.impl == "reference":
+        run_reference_arm(args, cfg)
+        return
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    pkg = importlib.import_module(PKG_NAME)
+    L = importlib.import_module(PKG_NAME + "._lib")
+    prec = pkg.GMDN_PREC_FAST if args.precision == "fast" else pkg.GMDN_PREC_IEEE
+
+    B, H, T, dh, C, rule, ns = (cfg[k] for k in ("B", "H", "T", "dh", "chunk", "rule", "ns"))
+    host = pkg.workloads.mixer_inputs(B, H, T, dh, rule, C, seed=rank)
+    dev = host.to(device, torch.bfloat16)
+    leaves = [dev.q, dev.k, dev.v, dev.alpha, dev.beta, dev.mu] + ([dev.nu] if rule == 2 else [])
+    for t in leaves:
+        t.requires_grad_(True)
+    nu = dev.nu if rule == 2 else None
+
+    def step():
+        o = pkg.chunk_fast_weight(dev.q, dev.k, dev.v, dev.alpha, dev.beta, dev.mu, nu, rule,
+                                  ns, C, prec)
+        return torch.autograd.grad(o, leaves, dev.dO)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream(device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = L.kernel_launches()
+    L.prof_report()  # drop anything recorded so far
+    L.prof_enable(True)
+    with ClockSampler(device) as clocks:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    L.prof_enable(False)
+    kt = L.prof_report()
+    launches = L.kernel_launches() - launches0
+    elapsed = ev0.elapsed_time(ev1)  # ms
+    barrier()
+    if dist is not None:
+        t = torch.tensor([elapsed], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = t.item()
+    tokens_per_step = B * T * world
+    value = tokens_per_step * args.steps / (elapsed / 1e3)
+
+    # ---- end to end through the public API from pinned host memory ----
+    e2e = None
+    if not args.no_e2e:
+        pin = {n: getattr(host, n).to(torch.bfloat16 if n in ("q", "k", "v", "dO")
+                                      else torch.float32).pin_memory()
+               for n in ("q", "k", "v", "alpha", "beta", "mu", "nu", "dO")
+               if getattr(host, n) is not None}
+        outs = {"o": torch.empty(B, H, T, dh, dtype=torch.bfloat16).pin_memory()}
+        for n in ("q", "k", "v"):
+            outs["d" + n] = torch.empty(B, H, T, dh, dtype=torch.bfloat16).pin_memory()
+        for n in ("alpha", "beta", "mu") + (("nu",) if rule == 2 else ()):
+            outs["d" + n] = torch.empty(B, H, T, dtype=torch.float32).pin_memory()
+        h2d = sum(t.numel() * t.element_size() for n, t in pin.items()
+                  if n != "nu" or rule == 2)
+        d2h = sum(t.numel() * t.element_size() for t in outs.values())
+
+        def e2e_step():
+            d = {n: t.to(device, non_blocking=True) for n, t in pin.items()}
+            ins = [d["q"], d["k"], d["v"], d["alpha"], d["beta"], d["mu"]] + \
+                ([d["nu"]] if rule == 2 else [])
+            for t in ins:
+                t.requires_grad_(True)
+            o = pkg.chunk_fast_weight(d["q"], d["k"], d["v"], d["alpha"], d["beta"], d["mu"],
+                                      d.get("nu") if rule == 2 else None, rule, ns, C, prec)
+            grads = torch.autograd.grad(o, ins, d["dO"])
+            outs["o"].copy_(o.detach(), non_blocking=True)
+            names = ["dq", "dk", "dv", "dalpha", "dbeta", "dmu"] + (["dnu"] if rule == 2 else [])
+            for n, g in zip(names, grads):
+                outs[n].copy_(g, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2e_steps = max(1, min(args.steps, 5))
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1)
+        if dist is not None:
+            t = torch.tensor([e_ms], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = t.item()
+        e2e = {"value": tokens_per_step * e2e_steps / (e_ms / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+               "ms_per_step": e_ms / e2e_steps}
+
+    # ---- roofline of the dominant kernel ----
+    peaks, peak_kind = load_peaks()
+    traffic = load_traffic()
+    roofline = None
+    kernel_times = {}
+    if kt:
+        for name, (ms, n) in kt.items():
+            kernel_times[name] = {"total_ms": ms, "launches": n, "avg_ms": ms / max(n, 1),
+                                  "share": ms / max(sum(v[0] for v in kt.values()), 1e-9)}
+        top = max(kt, key=lambda k: kt[k][0])
+        bound, work = kernel_work(top, cfg)
+        avg_s = kt[top][0] / kt[top][1] / 1e3
+        if bound == "tensor":
+            achieved = work / avg_s / 1e12
+            peak = peaks["bf16_tflops"]
+            unit = "TFLOP/s"
+        else:
+            achieved = work / avg_s / 1e9
+            peak = peaks["hbm_gbs"]
+            unit = "GB/s"
+        tr = traffic.get(args.config, {}).get(top)
+        roofline = {"kernel": top, "bound": bound, "achieved": achieved, "peak": peak,
+                    "unit": unit, "frac": achieved / peak, "traffic": tr,
+                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json bf16 burst)"
+                    if peak_kind == "measured" else "fallback"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(pkg, cfg)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": elapsed / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": args.config, "model": "mixer core fwd+bwd",
+                       "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": dh,
+                       "chunk": C, "rule": RULE_NAMES[rule], "ns": ns,
+                       "precision": args.precision, "parallelism": f"dp{world} (B*H shards)",
+                       "l2": "inputs larger than L2 (q,k,v,dO bf16 = 537 MB per rank)"},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": launches, "clocks": clocks.summary(),
+            "kernel_times": kernel_times,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,90 @@
+"""ctypes binding of ``libgmdn_b200.so`` (the C ABI in include/gmdn_scan.h).
+
+The library is built in-tree by ``build.py``.  There is no fallback: if the
+shared library is missing or cannot be loaded, importing this module raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libgmdn_b200.so")
+
+GMDN_PREC_IEEE = 0
+GMDN_PREC_FAST = 1
+
+ERR_NAMES = {1: "invalid argument", 2: "unsupported", 3: "workspace too small",
+             4: "CUDA error", 5: "device-side failure"}
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with "
+            f"`python {os.path.join(_HERE, 'build.py')}` (needs nvcc, targets sm_100a)")
+    return ctypes.CDLL(LIB_PATH)
+
+
+lib = _load()
+
+_p = ctypes.c_void_p
+_i = ctypes.c_int
+_z = ctypes.c_size_t
+
+lib.gmdn_abi_version.restype = _i
+lib.gmdn_abi_version.argtypes = []
+lib.gmdn_last_error_string.restype = ctypes.c_char_p
+lib.gmdn_last_error_string.argtypes = []
+lib.gmdn_kernel_launches.restype = ctypes.c_uint64
+lib.gmdn_kernel_launches.argtypes = []
+lib.gmdn_prof_enable.restype = None
+lib.gmdn_prof_enable.argtypes = [_i]
+lib.gmdn_prof_report.restype = ctypes.c_char_p
+lib.gmdn_prof_report.argtypes = []
+
+lib.gmdn_scan_saved_bytes.restype = _z
+lib.gmdn_scan_saved_bytes.argtypes = [_i] * 5
+lib.gmdn_scan_workspace_bytes.restype = _z
+lib.gmdn_scan_workspace_bytes.argtypes = [_i] * 7
+lib.gmdn_scan_fwd.restype = _i
+lib.gmdn_scan_fwd.argtypes = [_p] * 9 + [_z] + [_i] * 7 + [_p]
+lib.gmdn_scan_bwd.restype = _i
+lib.gmdn_scan_bwd.argtypes = [_p] * 16 + [_z] + [_i] * 7 + [_p]
+
+lib.gmdn_chunk_saved_bytes.restype = _z
+lib.gmdn_chunk_saved_bytes.argtypes = [_i] * 8
+lib.gmdn_chunk_workspace_bytes.restype = _z
+lib.gmdn_chunk_workspace_bytes.argtypes = [_i] * 8
+lib.gmdn_chunk_fwd.restype = _i
+lib.gmdn_chunk_fwd.argtypes = [_p] * 10 + [_z] + [_i] * 8 + [_p]
+lib.gmdn_chunk_bwd.restype = _i
+lib.gmdn_chunk_bwd.argtypes = [_p] * 17 + [_z] + [_i] * 8 + [_p]
+lib.gmdn_chunk_fwd_ex.restype = _i
+lib.gmdn_chunk_fwd_ex.argtypes = [_p] * 10 + [_z] + [_i] * 9 + [_p]
+lib.gmdn_chunk_bwd_ex.restype = _i
+lib.gmdn_chunk_bwd_ex.argtypes = [_p] * 17 + [_z] + [_i] * 9 + [_p]
+
+
+def check(rc: int, what: str) -> None:
+    """Raise RuntimeError carrying the library's message when rc != 0."""
+    if rc != 0:
+        msg = lib.gmdn_last_error_string().decode(errors="replace")
+        raise RuntimeError(f"{what} failed ({ERR_NAMES.get(rc, rc)}): {msg}")
+
+
+def kernel_launches() -> int:
+    return int(lib.gmdn_kernel_launches())
+
+
+def prof_enable(on: bool) -> None:
+    """Bracket every kernel launch with CUDA events on its own stream."""
+    lib.gmdn_prof_enable(1 if on else 0)
+
+
+def prof_report() -> dict:
+    """{kernel name: (total ms, launches)} since the previous report; waits for
+    the recorded events."""
+    import json
+    return {k: (v[0], v[1]) for k, v in json.loads(lib.gmdn_prof_report().decode()).items()}

@@ -1,0 +1,443 @@
+// C ABI of the gmdn B200 scan library (declared in include/gmdn_scan.h).
+//
+// Validates arguments, carves the caller's workspace / saved buffers and
+// enqueues the kernels on the caller's stream.  Nothing is allocated and
+// nothing synchronises the host.
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/gmdn_scan.h"
+#include "scan_kernels.h"
+#include "fast_path.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(GMDN_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
+}
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+// Sequential carving of a caller buffer into 256-byte aligned pieces.
+struct Carver {
+  char* base;
+  size_t used = 0;
+  explicit Carver(void* p) : base(static_cast<char*>(p)) {}
+  float* take(size_t n_floats) {
+    float* p = base ? reinterpret_cast<float*>(base + used) : nullptr;
+    used += align_up(n_floats * sizeof(float));
+    return p;
+  }
+};
+
+bool dh_ok(int dh) { return dh == 16 || dh == 32 || dh == 64 || dh == 128; }
+
+int check_common(int B, int H, int N, int dh, int rule, int ns, int precision) {
+  if (B < 0 || H < 0 || N < 0) return fail(GMDN_ERR_INVALID, "negative size B=%d H=%d N=%d", B, H, N);
+  if (rule < 0 || rule > 2) return fail(GMDN_ERR_INVALID, "rule must be 0, 1 or 2 (got %d)", rule);
+  if (ns < 0 || ns > 16) return fail(GMDN_ERR_INVALID, "ns must be in [0, 16] (got %d)", ns);
+  if (precision != GMDN_PREC_IEEE && precision != GMDN_PREC_FAST)
+    return fail(GMDN_ERR_INVALID, "precision must be 0 (ieee) or 1 (fast) (got %d)", precision);
+  if (!dh_ok(dh))
+    return fail(GMDN_ERR_UNSUPPORTED, "head dim %d not built (16, 32, 64, 128)", dh);
+  return GMDN_OK;
+}
+
+size_t mats(size_t count, int dh) { return count * static_cast<size_t>(dh) * dh; }
+
+size_t scan_scratch_floats(int BH, int dh, int ns) {
+  const int per = gmdn::scan_bwd_scratch_mats(ns) > gmdn::kScanFwdScratchMats
+                      ? gmdn::scan_bwd_scratch_mats(ns)
+                      : gmdn::kScanFwdScratchMats;
+  return mats(static_cast<size_t>(BH) * per, dh);
+}
+
+struct ScanSaved {
+  float *M_hist, *V_hist;
+  size_t bytes;
+};
+
+ScanSaved carve_scan_saved(void* saved, int BH, int N, int dh, int rule) {
+  Carver c(saved);
+  ScanSaved s{nullptr, nullptr, 0};
+  const size_t per = mats(static_cast<size_t>(BH) * N, dh);
+  if (rule != 0) s.M_hist = c.take(per);
+  if (rule == 2) s.V_hist = c.take(per);
+  s.bytes = c.used;
+  return s;
+}
+
+struct ChunkBufs {
+  // saved
+  float *S, *M_hist, *V_hist;
+  size_t saved_bytes;
+  // workspace
+  float *Kw, *Uv, *gS, *dUv, *dKw;
+  float *a_c, *b_c, *m_c, *n_c, *da_c, *db_c, *dm_c, *dn_c;
+  float* scratch;
+  size_t ws_bytes;
+};
+
+ChunkBufs carve_chunk(void* saved, void* ws, int BH, int N, int dh, int rule, int ns) {
+  ChunkBufs b{};
+  const size_t per = mats(static_cast<size_t>(BH) * N, dh);
+  const size_t sc = static_cast<size_t>(BH) * N;
+  Carver cs(saved);
+  b.S = cs.take(per);
+  b.M_hist = rule != 0 ? cs.take(per) : nullptr;
+  b.V_hist = rule == 2 ? cs.take(per) : nullptr;
+  b.saved_bytes = cs.used;
+  Carver cw(ws);
+  b.Kw = cw.take(per);
+  b.Uv = cw.take(per);
+  b.gS = cw.take(per);
+  b.dUv = cw.take(per);
+  b.dKw = cw.take(per);
+  b.a_c = cw.take(sc);
+  b.b_c = cw.take(sc);
+  b.m_c = cw.take(sc);
+  b.n_c = cw.take(sc);
+  b.da_c = cw.take(sc);
+  b.db_c = cw.take(sc);
+  b.dm_c = cw.take(sc);
+  b.dn_c = cw.take(sc);
+  b.scratch = cw.take(scan_scratch_floats(BH, dh, ns));
+  b.ws_bytes = cw.used;
+  return b;
+}
+
+int check_chunk(int B, int H, int T, int dh, int chunk, int rule, int ns, int precision) {
+  int rc = check_common(B, H, T, dh, rule, ns, precision);
+  if (rc) return rc;
+  if (chunk != 32 && chunk != 64)
+    return fail(GMDN_ERR_UNSUPPORTED, "chunk %d not built (32, 64)", chunk);
+  if (T % chunk)
+    return fail(GMDN_ERR_INVALID, "seq_len %d must be a multiple of chunk %d", T, chunk);
+  return GMDN_OK;
+}
+
+// Optional per-launch timing: when enabled, every kernel launch is bracketed
+// by two CUDA events on the launching stream; gmdn_prof_report() waits for
+// them and returns per-kernel totals.  Off by default (no events recorded).
+struct ProfRec {
+  const char* name;
+  cudaEvent_t start, stop;
+};
+std::mutex g_prof_mu;
+std::atomic<int> g_prof_on{0};
+std::vector<ProfRec> g_prof_recs;
+std::vector<cudaEvent_t> g_prof_pool;
+std::string g_prof_json;
+
+cudaEvent_t prof_event() {
+  if (!g_prof_pool.empty()) {
+    cudaEvent_t e = g_prof_pool.back();
+    g_prof_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+struct ProfScope {
+  cudaStream_t st;
+  const char* name;
+  cudaEvent_t a = nullptr, b = nullptr;
+  ProfScope(cudaStream_t s, const char* n) : st(s), name(n) {
+    if (g_prof_on.load(std::memory_order_relaxed)) {
+      std::lock_guard<std::mutex> lk(g_prof_mu);
+      a = prof_event();
+      b = prof_event();
+      cudaEventRecord(a, st);
+    }
+  }
+  void done() {
+    if (a) {
+      cudaEventRecord(b, st);
+      std::lock_guard<std::mutex> lk(g_prof_mu);
+      g_prof_recs.push_back({name, a, b});
+    }
+  }
+};
+
+#define GMDN_LAUNCH(call, what)                            \
+  do {                                                     \
+    ProfScope ps_(st, what);                               \
+    cudaError_t e_ = (call);                               \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what);     \
+    ps_.done();                                            \
+    g_launches.fetch_add(1, std::memory_order_relaxed);    \
+  } while (0)
+
+}  // namespace
+
+extern "C" {
+
+int gmdn_abi_version(void) { return 1; }
+
+const char* gmdn_last_error_string(void) { return g_last_error.c_str(); }
+
+uint64_t gmdn_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+void gmdn_prof_enable(int on) { g_prof_on.store(on ? 1 : 0); }
+
+const char* gmdn_prof_report(void) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  std::map<std::string, std::pair<double, int>> agg;
+  for (auto& r : g_prof_recs) {
+    float ms = 0.f;
+    if (cudaEventSynchronize(r.stop) == cudaSuccess &&
+        cudaEventElapsedTime(&ms, r.start, r.stop) == cudaSuccess) {
+      auto& e = agg[r.name];
+      e.first += ms;
+      e.second += 1;
+    }
+    g_prof_pool.push_back(r.start);
+    g_prof_pool.push_back(r.stop);
+  }
+  g_prof_recs.clear();
+  std::string js = "{";
+  bool first = true;
+  for (auto& kv : agg) {
+    char buf[256];
+    snprintf(buf, sizeof(buf), "%s\"%s\": [%.6f, %d]", first ? "" : ", ", kv.first.c_str(),
+             kv.second.first, kv.second.second);
+    js += buf;
+    first = false;
+  }
+  js += "}";
+  g_prof_json = js;
+  return g_prof_json.c_str();
+}
+
+size_t gmdn_scan_saved_bytes(int B, int H, int N, int dh, int rule) {
+  if (B < 0 || H < 0 || N < 0 || !dh_ok(dh)) return 0;
+  return carve_scan_saved(nullptr, B * H, N, dh, rule).bytes;
+}
+
+size_t gmdn_scan_workspace_bytes(int B, int H, int N, int dh, int rule, int ns, int precision) {
+  (void)N;
+  (void)rule;
+  (void)precision;
+  if (B < 0 || H < 0 || !dh_ok(dh) || ns < 0) return 0;
+  return align_up(scan_scratch_floats(B * H, dh, ns) * sizeof(float));
+}
+
+int gmdn_scan_fwd(const float* U, const float* K, const float* a, const float* b,
+                  const float* m, const float* n, float* S_out, void* saved,
+                  void* workspace, size_t workspace_bytes, int B, int H, int N, int dh,
+                  int rule, int ns, int precision, void* stream) {
+  g_last_error.clear();
+  int rc = check_common(B, H, N, dh, rule, ns, precision);
+  if (rc) return rc;
+  if (B * H * N == 0) return GMDN_OK;
+  if (!U || !K || !a || !b || !m || !n || !S_out)
+    return fail(GMDN_ERR_INVALID, "null input/output pointer");
+  if (rule != 0 && !saved) return fail(GMDN_ERR_INVALID, "muon/adam need the saved buffer");
+  const size_t need = gmdn_scan_workspace_bytes(B, H, N, dh, rule, ns, precision);
+  if (!workspace || workspace_bytes < need)
+    return fail(GMDN_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, need);
+  ScanSaved sv = carve_scan_saved(saved, B * H, N, dh, rule);
+  gmdn::ScanArgs p{};
+  p.U = U; p.K = K; p.a = a; p.b = b; p.m = m; p.n = n;
+  p.S = S_out; p.M_hist = sv.M_hist; p.V_hist = sv.V_hist;
+  p.scratch = static_cast<float*>(workspace);
+  p.BH = B * H; p.N = N; p.dh = dh; p.rule = rule; p.ns = ns;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (precision == GMDN_PREC_FAST && gmdn::fast_scan_supported(p)) {
+    GMDN_LAUNCH(gmdn::scan_fwd_fast(p, st), "scan_fwd_fast");
+  } else {
+    GMDN_LAUNCH(gmdn::scan_fwd_ieee(p, st), "scan_fwd_ieee");
+  }
+  return GMDN_OK;
+}
+
+int gmdn_scan_bwd(const float* U, const float* K, const float* a, const float* b,
+                  const float* m, const float* n, const float* S_all, const void* saved,
+                  const float* gS, float* dU, float* dK, float* da, float* db, float* dm,
+                  float* dn, void* workspace, size_t workspace_bytes, int B, int H, int N,
+                  int dh, int rule, int ns, int precision, void* stream) {
+  g_last_error.clear();
+  int rc = check_common(B, H, N, dh, rule, ns, precision);
+  if (rc) return rc;
+  if (B * H * N == 0) return GMDN_OK;
+  if (!U || !K || !a || !b || !m || !n || !S_all || !gS || !dU || !dK || !da || !db || !dm ||
+      !dn)
+    return fail(GMDN_ERR_INVALID, "null input/output pointer");
+  if (rule != 0 && !saved) return fail(GMDN_ERR_INVALID, "muon/adam need the saved buffer");
+  const size_t need = gmdn_scan_workspace_bytes(B, H, N, dh, rule, ns, precision);
+  if (!workspace || workspace_bytes < need)
+    return fail(GMDN_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes, need);
+  ScanSaved sv = carve_scan_saved(const_cast<void*>(saved), B * H, N, dh, rule);
+  gmdn::ScanArgs p{};
+  p.U = U; p.K = K; p.a = a; p.b = b; p.m = m; p.n = n;
+  p.S = const_cast<float*>(S_all); p.M_hist = sv.M_hist; p.V_hist = sv.V_hist;
+  p.gS = gS; p.dU = dU; p.dK = dK; p.da = da; p.db = db; p.dm = dm; p.dn = dn;
+  p.scratch = static_cast<float*>(workspace);
+  p.BH = B * H; p.N = N; p.dh = dh; p.rule = rule; p.ns = ns;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (precision == GMDN_PREC_FAST && gmdn::fast_scan_supported(p)) {
+    GMDN_LAUNCH(gmdn::scan_bwd_fast(p, st), "scan_bwd_fast");
+  } else {
+    GMDN_LAUNCH(gmdn::scan_bwd_ieee(p, st), "scan_bwd_ieee");
+  }
+  return GMDN_OK;
+}
+
+size_t gmdn_chunk_saved_bytes(int B, int H, int T, int dh, int chunk, int rule, int ns,
+                              int precision) {
+  (void)precision;
+  if (B < 0 || H < 0 || T < 0 || !dh_ok(dh) || chunk <= 0) return 0;
+  return carve_chunk(nullptr, nullptr, B * H, T / chunk, dh, rule, ns).saved_bytes;
+}
+
+size_t gmdn_chunk_workspace_bytes(int B, int H, int T, int dh, int chunk, int rule, int ns,
+                                  int precision) {
+  (void)precision;
+  if (B < 0 || H < 0 || T < 0 || !dh_ok(dh) || chunk <= 0 || ns < 0) return 0;
+  return carve_chunk(nullptr, nullptr, B * H, T / chunk, dh, rule, ns).ws_bytes;
+}
+
+static int chunk_setup(gmdn::ChunkArgs& p, ChunkBufs& bufs, const void* q, const void* k,
+                       const void* v, const float* alpha, const float* beta, const float* mu,
+                       const float* nu, void* saved, void* workspace, size_t workspace_bytes,
+                       int B, int H, int T, int dh, int chunk, int rule, int ns, int precision) {
+  int rc = check_chunk(B, H, T, dh, chunk, rule, ns, precision);
+  if (rc) return rc;
+  if (!q || !k || !v || !alpha || !beta || !mu) return fail(GMDN_ERR_INVALID, "null input pointer");
+  if (rule == 2 && !nu) return fail(GMDN_ERR_INVALID, "adam (rule 2) needs nu");
+  if (!saved) return fail(GMDN_ERR_INVALID, "null saved buffer");
+  const int N = T / chunk;
+  bufs = carve_chunk(saved, workspace, B * H, N, dh, rule, ns);
+  if (!workspace || workspace_bytes < bufs.ws_bytes)
+    return fail(GMDN_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes,
+                bufs.ws_bytes);
+  p = gmdn::ChunkArgs{};
+  p.q = q; p.k = k; p.v = v;
+  p.alpha = alpha; p.beta = beta; p.mu = mu; p.nu = (rule == 2) ? nu : nullptr;
+  p.Kw = bufs.Kw; p.Uv = bufs.Uv; p.S = bufs.S; p.gS = bufs.gS; p.dUv = bufs.dUv;
+  p.dKw = bufs.dKw;
+  p.a_c = bufs.a_c; p.b_c = bufs.b_c; p.m_c = bufs.m_c; p.n_c = bufs.n_c;
+  p.da_c = bufs.da_c; p.db_c = bufs.db_c; p.dm_c = bufs.dm_c; p.dn_c = bufs.dn_c;
+  p.BH = B * H; p.T = T; p.N = N; p.C = chunk; p.dh = dh; p.rule = rule;
+  p.io_f32 = false;
+  return GMDN_OK;
+}
+
+static gmdn::ScanArgs scan_args_from(const gmdn::ChunkArgs& c, const ChunkBufs& b, int ns) {
+  gmdn::ScanArgs s{};
+  s.U = b.Uv; s.K = b.Kw; s.a = b.a_c; s.b = b.b_c; s.m = b.m_c; s.n = b.n_c;
+  s.S = b.S; s.M_hist = b.M_hist; s.V_hist = b.V_hist;
+  s.gS = b.gS; s.dU = b.dUv; s.dK = b.dKw;
+  s.da = b.da_c; s.db = b.db_c; s.dm = b.dm_c; s.dn = b.dn_c;
+  s.scratch = b.scratch;
+  s.BH = c.BH; s.N = c.N; s.dh = c.dh; s.rule = c.rule; s.ns = ns;
+  return s;
+}
+
+int gmdn_chunk_fwd_ex(const void* q, const void* k, const void* v, const float* alpha,
+                      const float* beta, const float* mu, const float* nu, void* o, void* saved,
+                      void* workspace, size_t workspace_bytes, int B, int H, int T, int dh,
+                      int chunk, int rule, int ns, int precision, int io_f32, void* stream) {
+  g_last_error.clear();
+  if (B * H * T == 0) {
+    int rc = check_chunk(B, H, T, dh, chunk, rule, ns, precision);
+    return rc;
+  }
+  gmdn::ChunkArgs p;
+  ChunkBufs bufs;
+  int rc = chunk_setup(p, bufs, q, k, v, alpha, beta, mu, nu, saved, workspace, workspace_bytes,
+                       B, H, T, dh, chunk, rule, ns, precision);
+  if (rc) return rc;
+  if (!o) return fail(GMDN_ERR_INVALID, "null output pointer");
+  p.o = o;
+  p.io_f32 = io_f32 != 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  gmdn::ScanArgs sp = scan_args_from(p, bufs, ns);
+  GMDN_LAUNCH(gmdn::chunk_prep_ieee(p, st), "chunk_prep");
+  if (precision == GMDN_PREC_FAST && gmdn::fast_scan_supported(sp)) {
+    GMDN_LAUNCH(gmdn::scan_fwd_fast(sp, st), "scan_fwd_fast");
+  } else {
+    GMDN_LAUNCH(gmdn::scan_fwd_ieee(sp, st), "scan_fwd_ieee");
+  }
+  GMDN_LAUNCH(gmdn::chunk_out_ieee(p, st), "chunk_out");
+  return GMDN_OK;
+}
+
+int gmdn_chunk_bwd_ex(const void* q, const void* k, const void* v, const float* alpha,
+                      const float* beta, const float* mu, const float* nu, const void* dO,
+                      const void* saved, void* dq, void* dk, void* dv, float* dalpha,
+                      float* dbeta, float* dmu, float* dnu, void* workspace,
+                      size_t workspace_bytes, int B, int H, int T, int dh, int chunk, int rule,
+                      int ns, int precision, int io_f32, void* stream) {
+  g_last_error.clear();
+  if (B * H * T == 0) {
+    int rc = check_chunk(B, H, T, dh, chunk, rule, ns, precision);
+    return rc;
+  }
+  gmdn::ChunkArgs p;
+  ChunkBufs bufs;
+  int rc = chunk_setup(p, bufs, q, k, v, alpha, beta, mu, nu, const_cast<void*>(saved),
+                       workspace, workspace_bytes, B, H, T, dh, chunk, rule, ns, precision);
+  if (rc) return rc;
+  if (!dO || !dq || !dk || !dv || !dalpha || !dbeta || !dmu)
+    return fail(GMDN_ERR_INVALID, "null gradient pointer");
+  if (rule == 2 && !dnu) return fail(GMDN_ERR_INVALID, "adam (rule 2) needs dnu");
+  p.dO = dO; p.dq = dq; p.dk = dk; p.dv = dv;
+  p.dalpha = dalpha; p.dbeta = dbeta; p.dmu = dmu; p.dnu = dnu;
+  p.io_f32 = io_f32 != 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  gmdn::ScanArgs sp = scan_args_from(p, bufs, ns);
+  // Kw, Uv and the chunk gate products are recomputed rather than saved.
+  GMDN_LAUNCH(gmdn::chunk_prep_ieee(p, st), "chunk_prep");
+  GMDN_LAUNCH(gmdn::chunk_state_grad_ieee(p, st), "chunk_state_grad");
+  if (precision == GMDN_PREC_FAST && gmdn::fast_scan_supported(sp)) {
+    GMDN_LAUNCH(gmdn::scan_bwd_fast(sp, st), "scan_bwd_fast");
+  } else {
+    GMDN_LAUNCH(gmdn::scan_bwd_ieee(sp, st), "scan_bwd_ieee");
+  }
+  GMDN_LAUNCH(gmdn::chunk_token_grad_ieee(p, st), "chunk_token_grad");
+  return GMDN_OK;
+}
+
+int gmdn_chunk_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* alpha,
+                   const float* beta, const float* mu, const float* nu, uint16_t* o, void* saved,
+                   void* workspace, size_t workspace_bytes, int B, int H, int T, int dh,
+                   int chunk, int rule, int ns, int precision, void* stream) {
+  return gmdn_chunk_fwd_ex(q, k, v, alpha, beta, mu, nu, o, saved, workspace, workspace_bytes,
+                           B, H, T, dh, chunk, rule, ns, precision, 0, stream);
+}
+
+int gmdn_chunk_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* alpha,
+                   const float* beta, const float* mu, const float* nu, const uint16_t* dO,
+                   const void* saved, uint16_t* dq, uint16_t* dk, uint16_t* dv, float* dalpha,
+                   float* dbeta, float* dmu, float* dnu, void* workspace,
+                   size_t workspace_bytes, int B, int H, int T, int dh, int chunk, int rule,
+                   int ns, int precision, void* stream) {
+  return gmdn_chunk_bwd_ex(q, k, v, alpha, beta, mu, nu, dO, saved, dq, dk, dv, dalpha, dbeta,
+                           dmu, dnu, workspace, workspace_bytes, B, H, T, dh, chunk, rule, ns,
+                           precision, 0, stream);
+}
+
+}  // extern "C"

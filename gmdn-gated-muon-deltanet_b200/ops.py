@@ -1,0 +1,274 @@
+"""torch.library custom ops over the C ABI, with autograd and fake (meta) kernels.
+
+Two ops, matching the two layers of the reference they replace:
+
+``state_scan(U, K, a, b, m, n, rule, ns)``
+    fast_scan.py:403 ``fast_state_scan`` / ``_TritonScan`` (fast_scan.py:334-396):
+    pre-update states (B, H, N, dh, dh) of the chunk recurrence.
+
+``chunk_fast_weight(q, k, v, alpha, beta, mu, nu, rule, ns, chunk)``
+    train_ablation.py:142-187 (phases 1-3 of ``FastWeightMixer.forward``):
+    o (B, H, T, dh) from q, k, v and the per-token gates.
+
+Both run only on CUDA tensors through ``libgmdn_b200.so``; there is no CPU or
+eager fallback.  The ops are opaque to torch.compile (fake kernels give the
+output shapes), so a compiled trainer can call them.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+from torch import Tensor
+
+from ._lib import GMDN_PREC_FAST, GMDN_PREC_IEEE, check, lib
+
+__all__ = ["state_scan", "chunk_fast_weight", "GMDN_PREC_IEEE", "GMDN_PREC_FAST",
+           "ScanFunction"]
+
+
+def _ptr(t: Optional[Tensor]):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(None)
+
+
+def _stream(t: Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _require_cuda(name: str, *tensors: Optional[Tensor]) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(
+                f"{name}: the B200 op runs on CUDA tensors only (got a {t.device} tensor); "
+                "this build has no CPU or eager fallback")
+
+
+def _scratch(nbytes: int, like: Tensor) -> Tensor:
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=like.device)
+
+
+# ---------------------------------------------------------------------------
+# phase-2 state scan
+# ---------------------------------------------------------------------------
+
+@torch.library.custom_op("gmdn::state_scan_fwd", mutates_args=())
+def _state_scan_fwd(U: Tensor, K: Tensor, a: Tensor, b: Tensor, m: Tensor, n: Tensor,
+                    rule: int, ns: int, precision: int) -> tuple[Tensor, Tensor]:
+    B, H, N, dh, _ = U.shape
+    S = torch.empty_like(U)
+    saved = _scratch(lib.gmdn_scan_saved_bytes(B, H, N, dh, rule), U)
+    ws_bytes = lib.gmdn_scan_workspace_bytes(B, H, N, dh, rule, ns, precision)
+    ws = _scratch(ws_bytes, U)
+    with torch.cuda.device(U.device):
+        rc = lib.gmdn_scan_fwd(_ptr(U), _ptr(K), _ptr(a), _ptr(b), _ptr(m), _ptr(n), _ptr(S),
+                               _ptr(saved), _ptr(ws), ws_bytes, B, H, N, dh, rule, ns,
+                               precision, _stream(U))
+    check(rc, "gmdn_scan_fwd")
+    return S, saved
+
+
+@_state_scan_fwd.register_fake
+def _(U, K, a, b, m, n, rule, ns, precision):
+    B, H, N, dh, _ = U.shape
+    return torch.empty_like(U), U.new_empty(
+        max(int(lib.gmdn_scan_saved_bytes(B, H, N, dh, rule)), 1), dtype=torch.uint8)
+
+
+@torch.library.custom_op("gmdn::state_scan_bwd", mutates_args=())
+def _state_scan_bwd(U: Tensor, K: Tensor, a: Tensor, b: Tensor, m: Tensor, n: Tensor,
+                    S: Tensor, saved: Tensor, gS: Tensor, rule: int, ns: int,
+                    precision: int) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    B, H, N, dh, _ = U.shape
+    dU, dK = torch.empty_like(U), torch.empty_like(K)
+    da, db, dm, dn = (torch.empty_like(t) for t in (a, b, m, n))
+    ws_bytes = lib.gmdn_scan_workspace_bytes(B, H, N, dh, rule, ns, precision)
+    ws = _scratch(ws_bytes, U)
+    with torch.cuda.device(U.device):
+        rc = lib.gmdn_scan_bwd(_ptr(U), _ptr(K), _ptr(a), _ptr(b), _ptr(m), _ptr(n), _ptr(S),
+                               _ptr(saved), _ptr(gS), _ptr(dU), _ptr(dK), _ptr(da), _ptr(db),
+                               _ptr(dm), _ptr(dn), _ptr(ws), ws_bytes, B, H, N, dh, rule, ns,
+                               precision, _stream(U))
+    check(rc, "gmdn_scan_bwd")
+    return dU, dK, da, db, dm, dn
+
+
+@_state_scan_bwd.register_fake
+def _(U, K, a, b, m, n, S, saved, gS, rule, ns, precision):
+    return (torch.empty_like(U), torch.empty_like(K), torch.empty_like(a), torch.empty_like(b),
+            torch.empty_like(m), torch.empty_like(n))
+
+
+def _scan_setup(ctx, inputs, output):
+    U, K, a, b, m, n, rule, ns, precision = inputs
+    S, saved = output
+    ctx.save_for_backward(U, K, a, b, m, n, S, saved)
+    ctx.cfg = (rule, ns, precision)
+
+
+def _scan_backward(ctx, gS, _gsaved):
+    U, K, a, b, m, n, S, saved = ctx.saved_tensors
+    rule, ns, precision = ctx.cfg
+    grads = torch.ops.gmdn.state_scan_bwd(U, K, a, b, m, n, S, saved, gS.contiguous(), rule,
+                                          ns, precision)
+    return (*grads, None, None, None)
+
+
+_state_scan_fwd.register_autograd(_scan_backward, setup_context=_scan_setup)
+
+
+def _check_scan_args(U, K, a, b, m, n, rule, ns):
+    if U.dim() != 5 or U.shape[-1] != U.shape[-2]:
+        raise ValueError(f"U must be (B, H, N, dh, dh) with square states, got {tuple(U.shape)}")
+    if K.shape != U.shape:
+        raise ValueError(f"K shape {tuple(K.shape)} != U shape {tuple(U.shape)}")
+    for name, g in zip("abmn", (a, b, m, n)):
+        if g.shape != U.shape[:3]:
+            raise ValueError(f"gate {name} must be (B, H, N) = {tuple(U.shape[:3])}, "
+                             f"got {tuple(g.shape)}")
+    if rule not in (0, 1, 2):
+        raise ValueError(f"rule must be 0 (delta), 1 (muon) or 2 (adam), got {rule}")
+    if ns < 0:
+        raise ValueError(f"ns must be >= 0, got {ns}")
+
+
+def state_scan(U: Tensor, K: Tensor, a: Tensor, b: Tensor, m: Tensor, n: Tensor, rule: int,
+               ns: int, precision: int = GMDN_PREC_IEEE) -> Tensor:
+    """Pre-update state stack (B, H, N, dh, dh), differentiable in all six inputs."""
+    _check_scan_args(U, K, a, b, m, n, rule, ns)
+    _require_cuda("state_scan", U, K, a, b, m, n)
+    args = [t.float().contiguous() for t in (U, K, a, b, m, n)]
+    S, _ = torch.ops.gmdn.state_scan_fwd(*args, int(rule), int(ns), int(precision))
+    return S
+
+
+class ScanFunction:
+    """``_TritonScan``-compatible entry: ``ScanFunction.apply(U, K, a, b, m, n,
+    rule, ns)`` (fast_scan.py:334-396), using the precision set in the shim."""
+
+    precision = GMDN_PREC_FAST
+
+    @staticmethod
+    def apply(U, K, a, b, m, n, rule, ns):
+        return state_scan(U, K, a, b, m, n, rule, ns, ScanFunction.precision)
+
+
+# ---------------------------------------------------------------------------
+# mixer core (phases 1-3)
+# ---------------------------------------------------------------------------
+
+def _io_flag(q: Tensor) -> int:
+    if q.dtype == torch.bfloat16:
+        return 0
+    if q.dtype == torch.float32:
+        return 1
+    raise TypeError(f"q/k/v must be bfloat16 or float32, got {q.dtype}")
+
+
+@torch.library.custom_op("gmdn::chunk_fwd", mutates_args=())
+def _chunk_fwd(q: Tensor, k: Tensor, v: Tensor, alpha: Tensor, beta: Tensor, mu: Tensor,
+               nu: Optional[Tensor], rule: int, ns: int, chunk: int,
+               precision: int) -> tuple[Tensor, Tensor]:
+    B, H, T, dh = q.shape
+    o = torch.empty_like(q)
+    saved = _scratch(lib.gmdn_chunk_saved_bytes(B, H, T, dh, chunk, rule, ns, precision), q)
+    ws_bytes = lib.gmdn_chunk_workspace_bytes(B, H, T, dh, chunk, rule, ns, precision)
+    ws = _scratch(ws_bytes, q)
+    with torch.cuda.device(q.device):
+        rc = lib.gmdn_chunk_fwd_ex(_ptr(q), _ptr(k), _ptr(v), _ptr(alpha), _ptr(beta), _ptr(mu),
+                                   _ptr(nu), _ptr(o), _ptr(saved), _ptr(ws), ws_bytes, B, H, T,
+                                   dh, chunk, rule, ns, precision, _io_flag(q), _stream(q))
+    check(rc, "gmdn_chunk_fwd")
+    return o, saved
+
+
+@_chunk_fwd.register_fake
+def _(q, k, v, alpha, beta, mu, nu, rule, ns, chunk, precision):
+    B, H, T, dh = q.shape
+    nbytes = max(int(lib.gmdn_chunk_saved_bytes(B, H, T, dh, chunk, rule, ns, precision)), 1)
+    return torch.empty_like(q), q.new_empty(nbytes, dtype=torch.uint8)
+
+
+@torch.library.custom_op("gmdn::chunk_bwd", mutates_args=())
+def _chunk_bwd(q: Tensor, k: Tensor, v: Tensor, alpha: Tensor, beta: Tensor, mu: Tensor,
+               nu: Optional[Tensor], dO: Tensor, saved: Tensor, rule: int, ns: int, chunk: int,
+               precision: int) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    B, H, T, dh = q.shape
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dalpha, dbeta, dmu = torch.empty_like(alpha), torch.empty_like(beta), torch.empty_like(mu)
+    dnu = torch.empty_like(nu) if nu is not None else alpha.new_empty(0)
+    ws_bytes = lib.gmdn_chunk_workspace_bytes(B, H, T, dh, chunk, rule, ns, precision)
+    ws = _scratch(ws_bytes, q)
+    with torch.cuda.device(q.device):
+        rc = lib.gmdn_chunk_bwd_ex(_ptr(q), _ptr(k), _ptr(v), _ptr(alpha), _ptr(beta), _ptr(mu),
+                                   _ptr(nu), _ptr(dO), _ptr(saved), _ptr(dq), _ptr(dk), _ptr(dv),
+                                   _ptr(dalpha), _ptr(dbeta), _ptr(dmu),
+                                   _ptr(dnu if nu is not None else None), _ptr(ws), ws_bytes,
+                                   B, H, T, dh, chunk, rule, ns, precision, _io_flag(q),
+                                   _stream(q))
+    check(rc, "gmdn_chunk_bwd")
+    return dq, dk, dv, dalpha, dbeta, dmu, dnu
+
+
+@_chunk_bwd.register_fake
+def _(q, k, v, alpha, beta, mu, nu, dO, saved, rule, ns, chunk, precision):
+    dnu = torch.empty_like(nu) if nu is not None else alpha.new_empty(0)
+    return (torch.empty_like(q), torch.empty_like(k), torch.empty_like(v),
+            torch.empty_like(alpha), torch.empty_like(beta), torch.empty_like(mu), dnu)
+
+
+def _chunk_setup(ctx, inputs, output):
+    q, k, v, alpha, beta, mu, nu, rule, ns, chunk, precision = inputs
+    _, saved = output
+    ctx.has_nu = nu is not None
+    ctx.save_for_backward(q, k, v, alpha, beta, mu, nu if nu is not None else alpha.new_empty(0),
+                          saved)
+    ctx.cfg = (rule, ns, chunk, precision)
+
+
+def _chunk_backward(ctx, dO, _dsaved):
+    q, k, v, alpha, beta, mu, nu, saved = ctx.saved_tensors
+    nu = nu if ctx.has_nu else None
+    rule, ns, chunk, precision = ctx.cfg
+    dq, dk, dv, dalpha, dbeta, dmu, dnu = torch.ops.gmdn.chunk_bwd(
+        q, k, v, alpha, beta, mu, nu, dO.contiguous(), saved, rule, ns, chunk, precision)
+    return dq, dk, dv, dalpha, dbeta, dmu, (dnu if ctx.has_nu else None), None, None, None, None
+
+
+_chunk_fwd.register_autograd(_chunk_backward, setup_context=_chunk_setup)
+
+
+def chunk_fast_weight(q: Tensor, k: Tensor, v: Tensor, alpha: Tensor, beta: Tensor,
+                      mu: Tensor, nu: Optional[Tensor], rule: int, ns: int, chunk: int = 64,
+                      precision: int = GMDN_PREC_FAST) -> Tensor:
+    """Phases 1-3 of the reference mixer (train_ablation.py:142-187).
+
+    q, k, v: (B, H, T, dh), bf16 or fp32 (q and k already L2-normalised, as at
+    train_ablation.py:127-128).  alpha, beta, mu, nu: (B, H, T) gate values in
+    (0, 1); nu is read only by rule 2 (adam).  Returns o (B, H, T, dh) in the
+    dtype of q, before the per-head RMSNorm of train_ablation.py:188.
+    """
+    if q.dim() != 4:
+        raise ValueError(f"q must be (B, H, T, dh), got {tuple(q.shape)}")
+    B, H, T, dh = q.shape
+    if k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k and v must have the same shape")
+    if T % chunk:
+        raise ValueError(f"seq_len {T} must be a multiple of the chunk size {chunk}")
+    if rule not in (0, 1, 2):
+        raise ValueError(f"rule must be 0 (delta), 1 (muon) or 2 (adam), got {rule}")
+    if rule == 2 and nu is None:
+        raise ValueError("adam (rule 2) needs the nu gate")
+    for name, g in (("alpha", alpha), ("beta", beta), ("mu", mu), ("nu", nu)):
+        if g is not None and g.shape != (B, H, T):
+            raise ValueError(f"gate {name} must be (B, H, T) = {(B, H, T)}, got {tuple(g.shape)}")
+    _require_cuda("chunk_fast_weight", q, k, v, alpha, beta, mu, nu)
+    dt = q.dtype
+    q, k, v = (t.to(dt).contiguous() for t in (q, k, v))
+    gates = [g.float().contiguous() if g is not None else None for g in (alpha, beta, mu, nu)]
+    if rule != 2:
+        gates[3] = None
+    o, _ = torch.ops.gmdn.chunk_fwd(q, k, v, *gates, int(rule), int(ns), int(chunk),
+                                    int(precision))
+    return o

@@ -1,0 +1,156 @@
+/*
+ * gmdn_scan.h -- C ABI of the B200 (sm_100a) chunkwise gated fast-weight
+ * state scan: delta, muon and adam inner rules, forward and backward.
+ *
+ * Two layers of the reference are replaced:
+ *
+ *   1. the phase-2 state scan, fast_scan.py:403 `fast_state_scan(U, K, a, b,
+ *      m, n, rule, ns)` and its autograd Function `_TritonScan`
+ *      (fast_scan.py:334-396) -> gmdn_scan_fwd / gmdn_scan_bwd;
+ *   2. the mixer core around it, train_ablation.py:142-187 (phase 1
+ *      intra-chunk products, the scan, phase 3 output) -> gmdn_chunk_fwd /
+ *      gmdn_chunk_bwd.
+ *
+ * Conventions
+ *   - All tensors are dense, row-major, contiguous, on the current CUDA device.
+ *   - Scan tensors: U, K, S (B, H, N, dh, dh) fp32; gates a, b, m, n (B, H, N)
+ *     fp32.  Each state is stored [dv, dk] (rows are the value dimension), as
+ *     in the reference.  The forward writes the PRE-update states S_0..S_{N-1}.
+ *   - Mixer tensors: q, k, v, o and their gradients (B, H, T, dh) bf16 (raw
+ *     bits as uint16_t); gates alpha, beta, mu, nu (B, H, T) fp32.
+ *   - rule: 0 = delta, 1 = muon, 2 = adam.  ns: Newton-Schulz steps (muon).
+ *   - precision: GMDN_PREC_IEEE = exact fp32 products (the reference's
+ *     set_precision('ieee')); GMDN_PREC_FAST = tensor-core products (the
+ *     reference's default 'tf32' mode).
+ *   - Nothing is allocated inside: the caller passes device buffers of the
+ *     sizes the *_bytes() queries return.  No host synchronisation; all work is
+ *     enqueued on `stream` (a cudaStream_t, 0 = legacy default stream).
+ *   - Every entry point returns 0 on success or a GMDN_ERR_* code; the message
+ *     of the calling thread's last failure is gmdn_last_error_string().
+ *   - The functions keep no state between calls and may be called from any
+ *     host thread.
+ */
+#ifndef GMDN_SCAN_H_
+#define GMDN_SCAN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  GMDN_OK = 0,
+  GMDN_ERR_INVALID = 1,     /* bad shape, rule, ns or null pointer */
+  GMDN_ERR_UNSUPPORTED = 2, /* valid but not built (dh, chunk, precision) */
+  GMDN_ERR_WORKSPACE = 3,   /* workspace smaller than required */
+  GMDN_ERR_CUDA = 4,        /* a CUDA launch or device query failed */
+  GMDN_ERR_DEVICE = 5       /* a kernel reported a failure through its status word */
+};
+
+enum { GMDN_PREC_IEEE = 0, GMDN_PREC_FAST = 1 };
+
+/* Version of this ABI; bumped on any signature change. */
+int gmdn_abi_version(void);
+
+/* Message for the calling thread's most recent failed call ("" if none). */
+const char* gmdn_last_error_string(void);
+
+/* ---- phase-2 state scan: fast_scan.py:403 fast_state_scan ---------------- */
+
+/* Bytes of `saved` the forward fills for the backward (the pre-update M and V
+ * histories for muon / adam; replaces the M_all / V_all tensors that
+ * fast_scan.py:367-368 allocates). */
+size_t gmdn_scan_saved_bytes(int B, int H, int N, int dh, int rule);
+
+/* Scratch bytes for gmdn_scan_fwd / gmdn_scan_bwd. */
+size_t gmdn_scan_workspace_bytes(int B, int H, int N, int dh, int rule, int ns,
+                                 int precision);
+
+/* Forward: S_out <- pre-update states.  Replaces _TritonScan.forward
+ * (fast_scan.py:360-377) and _scan_fwd_kernel (fast_scan.py:206-248). */
+int gmdn_scan_fwd(const float* U, const float* K, const float* a, const float* b,
+                  const float* m, const float* n, float* S_out, void* saved,
+                  void* workspace, size_t workspace_bytes, int B, int H, int N,
+                  int dh, int rule, int ns, int precision, void* stream);
+
+/* Backward: cotangents of U, K, a, b, m, n for the cotangent gS of the state
+ * stack.  Gates the rule does not read get zeros (the reference's Triton
+ * backward leaves them uninitialised, fast_scan.py:386-389).  Replaces
+ * _TritonScan.backward (fast_scan.py:380-396) and _scan_bwd_kernel
+ * (fast_scan.py:269-331). */
+int gmdn_scan_bwd(const float* U, const float* K, const float* a, const float* b,
+                  const float* m, const float* n, const float* S_all,
+                  const void* saved, const float* gS, float* dU, float* dK,
+                  float* da, float* db, float* dm, float* dn, void* workspace,
+                  size_t workspace_bytes, int B, int H, int N, int dh, int rule,
+                  int ns, int precision, void* stream);
+
+/* ---- mixer core: train_ablation.py:142-187 ------------------------------- */
+
+/* Bytes of `saved` the chunk forward fills for the chunk backward. */
+size_t gmdn_chunk_saved_bytes(int B, int H, int T, int dh, int chunk, int rule,
+                              int ns, int precision);
+
+/* Scratch bytes for gmdn_chunk_fwd / gmdn_chunk_bwd. */
+size_t gmdn_chunk_workspace_bytes(int B, int H, int T, int dh, int chunk, int rule,
+                                  int ns, int precision);
+
+/* Forward of phases 1-3: o = (q - A k) S^T + A v per chunk with
+ * A = tril(q k^T) * beta (train_ablation.py:160-167, 184-187), the states S
+ * from the scan over Kw = k^T diag(w) k, Uv = v^T diag(w) k and the chunk
+ * gate products (train_ablation.py:150-182).  `nu` is read only by rule 2 and
+ * may be NULL otherwise. */
+int gmdn_chunk_fwd(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                   const float* alpha, const float* beta, const float* mu,
+                   const float* nu, uint16_t* o, void* saved, void* workspace,
+                   size_t workspace_bytes, int B, int H, int T, int dh, int chunk,
+                   int rule, int ns, int precision, void* stream);
+
+/* Backward of gmdn_chunk_fwd for the output cotangent dO.  Writes the
+ * cotangents of q, k, v (bf16) and of each gate (fp32); dnu may be NULL
+ * unless rule == 2.  Gates a rule does not read get zeros. */
+int gmdn_chunk_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                   const float* alpha, const float* beta, const float* mu,
+                   const float* nu, const uint16_t* dO, const void* saved,
+                   uint16_t* dq, uint16_t* dk, uint16_t* dv, float* dalpha,
+                   float* dbeta, float* dmu, float* dnu, void* workspace,
+                   size_t workspace_bytes, int B, int H, int T, int dh, int chunk,
+                   int rule, int ns, int precision, void* stream);
+
+/* Same as gmdn_chunk_fwd / gmdn_chunk_bwd with the activation dtype chosen at
+ * run time: io_f32 = 0 for bf16 q/k/v/o/dO/dq/dk/dv (the autocast-bf16 trainer,
+ * train_ablation.py:465-467), 1 for fp32 (the fp32 runs the 1e-4 parity bar
+ * is stated on).  Pointers are untyped for that reason. */
+int gmdn_chunk_fwd_ex(const void* q, const void* k, const void* v, const float* alpha,
+                      const float* beta, const float* mu, const float* nu, void* o,
+                      void* saved, void* workspace, size_t workspace_bytes, int B, int H,
+                      int T, int dh, int chunk, int rule, int ns, int precision, int io_f32,
+                      void* stream);
+
+int gmdn_chunk_bwd_ex(const void* q, const void* k, const void* v, const float* alpha,
+                      const float* beta, const float* mu, const float* nu, const void* dO,
+                      const void* saved, void* dq, void* dk, void* dv, float* dalpha,
+                      float* dbeta, float* dmu, float* dnu, void* workspace,
+                      size_t workspace_bytes, int B, int H, int T, int dh, int chunk,
+                      int rule, int ns, int precision, int io_f32, void* stream);
+
+/* Number of kernels this library has enqueued in this process (diagnostic;
+ * no reference counterpart). */
+uint64_t gmdn_kernel_launches(void);
+
+/* Per-launch timing for benchmarks (diagnostic; no reference counterpart).
+ * gmdn_prof_enable(1) brackets every subsequent kernel launch with two CUDA
+ * events on its stream; gmdn_prof_report() waits for the recorded events and
+ * returns a JSON object {"kernel": [total_ms, launches], ...} of everything
+ * recorded since the previous report (the string stays valid until the next
+ * call). */
+void gmdn_prof_enable(int on);
+const char* gmdn_prof_report(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GMDN_SCAN_H_ */

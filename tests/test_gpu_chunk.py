@@ -1,0 +1,143 @@
+"""GPU parity of the mixer core (phases 1-3, train_ablation.py:142-187)
+against the CPU oracle, forward output and every input gradient."""
+import os
+
+import pytest
+import torch
+
+from conftest import load_pkg
+from oracle_runs import mixer_oracle
+from parity import TOL_BF16, TOL_FP32, check
+
+pytestmark = pytest.mark.gpu
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+GRADS = ["dq", "dk", "dv", "dalpha", "dbeta", "dmu", "dnu"]
+
+
+def run_kernel(pkg, inp, rule, ns, chunk, precision, act_dtype):
+    names = ["q", "k", "v", "alpha", "beta", "mu", "nu"]
+    ins = []
+    for n in names:
+        t = getattr(inp, n)
+        if t is not None:
+            dt = act_dtype if n in ("q", "k", "v") else torch.float32
+            t = t.detach().to("cuda", dt).requires_grad_(True)
+        ins.append(t)
+    o = pkg.chunk_fast_weight(*ins, rule, ns, chunk, precision)
+    o.backward(inp.dO.to("cuda", act_dtype))
+    torch.cuda.synchronize()
+    grads = {"d" + n: t.grad.detach().float().cpu() for n, t in zip(names, ins) if t is not None}
+    return o.detach().float().cpu(), grads
+
+
+def round_inputs(inp, act_dtype):
+    """Inputs as the kernel sees them (activations rounded to act_dtype)."""
+    import copy
+    r = copy.copy(inp)
+    for n in ("q", "k", "v", "dO"):
+        setattr(r, n, getattr(inp, n).to(act_dtype).float())
+    return r
+
+
+def compare(pkg, inp, rule, ns, chunk, precision, act_dtype, tol, sl=None):
+    o, g = run_kernel(pkg, inp, rule, ns, chunk, precision, act_dtype)
+    ri = round_inputs(inp, act_dtype)
+    if sl is not None:
+        ri = slice_inputs(ri, *sl)
+        o = o[sl[0]:sl[0] + 1, sl[1]:sl[1] + 1]
+        g = {k: v[sl[0]:sl[0] + 1, sl[1]:sl[1] + 1] for k, v in g.items()}
+    o64, g64 = mixer_oracle(ri, rule, ns, chunk, torch.float64)
+    o32, g32 = mixer_oracle(ri, rule, ns, chunk, torch.float32)
+    check("o", o, o32, o64, tol)
+    for name in GRADS:
+        if name in g64:
+            check(name, g[name], g32[name], g64[name], tol)
+
+
+def slice_inputs(inp, b, h):
+    import copy
+    r = copy.copy(inp)
+    for n in ("q", "k", "v", "alpha", "beta", "mu", "nu", "dO"):
+        t = getattr(inp, n)
+        if t is not None:
+            setattr(r, n, t[b:b + 1, h:h + 1])
+    return r
+
+
+CONFIG0 = dict(B=2, H=4, T=256, dh=64)
+
+
+@pytest.mark.parametrize("rule,ns", [(0, 3), (1, 3), (1, 5), (2, 3)])
+@pytest.mark.parametrize("chunk", [32, 64])
+def test_config0_fp32_ieee(rule, ns, chunk):
+    """Config 0 shape (B2 H4 T256 dh64) in fp32: the 1e-4 bar."""
+    pkg = load_pkg()
+    inp = pkg.workloads.mixer_inputs(**CONFIG0, rule=rule, chunk=chunk, seed=rule)
+    compare(pkg, inp, rule, ns, chunk, pkg.GMDN_PREC_IEEE, torch.float32, TOL_FP32)
+
+
+@pytest.mark.parametrize("rule,ns", [(0, 3), (1, 5), (2, 3)])
+@pytest.mark.parametrize("precision", [0, 1])
+def test_bf16_inputs(rule, ns, precision):
+    """bf16 activations (the autocast trainer): the 2e-2 bar."""
+    pkg = load_pkg()
+    inp = pkg.workloads.mixer_inputs(2, 4, 512, 128, rule=rule, seed=20 + rule)
+    compare(pkg, inp, rule, ns, 64, precision, torch.bfloat16, TOL_BF16)
+
+
+@pytest.mark.parametrize("dh", [16, 32])
+def test_small_head_dims(dh):
+    pkg = load_pkg()
+    for rule, ns in ((0, 3), (1, 3), (2, 3)):
+        inp = pkg.workloads.mixer_inputs(1, 3, 128, dh, rule=rule, seed=40 + dh + rule)
+        compare(pkg, inp, rule, ns, 64, pkg.GMDN_PREC_IEEE, torch.float32, TOL_FP32)
+
+
+def test_trainer_gate_regime():
+    """alpha close to 1 (the trainer's gate prior, train_ablation.py:105) so the
+    decay term a_c is exercised, sigmoid nu for adam."""
+    pkg = load_pkg()
+    for rule, ns in ((0, 3), (1, 3), (2, 3)):
+        inp = pkg.workloads.mixer_inputs(1, 2, 256, 64, rule=rule, seed=50 + rule,
+                                         adam_fixed_moments=False)
+        inp.alpha = 0.9 + 0.1 * inp.alpha
+        compare(pkg, inp, rule, ns, 64, pkg.GMDN_PREC_IEEE, torch.float32, TOL_FP32)
+
+
+def test_golden_fixtures():
+    """The reference's own FastWeightMixer phases 1-3 (tests/golden/mixer.pt)."""
+    pkg = load_pkg()
+    import copy
+    for case in torch.load(os.path.join(GOLD, "mixer.pt"))["cases"]:
+        inp = pkg.workloads.MixerInputs(case["q"], case["k"], case["v"], case["alpha"],
+                                        case["beta"], case["mu"], case["nu"], case["dO"])
+        o, g = run_kernel(pkg, inp, case["rule"], case["ns"], case["chunk"],
+                          pkg.GMDN_PREC_IEEE, torch.float32)
+        ri = round_inputs(copy.copy(inp), torch.float32)
+        o32, g32 = mixer_oracle(ri, case["rule"], case["ns"], case["chunk"], torch.float32)
+        check(case["name"] + ":o", o, o32, case["o"], TOL_FP32)
+        for name in GRADS:
+            if case.get(name) is not None:
+                check(case["name"] + ":" + name, g[name], g32[name], case[name], TOL_FP32)
+
+
+@pytest.mark.parametrize("rule,ns", [(0, 3), (2, 3), (1, 5)])
+def test_config1_full_size_slices(rule, ns):
+    """B8 H16 T4096 dh128 bf16 (configs 1-3): slices of the full run against the
+    oracle on the same slice."""
+    pkg = load_pkg()
+    inp = pkg.workloads.mixer_inputs(8, 16, 4096, 128, rule=rule, seed=0)
+    for sl in ((0, 0), (7, 15)):
+        compare(pkg, inp, rule, ns, 64, pkg.GMDN_PREC_FAST, torch.bfloat16, TOL_BF16, sl=sl)
+
+
+def test_precisions_agree_closely():
+    pkg = load_pkg()
+    inp = pkg.workloads.mixer_inputs(2, 2, 256, 128, rule=0, seed=77)
+    o0, g0 = run_kernel(pkg, inp, 0, 3, 64, 0, torch.bfloat16)
+    o1, g1 = run_kernel(pkg, inp, 0, 3, 64, 1, torch.bfloat16)
+    from parity import rel
+    assert rel(o1, o0) < 2e-2
+    for k in g0:
+        assert rel(g1[k], g0[k]) < 2e-2, k

@@ -1,0 +1,143 @@
+"""GPU parity of the phase-2 state scan against the CPU oracle.
+
+Mirrors the reference's own check (test.py:41-68: eager vs kernel, every rule,
+ns 3 and 5, forward states and every input gradient, on the realistic PSD
+fixture of test.py:28-38), and extends it to other head dims, chunk counts,
+gate ranges, ns = 0, the golden fixtures recorded from the reference, and the
+full config-1 size through per-(b,h) slices.
+"""
+import os
+
+import pytest
+import torch
+
+import oracle
+from conftest import load_pkg
+from oracle_runs import scan_oracle
+from parity import TOL_FP32, check, rel
+
+pytestmark = pytest.mark.gpu
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+NAMES = ["dU", "dK", "da", "db", "dm", "dn"]
+
+
+def run_kernel(pkg, base, gS, rule, ns, precision):
+    ins = [t.detach().float().cuda().requires_grad_(True) for t in base]
+    S = pkg.state_scan(*ins, rule, ns, precision)
+    S.backward(gS.float().cuda())
+    torch.cuda.synchronize()
+    return S.detach().cpu(), [t.grad.detach().cpu() for t in ins]
+
+
+def compare(pkg, base, rule, ns, precision, tol, seed=7):
+    gS = torch.randn(base[0].shape, generator=torch.Generator().manual_seed(seed))
+    S64, g64 = scan_oracle(base, gS, rule, ns, torch.float64)
+    S32, g32 = scan_oracle(base, gS, rule, ns, torch.float32)
+    S, g = run_kernel(pkg, base, gS, rule, ns, precision)
+    check("S", S, S32, S64, tol)
+    for name, a, b32, b64 in zip(NAMES, g, g32, g64):
+        check(name, a, b32, b64, tol)
+
+
+@pytest.mark.parametrize("rule,ns", [(0, 3), (0, 5), (1, 3), (1, 5), (2, 3), (2, 5)])
+def test_reference_fixture_ieee(rule, ns):
+    """test.py part 1: B4 H12 N16 C64 dh64, ieee precision."""
+    pkg = load_pkg()
+    base = pkg.workloads.scan_inputs(4, 12, 16, 64, C=64, seed=rule * 10 + ns)
+    compare(pkg, base, rule, ns, pkg.GMDN_PREC_IEEE, TOL_FP32)
+
+
+@pytest.mark.parametrize("dh", [16, 32, 128])
+@pytest.mark.parametrize("rule,ns", [(0, 3), (1, 0), (1, 5), (2, 3)])
+@pytest.mark.parametrize("N", [1, 2, 9])
+def test_shapes_ieee(dh, rule, ns, N):
+    pkg = load_pkg()
+    base = pkg.workloads.scan_inputs(2, 3, N, dh, C=64, seed=100 + dh + N)
+    compare(pkg, base, rule, ns, pkg.GMDN_PREC_IEEE, TOL_FP32)
+
+
+@pytest.mark.parametrize("rule,ns", [(0, 3), (1, 5), (2, 3)])
+def test_wide_gates_ieee(rule, ns):
+    pkg = load_pkg()
+    base = pkg.workloads.scan_inputs(1, 4, 12, 64, C=64, seed=300 + rule, family="wide")
+    compare(pkg, base, rule, ns, pkg.GMDN_PREC_IEEE, TOL_FP32)
+
+
+@pytest.mark.parametrize("rule,ns", [(0, 3), (1, 5), (2, 3)])
+def test_fast_precision(rule, ns):
+    """set_precision('tf32') equivalent; bound of the reference's own tf32 check
+    (test.py:74 compares at 5e-2)."""
+    pkg = load_pkg()
+    base = pkg.workloads.scan_inputs(2, 4, 16, 128, C=64, seed=400 + rule)
+    compare(pkg, base, rule, ns, pkg.GMDN_PREC_FAST, 5e-2)
+
+
+def test_golden_fixtures():
+    """The reference's own float64 outputs (tests/golden/scan.pt)."""
+    pkg = load_pkg()
+    for case in torch.load(os.path.join(GOLD, "scan.pt"))["cases"]:
+        base = [case[k] for k in "U K a b m n".split()]
+        S, g = run_kernel(pkg, base, case["gS"], case["rule"], case["ns"], pkg.GMDN_PREC_IEEE)
+        S32, g32 = scan_oracle(base, case["gS"], case["rule"], case["ns"], torch.float32)
+        check(case["name"] + ":S", S, S32, case["S"], TOL_FP32)
+        for name, a, b32 in zip(NAMES, g, g32):
+            check(case["name"] + ":" + name, a, b32, case[name], TOL_FP32)
+
+
+def test_unused_gate_gradients_are_zero():
+    """The reference's Triton backward returns torch.empty_like garbage for
+    db/dm (delta) and dn (muon) (fast_scan.py:386-389); these must be zeros."""
+    pkg = load_pkg()
+    base = pkg.workloads.scan_inputs(2, 2, 4, 32, seed=5)
+    for rule, zero in ((0, ["db", "dm", "dn"]), (1, ["dn"])):
+        gS = torch.randn(base[0].shape)
+        _, g = run_kernel(pkg, base, gS, rule, 3, pkg.GMDN_PREC_IEEE)
+        for name in zero:
+            assert g[NAMES.index(name)].abs().max().item() == 0.0, (rule, name)
+
+
+@pytest.mark.parametrize("rule,ns", [(0, 3), (2, 3), (1, 5)])
+def test_full_size_slices(rule, ns):
+    """Config-1 scan size (B8 H16 N64 dh128): every (b,h) is independent, so a
+    slice of the full run must equal the oracle on that slice and, bit for bit,
+    the kernel run on that slice alone."""
+    pkg = load_pkg()
+    B, H, N, dh = 8, 16, 64, 128
+    base = pkg.workloads.scan_inputs(B, H, N, dh, C=64, seed=11 + rule)
+    gS = torch.randn(base[0].shape, generator=torch.Generator().manual_seed(3))
+    S, g = run_kernel(pkg, base, gS, rule, ns, pkg.GMDN_PREC_IEEE)
+    for (b, h) in ((0, 0), (5, 9), (7, 15)):
+        sl = [t[b:b + 1, h:h + 1] for t in base]
+        gsl = gS[b:b + 1, h:h + 1]
+        S64, g64 = scan_oracle(sl, gsl, rule, ns, torch.float64)
+        S32, g32 = scan_oracle(sl, gsl, rule, ns, torch.float32)
+        check("S", S[b:b + 1, h:h + 1], S32, S64, TOL_FP32)
+        for name, a, b32, b64 in zip(NAMES, g, g32, g64):
+            check(name, a[b:b + 1, h:h + 1], b32, b64, TOL_FP32)
+        S1, g1 = run_kernel(pkg, sl, gsl, rule, ns, pkg.GMDN_PREC_IEEE)
+        assert torch.equal(S1, S[b:b + 1, h:h + 1])
+        for a, a1 in zip(g, g1):
+            assert torch.equal(a1, a[b:b + 1, h:h + 1])
+
+
+def test_shim_matches_op():
+    pkg = load_pkg()
+    fs = pkg.fast_scan
+    base = pkg.workloads.scan_inputs(1, 2, 4, 64, seed=9)
+    fs.set_precision("ieee")
+    S_shim = fs.fast_state_scan(*[t.cuda() for t in base], 2, 3).cpu()
+    S_cls = fs._TritonScan.apply(*[t.cuda() for t in base], 2, 3).cpu()
+    S_op = pkg.state_scan(*[t.cuda() for t in base], 2, 3, pkg.GMDN_PREC_IEEE).cpu()
+    fs.set_precision("tf32")
+    assert torch.equal(S_shim, S_op) and torch.equal(S_cls, S_op)
+    S64 = oracle.scan_forward(*[t.double() for t in base], 2, 3)
+    assert rel(S_op, S64) < 1e-4
+
+
+def test_empty_chunk_axis():
+    pkg = load_pkg()
+    U = torch.zeros(2, 3, 0, 16, 16, device="cuda")
+    g = torch.zeros(2, 3, 0, device="cuda")
+    S = pkg.state_scan(U, U, g, g, g, g, 1, 3)
+    assert S.shape == (2, 3, 0, 16, 16)
