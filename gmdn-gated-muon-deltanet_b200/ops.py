@@ -105,11 +105,14 @@ def _scan_setup(ctx, inputs, output):
     S, saved = output
     ctx.save_for_backward(U, K, a, b, m, n, S, saved)
     ctx.cfg = (rule, ns, precision)
+    ctx.set_materialize_grads(False)  # never build a zero cotangent for `saved`
 
 
 def _scan_backward(ctx, gS, _gsaved):
     U, K, a, b, m, n, S, saved = ctx.saved_tensors
     rule, ns, precision = ctx.cfg
+    if gS is None:
+        gS = torch.zeros_like(S)
     grads = torch.ops.gmdn.state_scan_bwd(U, K, a, b, m, n, S, saved, gS.contiguous(), rule,
                                           ns, precision)
     return (*grads, None, None, None)
@@ -225,10 +228,13 @@ def _chunk_setup(ctx, inputs, output):
     ctx.save_for_backward(q, k, v, alpha, beta, mu, nu if nu is not None else alpha.new_empty(0),
                           saved)
     ctx.cfg = (rule, ns, chunk, precision)
+    ctx.set_materialize_grads(False)  # never build a zero cotangent for `saved`
 
 
 def _chunk_backward(ctx, dO, _dsaved):
     q, k, v, alpha, beta, mu, nu, saved = ctx.saved_tensors
+    if dO is None:
+        dO = torch.zeros_like(q)
     nu = nu if ctx.has_nu else None
     rule, ns, chunk, precision = ctx.cfg
     dq, dk, dv, dalpha, dbeta, dmu, dnu = torch.ops.gmdn.chunk_bwd(

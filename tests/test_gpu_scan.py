@@ -14,7 +14,7 @@ import torch
 import oracle
 from conftest import load_pkg
 from oracle_runs import scan_oracle
-from parity import TOL_FP32, check, rel
+from parity import TOL_FP32, check_outputs, perturb, rel
 
 pytestmark = pytest.mark.gpu
 
@@ -30,14 +30,21 @@ def run_kernel(pkg, base, gS, rule, ns, precision):
     return S.detach().cpu(), [t.grad.detach().cpu() for t in ins]
 
 
+def scan_ref_fn(base, gS, rule, ns, gold=None):
+    """ref_fn for parity.check_outputs; `gold` replaces the fp64 evaluation."""
+    def fn(dtype, seed):
+        if dtype == torch.float64 and gold is not None:
+            return gold
+        ins = base if seed is None else [perturb(t.float(), seed) for t in base]
+        S, g = scan_oracle(ins, gS, rule, ns, dtype)
+        return dict(zip(["S"] + NAMES, [S] + g))
+    return fn
+
+
 def compare(pkg, base, rule, ns, precision, tol, seed=7):
     gS = torch.randn(base[0].shape, generator=torch.Generator().manual_seed(seed))
-    S64, g64 = scan_oracle(base, gS, rule, ns, torch.float64)
-    S32, g32 = scan_oracle(base, gS, rule, ns, torch.float32)
     S, g = run_kernel(pkg, base, gS, rule, ns, precision)
-    check("S", S, S32, S64, tol)
-    for name, a, b32, b64 in zip(NAMES, g, g32, g64):
-        check(name, a, b32, b64, tol)
+    check_outputs(dict(zip(["S"] + NAMES, [S] + g)), scan_ref_fn(base, gS, rule, ns), tol)
 
 
 @pytest.mark.parametrize("rule,ns", [(0, 3), (0, 5), (1, 3), (1, 5), (2, 3), (2, 5)])
@@ -79,10 +86,10 @@ def test_golden_fixtures():
     for case in torch.load(os.path.join(GOLD, "scan.pt"))["cases"]:
         base = [case[k] for k in "U K a b m n".split()]
         S, g = run_kernel(pkg, base, case["gS"], case["rule"], case["ns"], pkg.GMDN_PREC_IEEE)
-        S32, g32 = scan_oracle(base, case["gS"], case["rule"], case["ns"], torch.float32)
-        check(case["name"] + ":S", S, S32, case["S"], TOL_FP32)
-        for name, a, b32 in zip(NAMES, g, g32):
-            check(case["name"] + ":" + name, a, b32, case[name], TOL_FP32)
+        gold = {n: case[n] for n in ["S"] + NAMES}
+        check_outputs(dict(zip(["S"] + NAMES, [S] + g)),
+                      scan_ref_fn(base, case["gS"], case["rule"], case["ns"], gold), TOL_FP32,
+                      prefix=case["name"] + ":")
 
 
 def test_unused_gate_gradients_are_zero():
@@ -110,11 +117,8 @@ def test_full_size_slices(rule, ns):
     for (b, h) in ((0, 0), (5, 9), (7, 15)):
         sl = [t[b:b + 1, h:h + 1] for t in base]
         gsl = gS[b:b + 1, h:h + 1]
-        S64, g64 = scan_oracle(sl, gsl, rule, ns, torch.float64)
-        S32, g32 = scan_oracle(sl, gsl, rule, ns, torch.float32)
-        check("S", S[b:b + 1, h:h + 1], S32, S64, TOL_FP32)
-        for name, a, b32, b64 in zip(NAMES, g, g32, g64):
-            check(name, a[b:b + 1, h:h + 1], b32, b64, TOL_FP32)
+        got = dict(zip(["S"] + NAMES, [S[b:b + 1, h:h + 1]] + [a[b:b + 1, h:h + 1] for a in g]))
+        check_outputs(got, scan_ref_fn(sl, gsl, rule, ns), TOL_FP32, prefix=f"({b},{h}):")
         S1, g1 = run_kernel(pkg, sl, gsl, rule, ns, pkg.GMDN_PREC_IEEE)
         assert torch.equal(S1, S[b:b + 1, h:h + 1])
         for a, a1 in zip(g, g1):
