@@ -61,6 +61,12 @@ lib.gmdn_chunk_fwd.restype = _i
 lib.gmdn_chunk_fwd.argtypes = [_p] * 10 + [_z] + [_i] * 8 + [_p]
 lib.gmdn_chunk_bwd.restype = _i
 lib.gmdn_chunk_bwd.argtypes = [_p] * 17 + [_z] + [_i] * 8 + [_p]
+lib.gmdn_chunk_saved_bytes_ex.restype = _z
+lib.gmdn_chunk_saved_bytes_ex.argtypes = [_i] * 9
+lib.gmdn_chunk_workspace_bytes_ex.restype = _z
+lib.gmdn_chunk_workspace_bytes_ex.argtypes = [_i] * 9
+lib.gmdn_chunk_status.restype = _i
+lib.gmdn_chunk_status.argtypes = [_p, _p]
 lib.gmdn_chunk_fwd_ex.restype = _i
 lib.gmdn_chunk_fwd_ex.argtypes = [_p] * 10 + [_z] + [_i] * 9 + [_p]
 lib.gmdn_chunk_bwd_ex.restype = _i

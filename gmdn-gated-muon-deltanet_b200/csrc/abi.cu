@@ -88,26 +88,42 @@ ScanSaved carve_scan_saved(void* saved, int BH, int N, int dh, int rule) {
 }
 
 struct ChunkBufs {
-  // saved
-  float *S, *M_hist, *V_hist;
+  // saved (forward -> backward)
+  float *S, *M_hist, *V_hist;   // exact path: fp32 states and moments
+  uint16_t* S_hist;             // tensor-core path: bf16 states
   size_t saved_bytes;
   // workspace
+  uint32_t* status;             // device status word (first 256 bytes)
   float *Kw, *Uv, *gS, *dUv, *dKw;
   float *a_c, *b_c, *m_c, *n_c, *da_c, *db_c, *dm_c, *dn_c;
   float* scratch;
   size_t ws_bytes;
 };
 
-ChunkBufs carve_chunk(void* saved, void* ws, int BH, int N, int dh, int rule, int ns) {
+// `fast`: the fused tensor-core forward runs; its backward currently
+// recomputes the fp32 state with the exact kernels, so the workspace also
+// holds S.
+ChunkBufs carve_chunk(void* saved, void* ws, int BH, int N, int dh, int rule, int ns,
+                      bool fast) {
   ChunkBufs b{};
   const size_t per = mats(static_cast<size_t>(BH) * N, dh);
   const size_t sc = static_cast<size_t>(BH) * N;
   Carver cs(saved);
-  b.S = cs.take(per);
-  b.M_hist = rule != 0 ? cs.take(per) : nullptr;
-  b.V_hist = rule == 2 ? cs.take(per) : nullptr;
+  if (fast) {
+    b.S_hist = reinterpret_cast<uint16_t*>(cs.take((per + 1) / 2));
+  } else {
+    b.S = cs.take(per);
+    b.M_hist = rule != 0 ? cs.take(per) : nullptr;
+    b.V_hist = rule == 2 ? cs.take(per) : nullptr;
+  }
   b.saved_bytes = cs.used;
   Carver cw(ws);
+  b.status = reinterpret_cast<uint32_t*>(cw.take(64));
+  if (fast) {
+    b.S = cw.take(per);
+    b.M_hist = rule != 0 ? cw.take(per) : nullptr;
+    b.V_hist = rule == 2 ? cw.take(per) : nullptr;
+  }
   b.Kw = cw.take(per);
   b.Uv = cw.take(per);
   b.gS = cw.take(per);
@@ -124,6 +140,14 @@ ChunkBufs carve_chunk(void* saved, void* ws, int BH, int N, int dh, int rule, in
   b.scratch = cw.take(scan_scratch_floats(BH, dh, ns));
   b.ws_bytes = cw.used;
   return b;
+}
+
+// Shape test for the fused forward, mirroring chunk_fwd_tc_supported().
+bool chunk_fast(int dh, int chunk, int rule, int precision, int io_f32, int N) {
+  if (precision != GMDN_PREC_FAST || io_f32) return false;
+  gmdn::ChunkArgs p{};
+  p.dh = dh; p.C = chunk; p.rule = rule; p.io_f32 = false; p.N = N;
+  return gmdn::chunk_fwd_tc_supported(p);
 }
 
 int check_chunk(int B, int H, int T, int dh, int chunk, int rule, int ns, int precision) {
@@ -265,11 +289,8 @@ int gmdn_scan_fwd(const float* U, const float* K, const float* a, const float* b
   p.scratch = static_cast<float*>(workspace);
   p.BH = B * H; p.N = N; p.dh = dh; p.rule = rule; p.ns = ns;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (precision == GMDN_PREC_FAST && gmdn::fast_scan_supported(p)) {
-    GMDN_LAUNCH(gmdn::scan_fwd_fast(p, st), "scan_fwd_fast");
-  } else {
-    GMDN_LAUNCH(gmdn::scan_fwd_ieee(p, st), "scan_fwd_ieee");
-  }
+  // Both precisions run the exact-fp32 kernels for the phase-2-only scan.
+  GMDN_LAUNCH(gmdn::scan_fwd_ieee(p, st), "scan_fwd_ieee");
   return GMDN_OK;
 }
 
@@ -297,39 +318,61 @@ int gmdn_scan_bwd(const float* U, const float* K, const float* a, const float* b
   p.scratch = static_cast<float*>(workspace);
   p.BH = B * H; p.N = N; p.dh = dh; p.rule = rule; p.ns = ns;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (precision == GMDN_PREC_FAST && gmdn::fast_scan_supported(p)) {
-    GMDN_LAUNCH(gmdn::scan_bwd_fast(p, st), "scan_bwd_fast");
-  } else {
-    GMDN_LAUNCH(gmdn::scan_bwd_ieee(p, st), "scan_bwd_ieee");
-  }
+  GMDN_LAUNCH(gmdn::scan_bwd_ieee(p, st), "scan_bwd_ieee");
   return GMDN_OK;
+}
+
+size_t gmdn_chunk_saved_bytes_ex(int B, int H, int T, int dh, int chunk, int rule, int ns,
+                                 int precision, int io_f32) {
+  if (B < 0 || H < 0 || T < 0 || !dh_ok(dh) || chunk <= 0) return 0;
+  const int N = T / chunk;
+  return carve_chunk(nullptr, nullptr, B * H, N, dh, rule, ns,
+                     chunk_fast(dh, chunk, rule, precision, io_f32, N)).saved_bytes;
+}
+
+size_t gmdn_chunk_workspace_bytes_ex(int B, int H, int T, int dh, int chunk, int rule, int ns,
+                                     int precision, int io_f32) {
+  if (B < 0 || H < 0 || T < 0 || !dh_ok(dh) || chunk <= 0 || ns < 0) return 0;
+  const int N = T / chunk;
+  return carve_chunk(nullptr, nullptr, B * H, N, dh, rule, ns,
+                     chunk_fast(dh, chunk, rule, precision, io_f32, N)).ws_bytes;
 }
 
 size_t gmdn_chunk_saved_bytes(int B, int H, int T, int dh, int chunk, int rule, int ns,
                               int precision) {
-  (void)precision;
-  if (B < 0 || H < 0 || T < 0 || !dh_ok(dh) || chunk <= 0) return 0;
-  return carve_chunk(nullptr, nullptr, B * H, T / chunk, dh, rule, ns).saved_bytes;
+  return gmdn_chunk_saved_bytes_ex(B, H, T, dh, chunk, rule, ns, precision, 0);
 }
 
 size_t gmdn_chunk_workspace_bytes(int B, int H, int T, int dh, int chunk, int rule, int ns,
                                   int precision) {
-  (void)precision;
-  if (B < 0 || H < 0 || T < 0 || !dh_ok(dh) || chunk <= 0 || ns < 0) return 0;
-  return carve_chunk(nullptr, nullptr, B * H, T / chunk, dh, rule, ns).ws_bytes;
+  return gmdn_chunk_workspace_bytes_ex(B, H, T, dh, chunk, rule, ns, precision, 0);
+}
+
+int gmdn_chunk_status(const void* workspace, void* stream) {
+  g_last_error.clear();
+  if (!workspace) return fail(GMDN_ERR_INVALID, "null workspace");
+  uint32_t v = 0;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(&v, workspace, sizeof(v), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "gmdn_chunk_status");
+  if (v) return fail(GMDN_ERR_DEVICE, "kernel status word 0x%x (1 = a wait timed out)", v);
+  return GMDN_OK;
 }
 
 static int chunk_setup(gmdn::ChunkArgs& p, ChunkBufs& bufs, const void* q, const void* k,
                        const void* v, const float* alpha, const float* beta, const float* mu,
                        const float* nu, void* saved, void* workspace, size_t workspace_bytes,
-                       int B, int H, int T, int dh, int chunk, int rule, int ns, int precision) {
+                       int B, int H, int T, int dh, int chunk, int rule, int ns, int precision,
+                       int io_f32, bool* fast) {
   int rc = check_chunk(B, H, T, dh, chunk, rule, ns, precision);
   if (rc) return rc;
   if (!q || !k || !v || !alpha || !beta || !mu) return fail(GMDN_ERR_INVALID, "null input pointer");
   if (rule == 2 && !nu) return fail(GMDN_ERR_INVALID, "adam (rule 2) needs nu");
   if (!saved) return fail(GMDN_ERR_INVALID, "null saved buffer");
   const int N = T / chunk;
-  bufs = carve_chunk(saved, workspace, B * H, N, dh, rule, ns);
+  *fast = chunk_fast(dh, chunk, rule, precision, io_f32, N);
+  bufs = carve_chunk(saved, workspace, B * H, N, dh, rule, ns, *fast);
   if (!workspace || workspace_bytes < bufs.ws_bytes)
     return fail(GMDN_ERR_WORKSPACE, "workspace %zu bytes < required %zu", workspace_bytes,
                 bufs.ws_bytes);
@@ -341,7 +384,7 @@ static int chunk_setup(gmdn::ChunkArgs& p, ChunkBufs& bufs, const void* q, const
   p.a_c = bufs.a_c; p.b_c = bufs.b_c; p.m_c = bufs.m_c; p.n_c = bufs.n_c;
   p.da_c = bufs.da_c; p.db_c = bufs.db_c; p.dm_c = bufs.dm_c; p.dn_c = bufs.dn_c;
   p.BH = B * H; p.T = T; p.N = N; p.C = chunk; p.dh = dh; p.rule = rule;
-  p.io_f32 = false;
+  p.io_f32 = io_f32 != 0;
   return GMDN_OK;
 }
 
@@ -361,26 +404,25 @@ int gmdn_chunk_fwd_ex(const void* q, const void* k, const void* v, const float* 
                       void* workspace, size_t workspace_bytes, int B, int H, int T, int dh,
                       int chunk, int rule, int ns, int precision, int io_f32, void* stream) {
   g_last_error.clear();
-  if (B * H * T == 0) {
-    int rc = check_chunk(B, H, T, dh, chunk, rule, ns, precision);
-    return rc;
-  }
+  if (B * H * T == 0) return check_chunk(B, H, T, dh, chunk, rule, ns, precision);
   gmdn::ChunkArgs p;
   ChunkBufs bufs;
+  bool fast = false;
   int rc = chunk_setup(p, bufs, q, k, v, alpha, beta, mu, nu, saved, workspace, workspace_bytes,
-                       B, H, T, dh, chunk, rule, ns, precision);
+                       B, H, T, dh, chunk, rule, ns, precision, io_f32, &fast);
   if (rc) return rc;
   if (!o) return fail(GMDN_ERR_INVALID, "null output pointer");
   p.o = o;
-  p.io_f32 = io_f32 != 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(bufs.status, 0, sizeof(uint32_t), st);
+  if (e != cudaSuccess) return cuda_fail(e, "status reset");
+  if (fast) {
+    GMDN_LAUNCH(gmdn::chunk_fwd_tc(p, bufs.S_hist, bufs.status, st), "chunk_fwd_tc");
+    return GMDN_OK;
+  }
   gmdn::ScanArgs sp = scan_args_from(p, bufs, ns);
   GMDN_LAUNCH(gmdn::chunk_prep_ieee(p, st), "chunk_prep");
-  if (precision == GMDN_PREC_FAST && gmdn::fast_scan_supported(sp)) {
-    GMDN_LAUNCH(gmdn::scan_fwd_fast(sp, st), "scan_fwd_fast");
-  } else {
-    GMDN_LAUNCH(gmdn::scan_fwd_ieee(sp, st), "scan_fwd_ieee");
-  }
+  GMDN_LAUNCH(gmdn::scan_fwd_ieee(sp, st), "scan_fwd_ieee");
   GMDN_LAUNCH(gmdn::chunk_out_ieee(p, st), "chunk_out");
   return GMDN_OK;
 }
@@ -392,31 +434,29 @@ int gmdn_chunk_bwd_ex(const void* q, const void* k, const void* v, const float* 
                       size_t workspace_bytes, int B, int H, int T, int dh, int chunk, int rule,
                       int ns, int precision, int io_f32, void* stream) {
   g_last_error.clear();
-  if (B * H * T == 0) {
-    int rc = check_chunk(B, H, T, dh, chunk, rule, ns, precision);
-    return rc;
-  }
+  if (B * H * T == 0) return check_chunk(B, H, T, dh, chunk, rule, ns, precision);
   gmdn::ChunkArgs p;
   ChunkBufs bufs;
+  bool fast = false;
   int rc = chunk_setup(p, bufs, q, k, v, alpha, beta, mu, nu, const_cast<void*>(saved),
-                       workspace, workspace_bytes, B, H, T, dh, chunk, rule, ns, precision);
+                       workspace, workspace_bytes, B, H, T, dh, chunk, rule, ns, precision,
+                       io_f32, &fast);
   if (rc) return rc;
   if (!dO || !dq || !dk || !dv || !dalpha || !dbeta || !dmu)
     return fail(GMDN_ERR_INVALID, "null gradient pointer");
   if (rule == 2 && !dnu) return fail(GMDN_ERR_INVALID, "adam (rule 2) needs dnu");
   p.dO = dO; p.dq = dq; p.dk = dk; p.dv = dv;
   p.dalpha = dalpha; p.dbeta = dbeta; p.dmu = dmu; p.dnu = dnu;
-  p.io_f32 = io_f32 != 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(bufs.status, 0, sizeof(uint32_t), st);
+  if (e != cudaSuccess) return cuda_fail(e, "status reset");
   gmdn::ScanArgs sp = scan_args_from(p, bufs, ns);
-  // Kw, Uv and the chunk gate products are recomputed rather than saved.
+  // Kw, Uv and the chunk gate products are recomputed rather than saved; on
+  // the tensor-core path the fp32 states are recomputed as well.
   GMDN_LAUNCH(gmdn::chunk_prep_ieee(p, st), "chunk_prep");
+  if (fast) GMDN_LAUNCH(gmdn::scan_fwd_ieee(sp, st), "scan_fwd_ieee");
   GMDN_LAUNCH(gmdn::chunk_state_grad_ieee(p, st), "chunk_state_grad");
-  if (precision == GMDN_PREC_FAST && gmdn::fast_scan_supported(sp)) {
-    GMDN_LAUNCH(gmdn::scan_bwd_fast(sp, st), "scan_bwd_fast");
-  } else {
-    GMDN_LAUNCH(gmdn::scan_bwd_ieee(sp, st), "scan_bwd_ieee");
-  }
+  GMDN_LAUNCH(gmdn::scan_bwd_ieee(sp, st), "scan_bwd_ieee");
   GMDN_LAUNCH(gmdn::chunk_token_grad_ieee(p, st), "chunk_token_grad");
   return GMDN_OK;
 }

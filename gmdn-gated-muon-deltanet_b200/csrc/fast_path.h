@@ -1,13 +1,21 @@
-// Tensor-core (tcgen05) scan path, selected by GMDN_PREC_FAST.
+// Tensor-core (tcgen05) paths, selected by GMDN_PREC_FAST.
 #pragma once
+
+#include <cuda.h>
 
 #include "scan_kernels.h"
 
 namespace gmdn {
 
-// True when the tensor-core kernels are built for this shape / rule.
-bool fast_scan_supported(const ScanArgs& p);
-cudaError_t scan_fwd_fast(const ScanArgs& p, cudaStream_t st);
-cudaError_t scan_bwd_fast(const ScanArgs& p, cudaStream_t st);
+// Fused mixer core forward (phases 1-3), delta rule, dh 128, chunk 64, bf16.
+bool chunk_fwd_tc_supported(const ChunkArgs& p);
+size_t chunk_fwd_tc_saved_bytes(int BH, int N);
+cudaError_t chunk_fwd_tc(const ChunkArgs& p, uint16_t* S_hist, uint32_t* status,
+                         cudaStream_t st);
+
+// rows x 128 bf16 row-major matrix as a TMA map with 64 x box_rows boxes and
+// 128-byte swizzle.
+cudaError_t make_tmap_rows128(CUtensorMap* map, const void* base, uint64_t rows,
+                              uint32_t box_rows);
 
 }  // namespace gmdn

@@ -1,0 +1,278 @@
+// Blackwell (sm_100a) tensor-core primitives: tcgen05 MMA with TMEM
+// accumulators, shared-memory matrix descriptors, TMA tile loads and
+// mbarriers with bounded waits.
+//
+// Layout conventions (bf16 operands, 128-byte swizzle):
+//   * A "tile" is R rows x 64 columns of bf16 (128 B per row) stored in the
+//     canonical SW128 arrangement: row r at byte r*128, its 16-byte chunk j at
+//     position j ^ (r % 8).  Tiles start on 1024-byte boundaries.  A wider
+//     matrix (R x 128) is two tiles ("panels") back to back.  This is what a
+//     TMA load with CU_TENSOR_MAP_SWIZZLE_128B and a 64-column box writes.
+//   * Read with K along the columns, a panel is a K-major operand: SBO = 1024
+//     (eight rows), advance 32 bytes per K=16 step inside the 128-byte row.
+//   * Read with K along the rows, it is an MN-major operand: LBO = byte
+//     distance between the 64-wide panels, SBO = 1024 (eight K rows), advance
+//     2048 bytes per K=16 step.
+//   * Accumulators: M=128 puts row m in TMEM lane m; M=64 puts row m in lane
+//     (m % 16) + 32 * (m / 16) (the first half of each 32-lane subpartition).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gmdn {
+namespace tc {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------------------
+// status word and bounded waits
+// ---------------------------------------------------------------------------
+
+// Bits of the per-launch status word a kernel ORs in on failure.
+enum : uint32_t {
+  kStatusWaitTimeout = 1u,  // an mbarrier wait gave up
+  kStatusBadShape = 2u,
+};
+
+// Upper bound of one wait: ~2 s of wall time (globaltimer is in ns).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase with the given parity to complete.  Gives up after
+// kWaitLimitNs, ORs kStatusWaitTimeout into *status and sets *abort (shared)
+// so that the other warps stop too.  Returns false on give-up or if another
+// warp already aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
+                                          volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      atomicOr(status, kStatusWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// fences
+// ---------------------------------------------------------------------------
+
+// Make generic-proxy shared-memory writes visible to the async proxy (the
+// tensor core and TMA), before signalling the thread that issues them.
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// TMEM allocation (one full warp executes these)
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// descriptors
+// ---------------------------------------------------------------------------
+
+// Shared-memory matrix descriptor, SW128 layout, sm_100 version field.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes,
+                                               uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= 1ull << 46;  // version = 1 (sm_100)
+  d |= 2ull << 61;  // layout type: SWIZZLE_128B
+  return d;
+}
+
+// K-major operand: rows = M (or N), K along the 128-byte rows.  `panel0` is
+// the first 64-column panel; `panel_stride` the byte distance to the next one
+// (K in [64, 128) lives there).  kstep counts K=16 steps.
+__device__ __forceinline__ uint64_t desc_kmajor(uint32_t panel0, uint32_t panel_stride,
+                                                int kstep) {
+  const uint32_t k = static_cast<uint32_t>(kstep) * 16u;
+  const uint32_t addr = panel0 + (k >> 6) * panel_stride + (k & 63u) * 2u;
+  return sw128_desc(addr, 16u, 1024u);
+}
+
+// MN-major operand: rows = K, M (or N) along the 128-byte rows, 64 per panel.
+__device__ __forceinline__ uint64_t desc_mnmajor(uint32_t panel0, uint32_t panel_stride,
+                                                 int kstep) {
+  const uint32_t addr = panel0 + static_cast<uint32_t>(kstep) * 2048u;
+  return sw128_desc(addr, panel_stride, 1024u);
+}
+
+// Instruction descriptor, kind::f16 with bf16 A/B and fp32 accumulation.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool b_mn,
+                                                  bool neg_a = false) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((neg_a ? 1u : 0u) << 13) |
+         ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------
+// MMA issue (one thread) and completion
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on `bar` when every MMA issued so far by this thread is done.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// TMEM -> registers.  32x32b: thread i of the warp reads lane (base lane + i),
+// N consecutive 32-bit columns.  The warp may touch only lanes
+// [32 * (warp % 4), 32 * (warp % 4) + 32).
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t tmem_lane_base(int warp) {
+  return static_cast<uint32_t>((warp & 3) * 32) << 16;
+}
+
+// ---------------------------------------------------------------------------
+// TMA: 2-D tiled bulk tensor load into shared memory, completion counted in
+// bytes on an mbarrier.  No multicast.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, int y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Plain 1-D bulk copy global -> shared (16-byte aligned, size multiple of 16).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// SW128 tile element addressing for threads that read or write tiles
+// ---------------------------------------------------------------------------
+
+// Byte offset of 16-byte chunk `chunk` (0..7) of row `row` inside a panel.
+__device__ __forceinline__ uint32_t sw128_chunk(int row, int chunk) {
+  return static_cast<uint32_t>(row) * 128u +
+         (static_cast<uint32_t>(chunk ^ (row & 7)) << 4);
+}
+
+// Byte offset of element `col` (0..63) of row `row` inside a panel (bf16).
+__device__ __forceinline__ uint32_t sw128_elem(int row, int col) {
+  return sw128_chunk(row, col >> 3) + static_cast<uint32_t>(col & 7) * 2u;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ float bf16_lo(uint32_t x) { return __uint_as_float(x << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t x) { return __uint_as_float(x & 0xFFFF0000u); }
+
+}  // namespace tc
+}  // namespace gmdn

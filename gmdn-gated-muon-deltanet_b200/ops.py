@@ -18,6 +18,7 @@ output shapes), so a compiled trainer can call them.
 from __future__ import annotations
 
 import ctypes
+import os
 from typing import Optional
 
 import torch
@@ -47,6 +48,16 @@ def _require_cuda(name: str, *tensors: Optional[Tensor]) -> None:
 
 def _scratch(nbytes: int, like: Tensor) -> Tensor:
     return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=like.device)
+
+
+# GMDN_CHECK_STATUS=1: after every mixer-core call, synchronise and read the
+# kernels' device status word (a bounded wait that gave up raises here).
+_CHECK_STATUS = os.environ.get("GMDN_CHECK_STATUS", "0") == "1"
+
+
+def _check_status(ws: Tensor, what: str) -> None:
+    if _CHECK_STATUS:
+        check(lib.gmdn_chunk_status(_ptr(ws), _stream(ws)), what)
 
 
 # ---------------------------------------------------------------------------
@@ -174,22 +185,26 @@ def _chunk_fwd(q: Tensor, k: Tensor, v: Tensor, alpha: Tensor, beta: Tensor, mu:
                nu: Optional[Tensor], rule: int, ns: int, chunk: int,
                precision: int) -> tuple[Tensor, Tensor]:
     B, H, T, dh = q.shape
+    io = _io_flag(q)
     o = torch.empty_like(q)
-    saved = _scratch(lib.gmdn_chunk_saved_bytes(B, H, T, dh, chunk, rule, ns, precision), q)
-    ws_bytes = lib.gmdn_chunk_workspace_bytes(B, H, T, dh, chunk, rule, ns, precision)
+    saved = _scratch(lib.gmdn_chunk_saved_bytes_ex(B, H, T, dh, chunk, rule, ns, precision, io),
+                     q)
+    ws_bytes = lib.gmdn_chunk_workspace_bytes_ex(B, H, T, dh, chunk, rule, ns, precision, io)
     ws = _scratch(ws_bytes, q)
     with torch.cuda.device(q.device):
         rc = lib.gmdn_chunk_fwd_ex(_ptr(q), _ptr(k), _ptr(v), _ptr(alpha), _ptr(beta), _ptr(mu),
                                    _ptr(nu), _ptr(o), _ptr(saved), _ptr(ws), ws_bytes, B, H, T,
-                                   dh, chunk, rule, ns, precision, _io_flag(q), _stream(q))
+                                   dh, chunk, rule, ns, precision, io, _stream(q))
     check(rc, "gmdn_chunk_fwd")
+    _check_status(ws, "gmdn_chunk_fwd (device)")
     return o, saved
 
 
 @_chunk_fwd.register_fake
 def _(q, k, v, alpha, beta, mu, nu, rule, ns, chunk, precision):
     B, H, T, dh = q.shape
-    nbytes = max(int(lib.gmdn_chunk_saved_bytes(B, H, T, dh, chunk, rule, ns, precision)), 1)
+    nbytes = max(int(lib.gmdn_chunk_saved_bytes_ex(B, H, T, dh, chunk, rule, ns, precision,
+                                                   _io_flag(q))), 1)
     return torch.empty_like(q), q.new_empty(nbytes, dtype=torch.uint8)
 
 
@@ -201,16 +216,17 @@ def _chunk_bwd(q: Tensor, k: Tensor, v: Tensor, alpha: Tensor, beta: Tensor, mu:
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     dalpha, dbeta, dmu = torch.empty_like(alpha), torch.empty_like(beta), torch.empty_like(mu)
     dnu = torch.empty_like(nu) if nu is not None else alpha.new_empty(0)
-    ws_bytes = lib.gmdn_chunk_workspace_bytes(B, H, T, dh, chunk, rule, ns, precision)
+    io = _io_flag(q)
+    ws_bytes = lib.gmdn_chunk_workspace_bytes_ex(B, H, T, dh, chunk, rule, ns, precision, io)
     ws = _scratch(ws_bytes, q)
     with torch.cuda.device(q.device):
         rc = lib.gmdn_chunk_bwd_ex(_ptr(q), _ptr(k), _ptr(v), _ptr(alpha), _ptr(beta), _ptr(mu),
                                    _ptr(nu), _ptr(dO), _ptr(saved), _ptr(dq), _ptr(dk), _ptr(dv),
                                    _ptr(dalpha), _ptr(dbeta), _ptr(dmu),
                                    _ptr(dnu if nu is not None else None), _ptr(ws), ws_bytes,
-                                   B, H, T, dh, chunk, rule, ns, precision, _io_flag(q),
-                                   _stream(q))
+                                   B, H, T, dh, chunk, rule, ns, precision, io, _stream(q))
     check(rc, "gmdn_chunk_bwd")
+    _check_status(ws, "gmdn_chunk_bwd (device)")
     return dq, dk, dv, dalpha, dbeta, dmu, dnu
 
 

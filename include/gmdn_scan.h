@@ -136,6 +136,20 @@ int gmdn_chunk_bwd_ex(const void* q, const void* k, const void* v, const float* 
                       size_t workspace_bytes, int B, int H, int T, int dh, int chunk,
                       int rule, int ns, int precision, int io_f32, void* stream);
 
+/* Buffer sizes for gmdn_chunk_fwd_ex / gmdn_chunk_bwd_ex with the given
+ * activation dtype (the layout of `saved` depends on it: the tensor-core path
+ * keeps the states in bf16). */
+size_t gmdn_chunk_saved_bytes_ex(int B, int H, int T, int dh, int chunk, int rule,
+                                 int ns, int precision, int io_f32);
+size_t gmdn_chunk_workspace_bytes_ex(int B, int H, int T, int dh, int chunk, int rule,
+                                     int ns, int precision, int io_f32);
+
+/* Reads the device status word the last chunk call on this workspace left
+ * (synchronises `stream`): GMDN_OK, or GMDN_ERR_DEVICE when a kernel gave up
+ * a bounded wait.  No reference counterpart (the reference has no device-side
+ * failure reporting). */
+int gmdn_chunk_status(const void* workspace, void* stream);
+
 /* Number of kernels this library has enqueued in this process (diagnostic;
  * no reference counterpart). */
 uint64_t gmdn_kernel_launches(void);

@@ -10,6 +10,10 @@ if ROOT not in sys.path:
 
 PKG_NAME = "gmdn-gated-muon-deltanet_b200"
 
+# Every mixer-core call in the tests reads back the kernels' device status word
+# (a bounded wait that gave up fails the test instead of passing silently).
+os.environ.setdefault("GMDN_CHECK_STATUS", "1")
+
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
