@@ -92,6 +92,7 @@ struct ChunkBufs {
   float *S, *M_hist, *V_hist;   // exact path: fp32 states and moments
   uint16_t* S_hist;             // tensor-core path: bf16 states
   size_t saved_bytes;
+  uint16_t* Sbar_hist;          // tensor-core path: bf16 state cotangents
   // workspace
   uint32_t* status;             // device status word (first 256 bytes)
   float *Kw, *Uv, *gS, *dUv, *dKw;
@@ -100,30 +101,28 @@ struct ChunkBufs {
   size_t ws_bytes;
 };
 
-// `fast`: the fused tensor-core forward runs; its backward currently
-// recomputes the fp32 state with the exact kernels, so the workspace also
-// holds S.
+// `fast`: the tensor-core path (fused forward, two-kernel backward).  Its
+// saved buffer holds the bf16 states S_j; its workspace the device status
+// word and the bf16 state cotangents Sb_{j+1}.
 ChunkBufs carve_chunk(void* saved, void* ws, int BH, int N, int dh, int rule, int ns,
                       bool fast) {
   ChunkBufs b{};
   const size_t per = mats(static_cast<size_t>(BH) * N, dh);
   const size_t sc = static_cast<size_t>(BH) * N;
   Carver cs(saved);
-  if (fast) {
-    b.S_hist = reinterpret_cast<uint16_t*>(cs.take((per + 1) / 2));
-  } else {
-    b.S = cs.take(per);
-    b.M_hist = rule != 0 ? cs.take(per) : nullptr;
-    b.V_hist = rule == 2 ? cs.take(per) : nullptr;
-  }
-  b.saved_bytes = cs.used;
   Carver cw(ws);
   b.status = reinterpret_cast<uint32_t*>(cw.take(64));
   if (fast) {
-    b.S = cw.take(per);
-    b.M_hist = rule != 0 ? cw.take(per) : nullptr;
-    b.V_hist = rule == 2 ? cw.take(per) : nullptr;
+    b.S_hist = reinterpret_cast<uint16_t*>(cs.take((per + 1) / 2));
+    b.saved_bytes = cs.used;
+    b.Sbar_hist = reinterpret_cast<uint16_t*>(cw.take((per + 1) / 2));
+    b.ws_bytes = cw.used;
+    return b;
   }
+  b.S = cs.take(per);
+  b.M_hist = rule != 0 ? cs.take(per) : nullptr;
+  b.V_hist = rule == 2 ? cs.take(per) : nullptr;
+  b.saved_bytes = cs.used;
   b.Kw = cw.take(per);
   b.Uv = cw.take(per);
   b.gS = cw.take(per);
@@ -450,11 +449,15 @@ int gmdn_chunk_bwd_ex(const void* q, const void* k, const void* v, const float* 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaMemsetAsync(bufs.status, 0, sizeof(uint32_t), st);
   if (e != cudaSuccess) return cuda_fail(e, "status reset");
+  if (fast) {
+    GMDN_LAUNCH(gmdn::chunk_bwd1_tc(p, bufs.Sbar_hist, bufs.status, st), "chunk_bwd1_tc");
+    GMDN_LAUNCH(gmdn::chunk_bwd2_tc(p, bufs.S_hist, bufs.Sbar_hist, bufs.status, st),
+                "chunk_bwd2_tc");
+    return GMDN_OK;
+  }
   gmdn::ScanArgs sp = scan_args_from(p, bufs, ns);
-  // Kw, Uv and the chunk gate products are recomputed rather than saved; on
-  // the tensor-core path the fp32 states are recomputed as well.
+  // Kw, Uv and the chunk gate products are recomputed rather than saved.
   GMDN_LAUNCH(gmdn::chunk_prep_ieee(p, st), "chunk_prep");
-  if (fast) GMDN_LAUNCH(gmdn::scan_fwd_ieee(sp, st), "scan_fwd_ieee");
   GMDN_LAUNCH(gmdn::chunk_state_grad_ieee(p, st), "chunk_state_grad");
   GMDN_LAUNCH(gmdn::scan_bwd_ieee(sp, st), "scan_bwd_ieee");
   GMDN_LAUNCH(gmdn::chunk_token_grad_ieee(p, st), "chunk_token_grad");

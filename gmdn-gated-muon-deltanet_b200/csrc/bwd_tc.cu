@@ -1,0 +1,781 @@
+// Tensor-core backward of the mixer core, delta rule, dh = 128, C = 64.
+//
+// The backward is written in the residual form of the chunk update: with
+// E_j = v_j - k_j S_j^T (the errors of chunk j against the frozen state) the
+// reference's G_j = Uv_j - S_j Kw_j (fast_scan.py:82, train_ablation.py:
+// 164-165) equals E_j^T (w k_j), and o_j = Qt_j S_j^T + A_j v_j
+// (train_ablation.py:166-167, 186) equals q_j S_j^T + A_j E_j.  Its chain
+// rule gives, for the state cotangent Sb_{j+1} = dL/dS_{j+1}:
+//
+//   dE_j     = A_j^T dO_j + (w k_j) Sb_{j+1}^T
+//   Sb_j     = a_j Sb_{j+1} + dO_j^T q_j - dE_j^T k_j
+//   dv_j     = dE_j
+//   dq_j     = dO_j S_j + dP_j k_j,            dP = tril(dO E^T) * beta_col
+//   dk_j     = -dE_j S_j + w * (E_j Sb_{j+1}) + dP_j^T q_j
+//   dbeta_s  = sum_t tril(dO E^T)[t][s] P[t][s] + k_s . (E_j Sb_{j+1})_s
+//   dalpha_s = <Sb_{j+1}, S_j> a_j / alpha_s
+//
+// (identical to the reference's autograd of train_ablation.py:142-187 with
+// fast_scan.py:72-95; checked against it in tests/).
+//
+// bw1: one CTA per (b, h) walks the chunks in reverse and produces Sb_{j+1}
+//      for every chunk (bf16, for bw2).  The chain products use split bf16
+//      (hi + lo) operands for Sb and dE.
+// bw2: one CTA per (b, h, chunk) computes every token and gate gradient of
+//      its chunk from q, k, v, dO, S_j and Sb_{j+1}.
+
+#include <cuda.h>
+
+#include "common.cuh"
+#include "fast_path.h"
+#include "tc.cuh"
+
+namespace gmdn {
+namespace {
+
+using namespace tc;
+
+constexpr int kC = 64;
+constexpr int kD = 128;
+constexpr uint32_t P64 = 8192;
+constexpr uint32_t P128 = 16384;
+constexpr uint32_t HI16 = 16u << 16;
+
+struct BwArgs {
+  const float* beta;
+  const float* alpha;
+  uint16_t* Sbar_hist;
+  uint16_t *dq, *dk, *dv;
+  float *dalpha, *dbeta, *dmu, *dnu;
+  uint32_t* status;
+  int N, T;
+};
+
+// ===========================================================================
+// bw1: reverse chain
+// ===========================================================================
+
+constexpr int kThreads1 = 320;
+constexpr uint32_t B1_Q = 0;          // q: 2 stages x 16 KB
+constexpr uint32_t B1_K = 32768;      // k: 2 stages
+constexpr uint32_t B1_G = 65536;      // dO: 2 stages
+constexpr uint32_t B1_WK = 98304;     // w * k
+constexpr uint32_t B1_AS = 114688;    // A (bf16), 1 panel x 64 rows
+constexpr uint32_t B1_DEH = 122880;   // dE^T hi, 1 panel x 128 rows
+constexpr uint32_t B1_DEL = 139264;   // dE^T lo
+constexpr uint32_t B1_SH = 155648;    // Sb hi, 2 panels x 128 rows
+constexpr uint32_t B1_SL = 188416;    // Sb lo
+constexpr uint32_t B1_GATE = 221184;  // beta: 2 stages x 64 floats
+constexpr uint32_t B1_BAR = 221696;
+constexpr uint32_t B1_SMEM = B1_BAR + 256 + 1024;
+
+constexpr uint32_t T1_C0 = 0, T1_C1 = 128, T1_E = 256, T1_P = 320;
+
+struct Bars1 {
+  uint64_t ld_full[2], ld_empty[2];
+  uint64_t wk_full, p_full, as_full, de_full, de_smem;
+  uint64_t c_full[2], c_empty[2];
+  uint64_t s_full, final_mma;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(Bars1) <= 256, "barrier block");
+
+__global__ void __launch_bounds__(kThreads1, 1)
+chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_g, BwArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                           ~static_cast<uintptr_t>(1023));
+  Bars1* bars = reinterpret_cast<Bars1*>(sm + B1_BAR);
+  float* gate_beta = reinterpret_cast<float*>(sm + B1_GATE);
+  volatile int* ab = &bars->abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.x;
+  const int N = args.N;
+  uint32_t* status = args.status;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bars->ld_full[s], 1);
+      mbar_init(&bars->ld_empty[s], 1 + 128);
+      mbar_init(&bars->c_full[s], 1);
+      mbar_init(&bars->c_empty[s], 128);
+    }
+    mbar_init(&bars->wk_full, 128);
+    mbar_init(&bars->p_full, 1);
+    mbar_init(&bars->as_full, 128);
+    mbar_init(&bars->de_full, 1);
+    mbar_init(&bars->de_smem, 128);
+    mbar_init(&bars->s_full, 128);
+    mbar_init(&bars->final_mma, 1);
+    bars->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(&bars->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+  const size_t tok0 = static_cast<size_t>(bh) * args.T;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA, reverse chunk order
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < N; ++i) {
+        const int j = N - 1 - i, s = i & 1;
+        const int row = static_cast<int>(tok0) + j * kC;
+        if (!wait_free(&bars->ld_empty[s], i >> 1, status, ab)) break;
+        mbar_expect_tx(&bars->ld_full[s], 6 * 8192 + 256);
+        tma_load_2d(sm + B1_Q + s * 16384, &tm_q, 0, row, &bars->ld_full[s]);
+        tma_load_2d(sm + B1_Q + s * 16384 + P64, &tm_q, 64, row, &bars->ld_full[s]);
+        tma_load_2d(sm + B1_K + s * 16384, &tm_k, 0, row, &bars->ld_full[s]);
+        tma_load_2d(sm + B1_K + s * 16384 + P64, &tm_k, 64, row, &bars->ld_full[s]);
+        tma_load_2d(sm + B1_G + s * 16384, &tm_g, 0, row, &bars->ld_full[s]);
+        tma_load_2d(sm + B1_G + s * 16384 + P64, &tm_g, 64, row, &bars->ld_full[s]);
+        bulk_load(gate_beta + s * 64, args.beta + tok0 + j * kC, 256, &bars->ld_full[s]);
+        issued = i + 1;
+      }
+      int dummy = 0;
+      for (int i = issued - 2; i < issued; ++i)
+        if (i >= 0) mbar_wait(&bars->ld_full[i & 1], (i >> 1) & 1, status, &dummy);
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      const uint32_t wk_s = smem_u32(sm + B1_WK);
+      const uint32_t as_s = smem_u32(sm + B1_AS);
+      const uint32_t deh_s = smem_u32(sm + B1_DEH);
+      const uint32_t del_s = smem_u32(sm + B1_DEL);
+      const uint32_t sh_s = smem_u32(sm + B1_SH);
+      const uint32_t sl_s = smem_u32(sm + B1_SL);
+      constexpr uint32_t ID_P = idesc_bf16(64, 64, false, false);
+      constexpr uint32_t ID_Z = idesc_bf16(128, 128, true, true);
+      constexpr uint32_t ID_X = idesc_bf16(128, 64, true, true);
+      constexpr uint32_t ID_Y = idesc_bf16(128, 64, false, false);
+      constexpr uint32_t ID_W = idesc_bf16(128, 128, false, true, true);
+      auto stage = [&](uint32_t base, int i) { return smem_u32(sm + base + (i & 1) * 16384); };
+      // P(i) = q k^T of step i's chunk
+      auto issue_P = [&](int i) -> bool {
+        if (!wait_use(&bars->ld_full[i & 1], i >> 1, status, ab)) return false;
+        tc_fence_after();
+        for (int k = 0; k < 8; ++k)
+          mma_bf16(tmem + T1_P, desc_kmajor(stage(B1_Q, i), P64, k),
+                   desc_kmajor(stage(B1_K, i), P64, k), ID_P, k > 0);
+        mma_commit(&bars->p_full);
+        return true;
+      };
+      // Z(i): C = dO^T q;  X(i): E^T = dO^T A
+      auto issue_ZX = [&](int i) -> bool {
+        const int r = i & 1;
+        if (i >= 2 && !wait_use(&bars->c_empty[r], (i >> 1) - 1, status, ab)) return false;
+        tc_fence_after();
+        for (int k = 0; k < 4; ++k)
+          mma_bf16(tmem + (r ? T1_C1 : T1_C0), desc_mnmajor(stage(B1_G, i), P64, k),
+                   desc_mnmajor(stage(B1_Q, i), P64, k), ID_Z, k > 0);
+        if (!wait_use(&bars->as_full, i, status, ab)) return false;
+        tc_fence_after();
+        for (int k = 0; k < 4; ++k)
+          mma_bf16(tmem + T1_E, desc_mnmajor(stage(B1_G, i), P64, k),
+                   desc_mnmajor(as_s, P64, k), ID_X, k > 0);
+        return true;
+      };
+      bool ok = N > 0 && issue_P(0) && issue_ZX(0);
+      for (int i = 0; ok && i < N; ++i) {
+        const int r = i & 1;
+        // Y(i): E^T += Sb_hi (wk)^T + Sb_lo (wk)^T
+        if (!wait_use(&bars->s_full, i, status, ab)) break;
+        if (!wait_use(&bars->wk_full, i, status, ab)) break;
+        tc_fence_after();
+        for (int k = 0; k < 8; ++k)
+          mma_bf16(tmem + T1_E, desc_kmajor(sh_s, P128, k), desc_kmajor(wk_s, P64, k), ID_Y, 1);
+        for (int k = 0; k < 8; ++k)
+          mma_bf16(tmem + T1_E, desc_kmajor(sl_s, P128, k), desc_kmajor(wk_s, P64, k), ID_Y, 1);
+        mma_commit(&bars->de_full);
+        // W(i): C -= dE^T_hi k + dE^T_lo k
+        if (!wait_use(&bars->de_smem, i, status, ab)) break;
+        tc_fence_after();
+        const uint32_t k_s = stage(B1_K, i);
+        for (int k = 0; k < 4; ++k)
+          mma_bf16(tmem + (r ? T1_C1 : T1_C0), desc_kmajor(deh_s, P128, k),
+                   desc_mnmajor(k_s, P64, k), ID_W, 1);
+        for (int k = 0; k < 4; ++k)
+          mma_bf16(tmem + (r ? T1_C1 : T1_C0), desc_kmajor(del_s, P128, k),
+                   desc_mnmajor(k_s, P64, k), ID_W, 1);
+        mma_commit(&bars->c_full[r]);
+        mma_commit(&bars->ld_empty[i & 1]);
+        if (i + 1 < N && !(issue_P(i + 1) && issue_ZX(i + 1))) break;
+      }
+      mma_commit(&bars->final_mma);
+      int dummy = 0;
+      mbar_wait(&bars->final_mma, 0, status, &dummy);
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------------ state cotangent rows
+    const int c = warp * 32 + lane;
+    const uint32_t lb = tmem_lane_base(warp);
+    uint8_t* Sh = sm + B1_SH;
+    uint8_t* Sl = sm + B1_SL;
+    float sb[kD];
+#pragma unroll
+    for (int i = 0; i < kD; ++i) sb[i] = 0.f;
+    {
+      const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int c8 = 0; c8 < 16; ++c8) {
+        *reinterpret_cast<uint4*>(Sh + (c8 >> 3) * P128 + sw128_chunk(c, c8 & 7)) = z;
+        *reinterpret_cast<uint4*>(Sl + (c8 >> 3) * P128 + sw128_chunk(c, c8 & 7)) = z;
+      }
+      if (N > 0) {
+        uint4* g = reinterpret_cast<uint4*>(
+            args.Sbar_hist + (static_cast<size_t>(bh) * N + N - 1) * kD * kD +
+            static_cast<size_t>(c) * kD);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) g[i] = z;
+      }
+    }
+    fence_async_smem();
+    mbar_arrive(&bars->s_full);
+    for (int i = 0; i < N; ++i) {
+      const int j = N - 1 - i, r = i & 1;
+      const float* al = args.alpha + tok0 + j * kC;
+      const float la = logf(fmaxf(__ldg(al + lane), kGateFloor)) +
+                       logf(fmaxf(__ldg(al + lane + 32), kGateFloor));
+      const float a = expf(warp_sum(la));
+      if (!wait_use(&bars->c_full[r], i >> 1, status, ab)) break;
+      tc_fence_after();
+      const uint32_t rc = tmem + lb + (r ? T1_C1 : T1_C0);
+#pragma unroll
+      for (int cc = 0; cc < 8; cc += 2) {
+        float g0[16], g1[16];
+        tmem_ld16(rc + cc * 16, g0);
+        tmem_ld16(rc + cc * 16 + 16, g1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          sb[cc * 16 + t] = fmaf(a, sb[cc * 16 + t], g0[t]);
+          sb[cc * 16 + 16 + t] = fmaf(a, sb[cc * 16 + 16 + t], g1[t]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->c_empty[r]);
+      uint4* gdst = nullptr;
+      if (j >= 1)
+        gdst = reinterpret_cast<uint4*>(args.Sbar_hist +
+                                        (static_cast<size_t>(bh) * N + j - 1) * kD * kD +
+                                        static_cast<size_t>(c) * kD);
+#pragma unroll
+      for (int c8 = 0; c8 < 16; ++c8) {
+        float hi[8], lo[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const float x = sb[c8 * 8 + t];
+          hi[t] = __bfloat162float(__float2bfloat16_rn(x));
+          lo[t] = x - hi[t];
+        }
+        const uint4 wh = pack8(hi);
+        *reinterpret_cast<uint4*>(Sh + (c8 >> 3) * P128 + sw128_chunk(c, c8 & 7)) = wh;
+        *reinterpret_cast<uint4*>(Sl + (c8 >> 3) * P128 + sw128_chunk(c, c8 & 7)) = pack8(lo);
+        if (gdst) gdst[c8] = wh;
+      }
+      fence_async_smem();
+      mbar_arrive(&bars->s_full);
+    }
+  } else {
+    // ------------------------------------------------------------ chunk-local (warps 4-7)
+    const int tb = threadIdx.x - 128;
+    const int sp = warp - 4;
+    const uint32_t lb = tmem_lane_base(warp);
+    const int row = sp * 32 + lane;
+    const int t16 = sp * 16 + (lane & 15);
+    auto build_wk = [&](int i) -> bool {
+      const int s = i & 1;
+      if (!wait_use(&bars->ld_full[s], i >> 1, status, ab)) return false;
+      const uint8_t* ks = sm + B1_K + s * 16384;
+      uint8_t* wk = sm + B1_WK;
+      const float* bs = gate_beta + s * 64;
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        const int id = tb + 128 * m;
+        const uint32_t off = static_cast<uint32_t>(id) * 16u;
+        const float w = bs[(id & 511) >> 3];
+        const uint4 x = *reinterpret_cast<const uint4*>(ks + off);
+        uint4 y;
+        y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
+        y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
+        y.z = pack_bf16(bf16_lo(x.z) * w, bf16_hi(x.z) * w);
+        y.w = pack_bf16(bf16_lo(x.w) * w, bf16_hi(x.w) * w);
+        *reinterpret_cast<uint4*>(wk + off) = y;
+      }
+      fence_async_smem();
+      mbar_arrive(&bars->wk_full);
+      mbar_arrive(&bars->ld_empty[s]);
+      return true;
+    };
+    auto build_as = [&](int i) -> bool {
+      const float* bs = gate_beta + (i & 1) * 64;
+      if (!wait_use(&bars->p_full, i, status, ab)) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int cc = 0; cc < 4; cc += 2) {
+        float p0[16], p1[16];
+        tmem_ld16(tmem + lb + T1_P + cc * 16, p0);
+        tmem_ld16(tmem + lb + T1_P + cc * 16 + 16, p1);
+        tmem_ld_wait();
+        if (lane < 16) {
+          float v8[8];
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float* src = h < 2 ? p0 + h * 8 : p1 + (h - 2) * 8;
+#pragma unroll
+            for (int x = 0; x < 8; ++x) {
+              const int sc = cc * 16 + h * 8 + x;
+              v8[x] = (sc <= t16) ? src[x] * bs[sc] : 0.f;
+            }
+            st_row8(sm + B1_AS, P64, t16, cc * 2 + h, v8);
+          }
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars->as_full);
+      return true;
+    };
+    bool ok = N > 0 && build_wk(0) && build_as(0);
+    for (int i = 0; ok && i < N; ++i) {
+      // dE^T (lanes = value row c, 64 token columns) -> hi / lo bf16
+      if (!wait_use(&bars->de_full, i, status, ab)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int cc = 0; cc < 4; cc += 2) {
+        float x0[16], x1[16];
+        tmem_ld16(tmem + lb + T1_E + cc * 16, x0);
+        tmem_ld16(tmem + lb + T1_E + cc * 16 + 16, x1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float* src = h < 2 ? x0 + h * 8 : x1 + (h - 2) * 8;
+          float hi[8], lo[8];
+#pragma unroll
+          for (int x = 0; x < 8; ++x) {
+            hi[x] = __bfloat162float(__float2bfloat16_rn(src[x]));
+            lo[x] = src[x] - hi[x];
+          }
+          st_row8(sm + B1_DEH, P128, row, cc * 2 + h, hi);
+          st_row8(sm + B1_DEL, P128, row, cc * 2 + h, lo);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars->de_smem);
+      if (i + 1 < N && !(build_wk(i + 1) && build_as(i + 1))) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ===========================================================================
+// bw2: token and gate gradients of one chunk
+// ===========================================================================
+
+constexpr int kThreads2 = 160;
+constexpr uint32_t B2_Q = 0, B2_K = 16384, B2_V = 32768, B2_G = 49152;
+constexpr uint32_t B2_S = 65536;      // S_j, 2 panels x 128 rows
+constexpr uint32_t B2_SB = 98304;     // Sb_{j+1}
+constexpr uint32_t B2_AS = 131072;    // A bf16 [t][s]
+constexpr uint32_t B2_E = 139264;     // E bf16 [s][c]
+constexpr uint32_t B2_WK = 155648;    // w * k
+constexpr uint32_t B2_DE = 172032;    // dE bf16 [s][c]
+constexpr uint32_t B2_DP = 188416;    // dP bf16 [t][s]
+constexpr uint32_t B2_I = 196608;     // identity
+constexpr uint32_t B2_RED = 204800;   // fp32 [64][65]: dA * P per (t, s)
+constexpr uint32_t B2_GATE = 221440;  // beta[64], alpha[64], dw[64], misc
+constexpr uint32_t B2_BAR = 222720;
+constexpr uint32_t B2_SMEM = B2_BAR + 256 + 1024;
+
+constexpr uint32_t T2_X0 = 0, T2_X1 = 64, T2_X2 = 192, T2_X3 = 320;
+
+struct Bars2 {
+  uint64_t ld_full, ph1, ep1, wk_full, ph2, ep2, ph3;
+  uint32_t tmem_base;
+  int abort_flag;
+  float da;
+};
+
+__global__ void __launch_bounds__(kThreads2, 1)
+chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
+                    const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_sb,
+                    BwArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                           ~static_cast<uintptr_t>(1023));
+  Bars2* bars = reinterpret_cast<Bars2*>(sm + B2_BAR);
+  float* gbeta = reinterpret_cast<float*>(sm + B2_GATE);
+  float* galpha = gbeta + 64;
+  float* gdw = galpha + 64;
+  float* red = reinterpret_cast<float*>(sm + B2_RED);
+  volatile int* ab = &bars->abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int N = args.N;
+  const int bh = blockIdx.x / N, j = blockIdx.x % N;
+  const size_t tok = static_cast<size_t>(bh) * args.T + static_cast<size_t>(j) * kC;
+  const int srow = (bh * N + j) * kD;  // first row of S_j / Sb_{j+1} in the histories
+  uint32_t* status = args.status;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bars->ld_full, 1);
+    mbar_init(&bars->ph1, 1);
+    mbar_init(&bars->ep1, 128);
+    mbar_init(&bars->wk_full, 128);
+    mbar_init(&bars->ph2, 1);
+    mbar_init(&bars->ep2, 128);
+    mbar_init(&bars->ph3, 1);
+    bars->abort_flag = 0;
+    bars->da = 0.f;
+    fence_mbar_init();
+  }
+  build_identity64(sm + B2_I, threadIdx.x, kThreads2);
+  if (warp == 4) {
+    tmem_alloc(&bars->tmem_base, 512);
+    tmem_relinquish();
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      mbar_expect_tx(&bars->ld_full, 8 * 8192 + 4 * 16384 + 512);
+      tma_load_2d(sm + B2_Q, &tm_q, 0, static_cast<int>(tok), &bars->ld_full);
+      tma_load_2d(sm + B2_Q + P64, &tm_q, 64, static_cast<int>(tok), &bars->ld_full);
+      tma_load_2d(sm + B2_K, &tm_k, 0, static_cast<int>(tok), &bars->ld_full);
+      tma_load_2d(sm + B2_K + P64, &tm_k, 64, static_cast<int>(tok), &bars->ld_full);
+      tma_load_2d(sm + B2_V, &tm_v, 0, static_cast<int>(tok), &bars->ld_full);
+      tma_load_2d(sm + B2_V + P64, &tm_v, 64, static_cast<int>(tok), &bars->ld_full);
+      tma_load_2d(sm + B2_G, &tm_g, 0, static_cast<int>(tok), &bars->ld_full);
+      tma_load_2d(sm + B2_G + P64, &tm_g, 64, static_cast<int>(tok), &bars->ld_full);
+      tma_load_2d(sm + B2_S, &tm_s, 0, srow, &bars->ld_full);
+      tma_load_2d(sm + B2_S + P128, &tm_s, 64, srow, &bars->ld_full);
+      tma_load_2d(sm + B2_SB, &tm_sb, 0, srow, &bars->ld_full);
+      tma_load_2d(sm + B2_SB + P128, &tm_sb, 64, srow, &bars->ld_full);
+      bulk_load(gbeta, args.beta + tok, 256, &bars->ld_full);
+      bulk_load(galpha, args.alpha + tok, 256, &bars->ld_full);
+      const uint32_t q_s = smem_u32(sm + B2_Q), k_s = smem_u32(sm + B2_K);
+      const uint32_t v_s = smem_u32(sm + B2_V), g_s = smem_u32(sm + B2_G);
+      const uint32_t s_s = smem_u32(sm + B2_S), sb_s = smem_u32(sm + B2_SB);
+      const uint32_t as_s = smem_u32(sm + B2_AS), e_s = smem_u32(sm + B2_E);
+      const uint32_t wk_s = smem_u32(sm + B2_WK), de_s = smem_u32(sm + B2_DE);
+      const uint32_t dp_s = smem_u32(sm + B2_DP), id_s = smem_u32(sm + B2_I);
+      constexpr uint32_t ID_P = idesc_bf16(64, 64, false, false);
+      constexpr uint32_t ID_KM = idesc_bf16(64, 128, false, true);        // A K-major, B MN-major
+      constexpr uint32_t ID_KK = idesc_bf16(64, 128, false, false);       // both K-major
+      constexpr uint32_t ID_KKN = idesc_bf16(64, 128, false, false, true);
+      constexpr uint32_t ID_KMN = idesc_bf16(64, 128, false, true, true);
+      constexpr uint32_t ID_MM = idesc_bf16(64, 128, true, true);         // both MN-major
+      constexpr uint32_t ID_DA = idesc_bf16(64, 64, false, false);
+      bool ok = wait_use(&bars->ld_full, 0, status, ab);
+      if (ok) {
+        tc_fence_after();
+        // phase 1: P = q k^T; E = I v - k S^T; dQ = dO S
+        for (int k = 0; k < 8; ++k)
+          mma_bf16(tmem + T2_X0, desc_kmajor(q_s, P64, k), desc_kmajor(k_s, P64, k), ID_P, k > 0);
+        for (int k = 0; k < 4; ++k)
+          mma_bf16(tmem + T2_X1, desc_kmajor(id_s, P64, k), desc_mnmajor(v_s, P64, k), ID_KM, k > 0);
+        for (int k = 0; k < 8; ++k)
+          mma_bf16(tmem + T2_X1, desc_kmajor(k_s, P64, k), desc_kmajor(s_s, P128, k), ID_KKN, 1);
+        for (int k = 0; k < 8; ++k)
+          mma_bf16(tmem + HI16 + T2_X1, desc_kmajor(g_s, P64, k), desc_mnmajor(s_s, P128, k),
+                   ID_KM, k > 0);
+        mma_commit(&bars->ph1);
+      }
+      ok = ok && wait_use(&bars->ep1, 0, status, ab) && wait_use(&bars->wk_full, 0, status, ab);
+      if (ok) {
+        tc_fence_after();
+        // phase 2: dE = A^T dO + wk Sb^T;  dA = dO E^T;  dWk = E Sb
+        for (int k = 0; k < 4; ++k)
+          mma_bf16(tmem + T2_X2, desc_mnmajor(as_s, P64, k), desc_mnmajor(g_s, P64, k), ID_MM, k > 0);
+        for (int k = 0; k < 8; ++k)
+          mma_bf16(tmem + T2_X2, desc_kmajor(wk_s, P64, k), desc_kmajor(sb_s, P128, k), ID_KK, 1);
+        for (int k = 0; k < 8; ++k)
+          mma_bf16(tmem + HI16 + T2_X0, desc_kmajor(g_s, P64, k), desc_kmajor(e_s, P64, k), ID_DA,
+                   k > 0);
+        for (int k = 0; k < 8; ++k)
+          mma_bf16(tmem + HI16 + T2_X2, desc_kmajor(e_s, P64, k), desc_mnmajor(sb_s, P128, k),
+                   ID_KM, k > 0);
+        mma_commit(&bars->ph2);
+      }
+      ok = ok && wait_use(&bars->ep2, 0, status, ab);
+      if (ok) {
+        tc_fence_after();
+        // phase 3: dq += dP k;  dK = -dE S + dP^T q
+        for (int k = 0; k < 4; ++k)
+          mma_bf16(tmem + HI16 + T2_X1, desc_kmajor(dp_s, P64, k), desc_mnmajor(k_s, P64, k), ID_KM,
+                   1);
+        for (int k = 0; k < 8; ++k)
+          mma_bf16(tmem + T2_X3, desc_kmajor(de_s, P64, k), desc_mnmajor(s_s, P128, k), ID_KMN,
+                   k > 0);
+        for (int k = 0; k < 4; ++k)
+          mma_bf16(tmem + T2_X3, desc_mnmajor(dp_s, P64, k), desc_mnmajor(q_s, P64, k), ID_MM, 1);
+        mma_commit(&bars->ph3);
+        int dummy = 0;
+        mbar_wait(&bars->ph3, 0, status, &dummy);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue warps 0-3
+    const int tid = threadIdx.x;               // 0..127
+    const uint32_t lb = tmem_lane_base(warp);
+    const bool hi = lane >= 16;
+    const int r16 = warp * 16 + (lane & 15);   // M=64 row of this lane's accumulator
+    bool ok = wait_use(&bars->ld_full, 0, status, ab);
+    if (ok) {
+      // w * k (delta: w = beta)
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        const int id = tid + 128 * m;
+        const uint32_t off = static_cast<uint32_t>(id) * 16u;
+        const float w = gbeta[(id & 511) >> 3];
+        const uint4 x = *reinterpret_cast<const uint4*>(sm + B2_K + off);
+        uint4 y;
+        y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
+        y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
+        y.z = pack_bf16(bf16_lo(x.z) * w, bf16_hi(x.z) * w);
+        y.w = pack_bf16(bf16_lo(x.w) * w, bf16_hi(x.w) * w);
+        *reinterpret_cast<uint4*>(sm + B2_WK + off) = y;
+      }
+      fence_async_smem();
+      mbar_arrive(&bars->wk_full);
+      // da = <Sb_{j+1}, S_j> (row tid of both)
+      float part = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < 16; ++c8) {
+        float a8[8], b8[8];
+        unpack8(ld_row8(sm + B2_S, P128, tid, c8), a8);
+        unpack8(ld_row8(sm + B2_SB, P128, tid, c8), b8);
+#pragma unroll
+        for (int x = 0; x < 8; ++x) part = fmaf(a8[x], b8[x], part);
+      }
+      part = warp_sum(part);
+      if (lane == 0) atomicAdd(&bars->da, part);
+    }
+    // ---- epilogue 1: A = tril(P) beta, E -> bf16 (rows of lanes 0-15)
+    ok = ok && wait_use(&bars->ph1, 0, status, ab);
+    if (ok) {
+      tc_fence_after();
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        float p[16];
+        tmem_ld16(tmem + lb + T2_X0 + cc * 16, p);
+        tmem_ld_wait();
+        if (!hi) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float v8[8];
+#pragma unroll
+            for (int x = 0; x < 8; ++x) {
+              const int sc = cc * 16 + h * 8 + x;
+              v8[x] = (sc <= r16) ? p[h * 8 + x] * gbeta[sc] : 0.f;
+            }
+            st_row8(sm + B2_AS, P64, r16, cc * 2 + h, v8);
+          }
+        }
+      }
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        float e[16];
+        tmem_ld16(tmem + lb + T2_X1 + cc * 16, e);
+        tmem_ld_wait();
+        if (!hi) {
+          st_row8(sm + B2_E, P64, r16, cc * 2, e);
+          st_row8(sm + B2_E, P64, r16, cc * 2 + 1, e + 8);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars->ep1);
+    }
+    // ---- epilogue 2: dE -> bf16 + dv; dP = tril(dA) beta; dbeta pieces; dw
+    ok = ok && wait_use(&bars->ph2, 0, status, ab);
+    if (ok) {
+      tc_fence_after();
+      // X0: P (lanes 0-15) and dA (lanes 16-31) of the same row t = r16
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        float x[16];
+        tmem_ld16(tmem + lb + T2_X0 + cc * 16, x);
+        tmem_ld_wait();
+        float other[16];
+#pragma unroll
+        for (int y = 0; y < 16; ++y) other[y] = __shfl_xor_sync(0xffffffffu, x[y], 16);
+        if (hi) {  // x = dA row t, other = P row t
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float v8[8];
+#pragma unroll
+            for (int y = 0; y < 8; ++y) {
+              const int sc = cc * 16 + h * 8 + y;
+              const float dam = (sc <= r16) ? x[h * 8 + y] : 0.f;
+              v8[y] = dam * gbeta[sc];
+              red[r16 * 65 + sc] = dam * other[h * 8 + y];
+            }
+            st_row8(sm + B2_DP, P64, r16, cc * 2 + h, v8);
+          }
+        }
+      }
+      // X2: dE (lanes 0-15) and dWk (lanes 16-31), row s = r16
+      uint4* dvp = reinterpret_cast<uint4*>(args.dv) + ((tok + r16) * kD) / 8;
+      float dw = 0.f;
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        float x[16];
+        tmem_ld16(tmem + lb + T2_X2 + cc * 16, x);
+        tmem_ld_wait();
+        if (!hi) {
+          st_row8(sm + B2_DE, P64, r16, cc * 2, x);
+          st_row8(sm + B2_DE, P64, r16, cc * 2 + 1, x + 8);
+          dvp[cc * 2] = pack8(x);
+          dvp[cc * 2 + 1] = pack8(x + 8);
+        } else {
+          float k8[8];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            unpack8(ld_row8(sm + B2_K, P64, r16, cc * 2 + h), k8);
+#pragma unroll
+            for (int y = 0; y < 8; ++y) dw = fmaf(k8[y], x[h * 8 + y], dw);
+          }
+        }
+      }
+      if (hi) gdw[r16] = dw;
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bars->ep2);
+    }
+    // ---- epilogue 3: dq, dk, gate gradients
+    ok = ok && wait_use(&bars->ph3, 0, status, ab);
+    if (ok) {
+      tc_fence_after();
+      const float w = gbeta[r16];
+      uint4* dqp = reinterpret_cast<uint4*>(args.dq) + ((tok + r16) * kD) / 8;
+      uint4* dkp = reinterpret_cast<uint4*>(args.dk) + ((tok + r16) * kD) / 8;
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        float x1[16], x2[16], x3[16];
+        tmem_ld16(tmem + lb + T2_X1 + cc * 16, x1);   // dq at lanes 16-31
+        tmem_ld16(tmem + lb + T2_X2 + cc * 16, x2);   // dWk at lanes 16-31
+        tmem_ld16(tmem + lb + T2_X3 + cc * 16, x3);   // dK part at lanes 0-15
+        tmem_ld_wait();
+        float dwk[16];
+#pragma unroll
+        for (int y = 0; y < 16; ++y) dwk[y] = __shfl_xor_sync(0xffffffffu, x2[y], 16);
+        if (hi) {
+          dqp[cc * 2] = pack8(x1);
+          dqp[cc * 2 + 1] = pack8(x1 + 8);
+        } else {
+#pragma unroll
+          for (int y = 0; y < 16; ++y) x3[y] = fmaf(w, dwk[y], x3[y]);
+          dkp[cc * 2] = pack8(x3);
+          dkp[cc * 2 + 1] = pack8(x3 + 8);
+        }
+      }
+    }
+    named_sync(1, 128);
+    if (ok && tid < kC) {
+      const int s = tid;
+      float db = gdw[s];
+      for (int t = s; t < kC; ++t) db += red[t * 65 + s];
+      float la = 0.f;
+      for (int t = 0; t < kC; ++t) la += logf(fmaxf(galpha[t], kGateFloor));
+      const float a_c = expf(la);
+      const float al = galpha[s];
+      const size_t g = tok + s;
+      args.dbeta[g] = db;
+      args.dalpha[g] = (al >= kGateFloor) ? bars->da * a_c / fmaxf(al, kGateFloor) : 0.f;
+      args.dmu[g] = 0.f;
+      if (args.dnu) args.dnu[g] = 0.f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+bool chunk_bwd_tc_supported(const ChunkArgs& p) { return chunk_fwd_tc_supported(p); }
+
+size_t chunk_bwd_tc_workspace_bytes(int BH, int N) {
+  return static_cast<size_t>(BH) * N * kD * kD * sizeof(uint16_t);
+}
+
+cudaError_t chunk_bwd1_tc(const ChunkArgs& p, uint16_t* Sbar_hist, uint32_t* status,
+                          cudaStream_t st) {
+  CUtensorMap mq, mk, mg;
+  const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
+  cudaError_t e;
+  if ((e = make_tmap_rows128(&mq, p.q, rows, 64)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mk, p.k, rows, 64)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mg, p.dO, rows, 64)) != cudaSuccess) return e;
+  BwArgs a{};
+  a.beta = p.beta;
+  a.alpha = p.alpha;
+  a.Sbar_hist = Sbar_hist;
+  a.status = status;
+  a.N = p.N;
+  a.T = p.T;
+  e = cudaFuncSetAttribute(chunk_bwd1_tc_delta, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           B1_SMEM);
+  if (e != cudaSuccess) return e;
+  chunk_bwd1_tc_delta<<<p.BH, kThreads1, B1_SMEM, st>>>(mq, mk, mg, a);
+  return cudaGetLastError();
+}
+
+cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const uint16_t* S_hist, const uint16_t* Sbar_hist,
+                          uint32_t* status, cudaStream_t st) {
+  CUtensorMap mq, mk, mv, mg, ms, msb;
+  const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
+  const uint64_t srows = static_cast<uint64_t>(p.BH) * p.N * kD;
+  cudaError_t e;
+  if ((e = make_tmap_rows128(&mq, p.q, rows, 64)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mk, p.k, rows, 64)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mv, p.v, rows, 64)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mg, p.dO, rows, 64)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&ms, S_hist, srows, 128)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&msb, Sbar_hist, srows, 128)) != cudaSuccess) return e;
+  BwArgs a{};
+  a.beta = p.beta;
+  a.alpha = p.alpha;
+  a.dq = static_cast<uint16_t*>(p.dq);
+  a.dk = static_cast<uint16_t*>(p.dk);
+  a.dv = static_cast<uint16_t*>(p.dv);
+  a.dalpha = p.dalpha;
+  a.dbeta = p.dbeta;
+  a.dmu = p.dmu;
+  a.dnu = p.dnu;
+  a.status = status;
+  a.N = p.N;
+  a.T = p.T;
+  e = cudaFuncSetAttribute(chunk_bwd2_tc_delta, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           B2_SMEM);
+  if (e != cudaSuccess) return e;
+  chunk_bwd2_tc_delta<<<p.BH * p.N, kThreads2, B2_SMEM, st>>>(mq, mk, mv, mg, ms, msb, a);
+  return cudaGetLastError();
+}
+
+}  // namespace gmdn

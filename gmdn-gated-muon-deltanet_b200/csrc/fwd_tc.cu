@@ -5,22 +5,26 @@
 //
 //   A(j)  Kw_j = k^T (w k)      M128 N128 K64   -> TMEM RK
 //         Uv_j = v^T (w k)      M128 N128 K64   -> TMEM RU[j%2]
-//         P_j  = q k^T          M64  N64  K128  -> TMEM RPQ
-//   B(j)  Qt_j^T = q^T I - k^T A_j^T            -> TMEM RPQ  (A_j = tril(P_j) * beta)
-//   C(j)  G_j = Uv_j - S_j Kw_j  (S_j = hi + lo, two bf16 passes)   -> RU[j%2]
-//   D(j)  o_j^T = S_j Qt_j^T + v^T A_j^T        -> TMEM RO
+//         P_j  = q k^T          M64  N64  K128  -> TMEM RX, lanes 0-15
+//   B(j)  Qt_j = I q - A_j k    M64  N128 K64   -> TMEM RX, lanes 0-15
+//         (A_j = tril(P_j) * beta_col, bf16 in shared memory)
+//   C(j)  G_j = Uv_j - S_j Kw_j (S_j = hi + lo, two bf16 passes) -> RU[j%2]
+//   D(j)  o_j = Qt_j S_j^T + A_j v_j   M64 N128 -> TMEM RX, lanes 16-31
 //   state S_{j+1} = a_j S_j + G_j  (fp32, in registers of warps 0-3)
 //
+// The MMA thread issues C(j), D(j), A(j+1), B(j+1) per step, so the next
+// chunk's loads and products overlap the sequential state update.
+//
 // Warp roles (320 threads): warps 0-3 own the fp32 state (one row of S per
-// thread) and run the sequential update; warps 4-7 drain the chunk-local
-// accumulators (Kw, P -> A, Qt, o) and build w*k; warp 8 issues TMA loads;
-// warp 9 allocates TMEM and issues every MMA from one thread.  All
-// hand-offs are mbarriers; every wait is bounded (tc.cuh) and a timeout
-// sets the status word and unwinds all roles.
+// thread), run the sequential update and store o; warps 4-7 drain the
+// chunk-local accumulators (Kw, P -> A, Qt) and build w*k; warp 8 issues TMA
+// loads; warp 9 allocates TMEM and issues every MMA from one thread.  All
+// hand-offs are mbarriers; every wait is bounded (tc.cuh) and a timeout sets
+// the status word and unwinds all roles.
 //
 // Bytes per chunk-head: q, k, v in (48 KB), o out (16 KB), S_j bf16 out for
 // the backward (32 KB).  Tensor work per chunk-head: 2*2*C*d^2 (Kw, Uv) +
-// 2*C^2*d (P) + 2*(C*d*C) (Qt) + 2*2*d^3 (state, hi+lo) + 2*(C*d^2 + C^2*d) (o).
+// 2*C^2*d (P) + 2*C^2*d (Qt) + 2*2*d^3 (state, hi+lo) + 2*(C*d^2 + C^2*d) (o).
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -56,8 +60,10 @@ constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr uint32_t P64 = 8192;    // panel stride of a 64-row tile
 constexpr uint32_t P128 = 16384;  // panel stride of a 128-row tile
 
-// TMEM columns
-constexpr uint32_t TM_U0 = 0, TM_U1 = 128, TM_K = 256, TM_PQ = 384, TM_O = 448;
+// TMEM columns.  RX holds two M=64 accumulators side by side: lanes 0-15 of
+// every subpartition for P / Qt, lanes 16-31 for o.
+constexpr uint32_t TM_U0 = 0, TM_U1 = 128, TM_K = 256, TM_X = 384;
+constexpr uint32_t TM_HI16 = 16u << 16;  // lane offset of the upper half
 
 struct Bars {
   uint64_t q_full, q_empty;
@@ -87,19 +93,6 @@ __device__ __forceinline__ bool wait_full(uint64_t* b, int use, uint32_t* st, Ba
 }
 __device__ __forceinline__ bool wait_empty(uint64_t* b, int use, uint32_t* st, Bars* B) {
   return mbar_wait(b, (static_cast<uint32_t>(use) & 1u) ^ 1u, st, &B->abort_flag);
-}
-
-// Write 8 floats of row `row`, columns [col8*8, col8*8+8) of a 2-panel bf16
-// tile (64 columns per panel) as one 16-byte swizzled chunk.
-__device__ __forceinline__ void st_row8(uint8_t* tile, uint32_t panel_stride, int row, int col8,
-                                        const float* v) {
-  uint4 w;
-  w.x = pack_bf16(v[0], v[1]);
-  w.y = pack_bf16(v[2], v[3]);
-  w.z = pack_bf16(v[4], v[5]);
-  w.w = pack_bf16(v[6], v[7]);
-  uint8_t* p = tile + (col8 >> 3) * panel_stride + sw128_chunk(row, col8 & 7);
-  *reinterpret_cast<uint4*>(p) = w;
 }
 
 __global__ void __launch_bounds__(kThreadsTc, 1)
@@ -138,21 +131,7 @@ chunk_fwd_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     bars->abort_flag = 0;
     fence_mbar_init();
   }
-  // 64 x 64 identity (bf16 1.0 = 0x3F80) in the SW128 layout
-  for (int r = threadIdx.x; r < 64; r += kThreadsTc) {
-    for (int c8 = 0; c8 < 8; ++c8) {
-      uint4 w = make_uint4(0, 0, 0, 0);
-      if ((r >> 3) == c8) {
-        const uint32_t one = 0x3F80u << (16 * (r & 1));
-        const int word = (r & 7) >> 1;
-        if (word == 0) w.x = one;
-        if (word == 1) w.y = one;
-        if (word == 2) w.z = one;
-        if (word == 3) w.w = one;
-      }
-      *reinterpret_cast<uint4*>(sm + OFF_I + sw128_chunk(r, c8)) = w;
-    }
-  }
+  build_identity64(sm + OFF_I, threadIdx.x, kThreadsTc);
   if (warp == 9) {
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
@@ -206,42 +185,51 @@ chunk_fwd_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       const uint32_t kw_s = smem_u32(sm + OFF_KW);
       constexpr uint32_t ID_KW = idesc_bf16(128, 128, true, true);
       constexpr uint32_t ID_P = idesc_bf16(64, 64, false, false);
-      constexpr uint32_t ID_QT = idesc_bf16(128, 64, true, false);
-      constexpr uint32_t ID_QTN = idesc_bf16(128, 64, true, false, true);
+      constexpr uint32_t ID_QT = idesc_bf16(64, 128, false, true);
+      constexpr uint32_t ID_QTN = idesc_bf16(64, 128, false, true, true);
       constexpr uint32_t ID_SC = idesc_bf16(128, 128, false, true, true);
-      constexpr uint32_t ID_O1 = idesc_bf16(128, 64, false, false);
-      constexpr uint32_t ID_O2 = idesc_bf16(128, 64, true, false);
-      for (int j = 0; j < N; ++j) {
-        const int s = j & 1;
+      constexpr uint32_t ID_O1 = idesc_bf16(64, 128, false, false);
+      constexpr uint32_t ID_O2 = idesc_bf16(64, 128, false, true);
+      // A(jj): Kw, Uv, P of chunk jj
+      auto issue_A = [&](int jj) -> bool {
+        const int s = jj & 1;
         const uint32_t k_s = smem_u32(sm + OFF_K + s * 16384);
         const uint32_t v_s = smem_u32(sm + OFF_V + s * 16384);
-        const uint32_t ru = tmem + (s ? TM_U1 : TM_U0);
-        // A(j)
-        if (!wait_full(&bars->kv_full[s], j >> 1, status, bars)) break;
-        if (!wait_full(&bars->q_full, j, status, bars)) break;
-        if (!wait_full(&bars->wk_full, j, status, bars)) break;
-        if (j >= 2 && !wait_full(&bars->g_empty[s], (j >> 1) - 1, status, bars)) break;
-        if (j >= 1 && !wait_full(&bars->kw_smem, j - 1, status, bars)) break;
-        if (j >= 1 && !wait_full(&bars->qt_smem, j - 1, status, bars)) break;
+        if (!wait_full(&bars->kv_full[s], jj >> 1, status, bars)) return false;
+        if (!wait_full(&bars->q_full, jj, status, bars)) return false;
+        if (!wait_full(&bars->wk_full, jj, status, bars)) return false;
+        if (jj >= 2 && !wait_full(&bars->g_empty[s], (jj >> 1) - 1, status, bars)) return false;
         tc_fence_after();
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + TM_K, desc_mnmajor(k_s, P64, k), desc_mnmajor(wk_s, P64, k), ID_KW, k > 0);
         for (int k = 0; k < 4; ++k)
-          mma_bf16(ru, desc_mnmajor(v_s, P64, k), desc_mnmajor(wk_s, P64, k), ID_KW, k > 0);
+          mma_bf16(tmem + (s ? TM_U1 : TM_U0), desc_mnmajor(v_s, P64, k),
+                   desc_mnmajor(wk_s, P64, k), ID_KW, k > 0);
         for (int k = 0; k < 8; ++k)
-          mma_bf16(tmem + TM_PQ, desc_kmajor(q_s, P64, k), desc_kmajor(k_s, P64, k), ID_P, k > 0);
+          mma_bf16(tmem + TM_X, desc_kmajor(q_s, P64, k), desc_kmajor(k_s, P64, k), ID_P, k > 0);
         mma_commit(&bars->kwp_full);
         mma_commit(&bars->wk_empty);
-        // B(j): Qt^T = q^T I - k^T A^T
-        if (!wait_full(&bars->as_full, j, status, bars)) break;
+        return true;
+      };
+      // B(jj): Qt = I q - A k
+      auto issue_B = [&](int jj) -> bool {
+        const uint32_t k_s = smem_u32(sm + OFF_K + (jj & 1) * 16384);
+        if (!wait_full(&bars->as_full, jj, status, bars)) return false;
         tc_fence_after();
         for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + TM_PQ, desc_mnmajor(q_s, P64, k), desc_kmajor(id_s, P64, k), ID_QT, k > 0);
+          mma_bf16(tmem + TM_X, desc_kmajor(id_s, P64, k), desc_mnmajor(q_s, P64, k), ID_QT, k > 0);
         for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + TM_PQ, desc_mnmajor(k_s, P64, k), desc_kmajor(as_s, P64, k), ID_QTN, 1);
+          mma_bf16(tmem + TM_X, desc_kmajor(as_s, P64, k), desc_mnmajor(k_s, P64, k), ID_QTN, 1);
         mma_commit(&bars->qt_full);
         mma_commit(&bars->q_empty);
-        // C(j): G = Uv - S_hi Kw - S_lo Kw (Kw read MN-major: B[a][b] = Kw[a][b])
+        return true;
+      };
+      bool ok = N > 0 && issue_A(0) && issue_B(0);
+      for (int j = 0; ok && j < N; ++j) {
+        const int s = j & 1;
+        const uint32_t v_s = smem_u32(sm + OFF_V + s * 16384);
+        const uint32_t ru = tmem + (s ? TM_U1 : TM_U0);
+        // C(j): G = Uv - S_hi Kw - S_lo Kw  (Kw read MN-major: B[a][b] = Kw[a][b])
         if (!wait_full(&bars->kw_smem, j, status, bars)) break;
         if (!wait_full(&bars->s_full, j, status, bars)) break;
         tc_fence_after();
@@ -250,16 +238,19 @@ chunk_fwd_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         for (int k = 0; k < 8; ++k)
           mma_bf16(ru, desc_kmajor(sl_s, P128, k), desc_mnmajor(kw_s, P128, k), ID_SC, 1);
         mma_commit(&bars->g_full[s]);
-        // D(j): o^T = S_hi Qt^T + v^T A^T
+        // D(j): o = Qt S_hi^T + A v  (lanes 16-31 of RX)
         if (!wait_full(&bars->qt_smem, j, status, bars)) break;
         if (!wait_empty(&bars->o_empty, j, status, bars)) break;
         tc_fence_after();
         for (int k = 0; k < 8; ++k)
-          mma_bf16(tmem + TM_O, desc_kmajor(sh_s, P128, k), desc_kmajor(qt_s, P64, k), ID_O1, k > 0);
+          mma_bf16(tmem + TM_HI16 + TM_X, desc_kmajor(qt_s, P64, k), desc_kmajor(sh_s, P128, k),
+                   ID_O1, k > 0);
         for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + TM_O, desc_mnmajor(v_s, P64, k), desc_kmajor(as_s, P64, k), ID_O2, 1);
+          mma_bf16(tmem + TM_HI16 + TM_X, desc_kmajor(as_s, P64, k), desc_mnmajor(v_s, P64, k),
+                   ID_O2, 1);
         mma_commit(&bars->o_full);
         mma_commit(&bars->kv_empty[s]);
+        if (j + 1 < N && !(issue_A(j + 1) && issue_B(j + 1))) break;
       }
       // every MMA issued so far has completed before TMEM is released
       mma_commit(&bars->final_mma);
@@ -267,7 +258,7 @@ chunk_fwd_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       mbar_wait(&bars->final_mma, 0, status, &dummy);
     }
   } else if (warp < 4) {
-    // ------------------------------------------------------------ state (rows of S)
+    // ------------------------------------------------------------ state rows, o store
     const int c = warp * 32 + lane;  // row of S = TMEM lane
     const uint32_t lb = tmem_lane_base(warp);
     uint8_t* Sh = sm + OFF_SH;
@@ -299,12 +290,16 @@ chunk_fwd_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       tc_fence_after();
       const uint32_t ru = tmem + lb + (s ? TM_U1 : TM_U0);
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        float g[16];
-        tmem_ld16(ru + cc * 16, g);
+      for (int cc = 0; cc < 8; cc += 2) {
+        float g0[16], g1[16];
+        tmem_ld16(ru + cc * 16, g0);
+        tmem_ld16(ru + cc * 16 + 16, g1);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) st[cc * 16 + i] = fmaf(a, st[cc * 16 + i], g[i]);
+        for (int i = 0; i < 16; ++i) {
+          st[cc * 16 + i] = fmaf(a, st[cc * 16 + i], g0[i]);
+          st[cc * 16 + 16 + i] = fmaf(a, st[cc * 16 + 16 + i], g1[i]);
+        }
       }
       tc_fence_before();
       mbar_arrive(&bars->g_empty[s]);
@@ -324,19 +319,35 @@ chunk_fwd_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
           hi[i] = __bfloat162float(__float2bfloat16_rn(x));
           lo[i] = x - hi[i];
         }
-        st_row8(Sh, P128, c, c8, hi);
-        st_row8(Sl, P128, c, c8, lo);
-        if (gdst) {
-          uint4 w;
-          w.x = pack_bf16(hi[0], hi[1]);
-          w.y = pack_bf16(hi[2], hi[3]);
-          w.z = pack_bf16(hi[4], hi[5]);
-          w.w = pack_bf16(hi[6], hi[7]);
-          gdst[c8] = w;
-        }
+        const uint4 wh = pack8(hi);
+        *reinterpret_cast<uint4*>(Sh + (c8 >> 3) * P128 + sw128_chunk(c, c8 & 7)) = wh;
+        *reinterpret_cast<uint4*>(Sl + (c8 >> 3) * P128 + sw128_chunk(c, c8 & 7)) = pack8(lo);
+        if (gdst) gdst[c8] = wh;
       }
       fence_async_smem();
       mbar_arrive(&bars->s_full);
+      // o rows: lanes 16-31 of each subpartition hold row 16*warp + lane - 16
+      tc_fence_after();
+      {
+        const int t = warp * 16 + (lane & 15);
+        uint4* odst = reinterpret_cast<uint4*>(args.o) +
+                      ((tok0 + static_cast<size_t>(j) * kC + t) * kD) / 8;
+#pragma unroll
+        for (int cc = 0; cc < 8; cc += 2) {
+          float x0[16], x1[16];
+          tmem_ld16(tmem + lb + TM_X + cc * 16, x0);
+          tmem_ld16(tmem + lb + TM_X + cc * 16 + 16, x1);
+          tmem_ld_wait();
+          if (lane >= 16) {
+            odst[cc * 2 + 0] = pack8(x0);
+            odst[cc * 2 + 1] = pack8(x0 + 8);
+            odst[cc * 2 + 2] = pack8(x1);
+            odst[cc * 2 + 3] = pack8(x1 + 8);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bars->o_empty);
     }
   } else {
     // ------------------------------------------------------------ chunk-local (warps 4-7)
@@ -344,8 +355,8 @@ chunk_fwd_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     const int sp = warp - 4;                   // TMEM subpartition
     const uint32_t lb = tmem_lane_base(warp);
     const int row = sp * 32 + lane;            // TMEM lane of this thread
-    bool ok = true;
-    // w * k for chunk jj (delta: w = beta)
+    const int t16 = sp * 16 + (lane & 15);     // M=64 row of lanes 0-15
+    // E1: w * k for chunk jj (delta: w = beta)
     auto build_wk = [&](int jj) -> bool {
       const int s = jj & 1;
       if (!wait_full(&bars->kv_full[s], jj >> 1, status, bars)) return false;
@@ -357,9 +368,8 @@ chunk_fwd_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       for (int m = 0; m < 8; ++m) {
         const int id = tb + 128 * m;            // 16-byte chunk id, 0..1023
         const uint32_t off = static_cast<uint32_t>(id) * 16u;
-        const int r = (id & 511) >> 3;          // row inside the panel
-        const float w = bs[r];
-        uint4 x = *reinterpret_cast<const uint4*>(ks + off);
+        const float w = bs[(id & 511) >> 3];    // row inside the panel
+        const uint4 x = *reinterpret_cast<const uint4*>(ks + off);
         uint4 y;
         y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
         y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
@@ -372,91 +382,78 @@ chunk_fwd_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       mbar_arrive(&bars->kv_empty[s]);
       return true;
     };
-    if (N > 0) ok = build_wk(0);
-    for (int j = 0; ok && j < N; ++j) {
-      const int s = j & 1;
-      const float* bs = gate_beta + s * 64;
-      // E2: P -> A = tril(P) * beta (bf16)
-      if (!wait_full(&bars->kwp_full, j, status, bars)) break;
-      if (j >= 1 && !wait_full(&bars->o_full, j - 1, status, bars)) break;
+    // E2: P -> A = tril(P) * beta (bf16)
+    auto build_as = [&](int jj) -> bool {
+      const float* bs = gate_beta + (jj & 1) * 64;
+      if (!wait_full(&bars->kwp_full, jj, status, bars)) return false;
+      if (jj >= 1 && !wait_full(&bars->o_full, jj - 1, status, bars)) return false;
       tc_fence_after();
-      {
-        const int t = sp * 16 + (lane & 15);
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          float p[16];
-          tmem_ld16(tmem + lb + TM_PQ + cc * 16, p);
-          tmem_ld_wait();
-          if (lane < 16) {
+      for (int cc = 0; cc < 4; cc += 2) {
+        float p0[16], p1[16];
+        tmem_ld16(tmem + lb + TM_X + cc * 16, p0);
+        tmem_ld16(tmem + lb + TM_X + cc * 16 + 16, p1);
+        tmem_ld_wait();
+        if (lane < 16) {
+          float v8[8];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              float v8[8];
+          for (int h = 0; h < 4; ++h) {
+            const float* src = h < 2 ? p0 + h * 8 : p1 + (h - 2) * 8;
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const int sc = cc * 16 + h * 8 + i;
-                v8[i] = (sc <= t) ? p[h * 8 + i] * bs[sc] : 0.f;
-              }
-              st_row8(sm + OFF_AS, P64, t, cc * 2 + h, v8);
+            for (int i = 0; i < 8; ++i) {
+              const int sc = cc * 16 + h * 8 + i;
+              v8[i] = (sc <= t16) ? src[i] * bs[sc] : 0.f;
             }
+            st_row8(sm + OFF_AS, P64, t16, cc * 2 + h, v8);
           }
         }
       }
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->as_full);
+      return true;
+    };
+    bool ok = N > 0 && build_wk(0) && build_as(0);
+    for (int j = 0; ok && j < N; ++j) {
       // E0: Kw -> bf16 shared (row a = lane row, all 128 columns)
+      if (!wait_full(&bars->kwp_full, j, status, bars)) break;
       if (j >= 1 && !wait_full(&bars->g_full[(j - 1) & 1], (j - 1) >> 1, status, bars)) break;
       tc_fence_after();
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        float x[16];
-        tmem_ld16(tmem + lb + TM_K + cc * 16, x);
+      for (int cc = 0; cc < 8; cc += 2) {
+        float x0[16], x1[16];
+        tmem_ld16(tmem + lb + TM_K + cc * 16, x0);
+        tmem_ld16(tmem + lb + TM_K + cc * 16 + 16, x1);
         tmem_ld_wait();
-        st_row8(sm + OFF_KW, P128, row, cc * 2, x);
-        st_row8(sm + OFF_KW, P128, row, cc * 2 + 1, x + 8);
+        st_row8(sm + OFF_KW, P128, row, cc * 2, x0);
+        st_row8(sm + OFF_KW, P128, row, cc * 2 + 1, x0 + 8);
+        st_row8(sm + OFF_KW, P128, row, cc * 2 + 2, x1);
+        st_row8(sm + OFF_KW, P128, row, cc * 2 + 3, x1 + 8);
       }
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->kw_smem);
-      // E3: Qt^T (lane = d, columns = t) -> Qt[t][d] bf16
+      // E3: Qt (lanes 0-15, row t, 128 columns) -> bf16 shared
       if (!wait_full(&bars->qt_full, j, status, bars)) break;
+      if (j >= 1 && !wait_full(&bars->o_full, j - 1, status, bars)) break;
       tc_fence_after();
-      {
-        uint8_t* qt = sm + OFF_QT + (row >> 6) * P64;
-        const int dcol = row & 63;
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          float x[16];
-          tmem_ld16(tmem + lb + TM_PQ + cc * 16, x);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            *reinterpret_cast<__nv_bfloat16*>(qt + sw128_elem(cc * 16 + i, dcol)) =
-                __float2bfloat16_rn(x[i]);
+      for (int cc = 0; cc < 8; cc += 2) {
+        float x0[16], x1[16];
+        tmem_ld16(tmem + lb + TM_X + cc * 16, x0);
+        tmem_ld16(tmem + lb + TM_X + cc * 16 + 16, x1);
+        tmem_ld_wait();
+        if (lane < 16) {
+          st_row8(sm + OFF_QT, P64, t16, cc * 2, x0);
+          st_row8(sm + OFF_QT, P64, t16, cc * 2 + 1, x0 + 8);
+          st_row8(sm + OFF_QT, P64, t16, cc * 2 + 2, x1);
+          st_row8(sm + OFF_QT, P64, t16, cc * 2 + 3, x1 + 8);
         }
       }
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->qt_smem);
-      // E1 for the next chunk
-      if (j + 1 < N && !build_wk(j + 1)) break;
-      // E5: o^T (lane = c, columns = t) -> o[t][c]
-      if (!wait_full(&bars->o_full, j, status, bars)) break;
-      tc_fence_after();
-      {
-        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(args.o) +
-                           (tok0 + static_cast<size_t>(j) * kC) * kD + row;
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          float x[16];
-          tmem_ld16(tmem + lb + TM_O + cc * 16, x);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) o[static_cast<size_t>(cc * 16 + i) * kD] = __float2bfloat16_rn(x[i]);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&bars->o_empty);
+      if (j + 1 < N && !(build_wk(j + 1) && build_as(j + 1))) break;
     }
   }
 
@@ -467,6 +464,10 @@ chunk_fwd_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     tmem_dealloc(tmem, 512);
   }
 }
+
+}  // namespace
+
+namespace {
 
 // ---------------------------------------------------------------------------
 // host side

@@ -83,6 +83,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Same, but the thread may be suspended (not spinning, so it leaves the
+// issue slots to the working warps) for up to `hint_ns` while the phase is
+// still open.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity,
+                                                    uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for the phase with the given parity to complete.  Gives up after
 // kWaitLimitNs, ORs kStatusWaitTimeout into *status and sets *abort (shared)
 // so that the other warps stop too.  Returns false on give-up or if another
@@ -92,7 +108,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if (*abort_flag) return false;
     if (global_ns() - t0 > kWaitLimitNs) {
       *abort_flag = 1;
@@ -273,6 +289,69 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 
 __device__ __forceinline__ float bf16_lo(uint32_t x) { return __uint_as_float(x << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t x) { return __uint_as_float(x & 0xFFFF0000u); }
+
+__device__ __forceinline__ uint4 pack8(const float* v) {
+  uint4 w;
+  w.x = pack_bf16(v[0], v[1]);
+  w.y = pack_bf16(v[2], v[3]);
+  w.z = pack_bf16(v[4], v[5]);
+  w.w = pack_bf16(v[6], v[7]);
+  return w;
+}
+
+__device__ __forceinline__ void unpack8(uint4 w, float* v) {
+  v[0] = bf16_lo(w.x); v[1] = bf16_hi(w.x);
+  v[2] = bf16_lo(w.y); v[3] = bf16_hi(w.y);
+  v[4] = bf16_lo(w.z); v[5] = bf16_hi(w.z);
+  v[6] = bf16_lo(w.w); v[7] = bf16_hi(w.w);
+}
+
+// Write 8 floats of row `row`, columns [col8*8, col8*8+8) of a bf16 tile made
+// of 64-column panels `panel_stride` bytes apart, as one swizzled 16-byte chunk.
+__device__ __forceinline__ void st_row8(uint8_t* tile, uint32_t panel_stride, int row, int col8,
+                                        const float* v) {
+  uint8_t* p = tile + (col8 >> 3) * panel_stride + sw128_chunk(row, col8 & 7);
+  *reinterpret_cast<uint4*>(p) = pack8(v);
+}
+
+__device__ __forceinline__ uint4 ld_row8(const uint8_t* tile, uint32_t panel_stride, int row,
+                                         int col8) {
+  return *reinterpret_cast<const uint4*>(tile + (col8 >> 3) * panel_stride +
+                                         sw128_chunk(row, col8 & 7));
+}
+
+// 64 x 64 bf16 identity in one SW128 panel (call with all threads of the CTA).
+__device__ __forceinline__ void build_identity64(uint8_t* panel, int tid, int nthreads) {
+  for (int r = tid; r < 64; r += nthreads) {
+    for (int c8 = 0; c8 < 8; ++c8) {
+      uint4 w = make_uint4(0, 0, 0, 0);
+      if ((r >> 3) == c8) {
+        const uint32_t one = 0x3F80u << (16 * (r & 1));
+        const int word = (r & 7) >> 1;
+        if (word == 0) w.x = one;
+        if (word == 1) w.y = one;
+        if (word == 2) w.z = one;
+        if (word == 3) w.w = one;
+      }
+      *reinterpret_cast<uint4*>(panel + sw128_chunk(r, c8)) = w;
+    }
+  }
+}
+
+// Phase-parity waits: `use` counts completions of the barrier.  wait_use waits
+// for completion `use`; wait_free for completion `use - 1` (immediately true
+// for use 0), the producer side of a ring slot.
+__device__ __forceinline__ bool wait_use(uint64_t* b, int use, uint32_t* st, volatile int* ab) {
+  return mbar_wait(b, static_cast<uint32_t>(use) & 1u, st, ab);
+}
+__device__ __forceinline__ bool wait_free(uint64_t* b, int use, uint32_t* st, volatile int* ab) {
+  return mbar_wait(b, (static_cast<uint32_t>(use) & 1u) ^ 1u, st, ab);
+}
+
+// Named barrier among `nthreads` threads (ids 1..15; 0 is __syncthreads).
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
 
 }  // namespace tc
 }  // namespace gmdn
