@@ -62,31 +62,43 @@ RULE_NAMES = {0: "delta", 1: "muon", 2: "adam"}
 # ---------------------------------------------------------------------------
 
 def kernel_work(name: str, cfg: dict) -> tuple[str, float]:
-    """(bound, algorithmic work per launch) of a library kernel.
+    """(bound, algorithmic work per launch) of a library kernel: flops for
+    tensor-bound kernels, bytes for HBM-bound ones.
 
-    Per chunk-head (C tokens, head dim d): phase-1 products Kw, Uv are
-    2 * 2*C*d^2 flops; A, Qt, Ov, o are 2*C^2*d + 2*C^2*d + 2*C^2*d + 2*C*d^2;
-    the scan step S K is 2*d^3 (muon adds 3 products per NS step).  The
-    backward kernels count the products they must evaluate.
+    Per chunk-head (C tokens, head dim d; config 1: C=64, d=128):
+      chunk_fwd_tc   the forward's products 2C^2d + 4Cd^2 + 4C^2d + 2Cd^2 (phases
+                     1 and 3) + 2d^3 (state product) = 13.63 MFLOP
+      chunk_bwd1_tc  the reverse chain's products: P = q k^T (2C^2d),
+                     dE^T = dO^T A + Sb (wk)^T (2C^2d + 2Cd^2), dO^T q and dE^T k
+                     (2 x 2Cd^2) = 8.39 MFLOP
+      chunk_bwd2_tc  bytes: q, k, v, dO in (4 C d 2), S_j and Sb_{j+1} in
+                     (2 d^2 2), gates in (2 C 4), dq, dk, dv out (3 C d 2), gate
+                     cotangents out (3 C 4) = 181,504 B
+    The exact-fp32 kernels count their products (CUDA-core fp32).
     """
     B, H, T, d, C = cfg["B"], cfg["H"], cfg["T"], cfg["dh"], cfg["chunk"]
     N = T // C
     units = B * H * N
     ns = cfg["ns"] if cfg["rule"] == 1 else 0
     mm = 2.0 * d ** 3
-    table = {
+    flops = {
+        "chunk_fwd_tc": 2 * C * C * d + 4 * C * d * d + 4 * C * C * d + 2 * C * d * d + mm,
+        "chunk_bwd1_tc": 2 * C * C * d + (2 * C * C * d + 2 * C * d * d) + 2 * (2 * C * d * d),
         "chunk_prep": 4.0 * C * d * d,
         "chunk_out": 6.0 * C * C * d + 2.0 * C * d * d,
         "chunk_state_grad": 4.0 * C * C * d + 2.0 * C * d * d,
         "chunk_token_grad": 14.0 * C * C * d + 10.0 * C * d * d,
         "scan_fwd_ieee": mm * (1 + 3 * ns),
         "scan_bwd_ieee": mm * (3 + 8 * ns),
-        "scan_fwd_fast": mm * (1 + 3 * ns),
-        "scan_bwd_fast": mm * (3 + 8 * ns),
     }
-    if name not in table:
-        return "tensor", float("nan")
-    return "tensor", table[name] * units
+    nbytes = {
+        "chunk_bwd2_tc": 4 * C * d * 2 + 2 * d * d * 2 + 2 * C * 4 + 3 * C * d * 2 + 3 * C * 4,
+    }
+    if name in nbytes:
+        return "hbm", float(nbytes[name] * units)
+    if name in flops:
+        return "tensor", float(flops[name] * units)
+    return "tensor", float("nan")
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -268,8 +280,12 @@ def main():
     ap.add_argument("--precision", default="fast", choices=["fast", "ieee"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override B of the workload (small ncu captures)")
     args = ap.parse_args()
-    cfg = CONFIGS[args.config]
+    cfg = dict(CONFIGS[args.config])
+    if args.batch:
+        cfg["B"] = args.batch
 
     if args.impl == "reference":
         run_reference_arm(args, cfg)
@@ -331,61 +347,80 @@ def main():
     launches = L.kernel_launches() - launches0
     elapsed = ev0.elapsed_time(ev1)  # ms
     barrier()
-    if dist is not None:
-        t = torch.tensor([elapsed], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed = t.item()
+    elapsed = pkg.sharding.max_over_ranks(elapsed, device)
     tokens_per_step = B * T * world
     value = tokens_per_step * args.steps / (elapsed / 1e3)
 
     # ---- end to end through the public API from pinned host memory ----
+    # Every step copies its inputs host->device and o plus every gradient
+    # device->host; copies run on their own streams so that step i+1's inputs
+    # and step i's results move while step i or i+1 computes (two device
+    # input buffers).
     e2e = None
     if not args.no_e2e:
-        pin = {n: getattr(host, n).to(torch.bfloat16 if n in ("q", "k", "v", "dO")
-                                      else torch.float32).pin_memory()
-               for n in ("q", "k", "v", "alpha", "beta", "mu", "nu", "dO")
-               if getattr(host, n) is not None}
+        act = ("q", "k", "v", "dO")
+        gate_names = ("alpha", "beta", "mu") + (("nu",) if rule == 2 else ())
+        pin = {n: getattr(host, n).to(torch.bfloat16 if n in act else torch.float32).pin_memory()
+               for n in act + gate_names}
         outs = {"o": torch.empty(B, H, T, dh, dtype=torch.bfloat16).pin_memory()}
         for n in ("q", "k", "v"):
             outs["d" + n] = torch.empty(B, H, T, dh, dtype=torch.bfloat16).pin_memory()
-        for n in ("alpha", "beta", "mu") + (("nu",) if rule == 2 else ()):
+        for n in gate_names:
             outs["d" + n] = torch.empty(B, H, T, dtype=torch.float32).pin_memory()
-        h2d = sum(t.numel() * t.element_size() for n, t in pin.items()
-                  if n != "nu" or rule == 2)
+        h2d = sum(t.numel() * t.element_size() for t in pin.values())
         d2h = sum(t.numel() * t.element_size() for t in outs.values())
+        dbuf = [{n: torch.empty(t.shape, dtype=t.dtype, device=device) for n, t in pin.items()}
+                for _ in range(2)]
+        s_h2d, s_d2h = torch.cuda.Stream(device), torch.cuda.Stream(device)
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_used = [torch.cuda.Event() for _ in range(2)]
+        gnames = ["dq", "dk", "dv"] + ["d" + n for n in gate_names]
 
-        def e2e_step():
-            d = {n: t.to(device, non_blocking=True) for n, t in pin.items()}
-            ins = [d["q"], d["k"], d["v"], d["alpha"], d["beta"], d["mu"]] + \
-                ([d["nu"]] if rule == 2 else [])
-            for t in ins:
-                t.requires_grad_(True)
-            o = pkg.chunk_fast_weight(d["q"], d["k"], d["v"], d["alpha"], d["beta"], d["mu"],
-                                      d.get("nu") if rule == 2 else None, rule, ns, C, prec)
-            grads = torch.autograd.grad(o, ins, d["dO"])
-            outs["o"].copy_(o.detach(), non_blocking=True)
-            names = ["dq", "dk", "dv", "dalpha", "dbeta", "dmu"] + (["dnu"] if rule == 2 else [])
-            for n, g in zip(names, grads):
-                outs[n].copy_(g, non_blocking=True)
+        def e2e_run(nsteps):
+            for i in range(nsteps):
+                b = i & 1
+                d = dbuf[b]
+                with torch.cuda.stream(s_h2d):
+                    if i >= 2:
+                        s_h2d.wait_event(ev_used[b])
+                    for n, t in pin.items():
+                        d[n].copy_(t, non_blocking=True)
+                    ev_in[b].record(s_h2d)
+                stream.wait_event(ev_in[b])
+                ins = [d[n].requires_grad_(True) for n in ("q", "k", "v") + gate_names]
+                o = pkg.chunk_fast_weight(d["q"], d["k"], d["v"], d["alpha"], d["beta"], d["mu"],
+                                          d.get("nu") if rule == 2 else None, rule, ns, C, prec)
+                grads = torch.autograd.grad(o, ins, d["dO"])
+                for t in ins:
+                    t.requires_grad_(False)
+                ev_used[b].record(stream)
+                with torch.cuda.stream(s_d2h):
+                    s_d2h.wait_event(ev_used[b])
+                    outs["o"].copy_(o.detach(), non_blocking=True)
+                    o.record_stream(s_d2h)
+                    for n, g in zip(gnames, grads):
+                        outs[n].copy_(g, non_blocking=True)
+                        g.record_stream(s_d2h)
 
-        e2e_step()
+        e2e_run(2)
         torch.cuda.synchronize()
         barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e2e_steps = max(1, min(args.steps, 5))
-        e0.record(stream)
-        for _ in range(e2e_steps):
-            e2e_step()
-        e1.record(stream)
+        e2e_steps = max(2, min(args.steps, 6))
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(s_h2d)
+        stream.wait_event(e0)
+        s_d2h.wait_event(e0)
+        e2e_run(e2e_steps)
+        s_d2h.wait_stream(stream)
+        s_d2h.wait_stream(s_h2d)
+        e1.record(s_d2h)
         torch.cuda.synchronize()
-        e_ms = e0.elapsed_time(e1)
-        if dist is not None:
-            t = torch.tensor([e_ms], device=device)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            e_ms = t.item()
+        e_ms = pkg.sharding.max_over_ranks(e0.elapsed_time(e1), device)
         e2e = {"value": tokens_per_step * e2e_steps / (e_ms / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-               "ms_per_step": e_ms / e2e_steps}
+               "ms_per_step": e_ms / e2e_steps,
+               "pipelining": "inputs of step i+1 and results of step i copied on side streams"}
 
     # ---- roofline of the dominant kernel ----
     peaks, peak_kind = load_peaks()
