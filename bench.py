@@ -110,12 +110,16 @@ def load_peaks() -> tuple[dict, str]:
 
 
 def load_traffic() -> dict:
-    """dram bytes per launch by kernel, from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    """DRAM bytes per launch by workload and kernel, from the committed ncu
+    summary (profiles/ncu_traffic.txt: `workload kernel bytes source`)."""
+    out: dict = {}
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
     if os.path.exists(p):
-        with open(p) as f:
-            return json.load(f)
-    return {}
+        for line in open(p):
+            parts = line.split()
+            if len(parts) >= 3 and not line.startswith("#"):
+                out.setdefault(parts[0], {})[parts[1]] = int(parts[2])
+    return out
 
 
 # ---------------------------------------------------------------------------
