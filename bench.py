@@ -127,66 +127,78 @@ def load_traffic() -> dict:
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clocks / throttle reasons sampled every 10 ms.  Started
+    before the warm-up (the tool takes ~0.2 s to come up); mark() brackets the
+    timed region and summary() keeps the samples inside it (the nearest one
+    when the region is shorter than the sampling period)."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device: torch.device):
+        import threading
+        self.rows: list = []
+        self.window = None
         self.proc = None
-        self.out = None
         try:
             uuid = str(torch.cuda.get_device_properties(device).uuid)
-            self.target = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
-        except Exception:
-            self.target = None
-
-    def __enter__(self):
-        try:
+            target = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
             cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                   "-lms", "100"]
-            if self.target:
-                cmd += ["-i", self.target]
+                   "-lms", "10", "-i", target]
             self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
-                                         text=True)
+                                         text=True, bufsize=1)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 3.0 and self.proc.poll() is None:
+                time.sleep(0.01)
         except Exception:
             self.proc = None
-        return self
 
-    def __exit__(self, *exc):
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append((time.time(), line))
+
+    def mark(self, start: bool):
+        now = time.time()
+        if start:
+            self.window = [now, None]
+        elif self.window:
+            self.window[1] = now
+
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-                self.out = ""
 
     def summary(self) -> dict | None:
-        if not self.out:
-            return None
-        rows = []
-        for line in self.out.strip().splitlines():
+        parsed = []
+        for ts, line in self.rows:
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 8:
+            if len(parts) < 7:
                 continue
             try:
-                rows.append(dict(sm=float(parts[0]), max=float(parts[1]),
-                                 power=float(parts[2]) if parts[2] not in ("[N/A]", "") else 0.0,
-                                 hw=parts[4], hwt=parts[5], swt=parts[6], pcap=parts[7]))
+                parsed.append(dict(ts=ts, sm=float(parts[0]), max=float(parts[1]),
+                                   reasons={k: parts[3 + i].lower() == "active" for i, k in
+                                            enumerate(("hw_slowdown", "hw_thermal_slowdown",
+                                                       "sw_thermal_slowdown", "sw_power_cap"))}))
             except ValueError:
                 continue
-        if not rows:
+        if not parsed or not self.window or self.window[1] is None:
             return None
-        loaded = [r for r in rows if r["power"] > 0.3 * max(x["power"] for x in rows)] or rows
-        reasons = set()
-        for r in loaded:
-            for key, label in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
-                               ("swt", "sw_thermal_slowdown"), ("pcap", "sw_power_cap")):
-                if r[key].lower() == "active":
-                    reasons.add(label)
-        return {"sm_mhz": statistics.median(r["sm"] for r in loaded),
-                "sm_max_mhz": max(r["max"] for r in loaded),
-                "samples": len(loaded), "reasons": sorted(reasons)}
+        lo, hi = self.window
+        inside = [r for r in parsed if lo <= r["ts"] <= hi + 0.02]
+        if not inside:
+            after = [r for r in parsed if r["ts"] >= lo]
+            inside = after[:1] or parsed[-1:]
+        reasons = sorted({k for r in inside for k, v in r["reasons"].items() if v})
+        return {"sm_mhz": statistics.median(r["sm"] for r in inside),
+                "sm_max_mhz": max(r["max"] for r in inside), "samples": len(inside),
+                "window_ms": round(1e3 * (hi - lo), 2), "reasons": reasons}
 
 
 # ---------------------------------------------------------------------------
@@ -329,6 +341,7 @@ def main():
         if dist is not None:
             dist.barrier()
 
+    clocks = ClockSampler(device)
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
@@ -340,12 +353,13 @@ def main():
     launches0 = L.kernel_launches()
     L.prof_report()  # drop anything recorded so far
     L.prof_enable(True)
-    with ClockSampler(device) as clocks:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            step()
-        ev1.record(stream)
-        torch.cuda.synchronize()
+    clocks.mark(True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks.mark(False)
     L.prof_enable(False)
     kt = L.prof_report()
     launches = L.kernel_launches() - launches0
@@ -452,6 +466,8 @@ def main():
                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json bf16 burst)"
                     if peak_kind == "measured" else "fallback"}
 
+    clocks.stop()
+    clock_info = clocks.summary()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(pkg, cfg)
@@ -468,7 +484,7 @@ def main():
                        "precision": args.precision, "parallelism": f"dp{world} (B*H shards)",
                        "l2": "inputs larger than L2 (q,k,v,dO bf16 = 537 MB per rank)"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-            "gpu_launches": launches, "clocks": clocks.summary(),
+            "gpu_launches": launches, "clocks": clock_info,
             "kernel_times": kernel_times,
         }
         print(json.dumps(line), flush=True)

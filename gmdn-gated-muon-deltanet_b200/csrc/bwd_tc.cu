@@ -387,29 +387,37 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 // ===========================================================================
 // bw2: token and gate gradients of one chunk
 // ===========================================================================
+//
+// Warps 0-7 drain accumulators (warp w reads TMEM subpartition w % 4; warps
+// w and w + 4 split the columns), warp 8 issues the TMA loads and the MMAs.
+// Accumulators: E^T (M=128) feeds dA and dWk through MN-major descriptors;
+// the outputs dq, dk, dv and the small C x C products are M=64 (row-major),
+// paired two per TMEM column range (lanes 0-15 / 16-31).
 
-constexpr int kThreads2 = 160;
+constexpr int kThreads2 = 288;
 constexpr uint32_t B2_Q = 0, B2_K = 16384, B2_V = 32768, B2_G = 49152;
 constexpr uint32_t B2_S = 65536;      // S_j, 2 panels x 128 rows
 constexpr uint32_t B2_SB = 98304;     // Sb_{j+1}
 constexpr uint32_t B2_AS = 131072;    // A bf16 [t][s]
-constexpr uint32_t B2_E = 139264;     // E bf16 [s][c]
+constexpr uint32_t B2_E = 139264;     // E^T bf16 [c][s], 1 panel x 128 rows
 constexpr uint32_t B2_WK = 155648;    // w * k
 constexpr uint32_t B2_DE = 172032;    // dE bf16 [s][c]
 constexpr uint32_t B2_DP = 188416;    // dP bf16 [t][s]
 constexpr uint32_t B2_I = 196608;     // identity
-constexpr uint32_t B2_RED = 204800;   // fp32 [64][65]: dA * P per (t, s)
-constexpr uint32_t B2_GATE = 221440;  // beta[64], alpha[64], dw[64], misc
+constexpr uint32_t B2_RED = 204800;   // fp32 [64][65]: tril(dA) * P per (t, s)
+constexpr uint32_t B2_GATE = 221440;  // beta[64], alpha[64], dw[2][64]
 constexpr uint32_t B2_BAR = 222720;
 constexpr uint32_t B2_SMEM = B2_BAR + 256 + 1024;
 
-constexpr uint32_t T2_X0 = 0, T2_X1 = 64, T2_X2 = 192, T2_X3 = 320;
+// TMEM: X0 P | dA, X1 dQ (lanes 16-31), X2 dE | dWk, X3 dK (lanes 0-15), XE E^T
+constexpr uint32_t T2_X0 = 0, T2_X1 = 64, T2_X2 = 192, T2_X3 = 320, T2_XE = 448;
 
 struct Bars2 {
   uint64_t ld_full, ph1, ep1, wk_full, ph2, ep2, ph3;
   uint32_t tmem_base;
   int abort_flag;
   float da;
+  float a_c;
 };
 
 __global__ void __launch_bounds__(kThreads2, 1)
@@ -423,7 +431,7 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   Bars2* bars = reinterpret_cast<Bars2*>(sm + B2_BAR);
   float* gbeta = reinterpret_cast<float*>(sm + B2_GATE);
   float* galpha = gbeta + 64;
-  float* gdw = galpha + 64;
+  float* gdw = galpha + 64;  // [2][64]: partial k.dWk of each column half
   float* red = reinterpret_cast<float*>(sm + B2_RED);
   volatile int* ab = &bars->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -436,17 +444,17 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   if (threadIdx.x == 0) {
     mbar_init(&bars->ld_full, 1);
     mbar_init(&bars->ph1, 1);
-    mbar_init(&bars->ep1, 128);
-    mbar_init(&bars->wk_full, 128);
+    mbar_init(&bars->ep1, 256);
+    mbar_init(&bars->wk_full, 256);
     mbar_init(&bars->ph2, 1);
-    mbar_init(&bars->ep2, 128);
+    mbar_init(&bars->ep2, 256);
     mbar_init(&bars->ph3, 1);
     bars->abort_flag = 0;
     bars->da = 0.f;
     fence_mbar_init();
   }
   build_identity64(sm + B2_I, threadIdx.x, kThreads2);
-  if (warp == 4) {
+  if (warp == 8) {
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
   }
@@ -456,7 +464,7 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       mbar_expect_tx(&bars->ld_full, 8 * 8192 + 4 * 16384 + 512);
       tma_load_2d(sm + B2_Q, &tm_q, 0, static_cast<int>(tok), &bars->ld_full);
@@ -482,20 +490,21 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       constexpr uint32_t ID_P = idesc_bf16(64, 64, false, false);
       constexpr uint32_t ID_KM = idesc_bf16(64, 128, false, true);        // A K-major, B MN-major
       constexpr uint32_t ID_KK = idesc_bf16(64, 128, false, false);       // both K-major
-      constexpr uint32_t ID_KKN = idesc_bf16(64, 128, false, false, true);
       constexpr uint32_t ID_KMN = idesc_bf16(64, 128, false, true, true);
       constexpr uint32_t ID_MM = idesc_bf16(64, 128, true, true);         // both MN-major
-      constexpr uint32_t ID_DA = idesc_bf16(64, 64, false, false);
+      constexpr uint32_t ID_EV = idesc_bf16(128, 64, true, false);        // E^T: v^T I
+      constexpr uint32_t ID_EK = idesc_bf16(128, 64, false, false, true); // E^T: -S k^T
+      constexpr uint32_t ID_DA = idesc_bf16(64, 64, false, true);         // dO E^T
       bool ok = wait_use(&bars->ld_full, 0, status, ab);
       if (ok) {
         tc_fence_after();
-        // phase 1: P = q k^T; E = I v - k S^T; dQ = dO S
+        // phase 1: P = q k^T; E^T = v^T - S k^T; dQ = dO S
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + T2_X0, desc_kmajor(q_s, P64, k), desc_kmajor(k_s, P64, k), ID_P, k > 0);
         for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + T2_X1, desc_kmajor(id_s, P64, k), desc_mnmajor(v_s, P64, k), ID_KM, k > 0);
+          mma_bf16(tmem + T2_XE, desc_mnmajor(v_s, P64, k), desc_kmajor(id_s, P64, k), ID_EV, k > 0);
         for (int k = 0; k < 8; ++k)
-          mma_bf16(tmem + T2_X1, desc_kmajor(k_s, P64, k), desc_kmajor(s_s, P128, k), ID_KKN, 1);
+          mma_bf16(tmem + T2_XE, desc_kmajor(s_s, P128, k), desc_kmajor(k_s, P64, k), ID_EK, 1);
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + HI16 + T2_X1, desc_kmajor(g_s, P64, k), desc_mnmajor(s_s, P128, k),
                    ID_KM, k > 0);
@@ -510,11 +519,11 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + T2_X2, desc_kmajor(wk_s, P64, k), desc_kmajor(sb_s, P128, k), ID_KK, 1);
         for (int k = 0; k < 8; ++k)
-          mma_bf16(tmem + HI16 + T2_X0, desc_kmajor(g_s, P64, k), desc_kmajor(e_s, P64, k), ID_DA,
+          mma_bf16(tmem + HI16 + T2_X0, desc_kmajor(g_s, P64, k), desc_mnmajor(e_s, P128, k), ID_DA,
                    k > 0);
         for (int k = 0; k < 8; ++k)
-          mma_bf16(tmem + HI16 + T2_X2, desc_kmajor(e_s, P64, k), desc_mnmajor(sb_s, P128, k),
-                   ID_KM, k > 0);
+          mma_bf16(tmem + HI16 + T2_X2, desc_mnmajor(e_s, P128, k), desc_mnmajor(sb_s, P128, k),
+                   ID_MM, k > 0);
         mma_commit(&bars->ph2);
       }
       ok = ok && wait_use(&bars->ep2, 0, status, ab);
@@ -535,17 +544,19 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
     }
   } else {
-    // ------------------------------------------------------------ epilogue warps 0-3
-    const int tid = threadIdx.x;               // 0..127
+    // ------------------------------------------------------------ epilogue warps 0-7
+    const int tid = threadIdx.x;               // 0..255
+    const int sp = warp & 3, half = warp >> 2; // subpartition, column half
     const uint32_t lb = tmem_lane_base(warp);
     const bool hi = lane >= 16;
-    const int r16 = warp * 16 + (lane & 15);   // M=64 row of this lane's accumulator
+    const int r16 = sp * 16 + (lane & 15);     // M=64 row of this lane's accumulator
+    const int c128 = sp * 32 + lane;           // M=128 row (TMEM lane)
     bool ok = wait_use(&bars->ld_full, 0, status, ab);
     if (ok) {
       // w * k (delta: w = beta)
 #pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        const int id = tid + 128 * m;
+      for (int m = 0; m < 4; ++m) {
+        const int id = tid + 256 * m;
         const uint32_t off = static_cast<uint32_t>(id) * 16u;
         const float w = gbeta[(id & 511) >> 3];
         const uint4 x = *reinterpret_cast<const uint4*>(sm + B2_K + off);
@@ -558,27 +569,34 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       fence_async_smem();
       mbar_arrive(&bars->wk_full);
-      // da = <Sb_{j+1}, S_j> (row tid of both)
+      // da = <Sb_{j+1}, S_j>: row c128, column half `half`
       float part = 0.f;
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
+      for (int c8 = 0; c8 < 8; ++c8) {
         float a8[8], b8[8];
-        unpack8(ld_row8(sm + B2_S, P128, tid, c8), a8);
-        unpack8(ld_row8(sm + B2_SB, P128, tid, c8), b8);
+        unpack8(ld_row8(sm + B2_S, P128, c128, half * 8 + c8), a8);
+        unpack8(ld_row8(sm + B2_SB, P128, c128, half * 8 + c8), b8);
 #pragma unroll
         for (int x = 0; x < 8; ++x) part = fmaf(a8[x], b8[x], part);
       }
       part = warp_sum(part);
       if (lane == 0) atomicAdd(&bars->da, part);
+      if (warp == 0) {  // chunk decay product a_c = prod clamp(alpha)
+        const float la = logf(fmaxf(galpha[lane], kGateFloor)) +
+                         logf(fmaxf(galpha[lane + 32], kGateFloor));
+        const float sum = warp_sum(la);
+        if (lane == 0) bars->a_c = expf(sum);
+      }
     }
-    // ---- epilogue 1: A = tril(P) beta, E -> bf16 (rows of lanes 0-15)
+    // ---- epilogue 1: A = tril(P) beta (lanes 0-15), E^T -> bf16 (all lanes)
     ok = ok && wait_use(&bars->ph1, 0, status, ab);
     if (ok) {
       tc_fence_after();
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c0 = half * 32 + cc * 16;
         float p[16];
-        tmem_ld16(tmem + lb + T2_X0 + cc * 16, p);
+        tmem_ld16(tmem + lb + T2_X0 + c0, p);
         tmem_ld_wait();
         if (!hi) {
 #pragma unroll
@@ -586,22 +604,21 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             float v8[8];
 #pragma unroll
             for (int x = 0; x < 8; ++x) {
-              const int sc = cc * 16 + h * 8 + x;
+              const int sc = c0 + h * 8 + x;
               v8[x] = (sc <= r16) ? p[h * 8 + x] * gbeta[sc] : 0.f;
             }
-            st_row8(sm + B2_AS, P64, r16, cc * 2 + h, v8);
+            st_row8(sm + B2_AS, P64, r16, (c0 >> 3) + h, v8);
           }
         }
       }
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c0 = half * 32 + cc * 16;
         float e[16];
-        tmem_ld16(tmem + lb + T2_X1 + cc * 16, e);
+        tmem_ld16(tmem + lb + T2_XE + c0, e);
         tmem_ld_wait();
-        if (!hi) {
-          st_row8(sm + B2_E, P64, r16, cc * 2, e);
-          st_row8(sm + B2_E, P64, r16, cc * 2 + 1, e + 8);
-        }
+        st_row8(sm + B2_E, P128, c128, c0 >> 3, e);
+        st_row8(sm + B2_E, P128, c128, (c0 >> 3) + 1, e + 8);
       }
       fence_async_smem();
       tc_fence_before();
@@ -613,9 +630,10 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       tc_fence_after();
       // X0: P (lanes 0-15) and dA (lanes 16-31) of the same row t = r16
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c0 = half * 32 + cc * 16;
         float x[16];
-        tmem_ld16(tmem + lb + T2_X0 + cc * 16, x);
+        tmem_ld16(tmem + lb + T2_X0 + c0, x);
         tmem_ld_wait();
         float other[16];
 #pragma unroll
@@ -626,39 +644,40 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             float v8[8];
 #pragma unroll
             for (int y = 0; y < 8; ++y) {
-              const int sc = cc * 16 + h * 8 + y;
+              const int sc = c0 + h * 8 + y;
               const float dam = (sc <= r16) ? x[h * 8 + y] : 0.f;
               v8[y] = dam * gbeta[sc];
               red[r16 * 65 + sc] = dam * other[h * 8 + y];
             }
-            st_row8(sm + B2_DP, P64, r16, cc * 2 + h, v8);
+            st_row8(sm + B2_DP, P64, r16, (c0 >> 3) + h, v8);
           }
         }
       }
-      // X2: dE (lanes 0-15) and dWk (lanes 16-31), row s = r16
+      // X2: dE (lanes 0-15) and dWk (lanes 16-31), row s = r16, 64 columns
       uint4* dvp = reinterpret_cast<uint4*>(args.dv) + ((tok + r16) * kD) / 8;
       float dw = 0.f;
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
+      for (int cc = 0; cc < 4; ++cc) {
+        const int c0 = half * 64 + cc * 16;
         float x[16];
-        tmem_ld16(tmem + lb + T2_X2 + cc * 16, x);
+        tmem_ld16(tmem + lb + T2_X2 + c0, x);
         tmem_ld_wait();
         if (!hi) {
-          st_row8(sm + B2_DE, P64, r16, cc * 2, x);
-          st_row8(sm + B2_DE, P64, r16, cc * 2 + 1, x + 8);
-          dvp[cc * 2] = pack8(x);
-          dvp[cc * 2 + 1] = pack8(x + 8);
+          st_row8(sm + B2_DE, P64, r16, c0 >> 3, x);
+          st_row8(sm + B2_DE, P64, r16, (c0 >> 3) + 1, x + 8);
+          dvp[c0 >> 3] = pack8(x);
+          dvp[(c0 >> 3) + 1] = pack8(x + 8);
         } else {
           float k8[8];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            unpack8(ld_row8(sm + B2_K, P64, r16, cc * 2 + h), k8);
+            unpack8(ld_row8(sm + B2_K, P64, r16, (c0 >> 3) + h), k8);
 #pragma unroll
             for (int y = 0; y < 8; ++y) dw = fmaf(k8[y], x[h * 8 + y], dw);
           }
         }
       }
-      if (hi) gdw[r16] = dw;
+      if (hi) gdw[half * 64 + r16] = dw;
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->ep2);
@@ -671,38 +690,36 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       uint4* dqp = reinterpret_cast<uint4*>(args.dq) + ((tok + r16) * kD) / 8;
       uint4* dkp = reinterpret_cast<uint4*>(args.dk) + ((tok + r16) * kD) / 8;
 #pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
+      for (int cc = 0; cc < 4; ++cc) {
+        const int c0 = half * 64 + cc * 16;
         float x1[16], x2[16], x3[16];
-        tmem_ld16(tmem + lb + T2_X1 + cc * 16, x1);   // dq at lanes 16-31
-        tmem_ld16(tmem + lb + T2_X2 + cc * 16, x2);   // dWk at lanes 16-31
-        tmem_ld16(tmem + lb + T2_X3 + cc * 16, x3);   // dK part at lanes 0-15
+        tmem_ld16(tmem + lb + T2_X1 + c0, x1);   // dq at lanes 16-31
+        tmem_ld16(tmem + lb + T2_X2 + c0, x2);   // dWk at lanes 16-31
+        tmem_ld16(tmem + lb + T2_X3 + c0, x3);   // dK part at lanes 0-15
         tmem_ld_wait();
         float dwk[16];
 #pragma unroll
         for (int y = 0; y < 16; ++y) dwk[y] = __shfl_xor_sync(0xffffffffu, x2[y], 16);
         if (hi) {
-          dqp[cc * 2] = pack8(x1);
-          dqp[cc * 2 + 1] = pack8(x1 + 8);
+          dqp[c0 >> 3] = pack8(x1);
+          dqp[(c0 >> 3) + 1] = pack8(x1 + 8);
         } else {
 #pragma unroll
           for (int y = 0; y < 16; ++y) x3[y] = fmaf(w, dwk[y], x3[y]);
-          dkp[cc * 2] = pack8(x3);
-          dkp[cc * 2 + 1] = pack8(x3 + 8);
+          dkp[c0 >> 3] = pack8(x3);
+          dkp[(c0 >> 3) + 1] = pack8(x3 + 8);
         }
       }
     }
-    named_sync(1, 128);
+    named_sync(1, 256);
     if (ok && tid < kC) {
       const int s = tid;
-      float db = gdw[s];
+      float db = gdw[s] + gdw[64 + s];
       for (int t = s; t < kC; ++t) db += red[t * 65 + s];
-      float la = 0.f;
-      for (int t = 0; t < kC; ++t) la += logf(fmaxf(galpha[t], kGateFloor));
-      const float a_c = expf(la);
       const float al = galpha[s];
       const size_t g = tok + s;
       args.dbeta[g] = db;
-      args.dalpha[g] = (al >= kGateFloor) ? bars->da * a_c / fmaxf(al, kGateFloor) : 0.f;
+      args.dalpha[g] = (al >= kGateFloor) ? bars->da * bars->a_c / fmaxf(al, kGateFloor) : 0.f;
       args.dmu[g] = 0.f;
       if (args.dnu) args.dnu[g] = 0.f;
     }
@@ -710,7 +727,7 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
