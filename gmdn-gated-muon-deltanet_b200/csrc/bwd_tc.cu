@@ -20,7 +20,9 @@
 //
 // bw1: one CTA per (b, h) walks the chunks in reverse and produces Sb_{j+1}
 //      for every chunk (bf16, for bw2).  The chain products use split bf16
-//      (hi + lo) operands for Sb and dE.
+//      (hi + lo) operands for Sb and dE; Sb hi/lo live in TMEM as the A
+//      operand of their product, so the recurrence never touches shared
+//      memory.
 // bw2: one CTA per (b, h, chunk) computes every token and gate gradient of
 //      its chunk from q, k, v, dO, S_j and Sb_{j+1}.
 
@@ -55,7 +57,7 @@ struct BwArgs {
 // bw1: reverse chain
 // ===========================================================================
 
-constexpr int kThreads1 = 320;
+constexpr int kThreads1 = 448;  // warps 0-7 state, 8-11 chunk-local, 12 TMA, 13 MMA
 constexpr uint32_t B1_Q = 0;          // q: 2 stages x 16 KB
 constexpr uint32_t B1_K = 32768;      // k: 2 stages
 constexpr uint32_t B1_G = 65536;      // dO: 2 stages
@@ -63,13 +65,13 @@ constexpr uint32_t B1_WK = 98304;     // w * k
 constexpr uint32_t B1_AS = 114688;    // A (bf16), 1 panel x 64 rows
 constexpr uint32_t B1_DEH = 122880;   // dE^T hi, 1 panel x 128 rows
 constexpr uint32_t B1_DEL = 139264;   // dE^T lo
-constexpr uint32_t B1_SH = 155648;    // Sb hi, 2 panels x 128 rows
-constexpr uint32_t B1_SL = 188416;    // Sb lo
-constexpr uint32_t B1_GATE = 221184;  // beta: 2 stages x 64 floats
-constexpr uint32_t B1_BAR = 221696;
+constexpr uint32_t B1_GATE = 155648;  // beta: 2 stages x 64 floats
+constexpr uint32_t B1_BAR = 156160;
 constexpr uint32_t B1_SMEM = B1_BAR + 256 + 1024;
 
-constexpr uint32_t T1_C0 = 0, T1_C1 = 128, T1_E = 256, T1_P = 320;
+// TMEM: chain accumulators C0/C1, dE^T, P (lanes 0-15), Sb hi and lo packed
+// bf16 pairs (64 columns each = 128 values per lane).
+constexpr uint32_t T1_C0 = 0, T1_C1 = 128, T1_E = 256, T1_P = 320, T1_SH = 384, T1_SL = 448;
 
 struct Bars1 {
   uint64_t ld_full[2], ld_empty[2];
@@ -100,19 +102,19 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       mbar_init(&bars->ld_full[s], 1);
       mbar_init(&bars->ld_empty[s], 1 + 128);
       mbar_init(&bars->c_full[s], 1);
-      mbar_init(&bars->c_empty[s], 128);
+      mbar_init(&bars->c_empty[s], 256);
     }
     mbar_init(&bars->wk_full, 128);
     mbar_init(&bars->p_full, 1);
     mbar_init(&bars->as_full, 128);
     mbar_init(&bars->de_full, 1);
     mbar_init(&bars->de_smem, 128);
-    mbar_init(&bars->s_full, 128);
+    mbar_init(&bars->s_full, 256);
     mbar_init(&bars->final_mma, 1);
     bars->abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == 13) {
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
   }
@@ -122,7 +124,7 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   const uint32_t tmem = bars->tmem_base;
   const size_t tok0 = static_cast<size_t>(bh) * args.T;
 
-  if (warp == 8) {
+  if (warp == 12) {
     // ------------------------------------------------------------ TMA, reverse chunk order
     if (lane == 0) {
       int issued = 0;
@@ -144,15 +146,13 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       for (int i = issued - 2; i < issued; ++i)
         if (i >= 0) mbar_wait(&bars->ld_full[i & 1], (i >> 1) & 1, status, &dummy);
     }
-  } else if (warp == 9) {
+  } else if (warp == 13) {
     // ------------------------------------------------------------ MMA issue
     if (lane == 0) {
       const uint32_t wk_s = smem_u32(sm + B1_WK);
       const uint32_t as_s = smem_u32(sm + B1_AS);
       const uint32_t deh_s = smem_u32(sm + B1_DEH);
       const uint32_t del_s = smem_u32(sm + B1_DEL);
-      const uint32_t sh_s = smem_u32(sm + B1_SH);
-      const uint32_t sl_s = smem_u32(sm + B1_SL);
       constexpr uint32_t ID_P = idesc_bf16(64, 64, false, false);
       constexpr uint32_t ID_Z = idesc_bf16(128, 128, true, true);
       constexpr uint32_t ID_X = idesc_bf16(128, 64, true, true);
@@ -169,32 +169,32 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         mma_commit(&bars->p_full);
         return true;
       };
-      // Z(i): C = dO^T q;  X(i): E^T = dO^T A
-      auto issue_ZX = [&](int i) -> bool {
+      // Z(i): C = dO^T q (off the chain)
+      auto issue_Z = [&](int i) -> bool {
         const int r = i & 1;
         if (i >= 2 && !wait_use(&bars->c_empty[r], (i >> 1) - 1, status, ab)) return false;
         tc_fence_after();
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + (r ? T1_C1 : T1_C0), desc_mnmajor(stage(B1_G, i), P64, k),
                    desc_mnmajor(stage(B1_Q, i), P64, k), ID_Z, k > 0);
-        if (!wait_use(&bars->as_full, i, status, ab)) return false;
-        tc_fence_after();
-        for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + T1_E, desc_mnmajor(stage(B1_G, i), P64, k),
-                   desc_mnmajor(as_s, P64, k), ID_X, k > 0);
         return true;
       };
-      bool ok = N > 0 && issue_P(0) && issue_ZX(0);
+      bool ok = N > 0 && issue_P(0) && issue_Z(0);
       for (int i = 0; ok && i < N; ++i) {
         const int r = i & 1;
-        // Y(i): E^T += Sb_hi (wk)^T + Sb_lo (wk)^T
+        // Y(i): E^T = Sb_hi (wk)^T + Sb_lo (wk)^T  (Sb from TMEM);  X(i): E^T += dO^T A
         if (!wait_use(&bars->s_full, i, status, ab)) break;
         if (!wait_use(&bars->wk_full, i, status, ab)) break;
         tc_fence_after();
         for (int k = 0; k < 8; ++k)
-          mma_bf16(tmem + T1_E, desc_kmajor(sh_s, P128, k), desc_kmajor(wk_s, P64, k), ID_Y, 1);
+          mma_bf16_ts(tmem + T1_E, tmem + T1_SH + k * 8, desc_kmajor(wk_s, P64, k), ID_Y, k > 0);
         for (int k = 0; k < 8; ++k)
-          mma_bf16(tmem + T1_E, desc_kmajor(sl_s, P128, k), desc_kmajor(wk_s, P64, k), ID_Y, 1);
+          mma_bf16_ts(tmem + T1_E, tmem + T1_SL + k * 8, desc_kmajor(wk_s, P64, k), ID_Y, 1);
+        if (!wait_use(&bars->as_full, i, status, ab)) break;
+        tc_fence_after();
+        for (int k = 0; k < 4; ++k)
+          mma_bf16(tmem + T1_E, desc_mnmajor(stage(B1_G, i), P64, k),
+                   desc_mnmajor(as_s, P64, k), ID_X, 1);
         mma_commit(&bars->de_full);
         // W(i): C -= dE^T_hi k + dE^T_lo k
         if (!wait_use(&bars->de_smem, i, status, ab)) break;
@@ -208,37 +208,40 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                    desc_mnmajor(k_s, P64, k), ID_W, 1);
         mma_commit(&bars->c_full[r]);
         mma_commit(&bars->ld_empty[i & 1]);
-        if (i + 1 < N && !(issue_P(i + 1) && issue_ZX(i + 1))) break;
+        if (i + 1 < N && !(issue_P(i + 1) && issue_Z(i + 1))) break;
       }
       mma_commit(&bars->final_mma);
       int dummy = 0;
       mbar_wait(&bars->final_mma, 0, status, &dummy);
     }
-  } else if (warp < 4) {
+  } else if (warp < 8) {
     // ------------------------------------------------------------ state cotangent rows
-    const int c = warp * 32 + lane;
+    const int c = (warp & 3) * 32 + lane;   // row of Sb = TMEM lane
+    const int half = warp >> 2;             // columns [64 half, 64 half + 64)
     const uint32_t lb = tmem_lane_base(warp);
-    uint8_t* Sh = sm + B1_SH;
-    uint8_t* Sl = sm + B1_SL;
-    float sb[kD];
+    float sb[64];
 #pragma unroll
-    for (int i = 0; i < kD; ++i) sb[i] = 0.f;
+    for (int i = 0; i < 64; ++i) sb[i] = 0.f;
     {
-      const uint4 z = make_uint4(0, 0, 0, 0);
+      uint32_t zr[16];
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
-        *reinterpret_cast<uint4*>(Sh + (c8 >> 3) * P128 + sw128_chunk(c, c8 & 7)) = z;
-        *reinterpret_cast<uint4*>(Sl + (c8 >> 3) * P128 + sw128_chunk(c, c8 & 7)) = z;
+      for (int i = 0; i < 16; ++i) zr[i] = 0u;
+#pragma unroll
+      for (int b = 0; b < 2; ++b) {
+        tmem_st16(tmem + lb + T1_SH + half * 32 + b * 16, zr);
+        tmem_st16(tmem + lb + T1_SL + half * 32 + b * 16, zr);
       }
+      tmem_st_wait();
       if (N > 0) {
         uint4* g = reinterpret_cast<uint4*>(
             args.Sbar_hist + (static_cast<size_t>(bh) * N + N - 1) * kD * kD +
-            static_cast<size_t>(c) * kD);
+            static_cast<size_t>(c) * kD + half * 64);
+        const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) g[i] = z;
+        for (int i = 0; i < 8; ++i) g[i] = z;
       }
     }
-    fence_async_smem();
+    tc_fence_before();
     mbar_arrive(&bars->s_full);
     for (int i = 0; i < N; ++i) {
       const int j = N - 1 - i, r = i & 1;
@@ -248,47 +251,56 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       const float a = expf(warp_sum(la));
       if (!wait_use(&bars->c_full[r], i >> 1, status, ab)) break;
       tc_fence_after();
-      const uint32_t rc = tmem + lb + (r ? T1_C1 : T1_C0);
-#pragma unroll
-      for (int cc = 0; cc < 8; cc += 2) {
-        float g0[16], g1[16];
-        tmem_ld16(rc + cc * 16, g0);
-        tmem_ld16(rc + cc * 16 + 16, g1);
+      const uint32_t rc = tmem + lb + (r ? T1_C1 : T1_C0) + half * 64;
+      {
+        float g0[16], g1[16], g2[16], g3[16];
+        tmem_ld16(rc, g0);
+        tmem_ld16(rc + 16, g1);
+        tmem_ld16(rc + 32, g2);
+        tmem_ld16(rc + 48, g3);
         tmem_ld_wait();
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
-          sb[cc * 16 + t] = fmaf(a, sb[cc * 16 + t], g0[t]);
-          sb[cc * 16 + 16 + t] = fmaf(a, sb[cc * 16 + 16 + t], g1[t]);
+          sb[t] = fmaf(a, sb[t], g0[t]);
+          sb[16 + t] = fmaf(a, sb[16 + t], g1[t]);
+          sb[32 + t] = fmaf(a, sb[32 + t], g2[t]);
+          sb[48 + t] = fmaf(a, sb[48 + t], g3[t]);
         }
       }
       tc_fence_before();
       mbar_arrive(&bars->c_empty[r]);
+      // Sb_j as packed bf16 hi / lo pairs into TMEM (A operand of the next
+      // chain product); hi also to the history for bw2
       uint4* gdst = nullptr;
       if (j >= 1)
         gdst = reinterpret_cast<uint4*>(args.Sbar_hist +
                                         (static_cast<size_t>(bh) * N + j - 1) * kD * kD +
-                                        static_cast<size_t>(c) * kD);
+                                        static_cast<size_t>(c) * kD + half * 64);
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
-        float hi[8], lo[8];
+      for (int b = 0; b < 2; ++b) {
+        uint32_t ph[16], pl[16];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const float x = sb[c8 * 8 + t];
-          hi[t] = __bfloat162float(__float2bfloat16_rn(x));
-          lo[t] = x - hi[t];
+        for (int t = 0; t < 16; ++t) {
+          const float x0 = sb[b * 32 + 2 * t], x1 = sb[b * 32 + 2 * t + 1];
+          ph[t] = pack_bf16(x0, x1);
+          pl[t] = pack_bf16(x0 - bf16_lo(ph[t]), x1 - bf16_hi(ph[t]));
         }
-        const uint4 wh = pack8(hi);
-        *reinterpret_cast<uint4*>(Sh + (c8 >> 3) * P128 + sw128_chunk(c, c8 & 7)) = wh;
-        *reinterpret_cast<uint4*>(Sl + (c8 >> 3) * P128 + sw128_chunk(c, c8 & 7)) = pack8(lo);
-        if (gdst) gdst[c8] = wh;
+        tmem_st16(tmem + lb + T1_SH + half * 32 + b * 16, ph);
+        tmem_st16(tmem + lb + T1_SL + half * 32 + b * 16, pl);
+        if (gdst) {
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            gdst[b * 4 + q4] = make_uint4(ph[4 * q4], ph[4 * q4 + 1], ph[4 * q4 + 2], ph[4 * q4 + 3]);
+        }
       }
-      fence_async_smem();
+      tmem_st_wait();
+      tc_fence_before();
       mbar_arrive(&bars->s_full);
     }
   } else {
-    // ------------------------------------------------------------ chunk-local (warps 4-7)
-    const int tb = threadIdx.x - 128;
-    const int sp = warp - 4;
+    // ------------------------------------------------------------ chunk-local (warps 8-11)
+    const int tb = threadIdx.x - 256;
+    const int sp = warp - 8;
     const uint32_t lb = tmem_lane_base(warp);
     const int row = sp * 32 + lane;
     const int t16 = sp * 16 + (lane & 15);
@@ -350,23 +362,24 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       // dE^T (lanes = value row c, 64 token columns) -> hi / lo bf16
       if (!wait_use(&bars->de_full, i, status, ab)) break;
       tc_fence_after();
-#pragma unroll
-      for (int cc = 0; cc < 4; cc += 2) {
-        float x0[16], x1[16];
-        tmem_ld16(tmem + lb + T1_E + cc * 16, x0);
-        tmem_ld16(tmem + lb + T1_E + cc * 16 + 16, x1);
+      {
+        float x0[16], x1[16], x2[16], x3[16];
+        tmem_ld16(tmem + lb + T1_E, x0);
+        tmem_ld16(tmem + lb + T1_E + 16, x1);
+        tmem_ld16(tmem + lb + T1_E + 32, x2);
+        tmem_ld16(tmem + lb + T1_E + 48, x3);
         tmem_ld_wait();
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const float* src = h < 2 ? x0 + h * 8 : x1 + (h - 2) * 8;
+        for (int h = 0; h < 8; ++h) {
+          const float* src = (h < 2 ? x0 : h < 4 ? x1 : h < 6 ? x2 : x3) + (h & 1) * 8;
           float hi[8], lo[8];
 #pragma unroll
           for (int x = 0; x < 8; ++x) {
             hi[x] = __bfloat162float(__float2bfloat16_rn(src[x]));
             lo[x] = src[x] - hi[x];
           }
-          st_row8(sm + B1_DEH, P128, row, cc * 2 + h, hi);
-          st_row8(sm + B1_DEL, P128, row, cc * 2 + h, lo);
+          st_row8(sm + B1_DEH, P128, row, h, hi);
+          st_row8(sm + B1_DEL, P128, row, h, lo);
         }
       }
       fence_async_smem();
@@ -378,7 +391,7 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 13) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
