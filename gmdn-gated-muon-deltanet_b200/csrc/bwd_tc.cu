@@ -65,8 +65,9 @@ constexpr uint32_t B1_WK = 98304;     // w * k
 constexpr uint32_t B1_AS = 114688;    // A (bf16), 1 panel x 64 rows
 constexpr uint32_t B1_DEH = 122880;   // dE^T hi, 1 panel x 128 rows
 constexpr uint32_t B1_DEL = 139264;   // dE^T lo
-constexpr uint32_t B1_GATE = 155648;  // beta: 2 stages x 64 floats
-constexpr uint32_t B1_BAR = 156160;
+constexpr uint32_t B1_SS = 155648;    // Sb_j hi staging for the TMA store, 2 panels x 128 rows
+constexpr uint32_t B1_GATE = 188416;  // beta: 2 stages x 64 floats
+constexpr uint32_t B1_BAR = 188928;
 constexpr uint32_t B1_SMEM = B1_BAR + 256 + 1024;
 
 // TMEM: chain accumulators C0/C1, dE^T, P (lanes 0-15), Sb hi and lo packed
@@ -85,7 +86,8 @@ static_assert(sizeof(Bars1) <= 256, "barrier block");
 
 __global__ void __launch_bounds__(kThreads1, 1)
 chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_g, BwArgs args) {
+                    const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_sb,
+                    BwArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
@@ -163,6 +165,7 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       auto issue_P = [&](int i) -> bool {
         if (!wait_use(&bars->ld_full[i & 1], i >> 1, status, ab)) return false;
         tc_fence_after();
+        #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + T1_P, desc_kmajor(stage(B1_Q, i), P64, k),
                    desc_kmajor(stage(B1_K, i), P64, k), ID_P, k > 0);
@@ -174,6 +177,7 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         const int r = i & 1;
         if (i >= 2 && !wait_use(&bars->c_empty[r], (i >> 1) - 1, status, ab)) return false;
         tc_fence_after();
+        #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + (r ? T1_C1 : T1_C0), desc_mnmajor(stage(B1_G, i), P64, k),
                    desc_mnmajor(stage(B1_Q, i), P64, k), ID_Z, k > 0);
@@ -186,12 +190,15 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         if (!wait_use(&bars->s_full, i, status, ab)) break;
         if (!wait_use(&bars->wk_full, i, status, ab)) break;
         tc_fence_after();
+        #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16_ts(tmem + T1_E, tmem + T1_SH + k * 8, desc_kmajor(wk_s, P64, k), ID_Y, k > 0);
+        #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16_ts(tmem + T1_E, tmem + T1_SL + k * 8, desc_kmajor(wk_s, P64, k), ID_Y, 1);
         if (!wait_use(&bars->as_full, i, status, ab)) break;
         tc_fence_after();
+        #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + T1_E, desc_mnmajor(stage(B1_G, i), P64, k),
                    desc_mnmajor(as_s, P64, k), ID_X, 1);
@@ -200,9 +207,11 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         if (!wait_use(&bars->de_smem, i, status, ab)) break;
         tc_fence_after();
         const uint32_t k_s = stage(B1_K, i);
+        #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + (r ? T1_C1 : T1_C0), desc_kmajor(deh_s, P128, k),
                    desc_mnmajor(k_s, P64, k), ID_W, 1);
+        #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + (r ? T1_C1 : T1_C0), desc_kmajor(del_s, P128, k),
                    desc_mnmajor(k_s, P64, k), ID_W, 1);
@@ -270,33 +279,45 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       tc_fence_before();
       mbar_arrive(&bars->c_empty[r]);
       // Sb_j as packed bf16 hi / lo pairs into TMEM (A operand of the next
-      // chain product); hi also to the history for bw2
-      uint4* gdst = nullptr;
-      if (j >= 1)
-        gdst = reinterpret_cast<uint4*>(args.Sbar_hist +
-                                        (static_cast<size_t>(bh) * N + j - 1) * kD * kD +
-                                        static_cast<size_t>(c) * kD + half * 64);
+      // chain product)
+      uint32_t ph[32];
 #pragma unroll
       for (int b = 0; b < 2; ++b) {
-        uint32_t ph[16], pl[16];
+        uint32_t pl[16], hh[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
           const float x0 = sb[b * 32 + 2 * t], x1 = sb[b * 32 + 2 * t + 1];
-          ph[t] = pack_bf16(x0, x1);
-          pl[t] = pack_bf16(x0 - bf16_lo(ph[t]), x1 - bf16_hi(ph[t]));
+          ph[b * 16 + t] = pack_bf16(x0, x1);
+          hh[t] = ph[b * 16 + t];
+          pl[t] = pack_bf16(x0 - bf16_lo(hh[t]), x1 - bf16_hi(hh[t]));
         }
-        tmem_st16(tmem + lb + T1_SH + half * 32 + b * 16, ph);
+        tmem_st16(tmem + lb + T1_SH + half * 32 + b * 16, hh);
         tmem_st16(tmem + lb + T1_SL + half * 32 + b * 16, pl);
-        if (gdst) {
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4)
-            gdst[b * 4 + q4] = make_uint4(ph[4 * q4], ph[4 * q4 + 1], ph[4 * q4 + 2], ph[4 * q4 + 3]);
-        }
       }
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&bars->s_full);
+      // history for bw2: Sb_j hi (= Sb_{(j-1)+1}) through a staging tile and
+      // one TMA store
+      if (j >= 1) {
+        if (threadIdx.x == 0) bulk_wait_read0();
+        named_sync(2, 256);
+        uint8_t* panel = sm + B1_SS + half * P128;
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4)
+          *reinterpret_cast<uint4*>(panel + sw128_chunk(c, q4)) =
+              make_uint4(ph[4 * q4], ph[4 * q4 + 1], ph[4 * q4 + 2], ph[4 * q4 + 3]);
+        fence_async_smem();
+        named_sync(2, 256);
+        if (threadIdx.x == 0) {
+          const int srow = (bh * N + j - 1) * kD;
+          tma_store_2d(&tm_sb, 0, srow, sm + B1_SS);
+          tma_store_2d(&tm_sb, 64, srow, sm + B1_SS + P128);
+          bulk_commit();
+        }
+      }
     }
+    if (threadIdx.x == 0) bulk_wait0();
   } else {
     // ------------------------------------------------------------ chunk-local (warps 8-11)
     const int tb = threadIdx.x - 256;
@@ -437,7 +458,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
 chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
                     const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_sb,
-                    BwArgs args) {
+                    const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dk,
+                    const __grid_constant__ CUtensorMap tm_dv, BwArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
@@ -512,12 +534,16 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       if (ok) {
         tc_fence_after();
         // phase 1: P = q k^T; E^T = v^T - S k^T; dQ = dO S
+        #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + T2_X0, desc_kmajor(q_s, P64, k), desc_kmajor(k_s, P64, k), ID_P, k > 0);
+        #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + T2_XE, desc_mnmajor(v_s, P64, k), desc_kmajor(id_s, P64, k), ID_EV, k > 0);
+        #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + T2_XE, desc_kmajor(s_s, P128, k), desc_kmajor(k_s, P64, k), ID_EK, 1);
+        #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + HI16 + T2_X1, desc_kmajor(g_s, P64, k), desc_mnmajor(s_s, P128, k),
                    ID_KM, k > 0);
@@ -527,13 +553,17 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       if (ok) {
         tc_fence_after();
         // phase 2: dE = A^T dO + wk Sb^T;  dA = dO E^T;  dWk = E Sb
+        #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + T2_X2, desc_mnmajor(as_s, P64, k), desc_mnmajor(g_s, P64, k), ID_MM, k > 0);
+        #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + T2_X2, desc_kmajor(wk_s, P64, k), desc_kmajor(sb_s, P128, k), ID_KK, 1);
+        #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + HI16 + T2_X0, desc_kmajor(g_s, P64, k), desc_mnmajor(e_s, P128, k), ID_DA,
                    k > 0);
+        #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + HI16 + T2_X2, desc_mnmajor(e_s, P128, k), desc_mnmajor(sb_s, P128, k),
                    ID_MM, k > 0);
@@ -543,12 +573,15 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       if (ok) {
         tc_fence_after();
         // phase 3: dq += dP k;  dK = -dE S + dP^T q
+        #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + HI16 + T2_X1, desc_kmajor(dp_s, P64, k), desc_mnmajor(k_s, P64, k), ID_KM,
                    1);
+        #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + T2_X3, desc_kmajor(de_s, P64, k), desc_mnmajor(s_s, P128, k), ID_KMN,
                    k > 0);
+        #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + T2_X3, desc_mnmajor(dp_s, P64, k), desc_mnmajor(q_s, P64, k), ID_MM, 1);
         mma_commit(&bars->ph3);
@@ -666,8 +699,8 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           }
         }
       }
-      // X2: dE (lanes 0-15) and dWk (lanes 16-31), row s = r16, 64 columns
-      uint4* dvp = reinterpret_cast<uint4*>(args.dv) + ((tok + r16) * kD) / 8;
+      // X2: dE (lanes 0-15) and dWk (lanes 16-31), row s = r16, 64 columns.
+      // dv = dE is staged in the v tile (v's last reader was phase 1).
       float dw = 0.f;
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
@@ -678,8 +711,8 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         if (!hi) {
           st_row8(sm + B2_DE, P64, r16, c0 >> 3, x);
           st_row8(sm + B2_DE, P64, r16, (c0 >> 3) + 1, x + 8);
-          dvp[c0 >> 3] = pack8(x);
-          dvp[(c0 >> 3) + 1] = pack8(x + 8);
+          st_row8(sm + B2_V, P64, r16, c0 >> 3, x);
+          st_row8(sm + B2_V, P64, r16, (c0 >> 3) + 1, x + 8);
         } else {
           float k8[8];
 #pragma unroll
@@ -694,14 +727,19 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->ep2);
+      named_sync(1, 256);
+      if (tid == 0) {
+        tma_store_2d(&tm_dv, 0, static_cast<int>(tok), sm + B2_V);
+        tma_store_2d(&tm_dv, 64, static_cast<int>(tok), sm + B2_V + P64);
+        bulk_commit();
+      }
     }
     // ---- epilogue 3: dq, dk, gate gradients
     ok = ok && wait_use(&bars->ph3, 0, status, ab);
     if (ok) {
       tc_fence_after();
       const float w = gbeta[r16];
-      uint4* dqp = reinterpret_cast<uint4*>(args.dq) + ((tok + r16) * kD) / 8;
-      uint4* dkp = reinterpret_cast<uint4*>(args.dk) + ((tok + r16) * kD) / 8;
+      // dq staged in the q tile and dk in the k tile (both last read by phase 3)
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         const int c0 = half * 64 + cc * 16;
@@ -714,17 +752,25 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 #pragma unroll
         for (int y = 0; y < 16; ++y) dwk[y] = __shfl_xor_sync(0xffffffffu, x2[y], 16);
         if (hi) {
-          dqp[c0 >> 3] = pack8(x1);
-          dqp[(c0 >> 3) + 1] = pack8(x1 + 8);
+          st_row8(sm + B2_Q, P64, r16, c0 >> 3, x1);
+          st_row8(sm + B2_Q, P64, r16, (c0 >> 3) + 1, x1 + 8);
         } else {
 #pragma unroll
           for (int y = 0; y < 16; ++y) x3[y] = fmaf(w, dwk[y], x3[y]);
-          dkp[c0 >> 3] = pack8(x3);
-          dkp[(c0 >> 3) + 1] = pack8(x3 + 8);
+          st_row8(sm + B2_K, P64, r16, c0 >> 3, x3);
+          st_row8(sm + B2_K, P64, r16, (c0 >> 3) + 1, x3 + 8);
         }
       }
+      fence_async_smem();
     }
     named_sync(1, 256);
+    if (ok && tid == 0) {
+      tma_store_2d(&tm_dq, 0, static_cast<int>(tok), sm + B2_Q);
+      tma_store_2d(&tm_dq, 64, static_cast<int>(tok), sm + B2_Q + P64);
+      tma_store_2d(&tm_dk, 0, static_cast<int>(tok), sm + B2_K);
+      tma_store_2d(&tm_dk, 64, static_cast<int>(tok), sm + B2_K + P64);
+      bulk_commit();
+    }
     if (ok && tid < kC) {
       const int s = tid;
       float db = gdw[s] + gdw[64 + s];
@@ -736,6 +782,7 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       args.dmu[g] = 0.f;
       if (args.dnu) args.dnu[g] = 0.f;
     }
+    if (tid == 0) bulk_wait0();
   }
 
   tc_fence_before();
@@ -756,12 +803,15 @@ size_t chunk_bwd_tc_workspace_bytes(int BH, int N) {
 
 cudaError_t chunk_bwd1_tc(const ChunkArgs& p, uint16_t* Sbar_hist, uint32_t* status,
                           cudaStream_t st) {
-  CUtensorMap mq, mk, mg;
+  CUtensorMap mq, mk, mg, msb;
   const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
   cudaError_t e;
   if ((e = make_tmap_rows128(&mq, p.q, rows, 64)) != cudaSuccess) return e;
   if ((e = make_tmap_rows128(&mk, p.k, rows, 64)) != cudaSuccess) return e;
   if ((e = make_tmap_rows128(&mg, p.dO, rows, 64)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&msb, Sbar_hist, static_cast<uint64_t>(p.BH) * p.N * kD, 128)) !=
+      cudaSuccess)
+    return e;
   BwArgs a{};
   a.beta = p.beta;
   a.alpha = p.alpha;
@@ -772,16 +822,19 @@ cudaError_t chunk_bwd1_tc(const ChunkArgs& p, uint16_t* Sbar_hist, uint32_t* sta
   e = cudaFuncSetAttribute(chunk_bwd1_tc_delta, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            B1_SMEM);
   if (e != cudaSuccess) return e;
-  chunk_bwd1_tc_delta<<<p.BH, kThreads1, B1_SMEM, st>>>(mq, mk, mg, a);
+  chunk_bwd1_tc_delta<<<p.BH, kThreads1, B1_SMEM, st>>>(mq, mk, mg, msb, a);
   return cudaGetLastError();
 }
 
 cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const uint16_t* S_hist, const uint16_t* Sbar_hist,
                           uint32_t* status, cudaStream_t st) {
-  CUtensorMap mq, mk, mv, mg, ms, msb;
+  CUtensorMap mq, mk, mv, mg, ms, msb, mdq, mdk, mdv;
   const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
   const uint64_t srows = static_cast<uint64_t>(p.BH) * p.N * kD;
   cudaError_t e;
+  if ((e = make_tmap_rows128(&mdq, p.dq, rows, 64)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mdk, p.dk, rows, 64)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mdv, p.dv, rows, 64)) != cudaSuccess) return e;
   if ((e = make_tmap_rows128(&mq, p.q, rows, 64)) != cudaSuccess) return e;
   if ((e = make_tmap_rows128(&mk, p.k, rows, 64)) != cudaSuccess) return e;
   if ((e = make_tmap_rows128(&mv, p.v, rows, 64)) != cudaSuccess) return e;
@@ -804,7 +857,8 @@ cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const uint16_t* S_hist, const uint
   e = cudaFuncSetAttribute(chunk_bwd2_tc_delta, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            B2_SMEM);
   if (e != cudaSuccess) return e;
-  chunk_bwd2_tc_delta<<<p.BH * p.N, kThreads2, B2_SMEM, st>>>(mq, mk, mv, mg, ms, msb, a);
+  chunk_bwd2_tc_delta<<<p.BH * p.N, kThreads2, B2_SMEM, st>>>(mq, mk, mv, mg, ms, msb, mdq, mdk,
+                                                              mdv, a);
   return cudaGetLastError();
 }
 

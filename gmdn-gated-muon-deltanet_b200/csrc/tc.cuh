@@ -171,18 +171,25 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_byte
 // K-major operand: rows = M (or N), K along the 128-byte rows.  `panel0` is
 // the first 64-column panel; `panel_stride` the byte distance to the next one
 // (K in [64, 128) lives there).  kstep counts K=16 steps.
+//
+// The descriptor of the panel is built once and the step offset is added to
+// its start-address field (bits 0-13, address / 16; no carry for shared
+// addresses below 256 KB).  With the panel loop-invariant and the step a
+// constant of an unrolled loop this is one add per MMA: the single issuing
+// thread otherwise spends ~200 cycles of dependent integer work per MMA and
+// becomes the bottleneck (measured: 245 vs 64 cycles per 128x128x16 MMA).
 __device__ __forceinline__ uint64_t desc_kmajor(uint32_t panel0, uint32_t panel_stride,
                                                 int kstep) {
   const uint32_t k = static_cast<uint32_t>(kstep) * 16u;
-  const uint32_t addr = panel0 + (k >> 6) * panel_stride + (k & 63u) * 2u;
-  return sw128_desc(addr, 16u, 1024u);
+  const uint32_t off = (k >> 6) * panel_stride + (k & 63u) * 2u;
+  return sw128_desc(panel0, 16u, 1024u) + static_cast<uint64_t>(off >> 4);
 }
 
 // MN-major operand: rows = K, M (or N) along the 128-byte rows, 64 per panel.
 __device__ __forceinline__ uint64_t desc_mnmajor(uint32_t panel0, uint32_t panel_stride,
                                                  int kstep) {
-  const uint32_t addr = panel0 + static_cast<uint32_t>(kstep) * 2048u;
-  return sw128_desc(addr, panel_stride, 1024u);
+  return sw128_desc(panel0, panel_stride, 1024u) +
+         static_cast<uint64_t>(static_cast<uint32_t>(kstep) * 128u);
 }
 
 // Instruction descriptor, kind::f16 with bf16 A/B and fp32 accumulation.
@@ -281,6 +288,25 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int x, 
       "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
+}
+
+// 2-D tiled bulk tensor store shared -> global (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const void* tmap, int x, int y, const void* src) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(tmap),
+      "r"(x), "r"(y), "r"(smem_u32(src))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until committed bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until committed bulk stores are complete.
+__device__ __forceinline__ void bulk_wait0() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 // Plain 1-D bulk copy global -> shared (16-byte aligned, size multiple of 16).
