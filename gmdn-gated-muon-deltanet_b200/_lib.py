@@ -50,6 +50,8 @@ lib.gmdn_scan_workspace_bytes.restype = _z
 lib.gmdn_scan_workspace_bytes.argtypes = [_i] * 7
 lib.gmdn_scan_fwd.restype = _i
 lib.gmdn_scan_fwd.argtypes = [_p] * 9 + [_z] + [_i] * 7 + [_p]
+lib.gmdn_scan_fwd_noalloc.restype = _i
+lib.gmdn_scan_fwd_noalloc.argtypes = [_p] * 8 + [_i] * 7 + [_p]
 lib.gmdn_scan_bwd.restype = _i
 lib.gmdn_scan_bwd.argtypes = [_p] * 16 + [_z] + [_i] * 7 + [_p]
 

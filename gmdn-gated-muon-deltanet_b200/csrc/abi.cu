@@ -484,3 +484,85 @@ int gmdn_chunk_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, cons
 }
 
 }  // extern "C"
+
+// ---- allocation-free variant of gmdn_scan_fwd --------------------------------
+//
+// Scratch of the exact-fp32 scan forward for callers that cannot allocate
+// device memory (their runtime hands a call only its operand and result
+// buffers).  One file-scope array per device: every GPU that loads this
+// library holds GMDN_NOALLOC_SCRATCH_BYTES of it until the process exits.  In
+// host code `g_noalloc_scratch` names the symbol only; its device address
+// comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[GMDN_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoallocMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device.  The first call
+// on a device looks it up (which may load this library's device code onto that
+// device); later calls read the cached pointer.
+int noalloc_scratch(float** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kNoallocMaxDevices)
+    return fail(GMDN_ERR_DEVICE, "device ordinal %d beyond the %d the static scratch tracks",
+                dev, kNoallocMaxDevices);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static scan scratch)");
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return GMDN_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int gmdn_scan_fwd_noalloc(const float* U, const float* K, const float* a, const float* b,
+                          const float* m, const float* n, float* S_out, void* saved, int B,
+                          int H, int N, int dh, int rule, int ns, int precision,
+                          void* stream) {
+  g_last_error.clear();
+  int rc = check_common(B, H, N, dh, rule, ns, precision);
+  if (rc) return rc;
+  if (B * H * N == 0) return GMDN_OK;
+  if (!U || !K || !a || !b || !m || !n || !S_out)
+    return fail(GMDN_ERR_INVALID, "null input/output pointer");
+  if (rule != 0 && !saved) return fail(GMDN_ERR_INVALID, "muon/adam need the saved buffer");
+  // The forward kernel uses kScanFwdScratchMats dh x dh fp32 matrices per (b,h).
+  const size_t per_bh = mats(gmdn::kScanFwdScratchMats, dh) * sizeof(float);
+  const size_t need = static_cast<size_t>(B) * H * per_bh;
+  if (need > GMDN_NOALLOC_SCRATCH_BYTES)
+    return fail(GMDN_ERR_WORKSPACE,
+                "gmdn_scan_fwd_noalloc: B*H = %d at dh = %d needs %zu scratch bytes, more than "
+                "the %zu-byte static scratch (at most %zu (b,h) pairs at this dh); call "
+                "gmdn_scan_fwd with a workspace instead",
+                B * H, dh, need, static_cast<size_t>(GMDN_NOALLOC_SCRATCH_BYTES),
+                static_cast<size_t>(GMDN_NOALLOC_SCRATCH_BYTES) / per_bh);
+  float* scratch = nullptr;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  ScanSaved sv = carve_scan_saved(saved, B * H, N, dh, rule);
+  gmdn::ScanArgs p{};
+  p.U = U; p.K = K; p.a = a; p.b = b; p.m = m; p.n = n;
+  p.S = S_out; p.M_hist = sv.M_hist; p.V_hist = sv.V_hist;
+  p.scratch = scratch;
+  p.BH = B * H; p.N = N; p.dh = dh; p.rule = rule; p.ns = ns;
+  // The kernel zeroes its state and moment matrices before the first chunk and
+  // writes every other scratch matrix before reading it, so what an earlier
+  // call left in the array never reaches the result.
+  cudaError_t e = gmdn::scan_fwd_ieee(p, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "scan_fwd_ieee (static scratch)");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return GMDN_OK;
+}
+
+}  // extern "C"

@@ -87,6 +87,38 @@ int gmdn_scan_bwd(const float* U, const float* K, const float* a, const float* b
                   size_t workspace_bytes, int B, int H, int N, int dh, int rule,
                   int ns, int precision, void* stream);
 
+/* Size of the device scratch array gmdn_scan_fwd_noalloc uses: 16 MiB, held
+ * by every GPU that loads this library until the process exits. */
+#define GMDN_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+/* gmdn_scan_fwd without a workspace: same arguments, results and precision,
+ * but its scratch is a fixed device array inside this library, so the call
+ * allocates nothing.  No counterpart in the reference (its Triton wrapper
+ * allocates with torch, fast_scan.py:366-368).
+ *
+ * For callers that cannot allocate device memory: a runtime that owns every
+ * device buffer and hands a foreign call only its operands and results (a
+ * framework's custom-call hook, a fixed-pool embedded runtime).  A cudaMalloc
+ * from inside such a call goes around that runtime's memory pool: it can fail
+ * once the pool has reserved the GPU, and cudaMalloc / cudaFree may
+ * synchronise the device and stall the caller's other streams.
+ *
+ * Limit: B*H*6*dh*dh*4 bytes <= GMDN_NOALLOC_SCRATCH_BYTES, i.e. at most 42
+ * (b,h) pairs at dh 128, 170 at dh 64, 682 at dh 32, 2730 at dh 16; larger
+ * calls return GMDN_ERR_WORKSPACE with the limit in the message.  The caller
+ * still passes inputs, S_out and (muon / adam) `saved`.
+ *
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture.  Every call on a device shares the one array,
+ * which keeps the last call's contents (the kernel clears what must start at
+ * zero): calls that overlap on the GPU, from two streams or two host threads,
+ * race on it and give wrong results, so keep them in order on one stream. */
+int gmdn_scan_fwd_noalloc(const float* U, const float* K, const float* a,
+                          const float* b, const float* m, const float* n,
+                          float* S_out, void* saved, int B, int H, int N, int dh,
+                          int rule, int ns, int precision, void* stream);
+
 /* ---- mixer core: train_ablation.py:142-187 ------------------------------- */
 
 /* Bytes of `saved` the chunk forward fills for the chunk backward. */
