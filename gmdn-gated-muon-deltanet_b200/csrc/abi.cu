@@ -90,9 +90,8 @@ ScanSaved carve_scan_saved(void* saved, int BH, int N, int dh, int rule) {
 struct ChunkBufs {
   // saved (forward -> backward)
   float *S, *M_hist, *V_hist;   // exact path: fp32 states and moments
-  uint16_t* S_hist;             // tensor-core path: bf16 states
+  gmdn::TcBufs tc;              // tensor-core path
   size_t saved_bytes;
-  uint16_t* Sbar_hist;          // tensor-core path: bf16 state cotangents
   // workspace
   uint32_t* status;             // device status word (first 256 bytes)
   float *Kw, *Uv, *gS, *dUv, *dKw;
@@ -102,8 +101,9 @@ struct ChunkBufs {
 };
 
 // `fast`: the tensor-core path (fused forward, two-kernel backward).  Its
-// saved buffer holds the bf16 states S_j; its workspace the device status
-// word and the bf16 state cotangents Sb_{j+1}.
+// saved buffer holds the bf16 states S_j (adam: also G_j and the pre-update
+// moments); its workspace the device status word, the bf16 cotangents of G_j
+// and, for adam, the fp32 moment slabs and the chunk-scalar cotangents.
 ChunkBufs carve_chunk(void* saved, void* ws, int BH, int N, int dh, int rule, int ns,
                       bool fast) {
   ChunkBufs b{};
@@ -113,9 +113,24 @@ ChunkBufs carve_chunk(void* saved, void* ws, int BH, int N, int dh, int rule, in
   Carver cw(ws);
   b.status = reinterpret_cast<uint32_t*>(cw.take(64));
   if (fast) {
-    b.S_hist = reinterpret_cast<uint16_t*>(cs.take((per + 1) / 2));
+    auto half_mats = [&](Carver& c) { return reinterpret_cast<uint16_t*>(c.take((per + 1) / 2)); };
+    b.tc.status = b.status;
+    b.tc.S_hist = half_mats(cs);
+    if (rule == 2) {
+      b.tc.G_hist = half_mats(cs);
+      b.tc.Mp_hist = half_mats(cs);
+      b.tc.Vp_hist = half_mats(cs);
+    }
     b.saved_bytes = cs.used;
-    b.Sbar_hist = reinterpret_cast<uint16_t*>(cw.take((per + 1) / 2));
+    b.tc.Gbar_hist = half_mats(cw);
+    if (rule == 2) {
+      b.tc.M_ws = cw.take(mats(BH, dh));
+      b.tc.V_ws = cw.take(mats(BH, dh));
+      b.tc.dac = cw.take(sc);
+      b.tc.dbc = cw.take(sc);
+      b.tc.dmc = cw.take(sc);
+      b.tc.dnc = cw.take(sc);
+    }
     b.ws_bytes = cw.used;
     return b;
   }
@@ -416,7 +431,7 @@ int gmdn_chunk_fwd_ex(const void* q, const void* k, const void* v, const float* 
   cudaError_t e = cudaMemsetAsync(bufs.status, 0, sizeof(uint32_t), st);
   if (e != cudaSuccess) return cuda_fail(e, "status reset");
   if (fast) {
-    GMDN_LAUNCH(gmdn::chunk_fwd_tc(p, bufs.S_hist, bufs.status, st), "chunk_fwd_tc");
+    GMDN_LAUNCH(gmdn::chunk_fwd_tc(p, bufs.tc, st), "chunk_fwd_tc");
     return GMDN_OK;
   }
   gmdn::ScanArgs sp = scan_args_from(p, bufs, ns);
@@ -450,9 +465,8 @@ int gmdn_chunk_bwd_ex(const void* q, const void* k, const void* v, const float* 
   cudaError_t e = cudaMemsetAsync(bufs.status, 0, sizeof(uint32_t), st);
   if (e != cudaSuccess) return cuda_fail(e, "status reset");
   if (fast) {
-    GMDN_LAUNCH(gmdn::chunk_bwd1_tc(p, bufs.Sbar_hist, bufs.status, st), "chunk_bwd1_tc");
-    GMDN_LAUNCH(gmdn::chunk_bwd2_tc(p, bufs.S_hist, bufs.Sbar_hist, bufs.status, st),
-                "chunk_bwd2_tc");
+    GMDN_LAUNCH(gmdn::chunk_bwd1_tc(p, bufs.tc, st), "chunk_bwd1_tc");
+    GMDN_LAUNCH(gmdn::chunk_bwd2_tc(p, bufs.tc, st), "chunk_bwd2_tc");
     return GMDN_OK;
   }
   gmdn::ScanArgs sp = scan_args_from(p, bufs, ns);

@@ -1,4 +1,4 @@
-// Tensor-core backward of the mixer core, delta rule, dh = 128, C = 64.
+// Tensor-core backward of the mixer core, delta and adam rules, dh = 128, C = 64.
 //
 // The backward is written in the residual form of the chunk update: with
 // E_j = v_j - k_j S_j^T (the errors of chunk j against the frozen state) the
@@ -18,13 +18,22 @@
 // (identical to the reference's autograd of train_ablation.py:142-187 with
 // fast_scan.py:72-95; checked against it in tests/).
 //
-// bw1: one CTA per (b, h) walks the chunks in reverse and produces Sb_{j+1}
-//      for every chunk (bf16, for bw2).  The chain products use split bf16
+// Adam (w = 1) replaces Sb_{j+1} in dE_j and dk_j by Gb_j, the cotangent of
+// G_j, which the reverse chain forms per element from Sb_{j+1}, the moment
+// cotangents Mb, Vb and the forward's G_j, M_j, V_j (fast_scan.py:168-182):
+//
+//   Mi = mu M_j + (1 - mu) G,  Vi = nu V_j + (1 - nu) G^2,  den = sqrt(Vi) + 1e-6
+//   Mt = Mb + b Sb / den,      Vt = Vb - b Sb Mi / den^2 / (2 max(sqrt(Vi), 1e-12))
+//   Gb = (1 - mu) Mt + 2 (1 - nu) G Vt,   Mb <- mu Mt,   Vb <- nu Vt
+//   da_c = <Sb, S_j>, db_c = <Sb, Mi / den>, dmu_c = <Mt, M_j - G>, dnu_c = <Vt, V_j - G^2>
+//
+// bw1: one CTA per (b, h) walks the chunks in reverse and produces Gb_j
+//      (= Sb_{j+1} for delta) for every chunk (bf16, for bw2).  The chain products use split bf16
 //      (hi + lo) operands for Sb and dE; Sb hi/lo live in TMEM as the A
 //      operand of their product, so the recurrence never touches shared
 //      memory.
 // bw2: one CTA per (b, h, chunk) computes every token and gate gradient of
-//      its chunk from q, k, v, dO, S_j and Sb_{j+1}.
+//      its chunk from q, k, v, dO, S_j and Gb_j.
 
 #include <cuda.h>
 
@@ -46,7 +55,12 @@ constexpr uint32_t HI16 = 16u << 16;
 struct BwArgs {
   const float* beta;
   const float* alpha;
-  uint16_t* Sbar_hist;
+  const float *mu, *nu;
+  uint16_t* Gbar_hist;
+  const uint16_t* S_hist;
+  const uint16_t *G_hist, *Mp_hist, *Vp_hist;  // adam
+  float *M_ws, *V_ws;                          // adam: Mb, Vb slabs
+  float *dac, *dbc, *dmc, *dnc;                // adam: chunk-scalar cotangents
   uint16_t *dq, *dk, *dv;
   float *dalpha, *dbeta, *dmu, *dnu;
   uint32_t* status;
@@ -65,12 +79,13 @@ constexpr uint32_t B1_WK = 98304;     // w * k
 constexpr uint32_t B1_AS = 114688;    // A (bf16), 1 panel x 64 rows
 constexpr uint32_t B1_DEH = 122880;   // dE^T hi, 1 panel x 128 rows
 constexpr uint32_t B1_DEL = 139264;   // dE^T lo
-constexpr uint32_t B1_SS = 155648;    // Sb_j hi staging for the TMA store, 2 panels x 128 rows
+constexpr uint32_t B1_SS = 155648;    // Gb hi staging for the TMA store, 2 panels x 128 rows
 constexpr uint32_t B1_GATE = 188416;  // beta: 2 stages x 64 floats
-constexpr uint32_t B1_BAR = 188928;
+constexpr uint32_t B1_RED = 188928;   // adam: per-warp partial chunk-scalar cotangents [8][4]
+constexpr uint32_t B1_BAR = 189056;
 constexpr uint32_t B1_SMEM = B1_BAR + 256 + 1024;
 
-// TMEM: chain accumulators C0/C1, dE^T, P (lanes 0-15), Sb hi and lo packed
+// TMEM: chain accumulators C0/C1, dE^T, P (lanes 0-15), Gb hi and lo packed
 // bf16 pairs (64 columns each = 128 values per lane).
 constexpr uint32_t T1_C0 = 0, T1_C1 = 128, T1_E = 256, T1_P = 320, T1_SH = 384, T1_SL = 448;
 
@@ -84,8 +99,9 @@ struct Bars1 {
 };
 static_assert(sizeof(Bars1) <= 256, "barrier block");
 
+template <int RULE>
 __global__ void __launch_bounds__(kThreads1, 1)
-chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_sb,
                     BwArgs args) {
   extern __shared__ uint8_t smem_raw[];
@@ -243,15 +259,127 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       tmem_st_wait();
       if (N > 0) {
         uint4* g = reinterpret_cast<uint4*>(
-            args.Sbar_hist + (static_cast<size_t>(bh) * N + N - 1) * kD * kD +
+            args.Gbar_hist + (static_cast<size_t>(bh) * N + N - 1) * kD * kD +
             static_cast<size_t>(c) * kD + half * 64);
         const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
         for (int i = 0; i < 8; ++i) g[i] = z;
+        if (RULE == 2 && threadIdx.x == 0) {
+          const size_t last = static_cast<size_t>(bh) * N + N - 1;
+          args.dac[last] = args.dbc[last] = args.dmc[last] = args.dnc[last] = 0.f;
+        }
       }
     }
     tc_fence_before();
     mbar_arrive(&bars->s_full);
+    // Adam: Gb_jm, Mb, Vb and the chunk-scalar cotangents of chunk jm from
+    // sb = Sb_{jm+1}; Gb_jm hi / lo go to TMEM for the next chain product and
+    // Gb_jm hi to the history.  Works in 8-column groups to stay in registers.
+    auto adam_pass = [&](int jm) -> bool {
+      const size_t mm = static_cast<size_t>(bh) * N + jm;
+      const float* be = args.beta + tok0 + jm * kC;
+      const float* mu = args.mu + tok0 + jm * kC;
+      const float* nu = args.nu + tok0 + jm * kC;
+      const float b = warp_sum(__ldg(be + lane) + __ldg(be + lane + 32)) * (1.f / kC);
+      const float mc = expf(warp_sum(logf(fmaxf(__ldg(mu + lane), kGateFloor)) +
+                                     logf(fmaxf(__ldg(mu + lane + 32), kGateFloor))));
+      const float nc = expf(warp_sum(logf(fmaxf(__ldg(nu + lane), kGateFloor)) +
+                                     logf(fmaxf(__ldg(nu + lane + 32), kGateFloor))));
+      const bool have_bar = jm + 2 < N;   // Mb, Vb of chunk jm + 1 exist (else zero)
+      const uint4* srow = reinterpret_cast<const uint4*>(args.S_hist + (mm * kD + c) * kD + half * 64);
+      float pda = 0.f, pdb = 0.f, pdm = 0.f, pdn = 0.f;
+      if (threadIdx.x == 0) bulk_wait_read0();
+      named_sync(2, 256);
+      uint8_t* panel = sm + B1_SS + half * P128;
+#pragma unroll
+      for (int g8 = 0; g8 < 8; ++g8) {
+        float g[8], mp[8], vp[8], sv[8], mb[8], vb[8], gb[8];
+        unpack8(*slab_bf16(const_cast<uint16_t*>(args.G_hist), mm, half, g8, c), g);
+        unpack8(*slab_bf16(const_cast<uint16_t*>(args.Mp_hist), mm, half, g8, c), mp);
+        unpack8(*slab_bf16(const_cast<uint16_t*>(args.Vp_hist), mm, half, g8, c), vp);
+        unpack8(srow[g8], sv);
+        float4* mbp = slab_f32(args.M_ws, bh, half, 2 * g8, c);
+        float4* vbp = slab_f32(args.V_ws, bh, half, 2 * g8, c);
+        if (have_bar) {
+          const float4 m0 = mbp[0], m1 = mbp[128], v0 = vbp[0], v1 = vbp[128];
+          mb[0] = m0.x; mb[1] = m0.y; mb[2] = m0.z; mb[3] = m0.w;
+          mb[4] = m1.x; mb[5] = m1.y; mb[6] = m1.z; mb[7] = m1.w;
+          vb[0] = v0.x; vb[1] = v0.y; vb[2] = v0.z; vb[3] = v0.w;
+          vb[4] = v1.x; vb[5] = v1.y; vb[6] = v1.z; vb[7] = v1.w;
+        } else {
+#pragma unroll
+          for (int t = 0; t < 8; ++t) mb[t] = vb[t] = 0.f;
+        }
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const float sbar = sb[8 * g8 + t];
+          const float mi = fmaf(mc, mp[t], (1.f - mc) * g[t]);
+          const float vi = fmaf(nc, vp[t], (1.f - nc) * (g[t] * g[t]));
+          const float root = sqrtf(vi);
+          const float den = root + kEpsAdam;
+          pda = fmaf(sbar, sv[t], pda);
+          pdb = fmaf(sbar, mi / den, pdb);
+          const float ub = b * sbar;
+          const float mt = mb[t] + ub / den;
+          const float vt = vb[t] - ub * mi / (den * den) / (2.f * fmaxf(root, 1e-12f));
+          pdm = fmaf(mt, mp[t] - g[t], pdm);
+          pdn = fmaf(vt, vp[t] - g[t] * g[t], pdn);
+          mb[t] = mc * mt;
+          vb[t] = nc * vt;
+          gb[t] = fmaf(1.f - mc, mt, 2.f * (1.f - nc) * g[t] * vt);
+        }
+        if (jm >= 1) {
+          mbp[0] = make_float4(mb[0], mb[1], mb[2], mb[3]);
+          mbp[128] = make_float4(mb[4], mb[5], mb[6], mb[7]);
+          vbp[0] = make_float4(vb[0], vb[1], vb[2], vb[3]);
+          vbp[128] = make_float4(vb[4], vb[5], vb[6], vb[7]);
+        }
+        const uint4 hh = pack8(gb);
+        uint4 pl;
+        pl.x = pack_bf16(gb[0] - bf16_lo(hh.x), gb[1] - bf16_hi(hh.x));
+        pl.y = pack_bf16(gb[2] - bf16_lo(hh.y), gb[3] - bf16_hi(hh.y));
+        pl.z = pack_bf16(gb[4] - bf16_lo(hh.z), gb[5] - bf16_hi(hh.z));
+        pl.w = pack_bf16(gb[6] - bf16_lo(hh.w), gb[7] - bf16_hi(hh.w));
+        tmem_st4(tmem + lb + T1_SH + half * 32 + g8 * 4, hh);
+        tmem_st4(tmem + lb + T1_SL + half * 32 + g8 * 4, pl);
+        *reinterpret_cast<uint4*>(panel + sw128_chunk(c, g8)) = hh;
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&bars->s_full);
+      float* red = reinterpret_cast<float*>(sm + B1_RED);
+      pda = warp_sum(pda);
+      pdb = warp_sum(pdb);
+      pdm = warp_sum(pdm);
+      pdn = warp_sum(pdn);
+      if (lane == 0) {
+        red[warp * 4 + 0] = pda;
+        red[warp * 4 + 1] = pdb;
+        red[warp * 4 + 2] = pdm;
+        red[warp * 4 + 3] = pdn;
+      }
+      fence_async_smem();
+      named_sync(2, 256);
+      if (threadIdx.x == 0) {
+        const int hrow = (bh * N + jm) * kD;
+        tma_store_2d(&tm_sb, 0, hrow, sm + B1_SS);
+        tma_store_2d(&tm_sb, 64, hrow, sm + B1_SS + P128);
+        bulk_commit();
+        float t0 = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          t0 += red[w * 4 + 0];
+          t1 += red[w * 4 + 1];
+          t2 += red[w * 4 + 2];
+          t3 += red[w * 4 + 3];
+        }
+        args.dac[mm] = t0;
+        args.dbc[mm] = t1;
+        args.dmc[mm] = t2;
+        args.dnc[mm] = t3;
+      }
+      return true;
+    };
     for (int i = 0; i < N; ++i) {
       const int j = N - 1 - i, r = i & 1;
       const float* al = args.alpha + tok0 + j * kC;
@@ -278,6 +406,9 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       tc_fence_before();
       mbar_arrive(&bars->c_empty[r]);
+      if constexpr (RULE == 2) {
+        if (j >= 1 && !adam_pass(j - 1)) break;
+      } else {
       // Sb_j as packed bf16 hi / lo pairs into TMEM (A operand of the next
       // chain product)
       uint32_t ph[32];
@@ -316,6 +447,7 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           bulk_commit();
         }
       }
+      }
     }
     if (threadIdx.x == 0) bulk_wait0();
   } else {
@@ -335,13 +467,15 @@ chunk_bwd1_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       for (int m = 0; m < 8; ++m) {
         const int id = tb + 128 * m;
         const uint32_t off = static_cast<uint32_t>(id) * 16u;
-        const float w = bs[(id & 511) >> 3];
         const uint4 x = *reinterpret_cast<const uint4*>(ks + off);
-        uint4 y;
-        y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
-        y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
-        y.z = pack_bf16(bf16_lo(x.z) * w, bf16_hi(x.z) * w);
-        y.w = pack_bf16(bf16_lo(x.w) * w, bf16_hi(x.w) * w);
+        uint4 y = x;
+        if constexpr (RULE == 0) {  // delta: w = beta; adam: w = 1
+          const float w = bs[(id & 511) >> 3];
+          y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
+          y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
+          y.z = pack_bf16(bf16_lo(x.z) * w, bf16_hi(x.z) * w);
+          y.w = pack_bf16(bf16_lo(x.w) * w, bf16_hi(x.w) * w);
+        }
         *reinterpret_cast<uint4*>(wk + off) = y;
       }
       fence_async_smem();
@@ -451,11 +585,12 @@ struct Bars2 {
   uint32_t tmem_base;
   int abort_flag;
   float da;
-  float a_c;
+  float a_c, m_c, n_c;
 };
 
+template <int RULE>
 __global__ void __launch_bounds__(kThreads2, 1)
-chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
                     const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_sb,
                     const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dk,
@@ -473,7 +608,7 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   const int N = args.N;
   const int bh = blockIdx.x / N, j = blockIdx.x % N;
   const size_t tok = static_cast<size_t>(bh) * args.T + static_cast<size_t>(j) * kC;
-  const int srow = (bh * N + j) * kD;  // first row of S_j / Sb_{j+1} in the histories
+  const int srow = (bh * N + j) * kD;  // first row of S_j / Gb_j in the histories
   uint32_t* status = args.status;
 
   if (threadIdx.x == 0) {
@@ -599,39 +734,50 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     const int c128 = sp * 32 + lane;           // M=128 row (TMEM lane)
     bool ok = wait_use(&bars->ld_full, 0, status, ab);
     if (ok) {
-      // w * k (delta: w = beta)
+      // w * k (delta: w = beta; adam: w = 1)
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
         const int id = tid + 256 * m;
         const uint32_t off = static_cast<uint32_t>(id) * 16u;
-        const float w = gbeta[(id & 511) >> 3];
         const uint4 x = *reinterpret_cast<const uint4*>(sm + B2_K + off);
-        uint4 y;
-        y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
-        y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
-        y.z = pack_bf16(bf16_lo(x.z) * w, bf16_hi(x.z) * w);
-        y.w = pack_bf16(bf16_lo(x.w) * w, bf16_hi(x.w) * w);
+        uint4 y = x;
+        if constexpr (RULE == 0) {
+          const float w = gbeta[(id & 511) >> 3];
+          y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
+          y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
+          y.z = pack_bf16(bf16_lo(x.z) * w, bf16_hi(x.z) * w);
+          y.w = pack_bf16(bf16_lo(x.w) * w, bf16_hi(x.w) * w);
+        }
         *reinterpret_cast<uint4*>(sm + B2_WK + off) = y;
       }
       fence_async_smem();
       mbar_arrive(&bars->wk_full);
-      // da = <Sb_{j+1}, S_j>: row c128, column half `half`
-      float part = 0.f;
+      if constexpr (RULE == 0) {
+        // da = <Sb_{j+1}, S_j>: row c128, column half `half` (adam: from the chain)
+        float part = 0.f;
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        float a8[8], b8[8];
-        unpack8(ld_row8(sm + B2_S, P128, c128, half * 8 + c8), a8);
-        unpack8(ld_row8(sm + B2_SB, P128, c128, half * 8 + c8), b8);
+        for (int c8 = 0; c8 < 8; ++c8) {
+          float a8[8], b8[8];
+          unpack8(ld_row8(sm + B2_S, P128, c128, half * 8 + c8), a8);
+          unpack8(ld_row8(sm + B2_SB, P128, c128, half * 8 + c8), b8);
 #pragma unroll
-        for (int x = 0; x < 8; ++x) part = fmaf(a8[x], b8[x], part);
+          for (int x = 0; x < 8; ++x) part = fmaf(a8[x], b8[x], part);
+        }
+        part = warp_sum(part);
+        if (lane == 0) atomicAdd(&bars->da, part);
       }
-      part = warp_sum(part);
-      if (lane == 0) atomicAdd(&bars->da, part);
       if (warp == 0) {  // chunk decay product a_c = prod clamp(alpha)
         const float la = logf(fmaxf(galpha[lane], kGateFloor)) +
                          logf(fmaxf(galpha[lane + 32], kGateFloor));
         const float sum = warp_sum(la);
         if (lane == 0) bars->a_c = expf(sum);
+      }
+      if (RULE == 2 && (warp == 1 || warp == 2)) {  // mu_c, nu_c
+        const float* gsrc = (warp == 1 ? args.mu : args.nu) + tok;
+        const float lg = logf(fmaxf(__ldg(gsrc + lane), kGateFloor)) +
+                         logf(fmaxf(__ldg(gsrc + lane + 32), kGateFloor));
+        const float sum = warp_sum(lg);
+        if (lane == 0) (warp == 1 ? bars->m_c : bars->n_c) = expf(sum);
       }
     }
     // ---- epilogue 1: A = tril(P) beta (lanes 0-15), E^T -> bf16 (all lanes)
@@ -723,7 +869,7 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           }
         }
       }
-      if (hi) gdw[half * 64 + r16] = dw;
+      if (RULE == 0 && hi) gdw[half * 64 + r16] = dw;
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->ep2);
@@ -738,7 +884,7 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     ok = ok && wait_use(&bars->ph3, 0, status, ab);
     if (ok) {
       tc_fence_after();
-      const float w = gbeta[r16];
+      const float w = RULE == 0 ? gbeta[r16] : 1.f;
       // dq staged in the q tile and dk in the k tile (both last read by phase 3)
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
@@ -773,14 +919,26 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     }
     if (ok && tid < kC) {
       const int s = tid;
-      float db = gdw[s] + gdw[64 + s];
+      float db = 0.f;
       for (int t = s; t < kC; ++t) db += red[t * 65 + s];
       const float al = galpha[s];
       const size_t g = tok + s;
-      args.dbeta[g] = db;
-      args.dalpha[g] = (al >= kGateFloor) ? bars->da * bars->a_c / fmaxf(al, kGateFloor) : 0.f;
-      args.dmu[g] = 0.f;
-      if (args.dnu) args.dnu[g] = 0.f;
+      if constexpr (RULE == 2) {
+        // chunk scalars: b_c = mean(beta), a_c / mu_c / nu_c = prod of the clamped gates
+        const size_t gi = static_cast<size_t>(bh) * N + j;
+        args.dbeta[g] = db + args.dbc[gi] * (1.f / kC);
+        args.dalpha[g] =
+            (al >= kGateFloor) ? args.dac[gi] * bars->a_c / fmaxf(al, kGateFloor) : 0.f;
+        const float mu = __ldg(args.mu + g), nu = __ldg(args.nu + g);
+        args.dmu[g] = (mu >= kGateFloor) ? args.dmc[gi] * bars->m_c / fmaxf(mu, kGateFloor) : 0.f;
+        args.dnu[g] = (nu >= kGateFloor) ? args.dnc[gi] * bars->n_c / fmaxf(nu, kGateFloor) : 0.f;
+      } else {
+        args.dbeta[g] = db + gdw[s] + gdw[64 + s];
+        args.dalpha[g] =
+            (al >= kGateFloor) ? bars->da * bars->a_c / fmaxf(al, kGateFloor) : 0.f;
+        args.dmu[g] = 0.f;
+        if (args.dnu) args.dnu[g] = 0.f;
+      }
     }
     if (tid == 0) bulk_wait0();
   }
@@ -797,53 +955,25 @@ chunk_bwd2_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 
 bool chunk_bwd_tc_supported(const ChunkArgs& p) { return chunk_fwd_tc_supported(p); }
 
-size_t chunk_bwd_tc_workspace_bytes(int BH, int N) {
-  return static_cast<size_t>(BH) * N * kD * kD * sizeof(uint16_t);
-}
+namespace {
 
-cudaError_t chunk_bwd1_tc(const ChunkArgs& p, uint16_t* Sbar_hist, uint32_t* status,
-                          cudaStream_t st) {
-  CUtensorMap mq, mk, mg, msb;
-  const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
-  cudaError_t e;
-  if ((e = make_tmap_rows128(&mq, p.q, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mk, p.k, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mg, p.dO, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&msb, Sbar_hist, static_cast<uint64_t>(p.BH) * p.N * kD, 128)) !=
-      cudaSuccess)
-    return e;
+BwArgs bw_args(const ChunkArgs& p, const TcBufs& b) {
   BwArgs a{};
   a.beta = p.beta;
   a.alpha = p.alpha;
-  a.Sbar_hist = Sbar_hist;
-  a.status = status;
-  a.N = p.N;
-  a.T = p.T;
-  e = cudaFuncSetAttribute(chunk_bwd1_tc_delta, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           B1_SMEM);
-  if (e != cudaSuccess) return e;
-  chunk_bwd1_tc_delta<<<p.BH, kThreads1, B1_SMEM, st>>>(mq, mk, mg, msb, a);
-  return cudaGetLastError();
-}
-
-cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const uint16_t* S_hist, const uint16_t* Sbar_hist,
-                          uint32_t* status, cudaStream_t st) {
-  CUtensorMap mq, mk, mv, mg, ms, msb, mdq, mdk, mdv;
-  const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
-  const uint64_t srows = static_cast<uint64_t>(p.BH) * p.N * kD;
-  cudaError_t e;
-  if ((e = make_tmap_rows128(&mdq, p.dq, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mdk, p.dk, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mdv, p.dv, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mq, p.q, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mk, p.k, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mv, p.v, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mg, p.dO, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&ms, S_hist, srows, 128)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&msb, Sbar_hist, srows, 128)) != cudaSuccess) return e;
-  BwArgs a{};
-  a.beta = p.beta;
-  a.alpha = p.alpha;
+  a.mu = p.mu;
+  a.nu = p.nu;
+  a.Gbar_hist = b.Gbar_hist;
+  a.S_hist = b.S_hist;
+  a.G_hist = b.G_hist;
+  a.Mp_hist = b.Mp_hist;
+  a.Vp_hist = b.Vp_hist;
+  a.M_ws = b.M_ws;
+  a.V_ws = b.V_ws;
+  a.dac = b.dac;
+  a.dbc = b.dbc;
+  a.dmc = b.dmc;
+  a.dnc = b.dnc;
   a.dq = static_cast<uint16_t*>(p.dq);
   a.dk = static_cast<uint16_t*>(p.dk);
   a.dv = static_cast<uint16_t*>(p.dv);
@@ -851,15 +981,74 @@ cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const uint16_t* S_hist, const uint
   a.dbeta = p.dbeta;
   a.dmu = p.dmu;
   a.dnu = p.dnu;
-  a.status = status;
+  a.status = b.status;
   a.N = p.N;
   a.T = p.T;
-  e = cudaFuncSetAttribute(chunk_bwd2_tc_delta, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           B2_SMEM);
+  return a;
+}
+
+bool adam_bufs_ok(const ChunkArgs& p, const TcBufs& b) {
+  return p.nu && b.G_hist && b.Mp_hist && b.Vp_hist && b.M_ws && b.V_ws && b.dac && b.dbc &&
+         b.dmc && b.dnc;
+}
+
+template <int RULE>
+cudaError_t launch_bw1(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mg,
+                       const CUtensorMap& msb, const BwArgs& a, int grid, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(chunk_bwd1_tc_kernel<RULE>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, B1_SMEM);
   if (e != cudaSuccess) return e;
-  chunk_bwd2_tc_delta<<<p.BH * p.N, kThreads2, B2_SMEM, st>>>(mq, mk, mv, mg, ms, msb, mdq, mdk,
-                                                              mdv, a);
+  chunk_bwd1_tc_kernel<RULE><<<grid, kThreads1, B1_SMEM, st>>>(mq, mk, mg, msb, a);
   return cudaGetLastError();
+}
+
+template <int RULE>
+cudaError_t launch_bw2(const CUtensorMap* m, const BwArgs& a, int grid, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(chunk_bwd2_tc_kernel<RULE>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, B2_SMEM);
+  if (e != cudaSuccess) return e;
+  chunk_bwd2_tc_kernel<RULE><<<grid, kThreads2, B2_SMEM, st>>>(m[0], m[1], m[2], m[3], m[4],
+                                                              m[5], m[6], m[7], m[8], a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t chunk_bwd1_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st) {
+  CUtensorMap mq, mk, mg, msb;
+  const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
+  cudaError_t e;
+  if ((e = make_tmap_rows128(&mq, p.q, rows, 64)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mk, p.k, rows, 64)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mg, p.dO, rows, 64)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&msb, b.Gbar_hist, static_cast<uint64_t>(p.BH) * p.N * kD, 128)) !=
+      cudaSuccess)
+    return e;
+  const BwArgs a = bw_args(p, b);
+  if (p.rule == 2) {
+    if (!adam_bufs_ok(p, b)) return cudaErrorInvalidValue;
+    return launch_bw1<2>(mq, mk, mg, msb, a, p.BH, st);
+  }
+  return launch_bw1<0>(mq, mk, mg, msb, a, p.BH, st);
+}
+
+cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st) {
+  // q, k, v, dO, S_j, Gb_j, dq, dk, dv
+  CUtensorMap m[9];
+  const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
+  const uint64_t srows = static_cast<uint64_t>(p.BH) * p.N * kD;
+  const void* base[9] = {p.q, p.k, p.v, p.dO, b.S_hist, b.Gbar_hist, p.dq, p.dk, p.dv};
+  for (int i = 0; i < 9; ++i) {
+    const bool hist = i == 4 || i == 5;
+    cudaError_t e = make_tmap_rows128(&m[i], base[i], hist ? srows : rows, hist ? 128 : 64);
+    if (e != cudaSuccess) return e;
+  }
+  const BwArgs a = bw_args(p, b);
+  if (p.rule == 2) {
+    if (!adam_bufs_ok(p, b) || !p.dnu) return cudaErrorInvalidValue;
+    return launch_bw2<2>(m, a, p.BH * p.N, st);
+  }
+  return launch_bw2<0>(m, a, p.BH * p.N, st);
 }
 
 }  // namespace gmdn

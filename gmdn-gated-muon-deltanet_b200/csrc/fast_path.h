@@ -7,21 +7,39 @@
 
 namespace gmdn {
 
-// Fused mixer core forward (phases 1-3), delta rule, dh 128, chunk 64, bf16.
+// Buffers of the tensor-core path, carved by the C ABI from the caller's
+// `saved` (forward -> backward) and `workspace` buffers.
+//
+// Per-thread slab layouts: the state warps own row c (a TMEM lane) and one
+// half (64 columns) of every dh x dh matrix.  Matrices only they touch are
+// stored so that one warp-wide 16-byte access covers 512 contiguous bytes:
+//   fp32 slab: float4 index ((bh * 2 + half) * 16 + f) * 128 + c, f = column / 4 in the half
+//   bf16 slab: uint4 index ((m * 2 + half) * 8 + g) * 128 + c, g = column / 8 in the half,
+//              m = bh * N + j (one matrix per chunk)
+struct TcBufs {
+  uint32_t* status;       // device status word (workspace)
+  uint16_t* S_hist;       // saved: S_j, bf16 row-major (every rule)
+  uint16_t* G_hist;       // saved, adam: G_j, bf16 slab
+  uint16_t* Mp_hist;      // saved, adam: pre-update M_j, bf16 slab
+  uint16_t* Vp_hist;      // saved, adam: pre-update V_j, bf16 slab
+  uint16_t* Gbar_hist;    // workspace: cotangent of G_j, bf16 row-major (delta: Sb_{j+1})
+  float* M_ws;            // workspace, adam: fp32 slab of M (forward) / Mbar (backward)
+  float* V_ws;            // workspace, adam: fp32 slab of V (forward) / Vbar (backward)
+  float *dac, *dbc, *dmc, *dnc;  // workspace, adam: cotangents of a_c, b_c, mu_c, nu_c
+};
+
+// Fused mixer core forward (phases 1-3), delta and adam rules, dh 128,
+// chunk 64, bf16.
 bool chunk_fwd_tc_supported(const ChunkArgs& p);
-size_t chunk_fwd_tc_saved_bytes(int BH, int N);
-cudaError_t chunk_fwd_tc(const ChunkArgs& p, uint16_t* S_hist, uint32_t* status,
-                         cudaStream_t st);
+cudaError_t chunk_fwd_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st);
 
 // Backward of the fused forward (same shapes): bw1 runs the reverse state
-// chain per (b, h) and writes Sb_{j+1} (bf16) per chunk; bw2 computes every
-// token and gate gradient per (b, h, chunk).
+// chain per (b, h) and writes the cotangent of G_j (bf16) per chunk, plus the
+// chunk-scalar cotangents for adam; bw2 computes every token and gate
+// gradient per (b, h, chunk).
 bool chunk_bwd_tc_supported(const ChunkArgs& p);
-size_t chunk_bwd_tc_workspace_bytes(int BH, int N);
-cudaError_t chunk_bwd1_tc(const ChunkArgs& p, uint16_t* Sbar_hist, uint32_t* status,
-                          cudaStream_t st);
-cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const uint16_t* S_hist, const uint16_t* Sbar_hist,
-                          uint32_t* status, cudaStream_t st);
+cudaError_t chunk_bwd1_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st);
+cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st);
 
 // rows x 128 bf16 row-major matrix as a TMA map with 64 x box_rows boxes and
 // 128-byte swizzle.

@@ -1,4 +1,5 @@
-// Fused tensor-core forward of the mixer core, delta rule, dh = 128, C = 64.
+// Fused tensor-core forward of the mixer core, delta and adam rules,
+// dh = 128, C = 64.
 //
 // One CTA per (batch, head) walks the N chunks in order.  The chunk update
 // of the reference (fast_scan.py:82-85 on the products of
@@ -7,7 +8,14 @@
 //
 //   G_j = Uv_j - S_j Kw_j = E_j^T (w k_j)
 //   o_j = Qt_j S_j^T + A_j v_j = q_j S_j^T + A_j E_j,  A_j = tril(q k^T) * beta
-//   S_{j+1} = a_j S_j + G_j
+//   S_{j+1} = a_j S_j + G_j                                   (delta, w = beta)
+//   M' = mu_c M + (1 - mu_c) G_j,  V' = nu_c V + (1 - nu_c) G_j^2,
+//   S_{j+1} = a_j S_j + b_c M' / (sqrt(V') + 1e-6)             (adam, w = 1)
+//
+// (fast_scan.py:82-94; chunk scalars train_ablation.py:169-175).  Adam keeps
+// the fp32 moments in a per-thread slab of global memory (128 KB per head, L2
+// resident) and writes G_j and the pre-update moments as bf16 for the
+// backward.
 //
 // Per chunk the MMA thread issues (M x N x K):
 //   E(j)   -E_j^T = -v_j^T I + S_j k_j^T   128 x 64 x 64, 128 x 64 x 128 (S hi, lo)
@@ -25,7 +33,7 @@
 // are mbarriers with bounded waits (tc.cuh).
 //
 // HBM per chunk-head: q, k, v in (48 KB), o out (16 KB), S_j bf16 out for the
-// backward (32 KB).
+// backward (32 KB); adam adds G_j, M_j, V_j bf16 out (96 KB).
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -76,13 +84,17 @@ static_assert(sizeof(Bars) <= 256, "barrier block");
 struct FwdArgs {
   const float* beta;
   const float* alpha;
+  const float *mu, *nu;
   uint16_t* S_hist;
+  uint16_t *G_hist, *Mp_hist, *Vp_hist;  // adam
+  float *M_ws, *V_ws;                    // adam
   uint32_t* status;
   int N, T;
 };
 
+template <int RULE>
 __global__ void __launch_bounds__(kThreadsTc, 1)
-chunk_fwd_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                    const __grid_constant__ CUtensorMap tm_sh, FwdArgs args) {
   extern __shared__ uint8_t smem_raw[];
@@ -253,6 +265,54 @@ chunk_fwd_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       const float la = logf(fmaxf(__ldg(al + lane), kGateFloor)) +
                        logf(fmaxf(__ldg(al + lane + 32), kGateFloor));
       const float a = expf(warp_sum(la));
+      if constexpr (RULE == 2) {
+        const float* be = args.beta + tok0 + j * kC;
+        const float* mu = args.mu + tok0 + j * kC;
+        const float* nu = args.nu + tok0 + j * kC;
+        const float b = warp_sum(__ldg(be + lane) + __ldg(be + lane + 32)) * (1.f / kC);
+        const float mc = expf(warp_sum(logf(fmaxf(__ldg(mu + lane), kGateFloor)) +
+                                       logf(fmaxf(__ldg(mu + lane + 32), kGateFloor))));
+        const float nc = expf(warp_sum(logf(fmaxf(__ldg(nu + lane), kGateFloor)) +
+                                       logf(fmaxf(__ldg(nu + lane + 32), kGateFloor))));
+        if (!wait_use(&bars->g_full, j, status, ab)) break;
+        tc_fence_after();
+        const size_t mj = static_cast<size_t>(bh) * N + j;
+        const uint32_t rg = tmem + lb + TM_G + half * 64;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float mv[16], vv[16], g[16];
+          float* mp = reinterpret_cast<float*>(slab_f32(args.M_ws, bh, half, 4 * q, c));
+          float* vp = reinterpret_cast<float*>(slab_f32(args.V_ws, bh, half, 4 * q, c));
+          if (j > 0) {
+            ld_f16x4(mp, mv);
+            ld_f16x4(vp, vv);
+          } else {
+#pragma unroll
+            for (int t = 0; t < 16; ++t) mv[t] = vv[t] = 0.f;
+          }
+          tmem_ld16(rg + 16 * q, g);
+          tmem_ld_wait();
+          // pre-update G_j, M_j, V_j for the backward
+          *slab_bf16(args.G_hist, mj, half, 2 * q, c) = pack8(g);
+          *slab_bf16(args.G_hist, mj, half, 2 * q + 1, c) = pack8(g + 8);
+          *slab_bf16(args.Mp_hist, mj, half, 2 * q, c) = pack8(mv);
+          *slab_bf16(args.Mp_hist, mj, half, 2 * q + 1, c) = pack8(mv + 8);
+          *slab_bf16(args.Vp_hist, mj, half, 2 * q, c) = pack8(vv);
+          *slab_bf16(args.Vp_hist, mj, half, 2 * q + 1, c) = pack8(vv + 8);
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            const float m1 = fmaf(mc, mv[t], (1.f - mc) * g[t]);
+            const float v1 = fmaf(nc, vv[t], (1.f - nc) * (g[t] * g[t]));
+            mv[t] = m1;
+            vv[t] = v1;
+            st[16 * q + t] = fmaf(a, st[16 * q + t], b * m1 / (sqrtf(v1) + kEpsAdam));
+          }
+          if (j + 1 < N) {
+            st_f16x4(mp, mv);
+            st_f16x4(vp, vv);
+          }
+        }
+      } else {
       if (!wait_use(&bars->g_full, j, status, ab)) break;
       tc_fence_after();
       {
@@ -270,6 +330,7 @@ chunk_fwd_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
           st[32 + t] = fmaf(a, st[32 + t], g2[t]);
           st[48 + t] = fmaf(a, st[48 + t], g3[t]);
         }
+      }
       }
       // S_{j+1} as packed bf16 hi / lo into TMEM (A operand of E and o1)
       uint32_t ph[32];
@@ -320,7 +381,7 @@ chunk_fwd_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
     const uint32_t lb = tmem_lane_base(warp);
     const int row = sp * 32 + lane;            // TMEM lane of this thread
     const int t16 = sp * 16 + (lane & 15);     // M=64 row of lanes 0-15
-    // w * k for chunk jj (delta: w = beta); Wk must be free (G(jj-1) done)
+    // w * k for chunk jj (delta: w = beta, adam: w = 1); Wk must be free (G(jj-1) done)
     auto build_wk = [&](int jj) -> bool {
       const int s = jj & 1;
       if (!wait_use(&bars->ld_full[s], jj >> 1, status, ab)) return false;
@@ -332,13 +393,15 @@ chunk_fwd_tc_delta(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       for (int m = 0; m < 8; ++m) {
         const int id = tb + 128 * m;            // 16-byte chunk id, 0..1023
         const uint32_t off = static_cast<uint32_t>(id) * 16u;
-        const float w = bs[(id & 511) >> 3];    // row inside the panel
         const uint4 x = *reinterpret_cast<const uint4*>(ks + off);
-        uint4 y;
-        y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
-        y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
-        y.z = pack_bf16(bf16_lo(x.z) * w, bf16_hi(x.z) * w);
-        y.w = pack_bf16(bf16_lo(x.w) * w, bf16_hi(x.w) * w);
+        uint4 y = x;
+        if constexpr (RULE == 0) {
+          const float w = bs[(id & 511) >> 3];  // row inside the panel
+          y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
+          y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
+          y.z = pack_bf16(bf16_lo(x.z) * w, bf16_hi(x.z) * w);
+          y.w = pack_bf16(bf16_lo(x.w) * w, bf16_hi(x.w) * w);
+        }
         *reinterpret_cast<uint4*>(wk + off) = y;
       }
       fence_async_smem();
@@ -490,37 +553,52 @@ cudaError_t make_tmap_rows128(CUtensorMap* map, const void* base, uint64_t rows,
 }
 
 bool chunk_fwd_tc_supported(const ChunkArgs& p) {
-  return p.rule == 0 && p.dh == kD && p.C == kC && !p.io_f32 && p.N >= 1 && encode_fn();
+  return (p.rule == 0 || p.rule == 2) && p.dh == kD && p.C == kC && !p.io_f32 && p.N >= 1 &&
+         encode_fn();
 }
 
-size_t chunk_fwd_tc_saved_bytes(int BH, int N) {
-  return static_cast<size_t>(BH) * N * kD * kD * sizeof(uint16_t);
+template <int RULE>
+cudaError_t launch_fwd_tc(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                          const CUtensorMap& mo, const CUtensorMap& msh, const FwdArgs& a,
+                          int grid, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(chunk_fwd_tc_kernel<RULE>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  chunk_fwd_tc_kernel<RULE><<<grid, kThreadsTc, SMEM_BYTES, st>>>(mq, mk, mv, mo, msh, a);
+  return cudaGetLastError();
 }
 
-cudaError_t chunk_fwd_tc(const ChunkArgs& p, uint16_t* S_hist, uint32_t* status,
-                         cudaStream_t st) {
+cudaError_t chunk_fwd_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st) {
   CUtensorMap mq, mk, mv, mo, msh;
   const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
   cudaError_t e;
-  if ((e = make_tmap_rows128(&msh, S_hist, static_cast<uint64_t>(p.BH) * p.N * kD, 128)) !=
+  if ((e = make_tmap_rows128(&msh, b.S_hist, static_cast<uint64_t>(p.BH) * p.N * kD, 128)) !=
       cudaSuccess)
     return e;
   if ((e = make_tmap_rows128(&mq, p.q, rows, 64)) != cudaSuccess) return e;
   if ((e = make_tmap_rows128(&mk, p.k, rows, 64)) != cudaSuccess) return e;
   if ((e = make_tmap_rows128(&mv, p.v, rows, 64)) != cudaSuccess) return e;
   if ((e = make_tmap_rows128(&mo, p.o, rows, 64)) != cudaSuccess) return e;
-  FwdArgs a;
+  FwdArgs a{};
   a.beta = p.beta;
   a.alpha = p.alpha;
-  a.S_hist = S_hist;
-  a.status = status;
+  a.mu = p.mu;
+  a.nu = p.nu;
+  a.S_hist = b.S_hist;
+  a.G_hist = b.G_hist;
+  a.Mp_hist = b.Mp_hist;
+  a.Vp_hist = b.Vp_hist;
+  a.M_ws = b.M_ws;
+  a.V_ws = b.V_ws;
+  a.status = b.status;
   a.N = p.N;
   a.T = p.T;
-  e = cudaFuncSetAttribute(chunk_fwd_tc_delta, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           SMEM_BYTES);
-  if (e != cudaSuccess) return e;
-  chunk_fwd_tc_delta<<<p.BH, kThreadsTc, SMEM_BYTES, st>>>(mq, mk, mv, mo, msh, a);
-  return cudaGetLastError();
+  if (p.rule == 2) {
+    if (!p.nu || !b.G_hist || !b.Mp_hist || !b.Vp_hist || !b.M_ws || !b.V_ws)
+      return cudaErrorInvalidValue;
+    return launch_fwd_tc<2>(mq, mk, mv, mo, msh, a, p.BH, st);
+  }
+  return launch_fwd_tc<0>(mq, mk, mv, mo, msh, a, p.BH, st);
 }
 
 }  // namespace gmdn

@@ -264,6 +264,12 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, uint4 r) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr),
+               "r"(r.x), "r"(r.y), "r"(r.z), "r"(r.w)
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -404,6 +410,30 @@ __device__ __forceinline__ bool wait_free(uint64_t* b, int use, uint32_t* st, vo
 // Named barrier among `nthreads` threads (ids 1..15; 0 is __syncthreads).
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Per-thread slabs (layouts in fast_path.h, TcBufs): row c, column half `half`.
+__device__ __forceinline__ float4* slab_f32(float* base, int bh, int half, int f, int c) {
+  return reinterpret_cast<float4*>(base) + ((static_cast<size_t>(bh) * 2 + half) * 16 + f) * 128 + c;
+}
+__device__ __forceinline__ uint4* slab_bf16(uint16_t* base, size_t m, int half, int g, int c) {
+  return reinterpret_cast<uint4*>(base) + ((m * 2 + half) * 8 + g) * 128 + c;
+}
+__device__ __forceinline__ void ld_f16x4(const float* base4, float* v) {
+  // 16 consecutive slab floats of one thread = 4 float4 at a 128-float4 stride
+#pragma unroll
+  for (int f = 0; f < 4; ++f) {
+    const float4 x = reinterpret_cast<const float4*>(base4)[f * 128];
+    v[4 * f] = x.x;
+    v[4 * f + 1] = x.y;
+    v[4 * f + 2] = x.z;
+    v[4 * f + 3] = x.w;
+  }
+}
+__device__ __forceinline__ void st_f16x4(float* base4, const float* v) {
+#pragma unroll
+  for (int f = 0; f < 4; ++f)
+    reinterpret_cast<float4*>(base4)[f * 128] = make_float4(v[4 * f], v[4 * f + 1], v[4 * f + 2], v[4 * f + 3]);
 }
 
 }  // namespace tc
