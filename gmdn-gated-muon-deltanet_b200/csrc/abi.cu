@@ -121,11 +121,16 @@ ChunkBufs carve_chunk(void* saved, void* ws, int BH, int N, int dh, int rule, in
       b.tc.Mp_hist = half_mats(cs);
       b.tc.Vp_hist = half_mats(cs);
     }
+    if (rule == 1) {
+      b.tc.M_hist = cs.take(per);
+      b.tc.X_hist = reinterpret_cast<uint8_t*>(cs.take(per * static_cast<size_t>(ns)));
+    }
     b.saved_bytes = cs.used;
     b.tc.Gbar_hist = half_mats(cw);
-    if (rule == 2) {
+    if (rule == 1) b.tc.Gbar_lo_hist = half_mats(cw);
+    if (rule != 0) {
       b.tc.M_ws = cw.take(mats(BH, dh));
-      b.tc.V_ws = cw.take(mats(BH, dh));
+      if (rule == 2) b.tc.V_ws = cw.take(mats(BH, dh));
       b.tc.dac = cw.take(sc);
       b.tc.dbc = cw.take(sc);
       b.tc.dmc = cw.take(sc);
@@ -161,7 +166,7 @@ bool chunk_fast(int dh, int chunk, int rule, int precision, int io_f32, int N) {
   if (precision != GMDN_PREC_FAST || io_f32) return false;
   gmdn::ChunkArgs p{};
   p.dh = dh; p.C = chunk; p.rule = rule; p.io_f32 = false; p.N = N;
-  return gmdn::chunk_fwd_tc_supported(p);
+  return gmdn::chunk_fwd_tc_supported(p) || gmdn::chunk_fwd_muon_tc_supported(p);
 }
 
 int check_chunk(int B, int H, int T, int dh, int chunk, int rule, int ns, int precision) {
@@ -431,7 +436,10 @@ int gmdn_chunk_fwd_ex(const void* q, const void* k, const void* v, const float* 
   cudaError_t e = cudaMemsetAsync(bufs.status, 0, sizeof(uint32_t), st);
   if (e != cudaSuccess) return cuda_fail(e, "status reset");
   if (fast) {
-    GMDN_LAUNCH(gmdn::chunk_fwd_tc(p, bufs.tc, st), "chunk_fwd_tc");
+    if (rule == 1)
+      GMDN_LAUNCH(gmdn::chunk_fwd_muon_tc(p, bufs.tc, ns, st), "chunk_fwd_muon_tc");
+    else
+      GMDN_LAUNCH(gmdn::chunk_fwd_tc(p, bufs.tc, st), "chunk_fwd_tc");
     return GMDN_OK;
   }
   gmdn::ScanArgs sp = scan_args_from(p, bufs, ns);
@@ -465,7 +473,10 @@ int gmdn_chunk_bwd_ex(const void* q, const void* k, const void* v, const float* 
   cudaError_t e = cudaMemsetAsync(bufs.status, 0, sizeof(uint32_t), st);
   if (e != cudaSuccess) return cuda_fail(e, "status reset");
   if (fast) {
-    GMDN_LAUNCH(gmdn::chunk_bwd1_tc(p, bufs.tc, st), "chunk_bwd1_tc");
+    if (rule == 1)
+      GMDN_LAUNCH(gmdn::chunk_bwd1_muon_tc(p, bufs.tc, ns, st), "chunk_bwd1_muon_tc");
+    else
+      GMDN_LAUNCH(gmdn::chunk_bwd1_tc(p, bufs.tc, st), "chunk_bwd1_tc");
     GMDN_LAUNCH(gmdn::chunk_bwd2_tc(p, bufs.tc, st), "chunk_bwd2_tc");
     return GMDN_OK;
   }

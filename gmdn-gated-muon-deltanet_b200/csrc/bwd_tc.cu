@@ -573,8 +573,8 @@ constexpr uint32_t B2_DE = 172032;    // dE bf16 [s][c]
 constexpr uint32_t B2_DP = 188416;    // dP bf16 [t][s]
 constexpr uint32_t B2_I = 196608;     // identity
 constexpr uint32_t B2_RED = 204800;   // fp32 [64][65]: tril(dA) * P per (t, s)
-constexpr uint32_t B2_GATE = 221440;  // beta[64], alpha[64], dw[2][64]
-constexpr uint32_t B2_BAR = 222720;
+constexpr uint32_t B2_GATE = 221440;  // beta[64], alpha[64], dw[2][64], mu[64], w[64]
+constexpr uint32_t B2_BAR = 222976;
 constexpr uint32_t B2_SMEM = B2_BAR + 256 + 1024;
 
 // TMEM: X0 P | dA, X1 dQ (lanes 16-31), X2 dE | dWk, X3 dK (lanes 0-15), XE E^T
@@ -593,6 +593,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
 chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
                     const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_sb,
+                    const __grid_constant__ CUtensorMap tm_sbl,
                     const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dk,
                     const __grid_constant__ CUtensorMap tm_dv, BwArgs args) {
   extern __shared__ uint8_t smem_raw[];
@@ -602,6 +603,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   float* gbeta = reinterpret_cast<float*>(sm + B2_GATE);
   float* galpha = gbeta + 64;
   float* gdw = galpha + 64;  // [2][64]: partial k.dWk of each column half
+  float* gmu = gdw + 128;    // muon: mu of the chunk
+  float* gw = gmu + 64;      // muon: token weights w_s = prod_{t>s} mu_t
   float* red = reinterpret_cast<float*>(sm + B2_RED);
   volatile int* ab = &bars->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -636,7 +639,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 
   if (warp == 8) {
     if (lane == 0) {
-      mbar_expect_tx(&bars->ld_full, 8 * 8192 + 4 * 16384 + 512);
+      mbar_expect_tx(&bars->ld_full,
+                     8 * 8192 + 4 * 16384 + 512 + (RULE == 1 ? 256 + 2 * 16384 : 0));
       tma_load_2d(sm + B2_Q, &tm_q, 0, static_cast<int>(tok), &bars->ld_full);
       tma_load_2d(sm + B2_Q + P64, &tm_q, 64, static_cast<int>(tok), &bars->ld_full);
       tma_load_2d(sm + B2_K, &tm_k, 0, static_cast<int>(tok), &bars->ld_full);
@@ -651,6 +655,13 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       tma_load_2d(sm + B2_SB + P128, &tm_sb, 64, srow, &bars->ld_full);
       bulk_load(gbeta, args.beta + tok, 256, &bars->ld_full);
       bulk_load(galpha, args.alpha + tok, 256, &bars->ld_full);
+      if (RULE == 1) {
+        bulk_load(gmu, args.mu + tok, 256, &bars->ld_full);
+        // lo half of Gb_j: its panels go to the dE tile and the reduction array,
+        // which epilogue 2 writes only after phase 2 has read them
+        tma_load_2d(sm + B2_DE, &tm_sbl, 0, srow, &bars->ld_full);
+        tma_load_2d(sm + B2_RED, &tm_sbl, 64, srow, &bars->ld_full);
+      }
       const uint32_t q_s = smem_u32(sm + B2_Q), k_s = smem_u32(sm + B2_K);
       const uint32_t v_s = smem_u32(sm + B2_V), g_s = smem_u32(sm + B2_G);
       const uint32_t s_s = smem_u32(sm + B2_S), sb_s = smem_u32(sm + B2_SB);
@@ -694,6 +705,13 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + T2_X2, desc_kmajor(wk_s, P64, k), desc_kmajor(sb_s, P128, k), ID_KK, 1);
+        if constexpr (RULE == 1) {
+          const uint32_t sbl_s = smem_u32(sm + B2_DE);   // panels 32 KB apart (dE tile, red)
+          #pragma unroll
+          for (int k = 0; k < 8; ++k)
+            mma_bf16(tmem + T2_X2, desc_kmajor(wk_s, P64, k), desc_kmajor(sbl_s, B2_RED - B2_DE, k),
+                     ID_KK, 1);
+        }
         #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + HI16 + T2_X0, desc_kmajor(g_s, P64, k), desc_mnmajor(e_s, P128, k), ID_DA,
@@ -702,6 +720,18 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + HI16 + T2_X2, desc_mnmajor(e_s, P128, k), desc_mnmajor(sb_s, P128, k),
                    ID_MM, k > 0);
+        if constexpr (RULE == 1) {
+          const uint32_t sbl_s = smem_u32(sm + B2_DE);
+          const uint32_t el_s = smem_u32(sm + B2_V);
+          #pragma unroll
+          for (int k = 0; k < 8; ++k)
+            mma_bf16(tmem + HI16 + T2_X2, desc_mnmajor(e_s, P128, k),
+                     desc_mnmajor(sbl_s, B2_RED - B2_DE, k), ID_MM, 1);
+          #pragma unroll
+          for (int k = 0; k < 8; ++k)
+            mma_bf16(tmem + HI16 + T2_X2, desc_mnmajor(el_s, P128, k), desc_mnmajor(sb_s, P128, k),
+                     ID_MM, 1);
+        }
         mma_commit(&bars->ph2);
       }
       ok = ok && wait_use(&bars->ep2, 0, status, ab);
@@ -734,15 +764,30 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     const int c128 = sp * 32 + lane;           // M=128 row (TMEM lane)
     bool ok = wait_use(&bars->ld_full, 0, status, ab);
     if (ok) {
-      // w * k (delta: w = beta; adam: w = 1)
+      if constexpr (RULE == 1) {  // w_s = exp(sum_{t>s} log clamp(mu_t)), log-space suffix sums
+        if (warp == 0) {
+          const float l0 = logf(fmaxf(gmu[2 * lane], kGateFloor));
+          const float l1 = logf(fmaxf(gmu[2 * lane + 1], kGateFloor));
+          float sfx = l0 + l1;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_down_sync(0xffffffffu, sfx, o);
+            if (lane + o < 32) sfx += y;
+          }
+          gw[2 * lane] = expf(sfx - l0);
+          gw[2 * lane + 1] = expf(sfx - l0 - l1);
+        }
+        named_sync(1, 256);
+      }
+      // w * k (delta: w = beta; muon: w = suffix product of mu; adam: w = 1)
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
         const int id = tid + 256 * m;
         const uint32_t off = static_cast<uint32_t>(id) * 16u;
         const uint4 x = *reinterpret_cast<const uint4*>(sm + B2_K + off);
         uint4 y = x;
-        if constexpr (RULE == 0) {
-          const float w = gbeta[(id & 511) >> 3];
+        if constexpr (RULE != 2) {
+          const float w = RULE == 0 ? gbeta[(id & 511) >> 3] : gw[(id & 511) >> 3];
           y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
           y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
           y.z = pack_bf16(bf16_lo(x.z) * w, bf16_hi(x.z) * w);
@@ -772,7 +817,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         const float sum = warp_sum(la);
         if (lane == 0) bars->a_c = expf(sum);
       }
-      if (RULE == 2 && (warp == 1 || warp == 2)) {  // mu_c, nu_c
+      if ((RULE == 2 && (warp == 1 || warp == 2)) || (RULE == 1 && warp == 1)) {  // mu_c, nu_c
         const float* gsrc = (warp == 1 ? args.mu : args.nu) + tok;
         const float lg = logf(fmaxf(__ldg(gsrc + lane), kGateFloor)) +
                          logf(fmaxf(__ldg(gsrc + lane + 32), kGateFloor));
@@ -811,6 +856,15 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tmem_ld_wait();
         st_row8(sm + B2_E, P128, c128, c0 >> 3, e);
         st_row8(sm + B2_E, P128, c128, (c0 >> 3) + 1, e + 8);
+        if constexpr (RULE == 1) {
+          // muon: E^T lo into the v tile (v's last reader was phase 1; dv staging
+          // writes it only after phase 2), so E Gb keeps ~16 bits against a large Gb
+          float lo[16];
+#pragma unroll
+          for (int t = 0; t < 16; ++t) lo[t] = e[t] - __bfloat162float(__float2bfloat16_rn(e[t]));
+          st_row8(sm + B2_V, P128, c128, c0 >> 3, lo);
+          st_row8(sm + B2_V, P128, c128, (c0 >> 3) + 1, lo + 8);
+        }
       }
       fence_async_smem();
       tc_fence_before();
@@ -869,7 +923,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           }
         }
       }
-      if (RULE == 0 && hi) gdw[half * 64 + r16] = dw;
+      if (RULE != 2 && hi) gdw[half * 64 + r16] = dw;
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->ep2);
@@ -884,7 +938,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     ok = ok && wait_use(&bars->ph3, 0, status, ab);
     if (ok) {
       tc_fence_after();
-      const float w = RULE == 0 ? gbeta[r16] : 1.f;
+      const float w = RULE == 0 ? gbeta[r16] : RULE == 1 ? gw[r16] : 1.f;
       // dq staged in the q tile and dk in the k tile (both last read by phase 3)
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
@@ -923,7 +977,23 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       for (int t = s; t < kC; ++t) db += red[t * 65 + s];
       const float al = galpha[s];
       const size_t g = tok + s;
-      if constexpr (RULE == 2) {
+      if constexpr (RULE == 1) {
+        // b_c = mean(beta); a_c, mu_c products; w_u = prod_{t>u} mu_t adds
+        // dmu_s += sum_{u<s} dw_u w_u / mu_s
+        const size_t gi = static_cast<size_t>(bh) * N + j;
+        args.dbeta[g] = db + args.dbc[gi] * (1.f / kC);
+        args.dalpha[g] =
+            (al >= kGateFloor) ? args.dac[gi] * bars->a_c / fmaxf(al, kGateFloor) : 0.f;
+        const float mu = gmu[s];
+        float dmu = 0.f;
+        if (mu >= kGateFloor) {
+          float pre = 0.f;
+          for (int u2 = 0; u2 < s; ++u2) pre = fmaf(gdw[u2] + gdw[64 + u2], gw[u2], pre);
+          dmu = (args.dmc[gi] * bars->m_c + pre) / fmaxf(mu, kGateFloor);
+        }
+        args.dmu[g] = dmu;
+        if (args.dnu) args.dnu[g] = 0.f;
+      } else if constexpr (RULE == 2) {
         // chunk scalars: b_c = mean(beta), a_c / mu_c / nu_c = prod of the clamped gates
         const size_t gi = static_cast<size_t>(bh) * N + j;
         args.dbeta[g] = db + args.dbc[gi] * (1.f / kC);
@@ -1008,7 +1078,7 @@ cudaError_t launch_bw2(const CUtensorMap* m, const BwArgs& a, int grid, cudaStre
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, B2_SMEM);
   if (e != cudaSuccess) return e;
   chunk_bwd2_tc_kernel<RULE><<<grid, kThreads2, B2_SMEM, st>>>(m[0], m[1], m[2], m[3], m[4],
-                                                              m[5], m[6], m[7], m[8], a);
+                                                              m[5], m[6], m[7], m[8], m[9], a);
   return cudaGetLastError();
 }
 
@@ -1033,13 +1103,14 @@ cudaError_t chunk_bwd1_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st) 
 }
 
 cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st) {
-  // q, k, v, dO, S_j, Gb_j, dq, dk, dv
-  CUtensorMap m[9];
+  // q, k, v, dO, S_j, Gb_j, Gb_j lo (muon; else Gb_j again), dq, dk, dv
+  CUtensorMap m[10];
   const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
   const uint64_t srows = static_cast<uint64_t>(p.BH) * p.N * kD;
-  const void* base[9] = {p.q, p.k, p.v, p.dO, b.S_hist, b.Gbar_hist, p.dq, p.dk, p.dv};
-  for (int i = 0; i < 9; ++i) {
-    const bool hist = i == 4 || i == 5;
+  const void* lo = (p.rule == 1 && b.Gbar_lo_hist) ? b.Gbar_lo_hist : b.Gbar_hist;
+  const void* base[10] = {p.q, p.k, p.v, p.dO, b.S_hist, b.Gbar_hist, lo, p.dq, p.dk, p.dv};
+  for (int i = 0; i < 10; ++i) {
+    const bool hist = i >= 4 && i <= 6;
     cudaError_t e = make_tmap_rows128(&m[i], base[i], hist ? srows : rows, hist ? 128 : 64);
     if (e != cudaSuccess) return e;
   }
@@ -1047,6 +1118,10 @@ cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st) 
   if (p.rule == 2) {
     if (!adam_bufs_ok(p, b) || !p.dnu) return cudaErrorInvalidValue;
     return launch_bw2<2>(m, a, p.BH * p.N, st);
+  }
+  if (p.rule == 1) {
+    if (!b.dac || !b.dbc || !b.dmc || !b.Gbar_lo_hist) return cudaErrorInvalidValue;
+    return launch_bw2<1>(m, a, p.BH * p.N, st);
   }
   return launch_bw2<0>(m, a, p.BH * p.N, st);
 }

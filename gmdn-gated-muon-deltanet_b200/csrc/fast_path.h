@@ -22,7 +22,12 @@ struct TcBufs {
   uint16_t* G_hist;       // saved, adam: G_j, bf16 slab
   uint16_t* Mp_hist;      // saved, adam: pre-update M_j, bf16 slab
   uint16_t* Vp_hist;      // saved, adam: pre-update V_j, bf16 slab
+  float* M_hist;          // saved, muon: M_{j+1} (post-update), fp32 slab per chunk
+  uint8_t* X_hist;        // saved, muon: Newton-Schulz inputs X_0..X_{ns-1}, split bf16
+                          //   SW128 tiles, 64 KB per step (hi 32 KB, lo 32 KB), ns per chunk
   uint16_t* Gbar_hist;    // workspace: cotangent of G_j, bf16 row-major (delta: Sb_{j+1})
+  uint16_t* Gbar_lo_hist; // workspace, muon: its bf16 remainder (Gb - bf16(Gb)); the muon
+                          //   cotangent is large while its contractions with k are small
   float* M_ws;            // workspace, adam: fp32 slab of M (forward) / Mbar (backward)
   float* V_ws;            // workspace, adam: fp32 slab of V (forward) / Vbar (backward)
   float *dac, *dbc, *dmc, *dnc;  // workspace, adam: cotangents of a_c, b_c, mu_c, nu_c
@@ -32,6 +37,14 @@ struct TcBufs {
 // chunk 64, bf16.
 bool chunk_fwd_tc_supported(const ChunkArgs& p);
 cudaError_t chunk_fwd_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st);
+
+// Fused mixer core forward, muon rule (Newton-Schulz on the tensor cores with
+// split bf16 operands), dh 128, chunk 64, bf16.
+bool chunk_fwd_muon_tc_supported(const ChunkArgs& p);
+cudaError_t chunk_fwd_muon_tc(const ChunkArgs& p, const TcBufs& b, int ns, cudaStream_t st);
+// Reverse chain of the muon forward (msign VJP with split bf16 products); the
+// token gradients then come from chunk_bwd2_tc.
+cudaError_t chunk_bwd1_muon_tc(const ChunkArgs& p, const TcBufs& b, int ns, cudaStream_t st);
 
 // Backward of the fused forward (same shapes): bw1 runs the reverse state
 // chain per (b, h) and writes the cotangent of G_j (bf16) per chunk, plus the

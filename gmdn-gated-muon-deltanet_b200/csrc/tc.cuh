@@ -200,6 +200,38 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn, bool 
          (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// tf32 operands (kind::tf32): fp32 containers, 32 per 128-byte row, K = 8 per
+// instruction.  K-major: panel = 32 K columns, kstep counts K=8 steps (32 bytes
+// along the row).  MN-major: rows = K, 32 M/N elements per row and panel, a
+// K=8 step is one 1024-byte swizzle atom.
+__device__ __forceinline__ uint64_t desc_kmajor_tf32(uint32_t panel0, uint32_t panel_stride,
+                                                     int kstep) {
+  const uint32_t k = static_cast<uint32_t>(kstep) * 8u;
+  const uint32_t off = (k >> 5) * panel_stride + (k & 31u) * 4u;
+  return sw128_desc(panel0, 16u, 1024u) + static_cast<uint64_t>(off >> 4);
+}
+__device__ __forceinline__ uint64_t desc_mnmajor_tf32(uint32_t panel0, uint32_t panel_stride,
+                                                      int kstep) {
+  return sw128_desc(panel0, panel_stride, 1024u) +
+         static_cast<uint64_t>(static_cast<uint32_t>(kstep) * 64u);
+}
+
+// Instruction descriptor, kind::tf32 with fp32 accumulation.
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn, bool b_mn,
+                                                  bool neg_a = false) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((neg_a ? 1u : 0u) << 13) |
+         ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// fp32 -> tf32 (round to nearest, ties away; low 13 bits cleared), so the
+// tensor core reads the operand exactly.
+__device__ __forceinline__ float round_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
 // ---------------------------------------------------------------------------
 // MMA issue (one thread) and completion
 // ---------------------------------------------------------------------------
@@ -222,6 +254,28 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// A operand in TMEM: an M x 8 fp32 slab, row m in lane m, element k in column
+// a_tmem + k.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
@@ -262,6 +316,12 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
       "r"(r[15])
       : "memory");
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
 }
 
 __device__ __forceinline__ void tmem_st4(uint32_t taddr, uint4 r) {
@@ -316,6 +376,13 @@ __device__ __forceinline__ void bulk_wait0() {
 }
 
 // Plain 1-D bulk copy global -> shared (16-byte aligned, size multiple of 16).
+// shared -> global bulk copy (16-byte aligned, size a multiple of 16), bulk group
+__device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+               "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
                                           uint64_t* bar) {
   asm volatile(
