@@ -61,44 +61,55 @@ RULE_NAMES = {0: "delta", 1: "muon", 2: "adam"}
 # algorithmic work per kernel launch (units: flops or bytes for one launch)
 # ---------------------------------------------------------------------------
 
-def kernel_work(name: str, cfg: dict) -> tuple[str, float]:
-    """(bound, algorithmic work per launch) of a library kernel: flops for
-    tensor-bound kernels, bytes for HBM-bound ones.
+def kernel_work(name: str, cfg: dict) -> tuple[str, float, float]:
+    """(bound, bf16 work, fp32-state work) per launch of a library kernel: flops
+    for tensor-bound kernels (the second figure counts the fp32-state products,
+    whose roofline rate is TF32, half the bf16 rate), bytes for HBM-bound ones.
 
-    Per chunk-head (C tokens, head dim d; config 1: C=64, d=128):
-      chunk_fwd_tc   the forward's products 2C^2d + 4Cd^2 + 4C^2d + 2Cd^2 (phases
-                     1 and 3) + 2d^3 (state product) = 13.63 MFLOP
-      chunk_bwd1_tc  the reverse chain's products: P = q k^T (2C^2d),
-                     dE^T = dO^T A + Sb (wk)^T (2C^2d + 2Cd^2), dO^T q and dE^T k
-                     (2 x 2Cd^2) = 8.39 MFLOP
-      chunk_bwd2_tc  bytes: q, k, v, dO in (4 C d 2), S_j and Sb_{j+1} in
-                     (2 d^2 2), gates in (2 C 4), dq, dk, dv out (3 C d 2), gate
-                     cotangents out (3 C 4) = 181,504 B
-    The exact-fp32 kernels count their products (CUDA-core fp32).
+    Per chunk-head (C tokens, head dim d; config 1: C=64, d=128; mm = 2 d^3):
+      chunk_fwd_tc        the forward's products 2C^2d + 4Cd^2 + 4C^2d + 2Cd^2 (phases
+                          1 and 3) + mm (state product) = 13.63 MFLOP (delta, adam)
+      chunk_fwd_muon_tc   the same + 3 ns mm of Newton-Schulz (fp32 state)
+      chunk_bwd1_tc       the reverse chain's products: P = q k^T (2C^2d),
+                          dE^T = dO^T A + Gb (wk)^T (2C^2d + 2Cd^2), dO^T q and dE^T k
+                          (2 x 2Cd^2) = 8.39 MFLOP (delta, adam)
+      chunk_bwd1_muon_tc  the same + 8 ns mm: the msign VJP, 3 recomputed and 5
+                          cotangent products per step (fp32 state)
+      chunk_bwd2_tc       bytes: q, k, v, dO in (4 C d 2), S_j and Gb_j in (2 d^2 2),
+                          gates in (2 C 4), dq, dk, dv out (3 C d 2), gate cotangents
+                          out (3 C 4) = 181,504 B; muon adds Gb_j lo (d^2 2) and mu (C 4)
+    Newton-Schulz counts the algorithmic products once (the kernels spend three
+    split-bf16 MMAs on each).  The exact-fp32 kernels count their products.
     """
     B, H, T, d, C = cfg["B"], cfg["H"], cfg["T"], cfg["dh"], cfg["chunk"]
     N = T // C
     units = B * H * N
     ns = cfg["ns"] if cfg["rule"] == 1 else 0
     mm = 2.0 * d ** 3
+    fwd = 2 * C * C * d + 4 * C * d * d + 4 * C * C * d + 2 * C * d * d + mm
+    bwd1 = 2 * C * C * d + (2 * C * C * d + 2 * C * d * d) + 2 * (2 * C * d * d)
     flops = {
-        "chunk_fwd_tc": 2 * C * C * d + 4 * C * d * d + 4 * C * C * d + 2 * C * d * d + mm,
-        "chunk_bwd1_tc": 2 * C * C * d + (2 * C * C * d + 2 * C * d * d) + 2 * (2 * C * d * d),
-        "chunk_prep": 4.0 * C * d * d,
-        "chunk_out": 6.0 * C * C * d + 2.0 * C * d * d,
-        "chunk_state_grad": 4.0 * C * C * d + 2.0 * C * d * d,
-        "chunk_token_grad": 14.0 * C * C * d + 10.0 * C * d * d,
-        "scan_fwd_ieee": mm * (1 + 3 * ns),
-        "scan_bwd_ieee": mm * (3 + 8 * ns),
+        "chunk_fwd_tc": (fwd, 0.0),
+        "chunk_fwd_muon_tc": (fwd, 3 * ns * mm),
+        "chunk_bwd1_tc": (bwd1, 0.0),
+        "chunk_bwd1_muon_tc": (bwd1, 8 * ns * mm),
+        "chunk_prep": (4.0 * C * d * d, 0.0),
+        "chunk_out": (6.0 * C * C * d + 2.0 * C * d * d, 0.0),
+        "chunk_state_grad": (4.0 * C * C * d + 2.0 * C * d * d, 0.0),
+        "chunk_token_grad": (14.0 * C * C * d + 10.0 * C * d * d, 0.0),
+        "scan_fwd_ieee": (0.0, mm * (1 + 3 * ns)),
+        "scan_bwd_ieee": (0.0, mm * (3 + 8 * ns)),
     }
-    nbytes = {
-        "chunk_bwd2_tc": 4 * C * d * 2 + 2 * d * d * 2 + 2 * C * 4 + 3 * C * d * 2 + 3 * C * 4,
-    }
+    bw2 = 4 * C * d * 2 + 2 * d * d * 2 + 2 * C * 4 + 3 * C * d * 2 + 3 * C * 4
+    if cfg["rule"] == 1:
+        bw2 += d * d * 2 + C * 4
+    nbytes = {"chunk_bwd2_tc": bw2}
     if name in nbytes:
-        return "hbm", float(nbytes[name] * units)
+        return "hbm", float(nbytes[name] * units), 0.0
     if name in flops:
-        return "tensor", float(flops[name] * units)
-    return "tensor", float("nan")
+        f16, f32 = flops[name]
+        return "tensor", float(f16 * units), float(f32 * units)
+    return "tensor", float("nan"), 0.0
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -450,12 +461,19 @@ def main():
             kernel_times[name] = {"total_ms": ms, "launches": n, "avg_ms": ms / max(n, 1),
                                   "share": ms / max(sum(v[0] for v in kt.values()), 1e-9)}
         top = max(kt, key=lambda k: kt[k][0])
-        bound, work = kernel_work(top, cfg)
+        bound, work, work32 = kernel_work(top, cfg)
         avg_s = kt[top][0] / kt[top][1] / 1e3
+        source = (f"{peak_kind} (MEASURED_PEAKS.json bf16 burst)" if peak_kind == "measured"
+                  else "fallback")
         if bound == "tensor":
-            achieved = work / avg_s / 1e12
-            peak = peaks["bf16_tflops"]
+            # bf16 products at the bf16 peak, fp32-state products at TF32 = bf16 / 2
+            bf16 = peaks["bf16_tflops"]
+            roof_s = work / (bf16 * 1e12) + work32 / (bf16 / 2 * 1e12)
+            achieved = (work + work32) / avg_s / 1e12
+            peak = (work + work32) / roof_s / 1e12 if roof_s > 0 else bf16
             unit = "TFLOP/s"
+            if work32 > 0:
+                source += "; fp32-state products at TF32 = bf16 / 2 (assumed, not measured)"
         else:
             achieved = work / avg_s / 1e9
             peak = peaks["hbm_gbs"]
@@ -463,8 +481,7 @@ def main():
         tr = traffic.get(args.config, {}).get(top)
         roofline = {"kernel": top, "bound": bound, "achieved": achieved, "peak": peak,
                     "unit": unit, "frac": achieved / peak, "traffic": tr,
-                    "peak_source": f"{peak_kind} (MEASURED_PEAKS.json bf16 burst)"
-                    if peak_kind == "measured" else "fallback"}
+                    "peak_source": source}
 
     clocks.stop()
     clock_info = clocks.summary()
