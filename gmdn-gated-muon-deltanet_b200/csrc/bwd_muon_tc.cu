@@ -604,7 +604,9 @@ chunk_bwd1_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       }
       tc_fence_before();
     }
-    if (tid == 0) bulk_wait0();
+    // shared memory must outlive the reads of the bulk stores; grid completion
+    // makes their global writes visible to the next kernel
+    if (tid == 0) bulk_wait_read0();
   } else {
     // ------------------------------------------------------------ chunk-local (warps 8-11)
     const int tb = threadIdx.x - 256;

@@ -65,6 +65,7 @@ struct BwArgs {
   float *dalpha, *dbeta, *dmu, *dnu;
   uint32_t* status;
   int N, T;
+  int tiles;   // bw2: B * H * N
 };
 
 // ===========================================================================
@@ -449,7 +450,9 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       }
       }
     }
-    if (threadIdx.x == 0) bulk_wait0();
+    // shared memory must outlive the reads of the bulk stores; grid completion
+    // makes their global writes visible to the next kernel
+    if (threadIdx.x == 0) bulk_wait_read0();
   } else {
     // ------------------------------------------------------------ chunk-local (warps 8-11)
     const int tb = threadIdx.x - 256;
@@ -565,29 +568,35 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 constexpr int kThreads2 = 288;
 constexpr uint32_t B2_Q = 0, B2_K = 16384, B2_V = 32768, B2_G = 49152;
 constexpr uint32_t B2_S = 65536;      // S_j, 2 panels x 128 rows
-constexpr uint32_t B2_SB = 98304;     // Sb_{j+1}
+constexpr uint32_t B2_SB = 98304;     // Gb_j
 constexpr uint32_t B2_AS = 131072;    // A bf16 [t][s]
-constexpr uint32_t B2_E = 139264;     // E^T bf16 [c][s], 1 panel x 128 rows
-constexpr uint32_t B2_WK = 155648;    // w * k
-constexpr uint32_t B2_DE = 172032;    // dE bf16 [s][c]
+constexpr uint32_t B2_E = 139264;     // E^T bf16 [c][s], 1 panel x 128 rows; then dq staging
+constexpr uint32_t B2_WK = 155648;    // w * k; then dk staging
+constexpr uint32_t B2_DE = 172032;    // dE bf16 [s][c] (= dv, stored from here)
 constexpr uint32_t B2_DP = 188416;    // dP bf16 [t][s]
 constexpr uint32_t B2_I = 196608;     // identity
 constexpr uint32_t B2_RED = 204800;   // fp32 [64][65]: tril(dA) * P per (t, s)
-constexpr uint32_t B2_GATE = 221440;  // beta[64], alpha[64], dw[2][64], mu[64], w[64]
-constexpr uint32_t B2_BAR = 222976;
+constexpr uint32_t B2_GATE = 221440;  // 2 x {beta, alpha, mu, w}[64] (double-buffered), dw[2][64]
+constexpr uint32_t B2_BAR = 224000;
 constexpr uint32_t B2_SMEM = B2_BAR + 256 + 1024;
 
 // TMEM: X0 P | dA, X1 dQ (lanes 16-31), X2 dE | dWk, X3 dK (lanes 0-15), XE E^T
 constexpr uint32_t T2_X0 = 0, T2_X1 = 64, T2_X2 = 192, T2_X3 = 320, T2_XE = 448;
 
 struct Bars2 {
-  uint64_t ld_full, ph1, ep1, wk_full, ph2, ep2, ph3;
+  uint64_t ld_full, ph1, ep1, wk_full, ph2, ep2, ph3, tm_free, lo_full, tail_done;
   uint32_t tmem_base;
   int abort_flag;
   float da;
   float a_c, m_c, n_c;
 };
+static_assert(sizeof(Bars2) <= 256, "barrier block");
 
+// Persistent: CTA b handles tiles b, b + G, b + 2G, ... (tile = bh * N + chunk).
+// Tile i+1's inputs load as soon as phase 3 of tile i has read its tiles:
+// dq and dk are staged in the E^T and w*k tiles and dv is stored from the dE
+// tile, so every input tile is free then, and the load overlaps epilogue 3,
+// the gate gradients and the store drain of tile i.
 template <int RULE>
 __global__ void __launch_bounds__(kThreads2, 1)
 chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -600,19 +609,17 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
   Bars2* bars = reinterpret_cast<Bars2*>(sm + B2_BAR);
-  float* gbeta = reinterpret_cast<float*>(sm + B2_GATE);
-  float* galpha = gbeta + 64;
-  float* gdw = galpha + 64;  // [2][64]: partial k.dWk of each column half
-  float* gmu = gdw + 128;    // muon: mu of the chunk
-  float* gw = gmu + 64;      // muon: token weights w_s = prod_{t>s} mu_t
+  float* gate0 = reinterpret_cast<float*>(sm + B2_GATE);   // [2][4][64]
+  float* gdw = gate0 + 512;  // [2][64]: partial k.dWk of each column half
   float* red = reinterpret_cast<float*>(sm + B2_RED);
   volatile int* ab = &bars->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int N = args.N;
-  const int bh = blockIdx.x / N, j = blockIdx.x % N;
-  const size_t tok = static_cast<size_t>(bh) * args.T + static_cast<size_t>(j) * kC;
-  const int srow = (bh * N + j) * kD;  // first row of S_j / Gb_j in the histories
+  const int tiles = args.tiles;
+  const int G = gridDim.x;
   uint32_t* status = args.status;
+  // gate buffer of local tile i: beta, alpha, mu, w
+  auto gates = [&](int i) { return gate0 + (i & 1) * 256; };
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->ld_full, 1);
@@ -622,6 +629,9 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     mbar_init(&bars->ph2, 1);
     mbar_init(&bars->ep2, 256);
     mbar_init(&bars->ph3, 1);
+    mbar_init(&bars->tm_free, 256);
+    mbar_init(&bars->lo_full, 1);
+    mbar_init(&bars->tail_done, 1);
     bars->abort_flag = 0;
     bars->da = 0.f;
     fence_mbar_init();
@@ -638,30 +648,38 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   const uint32_t tmem = bars->tmem_base;
 
   if (warp == 8) {
+    // ------------------------------------------------------------ loads and MMAs (one thread)
     if (lane == 0) {
-      mbar_expect_tx(&bars->ld_full,
-                     8 * 8192 + 4 * 16384 + 512 + (RULE == 1 ? 256 + 2 * 16384 : 0));
-      tma_load_2d(sm + B2_Q, &tm_q, 0, static_cast<int>(tok), &bars->ld_full);
-      tma_load_2d(sm + B2_Q + P64, &tm_q, 64, static_cast<int>(tok), &bars->ld_full);
-      tma_load_2d(sm + B2_K, &tm_k, 0, static_cast<int>(tok), &bars->ld_full);
-      tma_load_2d(sm + B2_K + P64, &tm_k, 64, static_cast<int>(tok), &bars->ld_full);
-      tma_load_2d(sm + B2_V, &tm_v, 0, static_cast<int>(tok), &bars->ld_full);
-      tma_load_2d(sm + B2_V + P64, &tm_v, 64, static_cast<int>(tok), &bars->ld_full);
-      tma_load_2d(sm + B2_G, &tm_g, 0, static_cast<int>(tok), &bars->ld_full);
-      tma_load_2d(sm + B2_G + P64, &tm_g, 64, static_cast<int>(tok), &bars->ld_full);
-      tma_load_2d(sm + B2_S, &tm_s, 0, srow, &bars->ld_full);
-      tma_load_2d(sm + B2_S + P128, &tm_s, 64, srow, &bars->ld_full);
-      tma_load_2d(sm + B2_SB, &tm_sb, 0, srow, &bars->ld_full);
-      tma_load_2d(sm + B2_SB + P128, &tm_sb, 64, srow, &bars->ld_full);
-      bulk_load(gbeta, args.beta + tok, 256, &bars->ld_full);
-      bulk_load(galpha, args.alpha + tok, 256, &bars->ld_full);
-      if (RULE == 1) {
-        bulk_load(gmu, args.mu + tok, 256, &bars->ld_full);
-        // lo half of Gb_j: its panels go to the dE tile and the reduction array,
-        // which epilogue 2 writes only after phase 2 has read them
-        tma_load_2d(sm + B2_DE, &tm_sbl, 0, srow, &bars->ld_full);
-        tma_load_2d(sm + B2_RED, &tm_sbl, 64, srow, &bars->ld_full);
-      }
+      auto issue_loads = [&](int i, int tile) {
+        const int bh = tile / N, j = tile % N;
+        const int tok = bh * args.T + j * kC;
+        const int srow = (bh * N + j) * kD;
+        float* gt = gates(i);
+        mbar_expect_tx(&bars->ld_full, 8 * 8192 + 4 * 16384 + 512 + (RULE == 1 ? 256 : 0));
+        tma_load_2d(sm + B2_Q, &tm_q, 0, tok, &bars->ld_full);
+        tma_load_2d(sm + B2_Q + P64, &tm_q, 64, tok, &bars->ld_full);
+        tma_load_2d(sm + B2_K, &tm_k, 0, tok, &bars->ld_full);
+        tma_load_2d(sm + B2_K + P64, &tm_k, 64, tok, &bars->ld_full);
+        tma_load_2d(sm + B2_V, &tm_v, 0, tok, &bars->ld_full);
+        tma_load_2d(sm + B2_V + P64, &tm_v, 64, tok, &bars->ld_full);
+        tma_load_2d(sm + B2_G, &tm_g, 0, tok, &bars->ld_full);
+        tma_load_2d(sm + B2_G + P64, &tm_g, 64, tok, &bars->ld_full);
+        tma_load_2d(sm + B2_S, &tm_s, 0, srow, &bars->ld_full);
+        tma_load_2d(sm + B2_S + P128, &tm_s, 64, srow, &bars->ld_full);
+        tma_load_2d(sm + B2_SB, &tm_sb, 0, srow, &bars->ld_full);
+        tma_load_2d(sm + B2_SB + P128, &tm_sb, 64, srow, &bars->ld_full);
+        bulk_load(gt, args.beta + tok, 256, &bars->ld_full);
+        bulk_load(gt + 64, args.alpha + tok, 256, &bars->ld_full);
+        if (RULE == 1) bulk_load(gt + 128, args.mu + tok, 256, &bars->ld_full);
+      };
+      // muon: lo half of Gb_j into the dE tile and the reduction array (free
+      // until epilogue 2 of the same tile)
+      auto issue_lo = [&](int tile) {
+        const int srow = tile * kD;   // tile = bh * N + j
+        mbar_expect_tx(&bars->lo_full, 2 * 16384);
+        tma_load_2d(sm + B2_DE, &tm_sbl, 0, srow, &bars->lo_full);
+        tma_load_2d(sm + B2_RED, &tm_sbl, 64, srow, &bars->lo_full);
+      };
       const uint32_t q_s = smem_u32(sm + B2_Q), k_s = smem_u32(sm + B2_K);
       const uint32_t v_s = smem_u32(sm + B2_V), g_s = smem_u32(sm + B2_G);
       const uint32_t s_s = smem_u32(sm + B2_S), sb_s = smem_u32(sm + B2_SB);
@@ -676,8 +694,14 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       constexpr uint32_t ID_EV = idesc_bf16(128, 64, true, false);        // E^T: v^T I
       constexpr uint32_t ID_EK = idesc_bf16(128, 64, false, false, true); // E^T: -S k^T
       constexpr uint32_t ID_DA = idesc_bf16(64, 64, false, true);         // dO E^T
-      bool ok = wait_use(&bars->ld_full, 0, status, ab);
-      if (ok) {
+      int i = 0;
+      if (static_cast<int>(blockIdx.x) < tiles) {
+        issue_loads(0, blockIdx.x);
+        if (RULE == 1) issue_lo(blockIdx.x);
+      }
+      for (int tile = blockIdx.x; tile < tiles; tile += G, ++i) {
+        if (!wait_use(&bars->ld_full, i, status, ab)) break;
+        if (i >= 1 && !wait_use(&bars->tm_free, i - 1, status, ab)) break;
         tc_fence_after();
         // phase 1: P = q k^T; E^T = v^T - S k^T; dQ = dO S
         #pragma unroll
@@ -694,11 +718,10 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           mma_bf16(tmem + HI16 + T2_X1, desc_kmajor(g_s, P64, k), desc_mnmajor(s_s, P128, k),
                    ID_KM, k > 0);
         mma_commit(&bars->ph1);
-      }
-      ok = ok && wait_use(&bars->ep1, 0, status, ab) && wait_use(&bars->wk_full, 0, status, ab);
-      if (ok) {
+        if (!wait_use(&bars->ep1, i, status, ab) || !wait_use(&bars->wk_full, i, status, ab)) break;
+        if (RULE == 1 && !wait_use(&bars->lo_full, i, status, ab)) break;
         tc_fence_after();
-        // phase 2: dE = A^T dO + wk Sb^T;  dA = dO E^T;  dWk = E Sb
+        // phase 2: dE = A^T dO + wk Gb^T;  dA = dO E^T;  dWk = E Gb
         #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + T2_X2, desc_mnmajor(as_s, P64, k), desc_mnmajor(g_s, P64, k), ID_MM, k > 0);
@@ -733,9 +756,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                      ID_MM, 1);
         }
         mma_commit(&bars->ph2);
-      }
-      ok = ok && wait_use(&bars->ep2, 0, status, ab);
-      if (ok) {
+        if (!wait_use(&bars->ep2, i, status, ab)) break;
         tc_fence_after();
         // phase 3: dq += dP k;  dK = -dE S + dP^T q
         #pragma unroll
@@ -750,9 +771,23 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + T2_X3, desc_mnmajor(dp_s, P64, k), desc_mnmajor(q_s, P64, k), ID_MM, 1);
         mma_commit(&bars->ph3);
-        int dummy = 0;
-        mbar_wait(&bars->ph3, 0, status, &dummy);
+        // every input tile has been read: load the next tile's
+        if (!wait_use(&bars->ph3, i, status, ab)) break;
+        const int next = tile + G;
+        if (next < tiles) {
+          issue_loads(i + 1, next);
+          if (RULE == 1) {
+            if (!wait_use(&bars->tail_done, i, status, ab)) break;
+            issue_lo(next);
+          }
+        }
       }
+      // no copy of ours may still be in flight when the CTA exits
+      int dummy = 0;
+      if (i >= 1 && static_cast<int>(blockIdx.x) + i * G < tiles)
+        mbar_wait(&bars->ld_full, i & 1, status, &dummy);
+      if (RULE == 1 && i >= 1 && static_cast<int>(blockIdx.x) + i * G < tiles)
+        mbar_wait(&bars->lo_full, i & 1, status, &dummy);
     }
   } else {
     // ------------------------------------------------------------ epilogue warps 0-7
@@ -762,8 +797,23 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     const bool hi = lane >= 16;
     const int r16 = sp * 16 + (lane & 15);     // M=64 row of this lane's accumulator
     const int c128 = sp * 32 + lane;           // M=128 row (TMEM lane)
-    bool ok = wait_use(&bars->ld_full, 0, status, ab);
-    if (ok) {
+    int i = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += G, ++i) {
+      const int bh = tile / N, j = tile % N;
+      const size_t tok = static_cast<size_t>(bh) * args.T + static_cast<size_t>(j) * kC;
+      float* gbeta = gates(i);
+      float* galpha = gbeta + 64;
+      float* gmu = gbeta + 128;
+      float* gw = gbeta + 192;
+      // the previous tile's gate gradients are done with red, gdw and the chunk
+      // scalars; its stores have read their staging tiles (E, w*k, dE)
+      named_sync(1, 256);
+      if (tid == 0) {
+        bulk_wait_read0();
+        bars->da = 0.f;
+      }
+      named_sync(1, 256);
+      if (!wait_use(&bars->ld_full, i, status, ab)) break;
       if constexpr (RULE == 1) {  // w_s = exp(sum_{t>s} log clamp(mu_t)), log-space suffix sums
         if (warp == 0) {
           const float l0 = logf(fmaxf(gmu[2 * lane], kGateFloor));
@@ -798,7 +848,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       fence_async_smem();
       mbar_arrive(&bars->wk_full);
       if constexpr (RULE == 0) {
-        // da = <Sb_{j+1}, S_j>: row c128, column half `half` (adam: from the chain)
+        // da = <Sb_{j+1}, S_j>: row c128, column half `half` (adam, muon: from the chain)
         float part = 0.f;
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {
@@ -824,10 +874,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         const float sum = warp_sum(lg);
         if (lane == 0) (warp == 1 ? bars->m_c : bars->n_c) = expf(sum);
       }
-    }
-    // ---- epilogue 1: A = tril(P) beta (lanes 0-15), E^T -> bf16 (all lanes)
-    ok = ok && wait_use(&bars->ph1, 0, status, ab);
-    if (ok) {
+      // ---- epilogue 1: A = tril(P) beta (lanes 0-15), E^T -> bf16 (all lanes)
+      if (!wait_use(&bars->ph1, i, status, ab)) break;
       tc_fence_after();
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
@@ -857,8 +905,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         st_row8(sm + B2_E, P128, c128, c0 >> 3, e);
         st_row8(sm + B2_E, P128, c128, (c0 >> 3) + 1, e + 8);
         if constexpr (RULE == 1) {
-          // muon: E^T lo into the v tile (v's last reader was phase 1; dv staging
-          // writes it only after phase 2), so E Gb keeps ~16 bits against a large Gb
+          // muon: E^T lo into the v tile (v's last reader was phase 1), so E Gb
+          // keeps ~16 bits against a large Gb
           float lo[16];
 #pragma unroll
           for (int t = 0; t < 16; ++t) lo[t] = e[t] - __bfloat162float(__float2bfloat16_rn(e[t]));
@@ -869,10 +917,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->ep1);
-    }
-    // ---- epilogue 2: dE -> bf16 + dv; dP = tril(dA) beta; dbeta pieces; dw
-    ok = ok && wait_use(&bars->ph2, 0, status, ab);
-    if (ok) {
+      // ---- epilogue 2: dE -> bf16 (also dv); dP = tril(dA) beta; dbeta pieces; dw
+      if (!wait_use(&bars->ph2, i, status, ab)) break;
       tc_fence_after();
       // X0: P (lanes 0-15) and dA (lanes 16-31) of the same row t = r16
 #pragma unroll
@@ -899,8 +945,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           }
         }
       }
-      // X2: dE (lanes 0-15) and dWk (lanes 16-31), row s = r16, 64 columns.
-      // dv = dE is staged in the v tile (v's last reader was phase 1).
+      // X2: dE (lanes 0-15) and dWk (lanes 16-31), row s = r16, 64 columns
       float dw = 0.f;
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
@@ -911,8 +956,6 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         if (!hi) {
           st_row8(sm + B2_DE, P64, r16, c0 >> 3, x);
           st_row8(sm + B2_DE, P64, r16, (c0 >> 3) + 1, x + 8);
-          st_row8(sm + B2_V, P64, r16, c0 >> 3, x);
-          st_row8(sm + B2_V, P64, r16, (c0 >> 3) + 1, x + 8);
         } else {
           float k8[8];
 #pragma unroll
@@ -928,18 +971,15 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       tc_fence_before();
       mbar_arrive(&bars->ep2);
       named_sync(1, 256);
-      if (tid == 0) {
-        tma_store_2d(&tm_dv, 0, static_cast<int>(tok), sm + B2_V);
-        tma_store_2d(&tm_dv, 64, static_cast<int>(tok), sm + B2_V + P64);
+      if (tid == 0) {   // dv = dE, straight from the dE tile
+        tma_store_2d(&tm_dv, 0, static_cast<int>(tok), sm + B2_DE);
+        tma_store_2d(&tm_dv, 64, static_cast<int>(tok), sm + B2_DE + P64);
         bulk_commit();
       }
-    }
-    // ---- epilogue 3: dq, dk, gate gradients
-    ok = ok && wait_use(&bars->ph3, 0, status, ab);
-    if (ok) {
+      // ---- epilogue 3: dq (staged in the E^T tile), dk (in the w*k tile), gate gradients
+      if (!wait_use(&bars->ph3, i, status, ab)) break;
       tc_fence_after();
       const float w = RULE == 0 ? gbeta[r16] : RULE == 1 ? gw[r16] : 1.f;
-      // dq staged in the q tile and dk in the k tile (both last read by phase 3)
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         const int c0 = half * 64 + cc * 16;
@@ -948,69 +988,83 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tmem_ld16(tmem + lb + T2_X2 + c0, x2);   // dWk at lanes 16-31
         tmem_ld16(tmem + lb + T2_X3 + c0, x3);   // dK part at lanes 0-15
         tmem_ld_wait();
+        if (cc == 3) {   // the next tile's products may overwrite TMEM now
+          tc_fence_before();
+          mbar_arrive(&bars->tm_free);
+        }
         float dwk[16];
 #pragma unroll
         for (int y = 0; y < 16; ++y) dwk[y] = __shfl_xor_sync(0xffffffffu, x2[y], 16);
         if (hi) {
-          st_row8(sm + B2_Q, P64, r16, c0 >> 3, x1);
-          st_row8(sm + B2_Q, P64, r16, (c0 >> 3) + 1, x1 + 8);
+          st_row8(sm + B2_E, P64, r16, c0 >> 3, x1);
+          st_row8(sm + B2_E, P64, r16, (c0 >> 3) + 1, x1 + 8);
         } else {
 #pragma unroll
           for (int y = 0; y < 16; ++y) x3[y] = fmaf(w, dwk[y], x3[y]);
-          st_row8(sm + B2_K, P64, r16, c0 >> 3, x3);
-          st_row8(sm + B2_K, P64, r16, (c0 >> 3) + 1, x3 + 8);
+          st_row8(sm + B2_WK, P64, r16, c0 >> 3, x3);
+          st_row8(sm + B2_WK, P64, r16, (c0 >> 3) + 1, x3 + 8);
         }
       }
       fence_async_smem();
-    }
-    named_sync(1, 256);
-    if (ok && tid == 0) {
-      tma_store_2d(&tm_dq, 0, static_cast<int>(tok), sm + B2_Q);
-      tma_store_2d(&tm_dq, 64, static_cast<int>(tok), sm + B2_Q + P64);
-      tma_store_2d(&tm_dk, 0, static_cast<int>(tok), sm + B2_K);
-      tma_store_2d(&tm_dk, 64, static_cast<int>(tok), sm + B2_K + P64);
-      bulk_commit();
-    }
-    if (ok && tid < kC) {
-      const int s = tid;
-      float db = 0.f;
-      for (int t = s; t < kC; ++t) db += red[t * 65 + s];
-      const float al = galpha[s];
-      const size_t g = tok + s;
-      if constexpr (RULE == 1) {
-        // b_c = mean(beta); a_c, mu_c products; w_u = prod_{t>u} mu_t adds
-        // dmu_s += sum_{u<s} dw_u w_u / mu_s
-        const size_t gi = static_cast<size_t>(bh) * N + j;
-        args.dbeta[g] = db + args.dbc[gi] * (1.f / kC);
-        args.dalpha[g] =
-            (al >= kGateFloor) ? args.dac[gi] * bars->a_c / fmaxf(al, kGateFloor) : 0.f;
-        const float mu = gmu[s];
-        float dmu = 0.f;
-        if (mu >= kGateFloor) {
-          float pre = 0.f;
-          for (int u2 = 0; u2 < s; ++u2) pre = fmaf(gdw[u2] + gdw[64 + u2], gw[u2], pre);
-          dmu = (args.dmc[gi] * bars->m_c + pre) / fmaxf(mu, kGateFloor);
+      named_sync(1, 256);
+      if (tid == 0) {
+        tma_store_2d(&tm_dq, 0, static_cast<int>(tok), sm + B2_E);
+        tma_store_2d(&tm_dq, 64, static_cast<int>(tok), sm + B2_E + P64);
+        tma_store_2d(&tm_dk, 0, static_cast<int>(tok), sm + B2_WK);
+        tma_store_2d(&tm_dk, 64, static_cast<int>(tok), sm + B2_WK + P64);
+        bulk_commit();
+      }
+      if (tid < kC) {
+        const int s = tid;
+        float db = 0.f;
+        for (int t = s; t < kC; ++t) db += red[t * 65 + s];
+        const float al = galpha[s];
+        const size_t g = tok + s;
+        if constexpr (RULE == 1) {
+          // b_c = mean(beta); a_c, mu_c products; w_u = prod_{t>u} mu_t adds
+          // dmu_s += sum_{u<s} dw_u w_u / mu_s
+          const size_t gi = static_cast<size_t>(bh) * N + j;
+          args.dbeta[g] = db + args.dbc[gi] * (1.f / kC);
+          args.dalpha[g] =
+              (al >= kGateFloor) ? args.dac[gi] * bars->a_c / fmaxf(al, kGateFloor) : 0.f;
+          const float mu = gmu[s];
+          float dmu = 0.f;
+          if (mu >= kGateFloor) {
+            float pre = 0.f;
+            for (int u2 = 0; u2 < s; ++u2) pre = fmaf(gdw[u2] + gdw[64 + u2], gw[u2], pre);
+            dmu = (args.dmc[gi] * bars->m_c + pre) / fmaxf(mu, kGateFloor);
+          }
+          args.dmu[g] = dmu;
+          if (args.dnu) args.dnu[g] = 0.f;
+        } else if constexpr (RULE == 2) {
+          // chunk scalars: b_c = mean(beta), a_c / mu_c / nu_c = prod of the clamped gates
+          const size_t gi = static_cast<size_t>(bh) * N + j;
+          args.dbeta[g] = db + args.dbc[gi] * (1.f / kC);
+          args.dalpha[g] =
+              (al >= kGateFloor) ? args.dac[gi] * bars->a_c / fmaxf(al, kGateFloor) : 0.f;
+          const float mu = __ldg(args.mu + g), nu = __ldg(args.nu + g);
+          args.dmu[g] = (mu >= kGateFloor) ? args.dmc[gi] * bars->m_c / fmaxf(mu, kGateFloor) : 0.f;
+          args.dnu[g] = (nu >= kGateFloor) ? args.dnc[gi] * bars->n_c / fmaxf(nu, kGateFloor) : 0.f;
+        } else {
+          args.dbeta[g] = db + gdw[s] + gdw[64 + s];
+          args.dalpha[g] =
+              (al >= kGateFloor) ? bars->da * bars->a_c / fmaxf(al, kGateFloor) : 0.f;
+          args.dmu[g] = 0.f;
+          if (args.dnu) args.dnu[g] = 0.f;
         }
-        args.dmu[g] = dmu;
-        if (args.dnu) args.dnu[g] = 0.f;
-      } else if constexpr (RULE == 2) {
-        // chunk scalars: b_c = mean(beta), a_c / mu_c / nu_c = prod of the clamped gates
-        const size_t gi = static_cast<size_t>(bh) * N + j;
-        args.dbeta[g] = db + args.dbc[gi] * (1.f / kC);
-        args.dalpha[g] =
-            (al >= kGateFloor) ? args.dac[gi] * bars->a_c / fmaxf(al, kGateFloor) : 0.f;
-        const float mu = __ldg(args.mu + g), nu = __ldg(args.nu + g);
-        args.dmu[g] = (mu >= kGateFloor) ? args.dmc[gi] * bars->m_c / fmaxf(mu, kGateFloor) : 0.f;
-        args.dnu[g] = (nu >= kGateFloor) ? args.dnc[gi] * bars->n_c / fmaxf(nu, kGateFloor) : 0.f;
-      } else {
-        args.dbeta[g] = db + gdw[s] + gdw[64 + s];
-        args.dalpha[g] =
-            (al >= kGateFloor) ? bars->da * bars->a_c / fmaxf(al, kGateFloor) : 0.f;
-        args.dmu[g] = 0.f;
-        if (args.dnu) args.dnu[g] = 0.f;
+      }
+      if constexpr (RULE == 1) {
+        // the dE tile (read by the dv store) and red are free for the next Gb lo
+        named_sync(1, 256);
+        if (tid == 0) {
+          bulk_wait_read0();
+          mbar_arrive(&bars->tail_done);
+        }
       }
     }
-    if (tid == 0) bulk_wait0();
+    // shared memory must outlive the reads of the bulk stores; grid completion
+    // makes their global writes visible to the next kernel
+    if (tid == 0) bulk_wait_read0();
   }
 
   tc_fence_before();
@@ -1072,11 +1126,19 @@ cudaError_t launch_bw1(const CUtensorMap& mq, const CUtensorMap& mk, const CUten
   return cudaGetLastError();
 }
 
+// bw2 is persistent: one CTA per SM (it needs all of the SM's shared memory)
+// walks the tiles with a stride of the grid size.
 template <int RULE>
-cudaError_t launch_bw2(const CUtensorMap* m, const BwArgs& a, int grid, cudaStream_t st) {
+cudaError_t launch_bw2(const CUtensorMap* m, BwArgs a, int tiles, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(chunk_bwd2_tc_kernel<RULE>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, B2_SMEM);
   if (e != cudaSuccess) return e;
+  int dev = 0, sms = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+    return e;
+  a.tiles = tiles;
+  const int grid = sms < tiles ? sms : tiles;
   chunk_bwd2_tc_kernel<RULE><<<grid, kThreads2, B2_SMEM, st>>>(m[0], m[1], m[2], m[3], m[4],
                                                               m[5], m[6], m[7], m[8], m[9], a);
   return cudaGetLastError();

@@ -514,7 +514,9 @@ chunk_fwd_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       }
       if (!ok) break;
     }
-    if (tid == 0) bulk_wait0();
+    // shared memory must outlive the reads of the bulk stores; grid completion
+    // makes their global writes visible to the next kernel
+    if (tid == 0) bulk_wait_read0();
   } else {
     // ------------------------------------------------------------ chunk-local (warps 8-11)
     const int tb = threadIdx.x - 256;          // 0..127
@@ -653,7 +655,9 @@ chunk_fwd_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       }
       if (j + 1 < N && !build_as(j + 1)) break;
     }
-    if (tb == 0) bulk_wait0();
+    // shared memory must outlive the reads of the bulk stores; grid completion
+    // makes their global writes visible to the next kernel
+    if (tb == 0) bulk_wait_read0();
   }
 
   tc_fence_before();

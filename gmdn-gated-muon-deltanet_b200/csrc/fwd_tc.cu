@@ -373,7 +373,9 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         }
       }
     }
-    if (threadIdx.x == 0) bulk_wait0();
+    // shared memory must outlive the reads of the bulk stores; grid completion
+    // makes their global writes visible to the next kernel
+    if (threadIdx.x == 0) bulk_wait_read0();
   } else {
     // ------------------------------------------------------------ chunk-local (warps 8-11)
     const int tb = threadIdx.x - 256;          // 0..127
@@ -503,7 +505,9 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         bulk_commit();
       }
     }
-    if (tb == 0) bulk_wait0();
+    // shared memory must outlive the reads of the bulk stores; grid completion
+    // makes their global writes visible to the next kernel
+    if (tb == 0) bulk_wait_read0();
   }
 
   tc_fence_before();
