@@ -569,15 +569,16 @@ constexpr int kThreads2 = 288;
 constexpr uint32_t B2_Q = 0, B2_K = 16384, B2_V = 32768, B2_G = 49152;
 constexpr uint32_t B2_S = 65536;      // S_j, 2 panels x 128 rows
 constexpr uint32_t B2_SB = 98304;     // Gb_j
-constexpr uint32_t B2_AS = 131072;    // A bf16 [t][s]
+constexpr uint32_t B2_AS = 131072;    // A bf16 [t][s]; then dk staging, panel 0
 constexpr uint32_t B2_E = 139264;     // E^T bf16 [c][s], 1 panel x 128 rows; then dq staging
-constexpr uint32_t B2_WK = 155648;    // w * k; then dk staging
+constexpr uint32_t B2_WK = 155648;    // w * k
 constexpr uint32_t B2_DE = 172032;    // dE bf16 [s][c] (= dv, stored from here)
-constexpr uint32_t B2_DP = 188416;    // dP bf16 [t][s]
+constexpr uint32_t B2_DP = 188416;    // dP bf16 [t][s]; then dk staging, panel 1
 constexpr uint32_t B2_I = 196608;     // identity
 constexpr uint32_t B2_RED = 204800;   // fp32 [64][65]: tril(dA) * P per (t, s)
-constexpr uint32_t B2_GATE = 221440;  // 2 x {beta, alpha, mu, w}[64] (double-buffered), dw[2][64]
-constexpr uint32_t B2_BAR = 224000;
+constexpr uint32_t B2_GATE = 221440;  // 2 x {beta, alpha, mu, w}[64] (double-buffered), dw[2][64],
+                                      // column-sum partials [4][64], muon prefix sums [64]
+constexpr uint32_t B2_BAR = 225280;
 constexpr uint32_t B2_SMEM = B2_BAR + 256 + 1024;
 
 // TMEM: X0 P | dA, X1 dQ (lanes 16-31), X2 dE | dWk, X3 dK (lanes 0-15), XE E^T
@@ -594,9 +595,11 @@ static_assert(sizeof(Bars2) <= 256, "barrier block");
 
 // Persistent: CTA b handles tiles b, b + G, b + 2G, ... (tile = bh * N + chunk).
 // Tile i+1's inputs load as soon as phase 3 of tile i has read its tiles:
-// dq and dk are staged in the E^T and w*k tiles and dv is stored from the dE
-// tile, so every input tile is free then, and the load overlaps epilogue 3,
-// the gate gradients and the store drain of tile i.
+// dq is staged in the E^T tile, dk in the A and dP tiles (one 64-column
+// panel each) and dv is stored from the dE tile, so every input tile is free
+// then, and the load overlaps epilogue 3, the gate gradients and the store
+// drain of tile i.  The w*k tile is free at once, so tile i+1's epilogue waits
+// for the stores' reads only before epilogue 1 writes A and E^T.
 template <int RULE>
 __global__ void __launch_bounds__(kThreads2, 1)
 chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -611,6 +614,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   Bars2* bars = reinterpret_cast<Bars2*>(sm + B2_BAR);
   float* gate0 = reinterpret_cast<float*>(sm + B2_GATE);   // [2][4][64]
   float* gdw = gate0 + 512;  // [2][64]: partial k.dWk of each column half
+  float* gpart = gdw + 128;  // [4][64]: partial column sums of red
+  float* gpre = gpart + 256; // [64]: muon, sum_{u<s} dw_u w_u
   float* red = reinterpret_cast<float*>(sm + B2_RED);
   volatile int* ab = &bars->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -805,13 +810,9 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       float* galpha = gbeta + 64;
       float* gmu = gbeta + 128;
       float* gw = gbeta + 192;
-      // the previous tile's gate gradients are done with red, gdw and the chunk
-      // scalars; its stores have read their staging tiles (E, w*k, dE)
+      // the previous tile's gate gradients are done with red, gdw and the chunk scalars
       named_sync(1, 256);
-      if (tid == 0) {
-        bulk_wait_read0();
-        bars->da = 0.f;
-      }
+      if (tid == 0) bars->da = 0.f;
       named_sync(1, 256);
       if (!wait_use(&bars->ld_full, i, status, ab)) break;
       if constexpr (RULE == 1) {  // w_s = exp(sum_{t>s} log clamp(mu_t)), log-space suffix sums
@@ -876,6 +877,9 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       }
       // ---- epilogue 1: A = tril(P) beta (lanes 0-15), E^T -> bf16 (all lanes)
       if (!wait_use(&bars->ph1, i, status, ab)) break;
+      // the previous tile's stores have read their staging (E^T, A, dP, dE tiles)
+      if (tid == 0) bulk_wait_read0();
+      named_sync(1, 256);
       tc_fence_after();
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
@@ -927,19 +931,14 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         float x[16];
         tmem_ld16(tmem + lb + T2_X0 + c0, x);
         tmem_ld_wait();
-        float other[16];
-#pragma unroll
-        for (int y = 0; y < 16; ++y) other[y] = __shfl_xor_sync(0xffffffffu, x[y], 16);
-        if (hi) {  // x = dA row t, other = P row t
+        if (hi) {  // x = dA row t
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             float v8[8];
 #pragma unroll
             for (int y = 0; y < 8; ++y) {
               const int sc = c0 + h * 8 + y;
-              const float dam = (sc <= r16) ? x[h * 8 + y] : 0.f;
-              v8[y] = dam * gbeta[sc];
-              red[r16 * 65 + sc] = dam * other[h * 8 + y];
+              v8[y] = (sc <= r16) ? x[h * 8 + y] * gbeta[sc] : 0.f;
             }
             st_row8(sm + B2_DP, P64, r16, (c0 >> 3) + h, v8);
           }
@@ -976,7 +975,26 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tma_store_2d(&tm_dv, 64, static_cast<int>(tok), sm + B2_DE + P64);
         bulk_commit();
       }
-      // ---- epilogue 3: dq (staged in the E^T tile), dk (in the w*k tile), gate gradients
+      // dbeta pieces tril(dA) * P per (t, s), off the critical path (phase 3 runs):
+      // X0 stays valid until the next tile's phase 1
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c0 = half * 32 + cc * 16;
+        float x[16];
+        tmem_ld16(tmem + lb + T2_X0 + c0, x);
+        tmem_ld_wait();
+        float other[16];
+#pragma unroll
+        for (int y = 0; y < 16; ++y) other[y] = __shfl_xor_sync(0xffffffffu, x[y], 16);
+        if (hi) {  // x = dA row t, other = P row t
+#pragma unroll
+          for (int y = 0; y < 16; ++y) {
+            const int sc = c0 + y;
+            red[r16 * 65 + sc] = (sc <= r16) ? x[y] * other[y] : 0.f;
+          }
+        }
+      }
+      // ---- epilogue 3: dq (staged in the E^T tile), dk (A and dP tiles), gate gradients
       if (!wait_use(&bars->ph3, i, status, ab)) break;
       tc_fence_after();
       const float w = RULE == 0 ? gbeta[r16] : RULE == 1 ? gw[r16] : 1.f;
@@ -1001,8 +1019,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         } else {
 #pragma unroll
           for (int y = 0; y < 16; ++y) x3[y] = fmaf(w, dwk[y], x3[y]);
-          st_row8(sm + B2_WK, P64, r16, c0 >> 3, x3);
-          st_row8(sm + B2_WK, P64, r16, (c0 >> 3) + 1, x3 + 8);
+          st_row8(sm + B2_AS, B2_DP - B2_AS, r16, c0 >> 3, x3);
+          st_row8(sm + B2_AS, B2_DP - B2_AS, r16, (c0 >> 3) + 1, x3 + 8);
         }
       }
       fence_async_smem();
@@ -1010,14 +1028,38 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       if (tid == 0) {
         tma_store_2d(&tm_dq, 0, static_cast<int>(tok), sm + B2_E);
         tma_store_2d(&tm_dq, 64, static_cast<int>(tok), sm + B2_E + P64);
-        tma_store_2d(&tm_dk, 0, static_cast<int>(tok), sm + B2_WK);
-        tma_store_2d(&tm_dk, 64, static_cast<int>(tok), sm + B2_WK + P64);
+        tma_store_2d(&tm_dk, 0, static_cast<int>(tok), sm + B2_AS);
+        tma_store_2d(&tm_dk, 64, static_cast<int>(tok), sm + B2_DP);
         bulk_commit();
       }
+      // dbeta's A part: sum_t red[t][s] (zero above the diagonal), four threads per
+      // column; muon: exclusive prefix sums of dw_u w_u by one warp
+      {
+        const int s = tid & 63, part = tid >> 6;
+        float acc = 0.f;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) acc += red[(part * 16 + u) * 65 + s];
+        gpart[part * 64 + s] = acc;
+        if constexpr (RULE == 1) {
+          if (warp == 0) {
+            const float x0 = (gdw[2 * lane] + gdw[64 + 2 * lane]) * gw[2 * lane];
+            const float x1 = (gdw[2 * lane + 1] + gdw[65 + 2 * lane]) * gw[2 * lane + 1];
+            float incl = x0 + x1;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const float y = __shfl_up_sync(0xffffffffu, incl, o);
+              if (lane >= o) incl += y;
+            }
+            const float excl = incl - x0 - x1;   // tokens < 2 lane
+            gpre[2 * lane] = excl;
+            gpre[2 * lane + 1] = excl + x0;
+          }
+        }
+      }
+      named_sync(1, 256);
       if (tid < kC) {
         const int s = tid;
-        float db = 0.f;
-        for (int t = s; t < kC; ++t) db += red[t * 65 + s];
+        const float db = gpart[s] + gpart[64 + s] + gpart[128 + s] + gpart[192 + s];
         const float al = galpha[s];
         const size_t g = tok + s;
         if constexpr (RULE == 1) {
@@ -1029,11 +1071,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
               (al >= kGateFloor) ? args.dac[gi] * bars->a_c / fmaxf(al, kGateFloor) : 0.f;
           const float mu = gmu[s];
           float dmu = 0.f;
-          if (mu >= kGateFloor) {
-            float pre = 0.f;
-            for (int u2 = 0; u2 < s; ++u2) pre = fmaf(gdw[u2] + gdw[64 + u2], gw[u2], pre);
-            dmu = (args.dmc[gi] * bars->m_c + pre) / fmaxf(mu, kGateFloor);
-          }
+          if (mu >= kGateFloor) dmu = (args.dmc[gi] * bars->m_c + gpre[s]) / fmaxf(mu, kGateFloor);
           args.dmu[g] = dmu;
           if (args.dnu) args.dnu[g] = 0.f;
         } else if constexpr (RULE == 2) {
