@@ -86,9 +86,13 @@ constexpr uint32_t B1_RED = 188928;   // adam: per-warp partial chunk-scalar cot
 constexpr uint32_t B1_BAR = 189056;
 constexpr uint32_t B1_SMEM = B1_BAR + 256 + 1024;
 
-// TMEM: chain accumulators C0/C1, dE^T, P (lanes 0-15), Gb hi and lo packed
-// bf16 pairs (64 columns each = 128 values per lane).
-constexpr uint32_t T1_C0 = 0, T1_C1 = 128, T1_E = 256, T1_P = 320, T1_SH = 384, T1_SL = 448;
+// TMEM: chain accumulator C, dE^T hi / lo (packed bf16 pairs, the A operand of
+// C -= dE^T k), D = Gb k^T + dO^T A' (dE^T = D diag(w)), P (lanes 0-15), Gb hi
+// and lo packed bf16 pairs (64 columns each = 128 values per lane).  The token
+// weights are applied in the drain of D (A' = A / w), so no w k tile exists and
+// the chain's operands other than the TMA-loaded tiles stay in TMEM.
+constexpr uint32_t T1_C = 0, T1_DEH = 128, T1_DEL = 160, T1_E = 256, T1_P = 320, T1_SH = 384,
+                   T1_SL = 448;
 
 struct Bars1 {
   uint64_t ld_full[2], ld_empty[2];
@@ -123,7 +127,6 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       mbar_init(&bars->c_full[s], 1);
       mbar_init(&bars->c_empty[s], 256);
     }
-    mbar_init(&bars->wk_full, 128);
     mbar_init(&bars->p_full, 1);
     mbar_init(&bars->as_full, 128);
     mbar_init(&bars->de_full, 1);
@@ -168,10 +171,7 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   } else if (warp == 13) {
     // ------------------------------------------------------------ MMA issue
     if (lane == 0) {
-      const uint32_t wk_s = smem_u32(sm + B1_WK);
       const uint32_t as_s = smem_u32(sm + B1_AS);
-      const uint32_t deh_s = smem_u32(sm + B1_DEH);
-      const uint32_t del_s = smem_u32(sm + B1_DEL);
       constexpr uint32_t ID_P = idesc_bf16(64, 64, false, false);
       constexpr uint32_t ID_Z = idesc_bf16(128, 128, true, true);
       constexpr uint32_t ID_X = idesc_bf16(128, 64, true, true);
@@ -189,30 +189,28 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         mma_commit(&bars->p_full);
         return true;
       };
-      // Z(i): C = dO^T q (off the chain)
+      // Z(i): C = dO^T q (off the chain); C must have been drained (step i-1)
       auto issue_Z = [&](int i) -> bool {
-        const int r = i & 1;
-        if (i >= 2 && !wait_use(&bars->c_empty[r], (i >> 1) - 1, status, ab)) return false;
+        if (i >= 1 && !wait_use(&bars->c_empty[0], i - 1, status, ab)) return false;
         tc_fence_after();
         #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + (r ? T1_C1 : T1_C0), desc_mnmajor(stage(B1_G, i), P64, k),
+          mma_bf16(tmem + T1_C, desc_mnmajor(stage(B1_G, i), P64, k),
                    desc_mnmajor(stage(B1_Q, i), P64, k), ID_Z, k > 0);
         return true;
       };
       bool ok = N > 0 && issue_P(0) && issue_Z(0);
       for (int i = 0; ok && i < N; ++i) {
-        const int r = i & 1;
-        // Y(i): E^T = Sb_hi (wk)^T + Sb_lo (wk)^T  (Sb from TMEM);  X(i): E^T += dO^T A
+        const uint32_t k_s = stage(B1_K, i);
+        // Y(i): D = Gb_hi k^T + Gb_lo k^T  (Gb from TMEM);  X(i): D += dO^T A'
         if (!wait_use(&bars->s_full, i, status, ab)) break;
-        if (!wait_use(&bars->wk_full, i, status, ab)) break;
         tc_fence_after();
         #pragma unroll
         for (int k = 0; k < 8; ++k)
-          mma_bf16_ts(tmem + T1_E, tmem + T1_SH + k * 8, desc_kmajor(wk_s, P64, k), ID_Y, k > 0);
+          mma_bf16_ts(tmem + T1_E, tmem + T1_SH + k * 8, desc_kmajor(k_s, P64, k), ID_Y, k > 0);
         #pragma unroll
         for (int k = 0; k < 8; ++k)
-          mma_bf16_ts(tmem + T1_E, tmem + T1_SL + k * 8, desc_kmajor(wk_s, P64, k), ID_Y, 1);
+          mma_bf16_ts(tmem + T1_E, tmem + T1_SL + k * 8, desc_kmajor(k_s, P64, k), ID_Y, 1);
         if (!wait_use(&bars->as_full, i, status, ab)) break;
         tc_fence_after();
         #pragma unroll
@@ -220,19 +218,16 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           mma_bf16(tmem + T1_E, desc_mnmajor(stage(B1_G, i), P64, k),
                    desc_mnmajor(as_s, P64, k), ID_X, 1);
         mma_commit(&bars->de_full);
-        // W(i): C -= dE^T_hi k + dE^T_lo k
+        // W(i): C -= dE^T_hi k + dE^T_lo k   (dE^T from TMEM)
         if (!wait_use(&bars->de_smem, i, status, ab)) break;
         tc_fence_after();
-        const uint32_t k_s = stage(B1_K, i);
         #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + (r ? T1_C1 : T1_C0), desc_kmajor(deh_s, P128, k),
-                   desc_mnmajor(k_s, P64, k), ID_W, 1);
+          mma_bf16_ts(tmem + T1_C, tmem + T1_DEH + k * 8, desc_mnmajor(k_s, P64, k), ID_W, 1);
         #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + (r ? T1_C1 : T1_C0), desc_kmajor(del_s, P128, k),
-                   desc_mnmajor(k_s, P64, k), ID_W, 1);
-        mma_commit(&bars->c_full[r]);
+          mma_bf16_ts(tmem + T1_C, tmem + T1_DEL + k * 8, desc_mnmajor(k_s, P64, k), ID_W, 1);
+        mma_commit(&bars->c_full[0]);
         mma_commit(&bars->ld_empty[i & 1]);
         if (i + 1 < N && !(issue_P(i + 1) && issue_Z(i + 1))) break;
       }
@@ -387,9 +382,9 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       const float la = logf(fmaxf(__ldg(al + lane), kGateFloor)) +
                        logf(fmaxf(__ldg(al + lane + 32), kGateFloor));
       const float a = expf(warp_sum(la));
-      if (!wait_use(&bars->c_full[r], i >> 1, status, ab)) break;
+      if (!wait_use(&bars->c_full[0], i, status, ab)) break;
       tc_fence_after();
-      const uint32_t rc = tmem + lb + (r ? T1_C1 : T1_C0) + half * 64;
+      const uint32_t rc = tmem + lb + T1_C + half * 64;
       {
         float g0[16], g1[16], g2[16], g3[16];
         tmem_ld16(rc, g0);
@@ -406,7 +401,7 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         }
       }
       tc_fence_before();
-      mbar_arrive(&bars->c_empty[r]);
+      mbar_arrive(&bars->c_empty[0]);
       if constexpr (RULE == 2) {
         if (j >= 1 && !adam_pass(j - 1)) break;
       } else {
@@ -460,32 +455,6 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     const uint32_t lb = tmem_lane_base(warp);
     const int row = sp * 32 + lane;
     const int t16 = sp * 16 + (lane & 15);
-    auto build_wk = [&](int i) -> bool {
-      const int s = i & 1;
-      if (!wait_use(&bars->ld_full[s], i >> 1, status, ab)) return false;
-      const uint8_t* ks = sm + B1_K + s * 16384;
-      uint8_t* wk = sm + B1_WK;
-      const float* bs = gate_beta + s * 64;
-#pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        const int id = tb + 128 * m;
-        const uint32_t off = static_cast<uint32_t>(id) * 16u;
-        const uint4 x = *reinterpret_cast<const uint4*>(ks + off);
-        uint4 y = x;
-        if constexpr (RULE == 0) {  // delta: w = beta; adam: w = 1
-          const float w = bs[(id & 511) >> 3];
-          y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
-          y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
-          y.z = pack_bf16(bf16_lo(x.z) * w, bf16_hi(x.z) * w);
-          y.w = pack_bf16(bf16_lo(x.w) * w, bf16_hi(x.w) * w);
-        }
-        *reinterpret_cast<uint4*>(wk + off) = y;
-      }
-      fence_async_smem();
-      mbar_arrive(&bars->wk_full);
-      mbar_arrive(&bars->ld_empty[s]);
-      return true;
-    };
     auto build_as = [&](int i) -> bool {
       const float* bs = gate_beta + (i & 1) * 64;
       if (!wait_use(&bars->p_full, i, status, ab)) return false;
@@ -504,7 +473,8 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 #pragma unroll
             for (int x = 0; x < 8; ++x) {
               const int sc = cc * 16 + h * 8 + x;
-              v8[x] = (sc <= t16) ? src[x] * bs[sc] : 0.f;
+              // A' = tril(P) beta / w: delta (w = beta) tril(P), adam tril(P) beta
+              v8[x] = (sc <= t16) ? (RULE == 0 ? src[x] : src[x] * bs[sc]) : 0.f;
             }
             st_row8(sm + B1_AS, P64, t16, cc * 2 + h, v8);
           }
@@ -515,35 +485,41 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       mbar_arrive(&bars->as_full);
       return true;
     };
-    bool ok = N > 0 && build_wk(0) && build_as(0);
+    bool ok = N > 0 && build_as(0);
     for (int i = 0; ok && i < N; ++i) {
-      // dE^T (lanes = value row c, 64 token columns) -> hi / lo bf16
+      // dE^T = D diag(w) (lanes = value row c, 64 token columns) -> packed bf16
+      // hi / lo pairs into TMEM (the A operand of C -= dE^T k)
       if (!wait_use(&bars->de_full, i, status, ab)) break;
       tc_fence_after();
       {
+        const float* ws = gate_beta + (i & 1) * 64;   // delta: w = beta; adam: w = 1
         float x0[16], x1[16], x2[16], x3[16];
         tmem_ld16(tmem + lb + T1_E, x0);
         tmem_ld16(tmem + lb + T1_E + 16, x1);
         tmem_ld16(tmem + lb + T1_E + 32, x2);
         tmem_ld16(tmem + lb + T1_E + 48, x3);
         tmem_ld_wait();
+        auto x = [&](int t) { return t < 16 ? x0[t] : t < 32 ? x1[t - 16] : t < 48 ? x2[t - 32] : x3[t - 48]; };
 #pragma unroll
-        for (int h = 0; h < 8; ++h) {
-          const float* src = (h < 2 ? x0 : h < 4 ? x1 : h < 6 ? x2 : x3) + (h & 1) * 8;
-          float hi[8], lo[8];
+        for (int b = 0; b < 2; ++b) {
+          uint32_t hh[16], ll[16];
 #pragma unroll
-          for (int x = 0; x < 8; ++x) {
-            hi[x] = __bfloat162float(__float2bfloat16_rn(src[x]));
-            lo[x] = src[x] - hi[x];
+          for (int t = 0; t < 16; ++t) {
+            const int s0 = b * 32 + 2 * t;
+            const float e0 = RULE == 0 ? x(s0) * ws[s0] : x(s0);
+            const float e1 = RULE == 0 ? x(s0 + 1) * ws[s0 + 1] : x(s0 + 1);
+            hh[t] = pack_bf16(e0, e1);
+            ll[t] = pack_bf16(e0 - bf16_lo(hh[t]), e1 - bf16_hi(hh[t]));
           }
-          st_row8(sm + B1_DEH, P128, row, h, hi);
-          st_row8(sm + B1_DEL, P128, row, h, lo);
+          tmem_st16(tmem + lb + T1_DEH + b * 16, hh);
+          tmem_st16(tmem + lb + T1_DEL + b * 16, ll);
         }
+        tmem_st_wait();
       }
-      fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->de_smem);
-      if (i + 1 < N && !(build_wk(i + 1) && build_as(i + 1))) break;
+      mbar_arrive(&bars->ld_empty[i & 1]);   // done with this stage's gates
+      if (i + 1 < N && !build_as(i + 1)) break;
     }
   }
 

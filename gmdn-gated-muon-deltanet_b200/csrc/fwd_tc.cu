@@ -20,15 +20,19 @@
 // Per chunk the MMA thread issues (M x N x K):
 //   E(j)   -E_j^T = -v_j^T I + S_j k_j^T   128 x 64 x 64, 128 x 64 x 128 (S hi, lo)
 //   o1(j)  o_j^T  = S_j q_j^T              128 x 64 x 128 (S hi)
-//   G(j)   G_j    = E_j^T (w k_j)          128 x 128 x 64 (E hi, lo)
-//   o2(j)  o_j^T += E_j^T A_j^T            128 x 64 x 64
+//   G(j)   G_j    = (w E_j)^T k_j          128 x 128 x 64 (w E hi, lo)
+//   o2(j)  o_j^T += (w E_j)^T A'_j^T       128 x 64 x 64,  A' = tril(q k^T) beta / w
 //   P(j+1) P      = q k^T                  64 x 64 x 128
-// S_j hi/lo (packed bf16) live in TMEM as the A operand of E and o1, so the
-// recurrence never touches shared memory; E hi/lo go through shared memory.
+// S_j hi/lo (packed bf16) live in TMEM as the A operand of E and o1, and the
+// token weights are folded into E: the drain writes w E as packed bf16 hi/lo
+// back into TMEM, where it is the A operand of G and o2.  Besides the
+// operands TMA brings in, the chain never touches shared memory (shared-memory
+// bandwidth, not the tensor core, bounded the chain when E and w k went
+// through it).
 //
 // Warp roles (448 threads): warps 0-7 own the fp32 state (row c of S,
 // 64 columns each) and run S_{j+1} = a_j S_j + G_j; warps 8-11 drain E,
-// build A and w*k, and stage o for a TMA store; warp 12 issues TMA loads;
+// build A, and stage o for a TMA store; warp 12 issues TMA loads;
 // warp 13 allocates TMEM and issues every MMA from one thread.  All hand-offs
 // are mbarriers with bounded waits (tc.cuh).
 //
@@ -71,6 +75,7 @@ constexpr uint32_t P128 = 16384;  // panel stride of a 128-row tile
 
 // TMEM columns
 constexpr uint32_t TM_E = 0, TM_G = 64, TM_O = 192, TM_P = 256, TM_SH = 384, TM_SL = 448;
+constexpr uint32_t TM_WEH = 320, TM_WEL = 352;   // w E^T hi / lo, packed bf16 pairs (64 tokens)
 
 struct Bars {
   uint64_t ld_full[2], ld_empty[2];
@@ -115,7 +120,6 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     }
     mbar_init(&bars->p_full, 1);
     mbar_init(&bars->as_full, 128);
-    mbar_init(&bars->wk_full, 128);
     mbar_init(&bars->e_full, 1);
     mbar_init(&bars->e_smem, 128);
     mbar_init(&bars->g_full, 1);
@@ -164,16 +168,13 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   } else if (warp == 13) {
     // ------------------------------------------------------------ MMA issue
     if (lane == 0) {
-      const uint32_t wk_s = smem_u32(sm + OFF_WK);
       const uint32_t as_s = smem_u32(sm + OFF_AS);
-      const uint32_t eh_s = smem_u32(sm + OFF_EH);
-      const uint32_t el_s = smem_u32(sm + OFF_EL);
       const uint32_t id_s = smem_u32(sm + OFF_I);
       constexpr uint32_t ID_P = idesc_bf16(64, 64, false, false);
       constexpr uint32_t ID_EV = idesc_bf16(128, 64, true, false, true);   // -v^T I
       constexpr uint32_t ID_ES = idesc_bf16(128, 64, false, false);        // S k^T (A in TMEM)
-      constexpr uint32_t ID_G = idesc_bf16(128, 128, false, true);         // E^T (wk)
-      constexpr uint32_t ID_O2 = idesc_bf16(128, 64, false, false);        // E^T A^T
+      constexpr uint32_t ID_G = idesc_bf16(128, 128, false, true);         // (w E)^T k (A in TMEM)
+      constexpr uint32_t ID_O2 = idesc_bf16(128, 64, false, false);        // (w E)^T A'^T (A in TMEM)
       auto stage = [&](uint32_t base, int j) { return smem_u32(sm + base + (j & 1) * 16384); };
       auto issue_P = [&](int j) -> bool {
         if (!wait_use(&bars->ld_full[j & 1], j >> 1, status, ab)) return false;
@@ -185,14 +186,20 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         mma_commit(&bars->p_full);
         return true;
       };
-      bool ok = N > 0 && issue_P(0);
-      for (int j = 0; ok && j < N; ++j) {
-        const uint32_t q_s = stage(OFF_Q, j), k_s = stage(OFF_K, j), v_s = stage(OFF_V, j);
-        // E(j): D = -v^T I + S_hi k^T + S_lo k^T = -E^T
-        tc_fence_after();
+      // -v_j^T I into the E accumulator (it must be free: E(j-1) drained)
+      auto issue_E1 = [&](int j) {
+        const uint32_t v_s = stage(OFF_V, j);
         #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + TM_E, desc_mnmajor(v_s, P64, k), desc_kmajor(id_s, P64, k), ID_EV, k > 0);
+      };
+      // Issue order per chunk keeps the one-thread issue queue short after G(j),
+      // which the state update waits for: P(j+1) goes in while E(j) is drained.
+      bool ok = N > 0 && issue_P(0);
+      if (ok) issue_E1(0);
+      for (int j = 0; ok && j < N; ++j) {
+        const uint32_t q_s = stage(OFF_Q, j), k_s = stage(OFF_K, j);
+        // E(j): D = -v^T I + S_hi k^T + S_lo k^T = -E^T
         if (!wait_use(&bars->s_full, j, status, ab)) break;
         tc_fence_after();
         #pragma unroll
@@ -208,26 +215,26 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16_ts(tmem + TM_O, tmem + TM_SH + k * 8, desc_kmajor(q_s, P64, k), ID_ES, k > 0);
-        // G(j) = E^T_hi wk + E^T_lo wk
-        if (!wait_use(&bars->e_smem, j, status, ab)) break;
-        if (!wait_use(&bars->wk_full, j, status, ab)) break;
-        tc_fence_after();
-        #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + TM_G, desc_kmajor(eh_s, P128, k), desc_mnmajor(wk_s, P64, k), ID_G, k > 0);
-        #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + TM_G, desc_kmajor(el_s, P128, k), desc_mnmajor(wk_s, P64, k), ID_G, 1);
-        mma_commit(&bars->g_full);
-        // o2(j): o^T += E^T_hi A^T
+        // P(j+1), once A(j) has read P(j)
         if (!wait_use(&bars->as_full, j, status, ab)) break;
+        if (j + 1 < N && !issue_P(j + 1)) break;
+        // G(j) = (w E)^T_hi k + (w E)^T_lo k   (A from TMEM)
+        if (!wait_use(&bars->e_smem, j, status, ab)) break;
         tc_fence_after();
         #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + TM_O, desc_kmajor(eh_s, P128, k), desc_kmajor(as_s, P64, k), ID_O2, 1);
+          mma_bf16_ts(tmem + TM_G, tmem + TM_WEH + k * 8, desc_mnmajor(k_s, P64, k), ID_G, k > 0);
+        #pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_bf16_ts(tmem + TM_G, tmem + TM_WEL + k * 8, desc_mnmajor(k_s, P64, k), ID_G, 1);
+        mma_commit(&bars->g_full);
+        // o2(j): o^T += (w E)^T_hi A'^T
+        #pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_bf16_ts(tmem + TM_O, tmem + TM_WEH + k * 8, desc_kmajor(as_s, P64, k), ID_O2, 1);
         mma_commit(&bars->o_full);
         mma_commit(&bars->ld_empty[j & 1]);
-        if (j + 1 < N && !issue_P(j + 1)) break;
+        if (j + 1 < N) issue_E1(j + 1);   // E(j) has been drained (e_smem)
       }
       // every MMA issued so far has completed before TMEM is released
       mma_commit(&bars->final_mma);
@@ -383,35 +390,8 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     const uint32_t lb = tmem_lane_base(warp);
     const int row = sp * 32 + lane;            // TMEM lane of this thread
     const int t16 = sp * 16 + (lane & 15);     // M=64 row of lanes 0-15
-    // w * k for chunk jj (delta: w = beta, adam: w = 1); Wk must be free (G(jj-1) done)
-    auto build_wk = [&](int jj) -> bool {
-      const int s = jj & 1;
-      if (!wait_use(&bars->ld_full[s], jj >> 1, status, ab)) return false;
-      if (jj >= 1 && !wait_use(&bars->g_full, jj - 1, status, ab)) return false;
-      const uint8_t* ks = sm + OFF_K + s * 16384;
-      uint8_t* wk = sm + OFF_WK;
-      const float* bs = gate_beta + s * 64;
-#pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        const int id = tb + 128 * m;            // 16-byte chunk id, 0..1023
-        const uint32_t off = static_cast<uint32_t>(id) * 16u;
-        const uint4 x = *reinterpret_cast<const uint4*>(ks + off);
-        uint4 y = x;
-        if constexpr (RULE == 0) {
-          const float w = bs[(id & 511) >> 3];  // row inside the panel
-          y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
-          y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
-          y.z = pack_bf16(bf16_lo(x.z) * w, bf16_hi(x.z) * w);
-          y.w = pack_bf16(bf16_lo(x.w) * w, bf16_hi(x.w) * w);
-        }
-        *reinterpret_cast<uint4*>(wk + off) = y;
-      }
-      fence_async_smem();
-      mbar_arrive(&bars->wk_full);
-      mbar_arrive(&bars->ld_empty[s]);
-      return true;
-    };
-    // P -> A = tril(P) * beta (bf16); A must be free (o2(jj-1) done)
+    // P -> A' = tril(P) * beta / w (bf16): delta (w = beta) tril(P), adam (w = 1)
+    // tril(P) * beta; A' must be free (o2(jj-1) done)
     auto build_as = [&](int jj) -> bool {
       const float* bs = gate_beta + (jj & 1) * 64;
       if (!wait_use(&bars->p_full, jj, status, ab)) return false;
@@ -431,7 +411,7 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               const int sc = cc * 16 + h * 8 + i;
-              v8[i] = (sc <= t16) ? src[i] * bs[sc] : 0.f;
+              v8[i] = (sc <= t16) ? (RULE == 0 ? src[i] : src[i] * bs[sc]) : 0.f;
             }
             st_row8(sm + OFF_AS, P64, t16, cc * 2 + h, v8);
           }
@@ -442,36 +422,41 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       mbar_arrive(&bars->as_full);
       return true;
     };
-    bool ok = N > 0 && build_wk(0) && build_as(0);
+    bool ok = N > 0 && build_as(0);
     for (int j = 0; ok && j < N; ++j) {
-      // E3: -E^T (lanes = value row c, 64 token columns) -> E^T hi / lo bf16
+      // E3: -E^T (lanes = value row c, 64 token columns) -> w E^T hi / lo, packed
+      // bf16 pairs back into TMEM (the A operand of G and o2)
       if (!wait_use(&bars->e_full, j, status, ab)) break;
       tc_fence_after();
       {
+        const float* ws = gate_beta + (j & 1) * 64;   // delta: w = beta; adam: w = 1
         float x0[16], x1[16], x2[16], x3[16];
         tmem_ld16(tmem + lb + TM_E, x0);
         tmem_ld16(tmem + lb + TM_E + 16, x1);
         tmem_ld16(tmem + lb + TM_E + 32, x2);
         tmem_ld16(tmem + lb + TM_E + 48, x3);
         tmem_ld_wait();
+        auto x = [&](int i) { return i < 16 ? x0[i] : i < 32 ? x1[i - 16] : i < 48 ? x2[i - 32] : x3[i - 48]; };
 #pragma unroll
-        for (int h = 0; h < 8; ++h) {
-          const float* src = (h < 2 ? x0 : h < 4 ? x1 : h < 6 ? x2 : x3) + (h & 1) * 8;
-          float hi[8], lo[8];
+        for (int b = 0; b < 2; ++b) {
+          uint32_t hh[16], ll[16];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float e = -src[i];
-            hi[i] = __bfloat162float(__float2bfloat16_rn(e));
-            lo[i] = e - hi[i];
+          for (int t = 0; t < 16; ++t) {
+            const int s0 = b * 32 + 2 * t;
+            const float e0 = RULE == 0 ? -x(s0) * ws[s0] : -x(s0);
+            const float e1 = RULE == 0 ? -x(s0 + 1) * ws[s0 + 1] : -x(s0 + 1);
+            hh[t] = pack_bf16(e0, e1);
+            ll[t] = pack_bf16(e0 - bf16_lo(hh[t]), e1 - bf16_hi(hh[t]));
           }
-          st_row8(sm + OFF_EH, P128, row, h, hi);
-          st_row8(sm + OFF_EL, P128, row, h, lo);
+          tmem_st16(tmem + lb + TM_WEH + b * 16, hh);
+          tmem_st16(tmem + lb + TM_WEL + b * 16, ll);
         }
+        tmem_st_wait();
       }
-      fence_async_smem();
       tc_fence_before();
       mbar_arrive(&bars->e_smem);
-      if (j + 1 < N && !(build_wk(j + 1) && build_as(j + 1))) break;
+      mbar_arrive(&bars->ld_empty[j & 1]);   // done with this stage's gates
+      if (j + 1 < N && !build_as(j + 1)) break;
       // E5: o^T (lanes = value column c, 64 token columns) -> staged o[t][c] -> TMA store
       if (!wait_use(&bars->o_full, j, status, ab)) break;
       tc_fence_after();
