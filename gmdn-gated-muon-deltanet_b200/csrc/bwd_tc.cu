@@ -561,7 +561,7 @@ constexpr uint32_t B2_SMEM = B2_BAR + 256 + 1024;
 constexpr uint32_t T2_X0 = 0, T2_X1 = 64, T2_X2 = 192, T2_X3 = 320, T2_XE = 448;
 
 struct Bars2 {
-  uint64_t ld_full, ph1, ep1, wk_full, ph2, ep2, ph3, tm_free, lo_full, tail_done;
+  uint64_t ld_a, ld_b, ph1, ep1, wk_full, ph2, ep2, ph3, tm_free, lo_full, tail_done;
   uint32_t tmem_base;
   int abort_flag;
   float da;
@@ -570,12 +570,17 @@ struct Bars2 {
 static_assert(sizeof(Bars2) <= 256, "barrier block");
 
 // Persistent: CTA b handles tiles b, b + G, b + 2G, ... (tile = bh * N + chunk).
-// Tile i+1's inputs load as soon as phase 3 of tile i has read its tiles:
-// dq is staged in the E^T tile, dk in the A and dP tiles (one 64-column
-// panel each) and dv is stored from the dE tile, so every input tile is free
-// then, and the load overlaps epilogue 3, the gate gradients and the store
-// drain of tile i.  The w*k tile is free at once, so tile i+1's epilogue waits
-// for the stores' reads only before epilogue 1 writes A and E^T.
+// Tile i+1's inputs load in two groups: v, dO and Gb_j once phase 2 of tile i
+// has read them (the load overlaps epilogue 2 and phase 3), q, k and S_j once
+// phase 3 has.  dq is staged in the E^T tile, dk in the A and dP tiles (one
+// 64-column panel each) and dv is stored from the dE tile, so no input tile
+// holds an output, and the second load overlaps epilogue 3, the gate
+// gradients and the store drain of tile i.  Tile i+1's epilogue waits for the
+// stores' reads only before epilogue 1 writes A and E^T.
+// Delta and adam apply the token weight w to the rows of dE in its drain
+// (delta: A = tril(P), dE = diag(beta) (A^T dO + k Gb^T); adam: w = 1), so
+// k Gb^T is issued with phase 1 and runs while epilogue 1 drains; muon builds
+// w * k (w_s = prod_{t>s} mu_t can underflow, so beta / w is no option).
 template <int RULE>
 __global__ void __launch_bounds__(kThreads2, 1)
 chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -603,7 +608,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   auto gates = [&](int i) { return gate0 + (i & 1) * 256; };
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars->ld_full, 1);
+    mbar_init(&bars->ld_a, 1);
+    mbar_init(&bars->ld_b, 1);
     mbar_init(&bars->ph1, 1);
     mbar_init(&bars->ep1, 256);
     mbar_init(&bars->wk_full, 256);
@@ -631,27 +637,35 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   if (warp == 8) {
     // ------------------------------------------------------------ loads and MMAs (one thread)
     if (lane == 0) {
-      auto issue_loads = [&](int i, int tile) {
+      // group a: v, dO, Gb_j and the gates (last read by phase 2)
+      auto issue_a = [&](int i, int tile) {
         const int bh = tile / N, j = tile % N;
         const int tok = bh * args.T + j * kC;
         const int srow = (bh * N + j) * kD;
         float* gt = gates(i);
-        mbar_expect_tx(&bars->ld_full, 8 * 8192 + 4 * 16384 + 512 + (RULE == 1 ? 256 : 0));
-        tma_load_2d(sm + B2_Q, &tm_q, 0, tok, &bars->ld_full);
-        tma_load_2d(sm + B2_Q + P64, &tm_q, 64, tok, &bars->ld_full);
-        tma_load_2d(sm + B2_K, &tm_k, 0, tok, &bars->ld_full);
-        tma_load_2d(sm + B2_K + P64, &tm_k, 64, tok, &bars->ld_full);
-        tma_load_2d(sm + B2_V, &tm_v, 0, tok, &bars->ld_full);
-        tma_load_2d(sm + B2_V + P64, &tm_v, 64, tok, &bars->ld_full);
-        tma_load_2d(sm + B2_G, &tm_g, 0, tok, &bars->ld_full);
-        tma_load_2d(sm + B2_G + P64, &tm_g, 64, tok, &bars->ld_full);
-        tma_load_2d(sm + B2_S, &tm_s, 0, srow, &bars->ld_full);
-        tma_load_2d(sm + B2_S + P128, &tm_s, 64, srow, &bars->ld_full);
-        tma_load_2d(sm + B2_SB, &tm_sb, 0, srow, &bars->ld_full);
-        tma_load_2d(sm + B2_SB + P128, &tm_sb, 64, srow, &bars->ld_full);
-        bulk_load(gt, args.beta + tok, 256, &bars->ld_full);
-        bulk_load(gt + 64, args.alpha + tok, 256, &bars->ld_full);
-        if (RULE == 1) bulk_load(gt + 128, args.mu + tok, 256, &bars->ld_full);
+        mbar_expect_tx(&bars->ld_a, 4 * 8192 + 2 * 16384 + 512 + (RULE == 1 ? 256 : 0));
+        tma_load_2d(sm + B2_V, &tm_v, 0, tok, &bars->ld_a);
+        tma_load_2d(sm + B2_V + P64, &tm_v, 64, tok, &bars->ld_a);
+        tma_load_2d(sm + B2_G, &tm_g, 0, tok, &bars->ld_a);
+        tma_load_2d(sm + B2_G + P64, &tm_g, 64, tok, &bars->ld_a);
+        tma_load_2d(sm + B2_SB, &tm_sb, 0, srow, &bars->ld_a);
+        tma_load_2d(sm + B2_SB + P128, &tm_sb, 64, srow, &bars->ld_a);
+        bulk_load(gt, args.beta + tok, 256, &bars->ld_a);
+        bulk_load(gt + 64, args.alpha + tok, 256, &bars->ld_a);
+        if (RULE == 1) bulk_load(gt + 128, args.mu + tok, 256, &bars->ld_a);
+      };
+      // group b: q, k, S_j (read by phase 3)
+      auto issue_b = [&](int tile) {
+        const int bh = tile / N, j = tile % N;
+        const int tok = bh * args.T + j * kC;
+        const int srow = (bh * N + j) * kD;
+        mbar_expect_tx(&bars->ld_b, 4 * 8192 + 2 * 16384);
+        tma_load_2d(sm + B2_Q, &tm_q, 0, tok, &bars->ld_b);
+        tma_load_2d(sm + B2_Q + P64, &tm_q, 64, tok, &bars->ld_b);
+        tma_load_2d(sm + B2_K, &tm_k, 0, tok, &bars->ld_b);
+        tma_load_2d(sm + B2_K + P64, &tm_k, 64, tok, &bars->ld_b);
+        tma_load_2d(sm + B2_S, &tm_s, 0, srow, &bars->ld_b);
+        tma_load_2d(sm + B2_S + P128, &tm_s, 64, srow, &bars->ld_b);
       };
       // muon: lo half of Gb_j into the dE tile and the reduction array (free
       // until epilogue 2 of the same tile)
@@ -676,12 +690,21 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       constexpr uint32_t ID_EK = idesc_bf16(128, 64, false, false, true); // E^T: -S k^T
       constexpr uint32_t ID_DA = idesc_bf16(64, 64, false, true);         // dO E^T
       int i = 0;
+      int pa = -1, pb = -1, pl = -1;  // local tile of a load group in flight, not yet waited on
       if (static_cast<int>(blockIdx.x) < tiles) {
-        issue_loads(0, blockIdx.x);
-        if (RULE == 1) issue_lo(blockIdx.x);
+        issue_a(0, blockIdx.x);
+        issue_b(blockIdx.x);
+        pa = pb = 0;
+        if (RULE == 1) {
+          issue_lo(blockIdx.x);
+          pl = 0;
+        }
       }
       for (int tile = blockIdx.x; tile < tiles; tile += G, ++i) {
-        if (!wait_use(&bars->ld_full, i, status, ab)) break;
+        if (!wait_use(&bars->ld_a, i, status, ab)) break;
+        pa = -1;
+        if (!wait_use(&bars->ld_b, i, status, ab)) break;
+        pb = -1;
         if (i >= 1 && !wait_use(&bars->tm_free, i - 1, status, ab)) break;
         tc_fence_after();
         // phase 1: P = q k^T; E^T = v^T - S k^T; dQ = dO S
@@ -699,18 +722,28 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           mma_bf16(tmem + HI16 + T2_X1, desc_kmajor(g_s, P64, k), desc_mnmajor(s_s, P128, k),
                    ID_KM, k > 0);
         mma_commit(&bars->ph1);
-        if (!wait_use(&bars->ep1, i, status, ab) || !wait_use(&bars->wk_full, i, status, ab)) break;
+        if constexpr (RULE != 1) {
+          // delta, adam: the k Gb^T part of dE needs no epilogue output (w is applied
+          // to the rows of dE in its drain), so it runs while epilogue 1 drains
+          #pragma unroll
+          for (int k = 0; k < 8; ++k)
+            mma_bf16(tmem + T2_X2, desc_kmajor(k_s, P64, k), desc_kmajor(sb_s, P128, k), ID_KK, k > 0);
+        }
+        if (!wait_use(&bars->ep1, i, status, ab)) break;
+        if (RULE == 1 && !wait_use(&bars->wk_full, i, status, ab)) break;
         if (RULE == 1 && !wait_use(&bars->lo_full, i, status, ab)) break;
+        if (RULE == 1) pl = -1;
         tc_fence_after();
         // phase 2: dE = A^T dO + wk Gb^T;  dA = dO E^T;  dWk = E Gb
         #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + T2_X2, desc_mnmajor(as_s, P64, k), desc_mnmajor(g_s, P64, k), ID_MM, k > 0);
-        #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          mma_bf16(tmem + T2_X2, desc_kmajor(wk_s, P64, k), desc_kmajor(sb_s, P128, k), ID_KK, 1);
+          mma_bf16(tmem + T2_X2, desc_mnmajor(as_s, P64, k), desc_mnmajor(g_s, P64, k), ID_MM,
+                   RULE != 1 || k > 0);
         if constexpr (RULE == 1) {
           const uint32_t sbl_s = smem_u32(sm + B2_DE);   // panels 32 KB apart (dE tile, red)
+          #pragma unroll
+          for (int k = 0; k < 8; ++k)
+            mma_bf16(tmem + T2_X2, desc_kmajor(wk_s, P64, k), desc_kmajor(sb_s, P128, k), ID_KK, 1);
           #pragma unroll
           for (int k = 0; k < 8; ++k)
             mma_bf16(tmem + T2_X2, desc_kmajor(wk_s, P64, k), desc_kmajor(sbl_s, B2_RED - B2_DE, k),
@@ -737,6 +770,12 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                      ID_MM, 1);
         }
         mma_commit(&bars->ph2);
+        const int next = tile + G;
+        if (next < tiles) {   // v, dO and Gb_j have been read: load the next tile's
+          if (!wait_use(&bars->ph2, i, status, ab)) break;
+          issue_a(i + 1, next);
+          pa = i + 1;
+        }
         if (!wait_use(&bars->ep2, i, status, ab)) break;
         tc_fence_after();
         // phase 3: dq += dP k;  dK = -dE S + dP^T q
@@ -752,23 +791,23 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + T2_X3, desc_mnmajor(dp_s, P64, k), desc_mnmajor(q_s, P64, k), ID_MM, 1);
         mma_commit(&bars->ph3);
-        // every input tile has been read: load the next tile's
+        // q, k and S_j have been read: load the next tile's
         if (!wait_use(&bars->ph3, i, status, ab)) break;
-        const int next = tile + G;
         if (next < tiles) {
-          issue_loads(i + 1, next);
+          issue_b(next);
+          pb = i + 1;
           if (RULE == 1) {
             if (!wait_use(&bars->tail_done, i, status, ab)) break;
             issue_lo(next);
+            pl = i + 1;
           }
         }
       }
       // no copy of ours may still be in flight when the CTA exits
       int dummy = 0;
-      if (i >= 1 && static_cast<int>(blockIdx.x) + i * G < tiles)
-        mbar_wait(&bars->ld_full, i & 1, status, &dummy);
-      if (RULE == 1 && i >= 1 && static_cast<int>(blockIdx.x) + i * G < tiles)
-        mbar_wait(&bars->lo_full, i & 1, status, &dummy);
+      if (pa >= 0) mbar_wait(&bars->ld_a, pa & 1, status, &dummy);
+      if (pb >= 0) mbar_wait(&bars->ld_b, pb & 1, status, &dummy);
+      if (pl >= 0) mbar_wait(&bars->lo_full, pl & 1, status, &dummy);
     }
   } else {
     // ------------------------------------------------------------ epilogue warps 0-7
@@ -790,7 +829,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       named_sync(1, 256);
       if (tid == 0) bars->da = 0.f;
       named_sync(1, 256);
-      if (!wait_use(&bars->ld_full, i, status, ab)) break;
+      if (!wait_use(&bars->ld_a, i, status, ab) || !wait_use(&bars->ld_b, i, status, ab)) break;
       if constexpr (RULE == 1) {  // w_s = exp(sum_{t>s} log clamp(mu_t)), log-space suffix sums
         if (warp == 0) {
           const float l0 = logf(fmaxf(gmu[2 * lane], kGateFloor));
@@ -806,24 +845,24 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         }
         named_sync(1, 256);
       }
-      // w * k (delta: w = beta; muon: w = suffix product of mu; adam: w = 1)
+      if constexpr (RULE == 1) {
+        // w * k, w = suffix product of mu (delta and adam apply w to the rows of dE)
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const int id = tid + 256 * m;
-        const uint32_t off = static_cast<uint32_t>(id) * 16u;
-        const uint4 x = *reinterpret_cast<const uint4*>(sm + B2_K + off);
-        uint4 y = x;
-        if constexpr (RULE != 2) {
-          const float w = RULE == 0 ? gbeta[(id & 511) >> 3] : gw[(id & 511) >> 3];
+        for (int m = 0; m < 4; ++m) {
+          const int id = tid + 256 * m;
+          const uint32_t off = static_cast<uint32_t>(id) * 16u;
+          const uint4 x = *reinterpret_cast<const uint4*>(sm + B2_K + off);
+          const float w = gw[(id & 511) >> 3];
+          uint4 y;
           y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
           y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
           y.z = pack_bf16(bf16_lo(x.z) * w, bf16_hi(x.z) * w);
           y.w = pack_bf16(bf16_lo(x.w) * w, bf16_hi(x.w) * w);
+          *reinterpret_cast<uint4*>(sm + B2_WK + off) = y;
         }
-        *reinterpret_cast<uint4*>(sm + B2_WK + off) = y;
+        fence_async_smem();
+        mbar_arrive(&bars->wk_full);
       }
-      fence_async_smem();
-      mbar_arrive(&bars->wk_full);
       if constexpr (RULE == 0) {
         // da = <Sb_{j+1}, S_j>: row c128, column half `half` (adam, muon: from the chain)
         float part = 0.f;
@@ -851,7 +890,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         const float sum = warp_sum(lg);
         if (lane == 0) (warp == 1 ? bars->m_c : bars->n_c) = expf(sum);
       }
-      // ---- epilogue 1: A = tril(P) beta (lanes 0-15), E^T -> bf16 (all lanes)
+      // ---- epilogue 1: A = tril(P) (delta) or tril(P) beta (lanes 0-15), E^T -> bf16
+      // (all lanes)
       if (!wait_use(&bars->ph1, i, status, ab)) break;
       // the previous tile's stores have read their staging (E^T, A, dP, dE tiles)
       if (tid == 0) bulk_wait_read0();
@@ -870,7 +910,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 #pragma unroll
             for (int x = 0; x < 8; ++x) {
               const int sc = c0 + h * 8 + x;
-              v8[x] = (sc <= r16) ? p[h * 8 + x] * gbeta[sc] : 0.f;
+              v8[x] = (sc <= r16) ? (RULE == 0 ? p[h * 8 + x] : p[h * 8 + x] * gbeta[sc]) : 0.f;
             }
             st_row8(sm + B2_AS, P64, r16, (c0 >> 3) + h, v8);
           }
@@ -920,8 +960,10 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           }
         }
       }
-      // X2: dE (lanes 0-15) and dWk (lanes 16-31), row s = r16, 64 columns
+      // X2: dE (lanes 0-15; delta: times beta_s) and dWk (lanes 16-31), row s = r16,
+      // 64 columns
       float dw = 0.f;
+      const float wde = RULE == 0 ? gbeta[r16] : 1.f;
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         const int c0 = half * 64 + cc * 16;
@@ -929,6 +971,10 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tmem_ld16(tmem + lb + T2_X2 + c0, x);
         tmem_ld_wait();
         if (!hi) {
+          if constexpr (RULE == 0) {
+#pragma unroll
+            for (int y = 0; y < 16; ++y) x[y] *= wde;
+          }
           st_row8(sm + B2_DE, P64, r16, c0 >> 3, x);
           st_row8(sm + B2_DE, P64, r16, (c0 >> 3) + 1, x + 8);
         } else {
