@@ -72,18 +72,16 @@ struct BwArgs {
 // bw1: reverse chain
 // ===========================================================================
 
-constexpr int kThreads1 = 448;  // warps 0-7 state, 8-11 chunk-local, 12 TMA, 13 MMA
-constexpr uint32_t B1_Q = 0;          // q: 2 stages x 16 KB
-constexpr uint32_t B1_K = 32768;      // k: 2 stages
-constexpr uint32_t B1_G = 65536;      // dO: 2 stages
-constexpr uint32_t B1_WK = 98304;     // w * k
-constexpr uint32_t B1_AS = 114688;    // A (bf16), 1 panel x 64 rows
-constexpr uint32_t B1_DEH = 122880;   // dE^T hi, 1 panel x 128 rows
-constexpr uint32_t B1_DEL = 139264;   // dE^T lo
+constexpr int kThreads1 = 448;  // warps 0-7 state, 8-11 chunk-local, 12 TMA + P, Z, 13 chain MMAs
+constexpr int kStages1 = 3;           // q, k, dO ring: the load of step i+3 goes in after step i
+constexpr uint32_t B1_Q = 0;          // q: 3 stages x 16 KB
+constexpr uint32_t B1_K = 49152;      // k: 3 stages
+constexpr uint32_t B1_G = 98304;      // dO: 3 stages
+constexpr uint32_t B1_AS = 147456;    // A' (bf16), 1 panel x 64 rows
 constexpr uint32_t B1_SS = 155648;    // Gb hi staging for the TMA store, 2 panels x 128 rows
-constexpr uint32_t B1_GATE = 188416;  // beta: 2 stages x 64 floats
-constexpr uint32_t B1_RED = 188928;   // adam: per-warp partial chunk-scalar cotangents [8][4]
-constexpr uint32_t B1_BAR = 189056;
+constexpr uint32_t B1_GATE = 188416;  // beta: 3 stages x 64 floats
+constexpr uint32_t B1_RED = 189184;   // adam: per-warp partial chunk-scalar cotangents [8][4]
+constexpr uint32_t B1_BAR = 189312;
 constexpr uint32_t B1_SMEM = B1_BAR + 256 + 1024;
 
 // TMEM: chain accumulator C, dE^T hi / lo (packed bf16 pairs, the A operand of
@@ -95,10 +93,10 @@ constexpr uint32_t T1_C = 0, T1_DEH = 128, T1_DEL = 160, T1_E = 256, T1_P = 320,
                    T1_SL = 448;
 
 struct Bars1 {
-  uint64_t ld_full[2], ld_empty[2];
+  uint64_t ld_full[kStages1], ld_empty[kStages1];
   uint64_t wk_full, p_full, as_full, de_full, de_smem;
   uint64_t c_full[2], c_empty[2];
-  uint64_t s_full, final_mma;
+  uint64_t s_full, final_mma, z_full, final_tma;
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -121,18 +119,22 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   uint32_t* status = args.status;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kStages1; ++s) {
       mbar_init(&bars->ld_full[s], 1);
-      mbar_init(&bars->ld_empty[s], 1 + 128);
+      mbar_init(&bars->ld_empty[s], 1 + 4);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->c_full[s], 1);
-      mbar_init(&bars->c_empty[s], 256);
+      mbar_init(&bars->c_empty[s], 8);
     }
     mbar_init(&bars->p_full, 1);
-    mbar_init(&bars->as_full, 128);
+    mbar_init(&bars->as_full, 4);
     mbar_init(&bars->de_full, 1);
-    mbar_init(&bars->de_smem, 128);
-    mbar_init(&bars->s_full, 256);
+    mbar_init(&bars->de_smem, 4);
+    mbar_init(&bars->s_full, 8);
     mbar_init(&bars->final_mma, 1);
+    mbar_init(&bars->z_full, 1);
+    mbar_init(&bars->final_tma, 1);
     bars->abort_flag = 0;
     fence_mbar_init();
   }
@@ -146,14 +148,22 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   const uint32_t tmem = bars->tmem_base;
   const size_t tok0 = static_cast<size_t>(bh) * args.T;
 
+  constexpr uint32_t ID_P = idesc_bf16(64, 64, false, false);
+  constexpr uint32_t ID_Z = idesc_bf16(128, 128, true, true);
+  auto stage = [&](uint32_t base, int i) { return smem_u32(sm + base + (i % kStages1) * 16384); };
   if (warp == 12) {
-    // ------------------------------------------------------------ TMA, reverse chunk order
+    // ------------------------------------------------------------ TMA (reverse chunk order)
+    // and the off-chain products P(i) = q k^T and Z(i): C = dO^T q.  An MMA issue
+    // blocks its thread while the tensor pipe is busy, so these go from this
+    // thread, each into a window where the pipe is otherwise idle (P(i+1) while
+    // dE(i) is drained, Z(i+1) while Sb_j is packed), and the MMA thread issues
+    // only the chain's products.
     if (lane == 0) {
       int issued = 0;
-      for (int i = 0; i < N; ++i) {
-        const int j = N - 1 - i, s = i & 1;
+      auto load = [&](int i) -> bool {
+        const int j = N - 1 - i, s = i % kStages1;
         const int row = static_cast<int>(tok0) + j * kC;
-        if (!wait_free(&bars->ld_empty[s], i >> 1, status, ab)) break;
+        if (!wait_free(&bars->ld_empty[s], i / kStages1, status, ab)) return false;
         mbar_expect_tx(&bars->ld_full[s], 6 * 8192 + 256);
         tma_load_2d(sm + B1_Q + s * 16384, &tm_q, 0, row, &bars->ld_full[s]);
         tma_load_2d(sm + B1_Q + s * 16384 + P64, &tm_q, 64, row, &bars->ld_full[s]);
@@ -163,24 +173,10 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tma_load_2d(sm + B1_G + s * 16384 + P64, &tm_g, 64, row, &bars->ld_full[s]);
         bulk_load(gate_beta + s * 64, args.beta + tok0 + j * kC, 256, &bars->ld_full[s]);
         issued = i + 1;
-      }
-      int dummy = 0;
-      for (int i = issued - 2; i < issued; ++i)
-        if (i >= 0) mbar_wait(&bars->ld_full[i & 1], (i >> 1) & 1, status, &dummy);
-    }
-  } else if (warp == 13) {
-    // ------------------------------------------------------------ MMA issue
-    if (lane == 0) {
-      const uint32_t as_s = smem_u32(sm + B1_AS);
-      constexpr uint32_t ID_P = idesc_bf16(64, 64, false, false);
-      constexpr uint32_t ID_Z = idesc_bf16(128, 128, true, true);
-      constexpr uint32_t ID_X = idesc_bf16(128, 64, true, true);
-      constexpr uint32_t ID_Y = idesc_bf16(128, 64, false, false);
-      constexpr uint32_t ID_W = idesc_bf16(128, 128, false, true, true);
-      auto stage = [&](uint32_t base, int i) { return smem_u32(sm + base + (i & 1) * 16384); };
-      // P(i) = q k^T of step i's chunk
+        return true;
+      };
       auto issue_P = [&](int i) -> bool {
-        if (!wait_use(&bars->ld_full[i & 1], i >> 1, status, ab)) return false;
+        if (!wait_use(&bars->ld_full[i % kStages1], i / kStages1, status, ab)) return false;
         tc_fence_after();
         #pragma unroll
         for (int k = 0; k < 8; ++k)
@@ -189,7 +185,7 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         mma_commit(&bars->p_full);
         return true;
       };
-      // Z(i): C = dO^T q (off the chain); C must have been drained (step i-1)
+      // C must have been drained (step i-1); ld_full(i) was waited for by issue_P(i)
       auto issue_Z = [&](int i) -> bool {
         if (i >= 1 && !wait_use(&bars->c_empty[0], i - 1, status, ab)) return false;
         tc_fence_after();
@@ -197,13 +193,43 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + T1_C, desc_mnmajor(stage(B1_G, i), P64, k),
                    desc_mnmajor(stage(B1_Q, i), P64, k), ID_Z, k > 0);
+        mma_commit(&bars->z_full);
         return true;
       };
-      bool ok = N > 0 && issue_P(0) && issue_Z(0);
-      for (int i = 0; ok && i < N; ++i) {
+      // Per step i, in the order the inputs are released: P(i+1) once A'(i) has
+      // been built from P(i) and X(i) has left the pipe, the load of step i+3
+      // once step i is done with its stage (W(i), dE drain), Z(i+1) once C(i)
+      // has been drained.
+      bool ok = true;
+      for (int i = 0; ok && i < kStages1 && i < N; ++i) ok = load(i);
+      ok = ok && N > 0 && issue_P(0) && issue_Z(0);
+      for (int i = 0; ok && i + 1 < N; ++i) {
+        if (!wait_use(&bars->as_full, i, status, ab) || !wait_use(&bars->de_full, i, status, ab) ||
+            !issue_P(i + 1))
+          break;
+        if (i + kStages1 < N && !load(i + kStages1)) break;
+        if (!issue_Z(i + 1)) break;
+      }
+      // no MMA or copy of this thread may still be in flight when the CTA exits
+      mma_commit(&bars->final_tma);
+      int dummy = 0;
+      mbar_wait(&bars->final_tma, 0, status, &dummy);
+      for (int i = issued - kStages1; i < issued; ++i)
+        if (i >= 0) mbar_wait(&bars->ld_full[i % kStages1], (i / kStages1) & 1, status, &dummy);
+    }
+  } else if (warp == 13) {
+    // ------------------------------------------------------------ chain MMAs
+    if (lane == 0) {
+      const uint32_t as_s = smem_u32(sm + B1_AS);
+      constexpr uint32_t ID_X = idesc_bf16(128, 64, true, true);
+      constexpr uint32_t ID_Y = idesc_bf16(128, 64, false, false);
+      constexpr uint32_t ID_W = idesc_bf16(128, 128, false, true, true);
+      for (int i = 0; i < N; ++i) {
         const uint32_t k_s = stage(B1_K, i);
         // Y(i): D = Gb_hi k^T + Gb_lo k^T  (Gb from TMEM);  X(i): D += dO^T A'
-        if (!wait_use(&bars->s_full, i, status, ab)) break;
+        if (!wait_use(&bars->ld_full[i % kStages1], i / kStages1, status, ab) ||
+            !wait_use(&bars->s_full, i, status, ab))
+          break;
         tc_fence_after();
         #pragma unroll
         for (int k = 0; k < 8; ++k)
@@ -218,8 +244,9 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           mma_bf16(tmem + T1_E, desc_mnmajor(stage(B1_G, i), P64, k),
                    desc_mnmajor(as_s, P64, k), ID_X, 1);
         mma_commit(&bars->de_full);
-        // W(i): C -= dE^T_hi k + dE^T_lo k   (dE^T from TMEM)
-        if (!wait_use(&bars->de_smem, i, status, ab)) break;
+        // W(i): C -= dE^T_hi k + dE^T_lo k   (dE^T from TMEM; C = dO^T q from Z(i))
+        if (!wait_use(&bars->de_smem, i, status, ab) || !wait_use(&bars->z_full, i, status, ab))
+          break;
         tc_fence_after();
         #pragma unroll
         for (int k = 0; k < 4; ++k)
@@ -228,8 +255,7 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         for (int k = 0; k < 4; ++k)
           mma_bf16_ts(tmem + T1_C, tmem + T1_DEL + k * 8, desc_mnmajor(k_s, P64, k), ID_W, 1);
         mma_commit(&bars->c_full[0]);
-        mma_commit(&bars->ld_empty[i & 1]);
-        if (i + 1 < N && !(issue_P(i + 1) && issue_Z(i + 1))) break;
+        mma_commit(&bars->ld_empty[i % kStages1]);
       }
       mma_commit(&bars->final_mma);
       int dummy = 0;
@@ -267,7 +293,7 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       }
     }
     tc_fence_before();
-    mbar_arrive(&bars->s_full);
+    mbar_arrive_warp(&bars->s_full);
     // Adam: Gb_jm, Mb, Vb and the chunk-scalar cotangents of chunk jm from
     // sb = Sb_{jm+1}; Gb_jm hi / lo go to TMEM for the next chain product and
     // Gb_jm hi to the history.  Works in 8-column groups to stay in registers.
@@ -342,7 +368,7 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars->s_full);
+      mbar_arrive_warp(&bars->s_full);
       float* red = reinterpret_cast<float*>(sm + B1_RED);
       pda = warp_sum(pda);
       pdb = warp_sum(pdb);
@@ -382,7 +408,7 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       const float la = logf(fmaxf(__ldg(al + lane), kGateFloor)) +
                        logf(fmaxf(__ldg(al + lane + 32), kGateFloor));
       const float a = expf(warp_sum(la));
-      if (!wait_use(&bars->c_full[0], i, status, ab)) break;
+      if (!wait_use_w(&bars->c_full[0], i, status, ab)) break;
       tc_fence_after();
       const uint32_t rc = tmem + lb + T1_C + half * 64;
       {
@@ -401,7 +427,7 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         }
       }
       tc_fence_before();
-      mbar_arrive(&bars->c_empty[0]);
+      mbar_arrive_warp(&bars->c_empty[0]);
       if constexpr (RULE == 2) {
         if (j >= 1 && !adam_pass(j - 1)) break;
       } else {
@@ -423,7 +449,7 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars->s_full);
+      mbar_arrive_warp(&bars->s_full);
       // history for bw2: Sb_j hi (= Sb_{(j-1)+1}) through a staging tile and
       // one TMA store
       if (j >= 1) {
@@ -456,8 +482,8 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     const int row = sp * 32 + lane;
     const int t16 = sp * 16 + (lane & 15);
     auto build_as = [&](int i) -> bool {
-      const float* bs = gate_beta + (i & 1) * 64;
-      if (!wait_use(&bars->p_full, i, status, ab)) return false;
+      const float* bs = gate_beta + (i % kStages1) * 64;
+      if (!wait_use_w(&bars->p_full, i, status, ab)) return false;
       tc_fence_after();
 #pragma unroll
       for (int cc = 0; cc < 4; cc += 2) {
@@ -482,17 +508,17 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       }
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(&bars->as_full);
+      mbar_arrive_warp(&bars->as_full);
       return true;
     };
     bool ok = N > 0 && build_as(0);
     for (int i = 0; ok && i < N; ++i) {
       // dE^T = D diag(w) (lanes = value row c, 64 token columns) -> packed bf16
       // hi / lo pairs into TMEM (the A operand of C -= dE^T k)
-      if (!wait_use(&bars->de_full, i, status, ab)) break;
+      if (!wait_use_w(&bars->de_full, i, status, ab)) break;
       tc_fence_after();
       {
-        const float* ws = gate_beta + (i & 1) * 64;   // delta: w = beta; adam: w = 1
+        const float* ws = gate_beta + (i % kStages1) * 64;   // delta: w = beta; adam: w = 1
         float x0[16], x1[16], x2[16], x3[16];
         tmem_ld16(tmem + lb + T1_E, x0);
         tmem_ld16(tmem + lb + T1_E + 16, x1);
@@ -517,8 +543,8 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tmem_st_wait();
       }
       tc_fence_before();
-      mbar_arrive(&bars->de_smem);
-      mbar_arrive(&bars->ld_empty[i & 1]);   // done with this stage's gates
+      mbar_arrive_warp(&bars->de_smem);
+      mbar_arrive_warp(&bars->ld_empty[i % kStages1]);   // done with this stage's gates
       if (i + 1 < N && !build_as(i + 1)) break;
     }
   }
@@ -561,7 +587,8 @@ constexpr uint32_t B2_SMEM = B2_BAR + 256 + 1024;
 constexpr uint32_t T2_X0 = 0, T2_X1 = 64, T2_X2 = 192, T2_X3 = 320, T2_XE = 448;
 
 struct Bars2 {
-  uint64_t ld_a, ld_b, ph1, ep1, wk_full, ph2, ep2, ph3, tm_free, lo_full, tail_done;
+  uint64_t ld_a, ld_b, ld_s, ph1, ep1, wk_full, da_done, ph2, ep2, s_free, ph3, tm_free, k_free,
+      lo_full, tail_done;
   uint32_t tmem_base;
   int abort_flag;
   float da;
@@ -570,12 +597,13 @@ struct Bars2 {
 static_assert(sizeof(Bars2) <= 256, "barrier block");
 
 // Persistent: CTA b handles tiles b, b + G, b + 2G, ... (tile = bh * N + chunk).
-// Tile i+1's inputs load in two groups: v, dO and Gb_j once phase 2 of tile i
-// has read them (the load overlaps epilogue 2 and phase 3), q, k and S_j once
-// phase 3 has.  dq is staged in the E^T tile, dk in the A and dP tiles (one
-// 64-column panel each) and dv is stored from the dE tile, so no input tile
-// holds an output, and the second load overlaps epilogue 3, the gate
-// gradients and the store drain of tile i.  Tile i+1's epilogue waits for the
+// Tile i+1's inputs load in three groups, each as soon as tile i is done with
+// it: v, dO and Gb_j after phase 2 (and delta's da), S_j after the first
+// products of phase 3, q and k after phase 3 and epilogue 2's dw.  dq is
+// staged in the E^T tile, dk in the A and dP tiles (one 64-column panel each)
+// and dv is stored from the dE tile, so no input tile holds an output, and the
+// last load overlaps epilogue 3, the gate gradients and the store drain of
+// tile i.  Tile i+1's epilogue waits for the
 // stores' reads only before epilogue 1 writes A and E^T.
 // Delta and adam apply the token weight w to the rows of dE in its drain
 // (delta: A = tril(P), dE = diag(beta) (A^T dO + k Gb^T); adam: w = 1), so
@@ -610,13 +638,17 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   if (threadIdx.x == 0) {
     mbar_init(&bars->ld_a, 1);
     mbar_init(&bars->ld_b, 1);
+    mbar_init(&bars->ld_s, 1);
     mbar_init(&bars->ph1, 1);
-    mbar_init(&bars->ep1, 256);
-    mbar_init(&bars->wk_full, 256);
+    mbar_init(&bars->ep1, 8);
+    mbar_init(&bars->wk_full, 8);
     mbar_init(&bars->ph2, 1);
-    mbar_init(&bars->ep2, 256);
+    mbar_init(&bars->ep2, 8);
+    mbar_init(&bars->s_free, 1);
     mbar_init(&bars->ph3, 1);
-    mbar_init(&bars->tm_free, 256);
+    mbar_init(&bars->k_free, 8);
+    mbar_init(&bars->da_done, 8);
+    mbar_init(&bars->tm_free, 8);
     mbar_init(&bars->lo_full, 1);
     mbar_init(&bars->tail_done, 1);
     bars->abort_flag = 0;
@@ -654,18 +686,22 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         bulk_load(gt + 64, args.alpha + tok, 256, &bars->ld_a);
         if (RULE == 1) bulk_load(gt + 128, args.mu + tok, 256, &bars->ld_a);
       };
-      // group b: q, k, S_j (read by phase 3)
+      // group s: S_j (read by the first products of phase 3)
+      auto issue_s = [&](int tile) {
+        const int srow = tile * kD;   // tile = bh * N + j
+        mbar_expect_tx(&bars->ld_s, 2 * 16384);
+        tma_load_2d(sm + B2_S, &tm_s, 0, srow, &bars->ld_s);
+        tma_load_2d(sm + B2_S + P128, &tm_s, 64, srow, &bars->ld_s);
+      };
+      // group b: q, k (read by phase 3; k also by epilogue 2)
       auto issue_b = [&](int tile) {
         const int bh = tile / N, j = tile % N;
         const int tok = bh * args.T + j * kC;
-        const int srow = (bh * N + j) * kD;
-        mbar_expect_tx(&bars->ld_b, 4 * 8192 + 2 * 16384);
+        mbar_expect_tx(&bars->ld_b, 4 * 8192);
         tma_load_2d(sm + B2_Q, &tm_q, 0, tok, &bars->ld_b);
         tma_load_2d(sm + B2_Q + P64, &tm_q, 64, tok, &bars->ld_b);
         tma_load_2d(sm + B2_K, &tm_k, 0, tok, &bars->ld_b);
         tma_load_2d(sm + B2_K + P64, &tm_k, 64, tok, &bars->ld_b);
-        tma_load_2d(sm + B2_S, &tm_s, 0, srow, &bars->ld_b);
-        tma_load_2d(sm + B2_S + P128, &tm_s, 64, srow, &bars->ld_b);
       };
       // muon: lo half of Gb_j into the dE tile and the reduction array (free
       // until epilogue 2 of the same tile)
@@ -690,11 +726,12 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       constexpr uint32_t ID_EK = idesc_bf16(128, 64, false, false, true); // E^T: -S k^T
       constexpr uint32_t ID_DA = idesc_bf16(64, 64, false, true);         // dO E^T
       int i = 0;
-      int pa = -1, pb = -1, pl = -1;  // local tile of a load group in flight, not yet waited on
+      int pa = -1, pb = -1, ps = -1, pl = -1;  // local tile of a load group in flight, not yet waited on
       if (static_cast<int>(blockIdx.x) < tiles) {
         issue_a(0, blockIdx.x);
+        issue_s(blockIdx.x);
         issue_b(blockIdx.x);
-        pa = pb = 0;
+        pa = pb = ps = 0;
         if (RULE == 1) {
           issue_lo(blockIdx.x);
           pl = 0;
@@ -703,6 +740,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       for (int tile = blockIdx.x; tile < tiles; tile += G, ++i) {
         if (!wait_use(&bars->ld_a, i, status, ab)) break;
         pa = -1;
+        if (!wait_use(&bars->ld_s, i, status, ab)) break;
+        ps = -1;
         if (!wait_use(&bars->ld_b, i, status, ab)) break;
         pb = -1;
         if (i >= 1 && !wait_use(&bars->tm_free, i - 1, status, ab)) break;
@@ -771,28 +810,35 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         }
         mma_commit(&bars->ph2);
         const int next = tile + G;
-        if (next < tiles) {   // v, dO and Gb_j have been read: load the next tile's
-          if (!wait_use(&bars->ph2, i, status, ab)) break;
+        if (next < tiles) {   // v, dO and Gb_j have been read (also by da): load the next tile's
+          if (!wait_use(&bars->ph2, i, status, ab) || !wait_use(&bars->da_done, i, status, ab)) break;
           issue_a(i + 1, next);
           pa = i + 1;
         }
         if (!wait_use(&bars->ep2, i, status, ab)) break;
         tc_fence_after();
-        // phase 3: dq += dP k;  dK = -dE S + dP^T q
-        #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + HI16 + T2_X1, desc_kmajor(dp_s, P64, k), desc_mnmajor(k_s, P64, k), ID_KM,
-                   1);
+        // phase 3: dK = -dE S (S_j's last reader) + dP^T q;  dq += dP k
         #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + T2_X3, desc_kmajor(de_s, P64, k), desc_mnmajor(s_s, P128, k), ID_KMN,
                    k > 0);
+        mma_commit(&bars->s_free);
         #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + T2_X3, desc_mnmajor(dp_s, P64, k), desc_mnmajor(q_s, P64, k), ID_MM, 1);
+        #pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_bf16(tmem + HI16 + T2_X1, desc_kmajor(dp_s, P64, k), desc_mnmajor(k_s, P64, k), ID_KM,
+                   1);
         mma_commit(&bars->ph3);
-        // q, k and S_j have been read: load the next tile's
+        if (next < tiles) {   // S_j has been read (da of tile i was taken before phase 2 ended)
+          if (!wait_use(&bars->s_free, i, status, ab)) break;
+          issue_s(next);
+          ps = i + 1;
+        }
+        // q and k have been read (k also by epilogue 2's dw): load the next tile's
         if (!wait_use(&bars->ph3, i, status, ab)) break;
+        if (!wait_use(&bars->k_free, i, status, ab)) break;
         if (next < tiles) {
           issue_b(next);
           pb = i + 1;
@@ -807,6 +853,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       int dummy = 0;
       if (pa >= 0) mbar_wait(&bars->ld_a, pa & 1, status, &dummy);
       if (pb >= 0) mbar_wait(&bars->ld_b, pb & 1, status, &dummy);
+      if (ps >= 0) mbar_wait(&bars->ld_s, ps & 1, status, &dummy);
       if (pl >= 0) mbar_wait(&bars->lo_full, pl & 1, status, &dummy);
     }
   } else {
@@ -829,7 +876,9 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       named_sync(1, 256);
       if (tid == 0) bars->da = 0.f;
       named_sync(1, 256);
-      if (!wait_use(&bars->ld_a, i, status, ab) || !wait_use(&bars->ld_b, i, status, ab)) break;
+      if (!wait_use_w(&bars->ld_a, i, status, ab) || !wait_use_w(&bars->ld_s, i, status, ab) ||
+          !wait_use_w(&bars->ld_b, i, status, ab))
+        break;
       if constexpr (RULE == 1) {  // w_s = exp(sum_{t>s} log clamp(mu_t)), log-space suffix sums
         if (warp == 0) {
           const float l0 = logf(fmaxf(gmu[2 * lane], kGateFloor));
@@ -861,21 +910,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           *reinterpret_cast<uint4*>(sm + B2_WK + off) = y;
         }
         fence_async_smem();
-        mbar_arrive(&bars->wk_full);
-      }
-      if constexpr (RULE == 0) {
-        // da = <Sb_{j+1}, S_j>: row c128, column half `half` (adam, muon: from the chain)
-        float part = 0.f;
-#pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          float a8[8], b8[8];
-          unpack8(ld_row8(sm + B2_S, P128, c128, half * 8 + c8), a8);
-          unpack8(ld_row8(sm + B2_SB, P128, c128, half * 8 + c8), b8);
-#pragma unroll
-          for (int x = 0; x < 8; ++x) part = fmaf(a8[x], b8[x], part);
-        }
-        part = warp_sum(part);
-        if (lane == 0) atomicAdd(&bars->da, part);
+        mbar_arrive_warp(&bars->wk_full);
       }
       if (warp == 0) {  // chunk decay product a_c = prod clamp(alpha)
         const float la = logf(fmaxf(galpha[lane], kGateFloor)) +
@@ -892,7 +927,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       }
       // ---- epilogue 1: A = tril(P) (delta) or tril(P) beta (lanes 0-15), E^T -> bf16
       // (all lanes)
-      if (!wait_use(&bars->ph1, i, status, ab)) break;
+      if (!wait_use_w(&bars->ph1, i, status, ab)) break;
       // the previous tile's stores have read their staging (E^T, A, dP, dE tiles)
       if (tid == 0) bulk_wait_read0();
       named_sync(1, 256);
@@ -936,9 +971,25 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       }
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(&bars->ep1);
+      mbar_arrive_warp(&bars->ep1);
+      if constexpr (RULE == 0) {
+        // da = <Sb_{j+1}, S_j> while phase 2 runs (phase 1 is bound by shared-memory
+        // reads): row c128, column half `half` (adam, muon: from the chain)
+        float part = 0.f;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          float a8[8], b8[8];
+          unpack8(ld_row8(sm + B2_S, P128, c128, half * 8 + c8), a8);
+          unpack8(ld_row8(sm + B2_SB, P128, c128, half * 8 + c8), b8);
+#pragma unroll
+          for (int x = 0; x < 8; ++x) part = fmaf(a8[x], b8[x], part);
+        }
+        part = warp_sum(part);
+        if (lane == 0) atomicAdd(&bars->da, part);
+      }
+      mbar_arrive_warp(&bars->da_done);
       // ---- epilogue 2: dE -> bf16 (also dv); dP = tril(dA) beta; dbeta pieces; dw
-      if (!wait_use(&bars->ph2, i, status, ab)) break;
+      if (!wait_use_w(&bars->ph2, i, status, ab)) break;
       tc_fence_after();
       // X0: P (lanes 0-15) and dA (lanes 16-31) of the same row t = r16
 #pragma unroll
@@ -960,9 +1011,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           }
         }
       }
-      // X2: dE (lanes 0-15; delta: times beta_s) and dWk (lanes 16-31), row s = r16,
-      // 64 columns
-      float dw = 0.f;
+      // X2: dE (lanes 0-15; delta: times beta_s), row s = r16, 64 columns
       const float wde = RULE == 0 ? gbeta[r16] : 1.f;
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
@@ -977,20 +1026,11 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           }
           st_row8(sm + B2_DE, P64, r16, c0 >> 3, x);
           st_row8(sm + B2_DE, P64, r16, (c0 >> 3) + 1, x + 8);
-        } else {
-          float k8[8];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            unpack8(ld_row8(sm + B2_K, P64, r16, (c0 >> 3) + h), k8);
-#pragma unroll
-            for (int y = 0; y < 8; ++y) dw = fmaf(k8[y], x[h * 8 + y], dw);
-          }
         }
       }
-      if (RULE != 2 && hi) gdw[half * 64 + r16] = dw;
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(&bars->ep2);
+      mbar_arrive_warp(&bars->ep2);
       named_sync(1, 256);
       if (tid == 0) {   // dv = dE, straight from the dE tile
         tma_store_2d(&tm_dv, 0, static_cast<int>(tok), sm + B2_DE);
@@ -1016,8 +1056,30 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           }
         }
       }
+      if constexpr (RULE != 2) {
+        // dw_s = k_s . dWk_s (lanes 16-31 of X2, row s = r16), read before k is reloaded
+        float dw = 0.f;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c0 = half * 64 + cc * 16;
+          float x[16];
+          tmem_ld16(tmem + lb + T2_X2 + c0, x);
+          tmem_ld_wait();
+          if (hi) {
+            float k8[8];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              unpack8(ld_row8(sm + B2_K, P64, r16, (c0 >> 3) + h), k8);
+#pragma unroll
+              for (int y = 0; y < 8; ++y) dw = fmaf(k8[y], x[h * 8 + y], dw);
+            }
+          }
+        }
+        if (hi) gdw[half * 64 + r16] = dw;
+      }
+      mbar_arrive_warp(&bars->k_free);
       // ---- epilogue 3: dq (staged in the E^T tile), dk (A and dP tiles), gate gradients
-      if (!wait_use(&bars->ph3, i, status, ab)) break;
+      if (!wait_use_w(&bars->ph3, i, status, ab)) break;
       tc_fence_after();
       const float w = RULE == 0 ? gbeta[r16] : RULE == 1 ? gw[r16] : 1.f;
 #pragma unroll
@@ -1030,7 +1092,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tmem_ld_wait();
         if (cc == 3) {   // the next tile's products may overwrite TMEM now
           tc_fence_before();
-          mbar_arrive(&bars->tm_free);
+          mbar_arrive_warp(&bars->tm_free);
         }
         float dwk[16];
 #pragma unroll

@@ -116,16 +116,16 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->ld_full[s], 1);
-      mbar_init(&bars->ld_empty[s], 1 + 128);
+      mbar_init(&bars->ld_empty[s], 1 + 4);
     }
     mbar_init(&bars->p_full, 1);
-    mbar_init(&bars->as_full, 128);
+    mbar_init(&bars->as_full, 4);
     mbar_init(&bars->e_full, 1);
-    mbar_init(&bars->e_smem, 128);
+    mbar_init(&bars->e_smem, 4);
     mbar_init(&bars->g_full, 1);
-    mbar_init(&bars->s_full, 256);
+    mbar_init(&bars->s_full, 8);
     mbar_init(&bars->o_full, 1);
-    mbar_init(&bars->o_empty, 128);
+    mbar_init(&bars->o_empty, 4);
     mbar_init(&bars->final_mma, 1);
     bars->abort_flag = 0;
     fence_mbar_init();
@@ -266,7 +266,7 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       for (int i = 0; i < 8; ++i) g[i] = z;
     }
     tc_fence_before();
-    mbar_arrive(&bars->s_full);
+    mbar_arrive_warp(&bars->s_full);
     for (int j = 0; j < N; ++j) {
       const float* al = args.alpha + tok0 + j * kC;
       const float la = logf(fmaxf(__ldg(al + lane), kGateFloor)) +
@@ -281,7 +281,7 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                                        logf(fmaxf(__ldg(mu + lane + 32), kGateFloor))));
         const float nc = expf(warp_sum(logf(fmaxf(__ldg(nu + lane), kGateFloor)) +
                                        logf(fmaxf(__ldg(nu + lane + 32), kGateFloor))));
-        if (!wait_use(&bars->g_full, j, status, ab)) break;
+        if (!wait_use_w(&bars->g_full, j, status, ab)) break;
         tc_fence_after();
         const size_t mj = static_cast<size_t>(bh) * N + j;
         const uint32_t rg = tmem + lb + TM_G + half * 64;
@@ -320,7 +320,7 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           }
         }
       } else {
-      if (!wait_use(&bars->g_full, j, status, ab)) break;
+      if (!wait_use_w(&bars->g_full, j, status, ab)) break;
       tc_fence_after();
       {
         const uint32_t rg = tmem + lb + TM_G + half * 64;
@@ -358,7 +358,7 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&bars->s_full);
+      mbar_arrive_warp(&bars->s_full);
       // history for the backward: S_{j+1} hi through a staging tile and one
       // TMA store (row-per-thread global stores would be 32 partial sectors
       // per instruction)
@@ -394,8 +394,8 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     // tril(P) * beta; A' must be free (o2(jj-1) done)
     auto build_as = [&](int jj) -> bool {
       const float* bs = gate_beta + (jj & 1) * 64;
-      if (!wait_use(&bars->p_full, jj, status, ab)) return false;
-      if (jj >= 1 && !wait_use(&bars->o_full, jj - 1, status, ab)) return false;
+      if (!wait_use_w(&bars->p_full, jj, status, ab)) return false;
+      if (jj >= 1 && !wait_use_w(&bars->o_full, jj - 1, status, ab)) return false;
       tc_fence_after();
 #pragma unroll
       for (int cc = 0; cc < 4; cc += 2) {
@@ -419,14 +419,14 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       fence_async_smem();
       tc_fence_before();
-      mbar_arrive(&bars->as_full);
+      mbar_arrive_warp(&bars->as_full);
       return true;
     };
     bool ok = N > 0 && build_as(0);
     for (int j = 0; ok && j < N; ++j) {
       // E3: -E^T (lanes = value row c, 64 token columns) -> w E^T hi / lo, packed
       // bf16 pairs back into TMEM (the A operand of G and o2)
-      if (!wait_use(&bars->e_full, j, status, ab)) break;
+      if (!wait_use_w(&bars->e_full, j, status, ab)) break;
       tc_fence_after();
       {
         const float* ws = gate_beta + (j & 1) * 64;   // delta: w = beta; adam: w = 1
@@ -454,11 +454,11 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         tmem_st_wait();
       }
       tc_fence_before();
-      mbar_arrive(&bars->e_smem);
-      mbar_arrive(&bars->ld_empty[j & 1]);   // done with this stage's gates
+      mbar_arrive_warp(&bars->e_smem);
+      mbar_arrive_warp(&bars->ld_empty[j & 1]);   // done with this stage's gates
       if (j + 1 < N && !build_as(j + 1)) break;
       // E5: o^T (lanes = value column c, 64 token columns) -> staged o[t][c] -> TMA store
-      if (!wait_use(&bars->o_full, j, status, ab)) break;
+      if (!wait_use_w(&bars->o_full, j, status, ab)) break;
       tc_fence_after();
       if (tb == 0) bulk_wait_read0();        // previous store has left the staging tile
       named_sync(1, 128);
@@ -472,7 +472,7 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         tmem_ld16(tmem + lb + TM_O + 48, x3);
         tmem_ld_wait();
         tc_fence_before();
-        mbar_arrive(&bars->o_empty);
+        mbar_arrive_warp(&bars->o_empty);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           *reinterpret_cast<__nv_bfloat16*>(os + sw128_elem(i, ccol)) = __float2bfloat16_rn(x0[i]);

@@ -64,6 +64,17 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
                : "memory");
 }
 
+// One arrival per warp: all 32 lanes call it (converged); lane 0 arrives after
+// the warp has synchronised, so the barrier's count is the number of warps.
+// Each lane's earlier fences (tcgen05 before_thread_sync, proxy.async) are
+// ordered before the arrival by the warp barrier.  An mbarrier arrival is an
+// atomic on one shared-memory word: 256 per-thread arrivals serialise on it
+// (measured: hand-offs of 150-300 cycles), 8 per-warp arrivals do not.
+__device__ __forceinline__ void mbar_arrive_warp(uint64_t* bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(
                    smem_u32(bar)),
@@ -472,6 +483,16 @@ __device__ __forceinline__ bool wait_use(uint64_t* b, int use, uint32_t* st, vol
 }
 __device__ __forceinline__ bool wait_free(uint64_t* b, int use, uint32_t* st, volatile int* ab) {
   return mbar_wait(b, (static_cast<uint32_t>(use) & 1u) ^ 1u, st, ab);
+}
+
+// Warp-uniform variants for roles whose warps arrive with mbar_arrive_warp:
+// every lane waits and the warp agrees on the outcome, so after a give-up the
+// whole warp leaves together and no lane is left behind in a later __syncwarp.
+__device__ __forceinline__ bool wait_use_w(uint64_t* b, int use, uint32_t* st, volatile int* ab) {
+  return __all_sync(0xffffffffu, wait_use(b, use, st, ab));
+}
+__device__ __forceinline__ bool wait_free_w(uint64_t* b, int use, uint32_t* st, volatile int* ab) {
+  return __all_sync(0xffffffffu, wait_free(b, use, st, ab));
 }
 
 // Named barrier among `nthreads` threads (ids 1..15; 0 is __syncthreads).
