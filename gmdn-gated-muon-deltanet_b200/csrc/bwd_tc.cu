@@ -573,11 +573,11 @@ constexpr uint32_t B2_S = 65536;      // S_j, 2 panels x 128 rows
 constexpr uint32_t B2_SB = 98304;     // Gb_j
 constexpr uint32_t B2_AS = 131072;    // A bf16 [t][s]; then dk staging, panel 0
 constexpr uint32_t B2_E = 139264;     // E^T bf16 [c][s], 1 panel x 128 rows; then dq staging
-constexpr uint32_t B2_WK = 155648;    // w * k
+constexpr uint32_t B2_WK = 155648;    // muon: w * k; delta, adam: q of odd local tiles
 constexpr uint32_t B2_DE = 172032;    // dE bf16 [s][c] (= dv, stored from here)
 constexpr uint32_t B2_DP = 188416;    // dP bf16 [t][s]; then dk staging, panel 1
 constexpr uint32_t B2_I = 196608;     // identity
-constexpr uint32_t B2_RED = 204800;   // fp32 [64][65]: tril(dA) * P per (t, s)
+constexpr uint32_t B2_RED = 204800;   // muon: Gb lo, panel 1; delta, adam: k of odd local tiles
 constexpr uint32_t B2_GATE = 221440;  // 2 x {beta, alpha, mu, w}[64] (double-buffered), dw[2][64],
                                       // column-sum partials [4][64], muon prefix sums [64]
 constexpr uint32_t B2_BAR = 225280;
@@ -587,8 +587,8 @@ constexpr uint32_t B2_SMEM = B2_BAR + 256 + 1024;
 constexpr uint32_t T2_X0 = 0, T2_X1 = 64, T2_X2 = 192, T2_X3 = 320, T2_XE = 448;
 
 struct Bars2 {
-  uint64_t ld_a, ld_b, ld_s, ph1, ep1, wk_full, da_done, ph2, ep2, s_free, ph3, tm_free, k_free,
-      lo_full, tail_done;
+  uint64_t ld_a, ld_b[2], ld_s, ph1a, ph1, ep1, wk_full, da_done, ph2, ep2, s_free, ph3, tm_free,
+      k_free, lo_full, tail_done;
   uint32_t tmem_base;
   int abort_flag;
   float da;
@@ -597,18 +597,22 @@ struct Bars2 {
 static_assert(sizeof(Bars2) <= 256, "barrier block");
 
 // Persistent: CTA b handles tiles b, b + G, b + 2G, ... (tile = bh * N + chunk).
-// Tile i+1's inputs load in three groups, each as soon as tile i is done with
-// it: v, dO and Gb_j after phase 2 (and delta's da), S_j after the first
-// products of phase 3, q and k after phase 3 and epilogue 2's dw.  dq is
-// staged in the E^T tile, dk in the A and dP tiles (one 64-column panel each)
-// and dv is stored from the dE tile, so no input tile holds an output, and the
-// last load overlaps epilogue 3, the gate gradients and the store drain of
-// tile i.  Tile i+1's epilogue waits for the
-// stores' reads only before epilogue 1 writes A and E^T.
+// Each input group of the next tile loads as soon as the current tile is done
+// with it: v, dO and Gb_j after phase 2 (and delta's da), S_j after the first
+// products of phase 3.  q and k are double-buffered for delta and adam (the
+// w k tile and the reduction array are not needed there), so the q, k of
+// local tile i+2 load once tile i is done with its buffer; muon loads the next
+// tile's q, k after phase 3.  Phase 1 runs the products that need no S_j
+// (P, v^T I) first, so A is built while S_j arrives.  dq is staged in the E^T
+// tile, dk in the A and dP tiles (one 64-column panel each) and dv is stored
+// from the dE tile, so no input tile holds an output; the next tile's
+// epilogue waits for the stores' reads only before it writes A and E^T.
 // Delta and adam apply the token weight w to the rows of dE in its drain
 // (delta: A = tril(P), dE = diag(beta) (A^T dO + k Gb^T); adam: w = 1), so
 // k Gb^T is issued with phase 1 and runs while epilogue 1 drains; muon builds
 // w * k (w_s = prod_{t>s} mu_t can underflow, so beta / w is no option).
+// The dbeta column sums of tril(dA) * P are reduced across lanes with
+// shuffles (no shared-memory array).
 template <int RULE>
 __global__ void __launch_bounds__(kThreads2, 1)
 chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -623,10 +627,15 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   Bars2* bars = reinterpret_cast<Bars2*>(sm + B2_BAR);
   float* gate0 = reinterpret_cast<float*>(sm + B2_GATE);   // [2][4][64]
   float* gdw = gate0 + 512;  // [2][64]: partial k.dWk of each column half
-  float* gpart = gdw + 128;  // [4][64]: partial column sums of red
+  float* gpart = gdw + 128;  // [4][64]: column sums of tril(dA) * P over 16-row groups
   float* gpre = gpart + 256; // [64]: muon, sum_{u<s} dw_u w_u
-  float* red = reinterpret_cast<float*>(sm + B2_RED);
   volatile int* ab = &bars->abort_flag;
+  // q, k buffers: two for delta and adam (local tile i uses buffer i & 1)
+  constexpr int kQK = RULE == 1 ? 1 : 2;
+  auto qk_buf = [&](int i) { return kQK == 2 ? (i & 1) : 0; };
+  auto qk_use = [&](int i) { return kQK == 2 ? (i >> 1) : i; };   // uses of that buffer before
+  auto q_off = [&](int i) { return qk_buf(i) ? B2_WK : B2_Q; };
+  auto k_off = [&](int i) { return qk_buf(i) ? B2_RED : B2_K; };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int N = args.N;
   const int tiles = args.tiles;
@@ -637,8 +646,10 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->ld_a, 1);
-    mbar_init(&bars->ld_b, 1);
+    mbar_init(&bars->ld_b[0], 1);
+    mbar_init(&bars->ld_b[1], 1);
     mbar_init(&bars->ld_s, 1);
+    mbar_init(&bars->ph1a, 1);
     mbar_init(&bars->ph1, 1);
     mbar_init(&bars->ep1, 8);
     mbar_init(&bars->wk_full, 8);
@@ -693,15 +704,17 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tma_load_2d(sm + B2_S, &tm_s, 0, srow, &bars->ld_s);
         tma_load_2d(sm + B2_S + P128, &tm_s, 64, srow, &bars->ld_s);
       };
-      // group b: q, k (read by phase 3; k also by epilogue 2)
-      auto issue_b = [&](int tile) {
+      // group b: q, k of local tile i into its buffer (read by phases 1 and 3; k also
+      // by epilogue 2)
+      auto issue_b = [&](int i, int tile) {
         const int bh = tile / N, j = tile % N;
         const int tok = bh * args.T + j * kC;
-        mbar_expect_tx(&bars->ld_b, 4 * 8192);
-        tma_load_2d(sm + B2_Q, &tm_q, 0, tok, &bars->ld_b);
-        tma_load_2d(sm + B2_Q + P64, &tm_q, 64, tok, &bars->ld_b);
-        tma_load_2d(sm + B2_K, &tm_k, 0, tok, &bars->ld_b);
-        tma_load_2d(sm + B2_K + P64, &tm_k, 64, tok, &bars->ld_b);
+        uint64_t* bar = &bars->ld_b[qk_buf(i)];
+        mbar_expect_tx(bar, 4 * 8192);
+        tma_load_2d(sm + q_off(i), &tm_q, 0, tok, bar);
+        tma_load_2d(sm + q_off(i) + P64, &tm_q, 64, tok, bar);
+        tma_load_2d(sm + k_off(i), &tm_k, 0, tok, bar);
+        tma_load_2d(sm + k_off(i) + P64, &tm_k, 64, tok, bar);
       };
       // muon: lo half of Gb_j into the dE tile and the reduction array (free
       // until epilogue 2 of the same tile)
@@ -711,7 +724,6 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tma_load_2d(sm + B2_DE, &tm_sbl, 0, srow, &bars->lo_full);
         tma_load_2d(sm + B2_RED, &tm_sbl, 64, srow, &bars->lo_full);
       };
-      const uint32_t q_s = smem_u32(sm + B2_Q), k_s = smem_u32(sm + B2_K);
       const uint32_t v_s = smem_u32(sm + B2_V), g_s = smem_u32(sm + B2_G);
       const uint32_t s_s = smem_u32(sm + B2_S), sb_s = smem_u32(sm + B2_SB);
       const uint32_t as_s = smem_u32(sm + B2_AS), e_s = smem_u32(sm + B2_E);
@@ -726,33 +738,42 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       constexpr uint32_t ID_EK = idesc_bf16(128, 64, false, false, true); // E^T: -S k^T
       constexpr uint32_t ID_DA = idesc_bf16(64, 64, false, true);         // dO E^T
       int i = 0;
-      int pa = -1, pb = -1, ps = -1, pl = -1;  // local tile of a load group in flight, not yet waited on
+      // local tile of a load group in flight, not yet waited on
+      int pa = -1, ps = -1, pl = -1, pb[2] = {-1, -1};
       if (static_cast<int>(blockIdx.x) < tiles) {
         issue_a(0, blockIdx.x);
+        issue_b(0, blockIdx.x);
         issue_s(blockIdx.x);
-        issue_b(blockIdx.x);
-        pa = pb = ps = 0;
+        pa = ps = pb[0] = 0;
+        if (kQK == 2 && static_cast<int>(blockIdx.x) + G < tiles) {
+          issue_b(1, blockIdx.x + G);
+          pb[1] = 1;
+        }
         if (RULE == 1) {
           issue_lo(blockIdx.x);
           pl = 0;
         }
       }
       for (int tile = blockIdx.x; tile < tiles; tile += G, ++i) {
+        const uint32_t q_s = smem_u32(sm + q_off(i)), k_s = smem_u32(sm + k_off(i));
         if (!wait_use(&bars->ld_a, i, status, ab)) break;
         pa = -1;
-        if (!wait_use(&bars->ld_s, i, status, ab)) break;
-        ps = -1;
-        if (!wait_use(&bars->ld_b, i, status, ab)) break;
-        pb = -1;
+        if (!wait_use(&bars->ld_b[qk_buf(i)], qk_use(i), status, ab)) break;
+        pb[qk_buf(i)] = -1;
         if (i >= 1 && !wait_use(&bars->tm_free, i - 1, status, ab)) break;
         tc_fence_after();
-        // phase 1: P = q k^T; E^T = v^T - S k^T; dQ = dO S
+        // phase 1a (no S_j): P = q k^T; E^T = v^T
         #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + T2_X0, desc_kmajor(q_s, P64, k), desc_kmajor(k_s, P64, k), ID_P, k > 0);
         #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + T2_XE, desc_mnmajor(v_s, P64, k), desc_kmajor(id_s, P64, k), ID_EV, k > 0);
+        mma_commit(&bars->ph1a);
+        // phase 1b: E^T -= S k^T; dQ = dO S
+        if (!wait_use(&bars->ld_s, i, status, ab)) break;
+        ps = -1;
+        tc_fence_after();
         #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + T2_XE, desc_kmajor(s_s, P128, k), desc_kmajor(k_s, P64, k), ID_EK, 1);
@@ -779,7 +800,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           mma_bf16(tmem + T2_X2, desc_mnmajor(as_s, P64, k), desc_mnmajor(g_s, P64, k), ID_MM,
                    RULE != 1 || k > 0);
         if constexpr (RULE == 1) {
-          const uint32_t sbl_s = smem_u32(sm + B2_DE);   // panels 32 KB apart (dE tile, red)
+          const uint32_t sbl_s = smem_u32(sm + B2_DE);   // panels 32 KB apart (dE tile, B2_RED)
           #pragma unroll
           for (int k = 0; k < 8; ++k)
             mma_bf16(tmem + T2_X2, desc_kmajor(wk_s, P64, k), desc_kmajor(sb_s, P128, k), ID_KK, 1);
@@ -839,9 +860,12 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         // q and k have been read (k also by epilogue 2's dw): load the next tile's
         if (!wait_use(&bars->ph3, i, status, ab)) break;
         if (!wait_use(&bars->k_free, i, status, ab)) break;
+        const int nb = tile + kQK * G;   // the tile whose q, k go into this tile's buffer
+        if (nb < tiles) {
+          issue_b(i + kQK, nb);
+          pb[qk_buf(i)] = i + kQK;
+        }
         if (next < tiles) {
-          issue_b(next);
-          pb = i + 1;
           if (RULE == 1) {
             if (!wait_use(&bars->tail_done, i, status, ab)) break;
             issue_lo(next);
@@ -852,7 +876,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       // no copy of ours may still be in flight when the CTA exits
       int dummy = 0;
       if (pa >= 0) mbar_wait(&bars->ld_a, pa & 1, status, &dummy);
-      if (pb >= 0) mbar_wait(&bars->ld_b, pb & 1, status, &dummy);
+      for (int b = 0; b < 2; ++b)
+        if (pb[b] >= 0) mbar_wait(&bars->ld_b[b], qk_use(pb[b]) & 1, status, &dummy);
       if (ps >= 0) mbar_wait(&bars->ld_s, ps & 1, status, &dummy);
       if (pl >= 0) mbar_wait(&bars->lo_full, pl & 1, status, &dummy);
     }
@@ -872,12 +897,13 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       float* galpha = gbeta + 64;
       float* gmu = gbeta + 128;
       float* gw = gbeta + 192;
-      // the previous tile's gate gradients are done with red, gdw and the chunk scalars
+      const uint32_t k_tile = k_off(i);
+      // the previous tile's gate gradients are done with gpart, gdw and the chunk scalars
       named_sync(1, 256);
       if (tid == 0) bars->da = 0.f;
       named_sync(1, 256);
-      if (!wait_use_w(&bars->ld_a, i, status, ab) || !wait_use_w(&bars->ld_s, i, status, ab) ||
-          !wait_use_w(&bars->ld_b, i, status, ab))
+      if (!wait_use_w(&bars->ld_a, i, status, ab) ||
+          !wait_use_w(&bars->ld_b[qk_buf(i)], qk_use(i), status, ab))
         break;
       if constexpr (RULE == 1) {  // w_s = exp(sum_{t>s} log clamp(mu_t)), log-space suffix sums
         if (warp == 0) {
@@ -900,7 +926,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         for (int m = 0; m < 4; ++m) {
           const int id = tid + 256 * m;
           const uint32_t off = static_cast<uint32_t>(id) * 16u;
-          const uint4 x = *reinterpret_cast<const uint4*>(sm + B2_K + off);
+          const uint4 x = *reinterpret_cast<const uint4*>(sm + k_tile + off);
           const float w = gw[(id & 511) >> 3];
           uint4 y;
           y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
@@ -925,9 +951,9 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         const float sum = warp_sum(lg);
         if (lane == 0) (warp == 1 ? bars->m_c : bars->n_c) = expf(sum);
       }
-      // ---- epilogue 1: A = tril(P) (delta) or tril(P) beta (lanes 0-15), E^T -> bf16
-      // (all lanes)
-      if (!wait_use_w(&bars->ph1, i, status, ab)) break;
+      // ---- epilogue 1: A = tril(P) (delta) or tril(P) beta (lanes 0-15) once P is
+      // done, then E^T -> bf16 (all lanes)
+      if (!wait_use_w(&bars->ph1a, i, status, ab)) break;
       // the previous tile's stores have read their staging (E^T, A, dP, dE tiles)
       if (tid == 0) bulk_wait_read0();
       named_sync(1, 256);
@@ -951,6 +977,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           }
         }
       }
+      if (!wait_use_w(&bars->ph1, i, status, ab)) break;
+      tc_fence_after();
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
         const int c0 = half * 32 + cc * 16;
@@ -973,6 +1001,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       tc_fence_before();
       mbar_arrive_warp(&bars->ep1);
       if constexpr (RULE == 0) {
+        if (!wait_use_w(&bars->ld_s, i, status, ab)) break;
         // da = <Sb_{j+1}, S_j> while phase 2 runs (phase 1 is bound by shared-memory
         // reads): row c128, column half `half` (adam, muon: from the chain)
         float part = 0.f;
@@ -1037,23 +1066,41 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tma_store_2d(&tm_dv, 64, static_cast<int>(tok), sm + B2_DE + P64);
         bulk_commit();
       }
-      // dbeta pieces tril(dA) * P per (t, s), off the critical path (phase 3 runs):
-      // X0 stays valid until the next tile's phase 1
+      // dbeta's A part: column sums over t of tril(dA) * P, off the critical path
+      // (phase 3 runs).  Lanes 16-31 hold dA row t = r16 (P row t from lane - 16);
+      // the 16 rows of a warp are summed by a butterfly over lanes 16-31 that
+      // leaves each lane two of the warp's 32 column sums.  X0 stays valid until
+      // the next tile's phase 1.
+      {
+        float v[32];
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        const int c0 = half * 32 + cc * 16;
-        float x[16];
-        tmem_ld16(tmem + lb + T2_X0 + c0, x);
-        tmem_ld_wait();
-        float other[16];
-#pragma unroll
-        for (int y = 0; y < 16; ++y) other[y] = __shfl_xor_sync(0xffffffffu, x[y], 16);
-        if (hi) {  // x = dA row t, other = P row t
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c0 = half * 32 + cc * 16;
+          float x[16];
+          tmem_ld16(tmem + lb + T2_X0 + c0, x);
+          tmem_ld_wait();
 #pragma unroll
           for (int y = 0; y < 16; ++y) {
-            const int sc = c0 + y;
-            red[r16 * 65 + sc] = (sc <= r16) ? x[y] * other[y] : 0.f;
+            const float other = __shfl_xor_sync(0xffffffffu, x[y], 16);
+            v[cc * 16 + y] = (hi && c0 + y <= r16) ? x[y] * other : 0.f;
           }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int m = 8 >> r, n = 16 >> r;   // lane bit exchanged, values kept
+          const bool up = (lane & m) != 0;
+#pragma unroll
+          for (int k = 0; k < n; ++k) {
+            const float send = up ? v[k] : v[n + k];
+            const float keep = up ? v[n + k] : v[k];
+            v[k] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+          }
+        }
+        if (hi) {
+          const int col = half * 32 + ((lane & 8) ? 16 : 0) + ((lane & 4) ? 8 : 0) +
+                          ((lane & 2) ? 4 : 0) + ((lane & 1) ? 2 : 0);
+          gpart[sp * 64 + col] = v[0];
+          gpart[sp * 64 + col + 1] = v[1];
         }
       }
       if constexpr (RULE != 2) {
@@ -1069,7 +1116,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             float k8[8];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              unpack8(ld_row8(sm + B2_K, P64, r16, (c0 >> 3) + h), k8);
+              unpack8(ld_row8(sm + k_tile, P64, r16, (c0 >> 3) + h), k8);
 #pragma unroll
               for (int y = 0; y < 8; ++y) dw = fmaf(k8[y], x[h * 8 + y], dw);
             }
@@ -1116,14 +1163,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tma_store_2d(&tm_dk, 64, static_cast<int>(tok), sm + B2_DP);
         bulk_commit();
       }
-      // dbeta's A part: sum_t red[t][s] (zero above the diagonal), four threads per
-      // column; muon: exclusive prefix sums of dw_u w_u by one warp
+      // muon: exclusive prefix sums of dw_u w_u by one warp
       {
-        const int s = tid & 63, part = tid >> 6;
-        float acc = 0.f;
-#pragma unroll
-        for (int u = 0; u < 16; ++u) acc += red[(part * 16 + u) * 65 + s];
-        gpart[part * 64 + s] = acc;
         if constexpr (RULE == 1) {
           if (warp == 0) {
             const float x0 = (gdw[2 * lane] + gdw[64 + 2 * lane]) * gw[2 * lane];
@@ -1176,7 +1217,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         }
       }
       if constexpr (RULE == 1) {
-        // the dE tile (read by the dv store) and red are free for the next Gb lo
+        // the dE tile (read by the dv store) is free for the next Gb lo
         named_sync(1, 256);
         if (tid == 0) {
           bulk_wait_read0();
