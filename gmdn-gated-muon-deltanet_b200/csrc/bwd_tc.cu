@@ -587,8 +587,8 @@ constexpr uint32_t B2_SMEM = B2_BAR + 256 + 1024;
 constexpr uint32_t T2_X0 = 0, T2_X1 = 64, T2_X2 = 192, T2_X3 = 320, T2_XE = 448;
 
 struct Bars2 {
-  uint64_t ld_a, ld_b[2], ld_s, ph1a, ph1, ep1, wk_full, da_done, ph2, ep2, s_free, ph3, tm_free,
-      k_free, lo_full, tail_done;
+  uint64_t ld_a, ld_b[2], ld_s, ph1a, ph1, ep1, wk_full, da_done, ph2, de_ready, ep2, s_free, ph3,
+      tm_free, k_free, lo_full, tail_done;
   uint32_t tmem_base;
   int abort_flag;
   float da;
@@ -654,6 +654,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     mbar_init(&bars->ep1, 8);
     mbar_init(&bars->wk_full, 8);
     mbar_init(&bars->ph2, 1);
+    mbar_init(&bars->de_ready, 8);
     mbar_init(&bars->ep2, 8);
     mbar_init(&bars->s_free, 1);
     mbar_init(&bars->ph3, 1);
@@ -836,14 +837,17 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           issue_a(i + 1, next);
           pa = i + 1;
         }
-        if (!wait_use(&bars->ep2, i, status, ab)) break;
+        if (!wait_use(&bars->de_ready, i, status, ab)) break;
         tc_fence_after();
-        // phase 3: dK = -dE S (S_j's last reader) + dP^T q;  dq += dP k
+        // phase 3: dK = -dE S (S_j's last reader, as soon as dE is in shared memory)
+        // + dP^T q;  dq += dP k
         #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + T2_X3, desc_kmajor(de_s, P64, k), desc_mnmajor(s_s, P128, k), ID_KMN,
                    k > 0);
         mma_commit(&bars->s_free);
+        if (!wait_use(&bars->ep2, i, status, ab)) break;
+        tc_fence_after();
         #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + T2_X3, desc_mnmajor(dp_s, P64, k), desc_mnmajor(q_s, P64, k), ID_MM, 1);
@@ -1017,9 +1021,29 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         if (lane == 0) atomicAdd(&bars->da, part);
       }
       mbar_arrive_warp(&bars->da_done);
-      // ---- epilogue 2: dE -> bf16 (also dv); dP = tril(dA) beta; dbeta pieces; dw
+      // ---- epilogue 2: dE -> bf16 (also dv), then dP = tril(dA) beta; dbeta pieces; dw
       if (!wait_use_w(&bars->ph2, i, status, ab)) break;
       tc_fence_after();
+      // X2: dE (lanes 0-15; delta: times beta_s), row s = r16, 64 columns
+      const float wde = RULE == 0 ? gbeta[r16] : 1.f;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const int c0 = half * 64 + cc * 16;
+        float x[16];
+        tmem_ld16(tmem + lb + T2_X2 + c0, x);
+        tmem_ld_wait();
+        if (!hi) {
+          if constexpr (RULE == 0) {
+#pragma unroll
+            for (int y = 0; y < 16; ++y) x[y] *= wde;
+          }
+          st_row8(sm + B2_DE, P64, r16, c0 >> 3, x);
+          st_row8(sm + B2_DE, P64, r16, (c0 >> 3) + 1, x + 8);
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      mbar_arrive_warp(&bars->de_ready);   // -dE S may start (S_j's last reader)
       // X0: P (lanes 0-15) and dA (lanes 16-31) of the same row t = r16
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
@@ -1038,23 +1062,6 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             }
             st_row8(sm + B2_DP, P64, r16, (c0 >> 3) + h, v8);
           }
-        }
-      }
-      // X2: dE (lanes 0-15; delta: times beta_s), row s = r16, 64 columns
-      const float wde = RULE == 0 ? gbeta[r16] : 1.f;
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const int c0 = half * 64 + cc * 16;
-        float x[16];
-        tmem_ld16(tmem + lb + T2_X2 + c0, x);
-        tmem_ld_wait();
-        if (!hi) {
-          if constexpr (RULE == 0) {
-#pragma unroll
-            for (int y = 0; y < 16; ++y) x[y] *= wde;
-          }
-          st_row8(sm + B2_DE, P64, r16, c0 >> 3, x);
-          st_row8(sm + B2_DE, P64, r16, (c0 >> 3) + 1, x + 8);
         }
       }
       fence_async_smem();
