@@ -463,9 +463,9 @@ def main():
         top = max(kt, key=lambda k: kt[k][0])
         bound, work, work32 = kernel_work(top, cfg)
         avg_s = kt[top][0] / kt[top][1] / 1e3
-        source = (f"{peak_kind} (MEASURED_PEAKS.json bf16 burst)" if peak_kind == "measured"
-                  else "fallback")
         if bound == "tensor":
+            source = ("measured (MEASURED_PEAKS.json bf16_tflops, burst)" if peak_kind == "measured"
+                      else "fallback (1.59 PFLOP/s)")
             # bf16 products at the bf16 peak, fp32-state products at TF32 = bf16 / 2
             bf16 = peaks["bf16_tflops"]
             roof_s = work / (bf16 * 1e12) + work32 / (bf16 / 2 * 1e12)
@@ -475,6 +475,8 @@ def main():
             if work32 > 0:
                 source += "; fp32-state products at TF32 = bf16 / 2 (assumed, not measured)"
         else:
+            source = ("measured (MEASURED_PEAKS.json hbm_gbs, copy)" if peak_kind == "measured"
+                      else "fallback (6.65 TB/s)")
             achieved = work / avg_s / 1e9
             peak = peaks["hbm_gbs"]
             unit = "GB/s"
