@@ -604,8 +604,8 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 
 constexpr int kThreads2 = 288;
 constexpr uint32_t B2_Q = 0, B2_K = 16384, B2_V = 32768, B2_G = 49152;
-constexpr uint32_t B2_S = 65536;      // S_j, 2 panels x 128 rows
-constexpr uint32_t B2_SB = 98304;     // Gb_j
+constexpr uint32_t B2_ST0 = 65536;    // S_j and Gb_j, 2 panels x 128 rows each, in
+constexpr uint32_t B2_ST1 = 98304;    // these two tiles with roles swapped every tile
 constexpr uint32_t B2_AS = 131072;    // A bf16 [t][s]; then dk staging, panel 0
 constexpr uint32_t B2_E = 139264;     // E^T bf16 [c][s], 1 panel x 128 rows; then dq staging
 constexpr uint32_t B2_WK = 155648;    // muon: w * k; delta, adam: q of odd local tiles
@@ -622,7 +622,7 @@ constexpr uint32_t B2_SMEM = B2_BAR + 256 + 1024;
 constexpr uint32_t T2_X0 = 0, T2_X1 = 64, T2_X2 = 192, T2_X3 = 320, T2_XE = 448;
 
 struct Bars2 {
-  uint64_t ld_a, ld_b[2], ld_s, ph1a, ph1, ep1, wk_full, da_done, ph2, de_ready, ep2, s_free, ph3,
+  uint64_t ld_a, ld_b[2], ld_sb, ph1a, ph1, ep1, wk_full, da_done, ph2, de_ready, ep2, s_free, ph3,
       tm_free, k_free, lo_full, tail_done;
   uint32_t tmem_base;
   int abort_flag;
@@ -633,8 +633,10 @@ static_assert(sizeof(Bars2) <= 256, "barrier block");
 
 // Persistent: CTA b handles tiles b, b + G, b + 2G, ... (tile = bh * N + chunk).
 // Each input group of the next tile loads as soon as the current tile is done
-// with it: v, dO and Gb_j after phase 2 (and delta's da), S_j after the first
-// products of phase 3.  q and k are double-buffered for delta and adam (the
+// with it: v, dO and S_j after phase 2 (and delta's da), Gb_j after the first
+// products of phase 3.  S_j and Gb_j swap their two tiles every tile, so the
+// next S_j (needed first, by phase 1) goes into the current Gb_j tile a phase
+// earlier than S_j's own tile frees.  q and k are double-buffered for delta and adam (the
 // w k tile and the reduction array are not needed there), so the q, k of
 // local tile i+2 load once tile i is done with its buffer; muon loads the next
 // tile's q, k after phase 3.  Phase 1 runs the products that need no S_j
@@ -671,6 +673,10 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   auto qk_use = [&](int i) { return kQK == 2 ? (i >> 1) : i; };   // uses of that buffer before
   auto q_off = [&](int i) { return qk_buf(i) ? B2_WK : B2_Q; };
   auto k_off = [&](int i) { return qk_buf(i) ? B2_RED : B2_K; };
+  // S_j and Gb_j of local tile i; tile i+1's S_j goes where tile i's Gb_j was
+  // (free after phase 2) and its Gb_j where tile i's S_j was (free after -dE S)
+  auto s_off = [&](int i) { return (i & 1) ? B2_ST1 : B2_ST0; };
+  auto sb_off = [&](int i) { return (i & 1) ? B2_ST0 : B2_ST1; };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int N = args.N;
   const int tiles = args.tiles;
@@ -683,7 +689,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     mbar_init(&bars->ld_a, 1);
     mbar_init(&bars->ld_b[0], 1);
     mbar_init(&bars->ld_b[1], 1);
-    mbar_init(&bars->ld_s, 1);
+    mbar_init(&bars->ld_sb, 1);
     mbar_init(&bars->ph1a, 1);
     mbar_init(&bars->ph1, 1);
     mbar_init(&bars->ep1, 8);
@@ -716,7 +722,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   if (warp == 8) {
     // ------------------------------------------------------------ loads and MMAs (one thread)
     if (lane == 0) {
-      // group a: v, dO, Gb_j and the gates (last read by phase 2)
+      // group a: v, dO, S_j and the gates (into tiles the previous tile's phase 2
+      // has done with)
       auto issue_a = [&](int i, int tile) {
         const int bh = tile / N, j = tile % N;
         const int tok = bh * args.T + j * kC;
@@ -727,18 +734,19 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tma_load_2d(sm + B2_V + P64, &tm_v, 64, tok, &bars->ld_a);
         tma_load_2d(sm + B2_G, &tm_g, 0, tok, &bars->ld_a);
         tma_load_2d(sm + B2_G + P64, &tm_g, 64, tok, &bars->ld_a);
-        tma_load_2d(sm + B2_SB, &tm_sb, 0, srow, &bars->ld_a);
-        tma_load_2d(sm + B2_SB + P128, &tm_sb, 64, srow, &bars->ld_a);
+        tma_load_2d(sm + s_off(i), &tm_s, 0, srow, &bars->ld_a);
+        tma_load_2d(sm + s_off(i) + P128, &tm_s, 64, srow, &bars->ld_a);
         bulk_load(gt, args.beta + tok, 256, &bars->ld_a);
         bulk_load(gt + 64, args.alpha + tok, 256, &bars->ld_a);
         if (RULE == 1) bulk_load(gt + 128, args.mu + tok, 256, &bars->ld_a);
       };
-      // group s: S_j (read by the first products of phase 3)
-      auto issue_s = [&](int tile) {
+      // group sb: Gb_j (into the tile the previous tile's -dE S has done with;
+      // first read by k Gb^T after phase 1)
+      auto issue_sb = [&](int i, int tile) {
         const int srow = tile * kD;   // tile = bh * N + j
-        mbar_expect_tx(&bars->ld_s, 2 * 16384);
-        tma_load_2d(sm + B2_S, &tm_s, 0, srow, &bars->ld_s);
-        tma_load_2d(sm + B2_S + P128, &tm_s, 64, srow, &bars->ld_s);
+        mbar_expect_tx(&bars->ld_sb, 2 * 16384);
+        tma_load_2d(sm + sb_off(i), &tm_sb, 0, srow, &bars->ld_sb);
+        tma_load_2d(sm + sb_off(i) + P128, &tm_sb, 64, srow, &bars->ld_sb);
       };
       // group b: q, k of local tile i into its buffer (read by phases 1 and 3; k also
       // by epilogue 2)
@@ -761,7 +769,6 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tma_load_2d(sm + B2_RED, &tm_sbl, 64, srow, &bars->lo_full);
       };
       const uint32_t v_s = smem_u32(sm + B2_V), g_s = smem_u32(sm + B2_G);
-      const uint32_t s_s = smem_u32(sm + B2_S), sb_s = smem_u32(sm + B2_SB);
       const uint32_t as_s = smem_u32(sm + B2_AS), e_s = smem_u32(sm + B2_E);
       const uint32_t wk_s = smem_u32(sm + B2_WK), de_s = smem_u32(sm + B2_DE);
       const uint32_t dp_s = smem_u32(sm + B2_DP), id_s = smem_u32(sm + B2_I);
@@ -779,7 +786,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       if (static_cast<int>(blockIdx.x) < tiles) {
         issue_a(0, blockIdx.x);
         issue_b(0, blockIdx.x);
-        issue_s(blockIdx.x);
+        issue_sb(0, blockIdx.x);
         pa = ps = pb[0] = 0;
         if (kQK == 2 && static_cast<int>(blockIdx.x) + G < tiles) {
           issue_b(1, blockIdx.x + G);
@@ -792,6 +799,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       }
       for (int tile = blockIdx.x; tile < tiles; tile += G, ++i) {
         const uint32_t q_s = smem_u32(sm + q_off(i)), k_s = smem_u32(sm + k_off(i));
+        const uint32_t s_s = smem_u32(sm + s_off(i)), sb_s = smem_u32(sm + sb_off(i));
         if (!wait_use(&bars->ld_a, i, status, ab)) break;
         pa = -1;
         if (!wait_use(&bars->ld_b[qk_buf(i)], qk_use(i), status, ab)) break;
@@ -807,8 +815,6 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           mma_bf16(tmem + T2_XE, desc_mnmajor(v_s, P64, k), desc_kmajor(id_s, P64, k), ID_EV, k > 0);
         mma_commit(&bars->ph1a);
         // phase 1b: E^T -= S k^T; dQ = dO S
-        if (!wait_use(&bars->ld_s, i, status, ab)) break;
-        ps = -1;
         tc_fence_after();
         #pragma unroll
         for (int k = 0; k < 8; ++k)
@@ -818,6 +824,9 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           mma_bf16(tmem + HI16 + T2_X1, desc_kmajor(g_s, P64, k), desc_mnmajor(s_s, P128, k),
                    ID_KM, k > 0);
         mma_commit(&bars->ph1);
+        if (!wait_use(&bars->ld_sb, i, status, ab)) break;
+        ps = -1;
+        tc_fence_after();
         if constexpr (RULE != 1) {
           // delta, adam: the k Gb^T part of dE needs no epilogue output (w is applied
           // to the rows of dE in its drain), so it runs while epilogue 1 drains
@@ -893,7 +902,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         mma_commit(&bars->ph3);
         if (next < tiles) {   // S_j has been read (da of tile i was taken before phase 2 ended)
           if (!wait_use(&bars->s_free, i, status, ab)) break;
-          issue_s(next);
+          issue_sb(i + 1, next);
           ps = i + 1;
         }
         // q and k have been read (k also by epilogue 2's dw): load the next tile's
@@ -917,7 +926,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       if (pa >= 0) mbar_wait(&bars->ld_a, pa & 1, status, &dummy);
       for (int b = 0; b < 2; ++b)
         if (pb[b] >= 0) mbar_wait(&bars->ld_b[b], qk_use(pb[b]) & 1, status, &dummy);
-      if (ps >= 0) mbar_wait(&bars->ld_s, ps & 1, status, &dummy);
+      if (ps >= 0) mbar_wait(&bars->ld_sb, ps & 1, status, &dummy);
       if (pl >= 0) mbar_wait(&bars->lo_full, pl & 1, status, &dummy);
     }
   } else {
@@ -1040,15 +1049,15 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       tc_fence_before();
       mbar_arrive_warp(&bars->ep1);
       if constexpr (RULE == 0) {
-        if (!wait_use_w(&bars->ld_s, i, status, ab)) break;
+        if (!wait_use_w(&bars->ld_sb, i, status, ab)) break;
         // da = <Sb_{j+1}, S_j> while phase 2 runs (phase 1 is bound by shared-memory
         // reads): row c128, column half `half` (adam, muon: from the chain)
         float part = 0.f;
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {
           float a8[8], b8[8];
-          unpack8(ld_row8(sm + B2_S, P128, c128, half * 8 + c8), a8);
-          unpack8(ld_row8(sm + B2_SB, P128, c128, half * 8 + c8), b8);
+          unpack8(ld_row8(sm + s_off(i), P128, c128, half * 8 + c8), a8);
+          unpack8(ld_row8(sm + sb_off(i), P128, c128, half * 8 + c8), b8);
 #pragma unroll
           for (int x = 0; x < 8; ++x) part = fmaf(a8[x], b8[x], part);
         }
