@@ -613,9 +613,9 @@ constexpr uint32_t B2_DE = 172032;    // dE bf16 [s][c] (= dv, stored from here)
 constexpr uint32_t B2_DP = 188416;    // dP bf16 [t][s]; then dk staging, panel 1
 constexpr uint32_t B2_I = 196608;     // identity
 constexpr uint32_t B2_RED = 204800;   // muon: Gb lo, panel 1; delta, adam: k of odd local tiles
-constexpr uint32_t B2_GATE = 221440;  // 2 x {beta, alpha, mu, w}[64] (double-buffered), dw[2][64],
-                                      // column-sum partials [4][64], muon prefix sums [64]
-constexpr uint32_t B2_BAR = 225280;
+constexpr uint32_t B2_GATE = 221440;  // 2 x {beta, alpha, mu, w}[64], 2 x dw[2][64], 2 x column-sum
+                                      // partials [4][64] (by local tile parity), muon prefix sums [64]
+constexpr uint32_t B2_BAR = 226816;
 constexpr uint32_t B2_SMEM = B2_BAR + 256 + 1024;
 
 // TMEM: X0 P | dA, X1 dQ (lanes 16-31), X2 dE | dWk, X3 dK (lanes 0-15), XE E^T
@@ -626,8 +626,8 @@ struct Bars2 {
       tm_free, k_free, lo_full, tail_done;
   uint32_t tmem_base;
   int abort_flag;
-  float da;
-  float a_c, m_c, n_c;
+  float da[2];                 // by local tile parity: a tile's gate gradients are
+  float a_c[2], m_c[2], n_c[2];   // written while the next tile runs
 };
 static_assert(sizeof(Bars2) <= 256, "barrier block");
 
@@ -663,9 +663,9 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                                            ~static_cast<uintptr_t>(1023));
   Bars2* bars = reinterpret_cast<Bars2*>(sm + B2_BAR);
   float* gate0 = reinterpret_cast<float*>(sm + B2_GATE);   // [2][4][64]
-  float* gdw = gate0 + 512;  // [2][64]: partial k.dWk of each column half
-  float* gpart = gdw + 128;  // [4][64]: column sums of tril(dA) * P over 16-row groups
-  float* gpre = gpart + 256; // [64]: muon, sum_{u<s} dw_u w_u
+  float* gdw0 = gate0 + 512;     // [2 tiles][2][64]: partial k.dWk of each column half
+  float* gpart0 = gdw0 + 256;    // [2 tiles][4][64]: column sums of tril(dA) * P, 16-row groups
+  float* gpre = gpart0 + 512;    // [64]: muon, sum_{u<s} dw_u w_u
   volatile int* ab = &bars->abort_flag;
   // q, k buffers: two for delta and adam (local tile i uses buffer i & 1)
   constexpr int kQK = RULE == 1 ? 1 : 2;
@@ -705,7 +705,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     mbar_init(&bars->lo_full, 1);
     mbar_init(&bars->tail_done, 1);
     bars->abort_flag = 0;
-    bars->da = 0.f;
+    bars->da[0] = bars->da[1] = 0.f;
     fence_mbar_init();
   }
   build_identity64(sm + B2_I, threadIdx.x, kThreads2);
@@ -937,6 +937,75 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     const bool hi = lane >= 16;
     const int r16 = sp * 16 + (lane & 15);     // M=64 row of this lane's accumulator
     const int c128 = sp * 32 + lane;           // M=128 row (TMEM lane)
+    // Gate gradients of local tile li (tile tl), run while the next tile's phase 2
+    // is in the pipe (the epilogue is idle then): its gate loads, column sums, dw
+    // and chunk scalars are kept by tile parity until the next tile's da_done.
+    auto gate_stage = [&](int li, int tl) {
+      const int bh = tl / N, j = tl % N;
+      const size_t tok = static_cast<size_t>(bh) * args.T + static_cast<size_t>(j) * kC;
+      const float* gbeta = gates(li);
+      const float* galpha = gbeta + 64;
+      const float* gmu = gbeta + 128;
+      const float* gw = gbeta + 192;
+      const float* gdw = gdw0 + (li & 1) * 128;
+      const float* gpart = gpart0 + (li & 1) * 256;
+      (void)gbeta;
+      (void)gmu;
+      (void)gw;
+      // muon: exclusive prefix sums of dw_u w_u by one warp
+      {
+        if constexpr (RULE == 1) {
+          if (warp == 0) {
+            const float x0 = (gdw[2 * lane] + gdw[64 + 2 * lane]) * gw[2 * lane];
+            const float x1 = (gdw[2 * lane + 1] + gdw[65 + 2 * lane]) * gw[2 * lane + 1];
+            float incl = x0 + x1;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+              const float y = __shfl_up_sync(0xffffffffu, incl, o);
+              if (lane >= o) incl += y;
+            }
+            const float excl = incl - x0 - x1;   // tokens < 2 lane
+            gpre[2 * lane] = excl;
+            gpre[2 * lane + 1] = excl + x0;
+          }
+        }
+      }
+      named_sync(1, 256);
+      if (tid < kC) {
+        const int s = tid;
+        const float db = gpart[s] + gpart[64 + s] + gpart[128 + s] + gpart[192 + s];
+        const float al = galpha[s];
+        const size_t g = tok + s;
+        if constexpr (RULE == 1) {
+          // b_c = mean(beta); a_c, mu_c products; w_u = prod_{t>u} mu_t adds
+          // dmu_s += sum_{u<s} dw_u w_u / mu_s
+          const size_t gi = static_cast<size_t>(bh) * N + j;
+          args.dbeta[g] = db + args.dbc[gi] * (1.f / kC);
+          args.dalpha[g] =
+              (al >= kGateFloor) ? args.dac[gi] * bars->a_c[li & 1] / fmaxf(al, kGateFloor) : 0.f;
+          const float mu = gmu[s];
+          float dmu = 0.f;
+          if (mu >= kGateFloor) dmu = (args.dmc[gi] * bars->m_c[li & 1] + gpre[s]) / fmaxf(mu, kGateFloor);
+          args.dmu[g] = dmu;
+          if (args.dnu) args.dnu[g] = 0.f;
+        } else if constexpr (RULE == 2) {
+          // chunk scalars: b_c = mean(beta), a_c / mu_c / nu_c = prod of the clamped gates
+          const size_t gi = static_cast<size_t>(bh) * N + j;
+          args.dbeta[g] = db + args.dbc[gi] * (1.f / kC);
+          args.dalpha[g] =
+              (al >= kGateFloor) ? args.dac[gi] * bars->a_c[li & 1] / fmaxf(al, kGateFloor) : 0.f;
+          const float mu = __ldg(args.mu + g), nu = __ldg(args.nu + g);
+          args.dmu[g] = (mu >= kGateFloor) ? args.dmc[gi] * bars->m_c[li & 1] / fmaxf(mu, kGateFloor) : 0.f;
+          args.dnu[g] = (nu >= kGateFloor) ? args.dnc[gi] * bars->n_c[li & 1] / fmaxf(nu, kGateFloor) : 0.f;
+        } else {
+          args.dbeta[g] = db + gdw[s] + gdw[64 + s];
+          args.dalpha[g] =
+              (al >= kGateFloor) ? bars->da[li & 1] * bars->a_c[li & 1] / fmaxf(al, kGateFloor) : 0.f;
+          args.dmu[g] = 0.f;
+          if (args.dnu) args.dnu[g] = 0.f;
+        }
+      }
+    };
     int i = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += G, ++i) {
       const int bh = tile / N, j = tile % N;
@@ -945,10 +1014,12 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       float* galpha = gbeta + 64;
       float* gmu = gbeta + 128;
       float* gw = gbeta + 192;
+      float* gdw = gdw0 + (i & 1) * 128;
+      float* gpart = gpart0 + (i & 1) * 256;
       const uint32_t k_tile = k_off(i);
-      // the previous tile's gate gradients are done with gpart, gdw and the chunk scalars
+      // the gate gradients of two tiles back are done with this parity's da
       named_sync(1, 256);
-      if (tid == 0) bars->da = 0.f;
+      if (tid == 0) bars->da[i & 1] = 0.f;
       named_sync(1, 256);
       if (!wait_use_w(&bars->ld_a, i, status, ab) ||
           !wait_use_w(&bars->ld_b[qk_buf(i)], qk_use(i), status, ab))
@@ -990,14 +1061,14 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         const float la = logf(fmaxf(galpha[lane], kGateFloor)) +
                          logf(fmaxf(galpha[lane + 32], kGateFloor));
         const float sum = warp_sum(la);
-        if (lane == 0) bars->a_c = expf(sum);
+        if (lane == 0) bars->a_c[i & 1] = expf(sum);
       }
       if ((RULE == 2 && (warp == 1 || warp == 2)) || (RULE == 1 && warp == 1)) {  // mu_c, nu_c
         const float* gsrc = (warp == 1 ? args.mu : args.nu) + tok;
         const float lg = logf(fmaxf(__ldg(gsrc + lane), kGateFloor)) +
                          logf(fmaxf(__ldg(gsrc + lane + 32), kGateFloor));
         const float sum = warp_sum(lg);
-        if (lane == 0) (warp == 1 ? bars->m_c : bars->n_c) = expf(sum);
+        if (lane == 0) (warp == 1 ? bars->m_c : bars->n_c)[i & 1] = expf(sum);
       }
       // ---- epilogue 1: A = tril(P) (delta) or tril(P) beta (lanes 0-15) once P is
       // done, then E^T -> bf16 (all lanes)
@@ -1048,6 +1119,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       fence_async_smem();
       tc_fence_before();
       mbar_arrive_warp(&bars->ep1);
+      if (i >= 1) gate_stage(i - 1, tile - G);
       if constexpr (RULE == 0) {
         if (!wait_use_w(&bars->ld_sb, i, status, ab)) break;
         // da = <Sb_{j+1}, S_j> while phase 2 runs (phase 1 is bound by shared-memory
@@ -1062,7 +1134,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           for (int x = 0; x < 8; ++x) part = fmaf(a8[x], b8[x], part);
         }
         part = warp_sum(part);
-        if (lane == 0) atomicAdd(&bars->da, part);
+        if (lane == 0) atomicAdd(&bars->da[i & 1], part);
       }
       mbar_arrive_warp(&bars->da_done);
       // ---- epilogue 2: dE -> bf16 (also dv), then dP = tril(dA) beta; dbeta pieces; dw
@@ -1214,59 +1286,6 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tma_store_2d(&tm_dk, 64, static_cast<int>(tok), sm + B2_DP);
         bulk_commit();
       }
-      // muon: exclusive prefix sums of dw_u w_u by one warp
-      {
-        if constexpr (RULE == 1) {
-          if (warp == 0) {
-            const float x0 = (gdw[2 * lane] + gdw[64 + 2 * lane]) * gw[2 * lane];
-            const float x1 = (gdw[2 * lane + 1] + gdw[65 + 2 * lane]) * gw[2 * lane + 1];
-            float incl = x0 + x1;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-              const float y = __shfl_up_sync(0xffffffffu, incl, o);
-              if (lane >= o) incl += y;
-            }
-            const float excl = incl - x0 - x1;   // tokens < 2 lane
-            gpre[2 * lane] = excl;
-            gpre[2 * lane + 1] = excl + x0;
-          }
-        }
-      }
-      named_sync(1, 256);
-      if (tid < kC) {
-        const int s = tid;
-        const float db = gpart[s] + gpart[64 + s] + gpart[128 + s] + gpart[192 + s];
-        const float al = galpha[s];
-        const size_t g = tok + s;
-        if constexpr (RULE == 1) {
-          // b_c = mean(beta); a_c, mu_c products; w_u = prod_{t>u} mu_t adds
-          // dmu_s += sum_{u<s} dw_u w_u / mu_s
-          const size_t gi = static_cast<size_t>(bh) * N + j;
-          args.dbeta[g] = db + args.dbc[gi] * (1.f / kC);
-          args.dalpha[g] =
-              (al >= kGateFloor) ? args.dac[gi] * bars->a_c / fmaxf(al, kGateFloor) : 0.f;
-          const float mu = gmu[s];
-          float dmu = 0.f;
-          if (mu >= kGateFloor) dmu = (args.dmc[gi] * bars->m_c + gpre[s]) / fmaxf(mu, kGateFloor);
-          args.dmu[g] = dmu;
-          if (args.dnu) args.dnu[g] = 0.f;
-        } else if constexpr (RULE == 2) {
-          // chunk scalars: b_c = mean(beta), a_c / mu_c / nu_c = prod of the clamped gates
-          const size_t gi = static_cast<size_t>(bh) * N + j;
-          args.dbeta[g] = db + args.dbc[gi] * (1.f / kC);
-          args.dalpha[g] =
-              (al >= kGateFloor) ? args.dac[gi] * bars->a_c / fmaxf(al, kGateFloor) : 0.f;
-          const float mu = __ldg(args.mu + g), nu = __ldg(args.nu + g);
-          args.dmu[g] = (mu >= kGateFloor) ? args.dmc[gi] * bars->m_c / fmaxf(mu, kGateFloor) : 0.f;
-          args.dnu[g] = (nu >= kGateFloor) ? args.dnc[gi] * bars->n_c / fmaxf(nu, kGateFloor) : 0.f;
-        } else {
-          args.dbeta[g] = db + gdw[s] + gdw[64 + s];
-          args.dalpha[g] =
-              (al >= kGateFloor) ? bars->da * bars->a_c / fmaxf(al, kGateFloor) : 0.f;
-          args.dmu[g] = 0.f;
-          if (args.dnu) args.dnu[g] = 0.f;
-        }
-      }
       if constexpr (RULE == 1) {
         // the dE tile (read by the dv store) is free for the next Gb lo
         named_sync(1, 256);
@@ -1276,6 +1295,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         }
       }
     }
+    if (i >= 1 && !*ab) gate_stage(i - 1, static_cast<int>(blockIdx.x) + (i - 1) * G);
     // shared memory must outlive the reads of the bulk stores; grid completion
     // makes their global writes visible to the next kernel
     if (tid == 0) bulk_wait_read0();
