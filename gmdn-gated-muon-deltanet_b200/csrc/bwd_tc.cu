@@ -618,12 +618,14 @@ constexpr uint32_t B2_GATE = 221440;  // 2 x {beta, alpha, mu, w}[64], 2 x dw[2]
 constexpr uint32_t B2_BAR = 226816;
 constexpr uint32_t B2_SMEM = B2_BAR + 256 + 1024;
 
-// TMEM: X0 P | dA, X1 dQ (lanes 16-31), X2 dE | dWk, X3 dK (lanes 0-15), XE E^T
-constexpr uint32_t T2_X0 = 0, T2_X1 = 64, T2_X2 = 192, T2_X3 = 320, T2_XE = 448;
+// TMEM: X0 P | dA, XE E^T, X2 dE | dWk, and two regions D[0], D[1] holding dK
+// (lanes 0-15) | dQ (lanes 16-31) of alternate tiles, so the next tile's phase 1
+// can run while epilogue 3 still reads this tile's dq and dK.
+constexpr uint32_t T2_X0 = 0, T2_XE = 64, T2_X2 = 128, T2_D0 = 256;
 
 struct Bars2 {
   uint64_t ld_a, ld_b[2], ld_sb, ph1a, ph1, ep1, wk_full, da_done, ph2, de_ready, ep2, s_free, ph3,
-      tm_free, k_free, lo_full, tail_done;
+      x2_free, d_free[2], k_free, lo_full, tail_done;
   uint32_t tmem_base;
   int abort_flag;
   float da[2];                 // by local tile parity: a tile's gate gradients are
@@ -677,6 +679,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   // (free after phase 2) and its Gb_j where tile i's S_j was (free after -dE S)
   auto s_off = [&](int i) { return (i & 1) ? B2_ST1 : B2_ST0; };
   auto sb_off = [&](int i) { return (i & 1) ? B2_ST0 : B2_ST1; };
+  auto d_tm = [&](int i) { return T2_D0 + static_cast<uint32_t>(i & 1) * 128u; };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int N = args.N;
   const int tiles = args.tiles;
@@ -701,7 +704,9 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     mbar_init(&bars->ph3, 1);
     mbar_init(&bars->k_free, 8);
     mbar_init(&bars->da_done, 8);
-    mbar_init(&bars->tm_free, 8);
+    mbar_init(&bars->x2_free, 8);
+    mbar_init(&bars->d_free[0], 8);
+    mbar_init(&bars->d_free[1], 8);
     mbar_init(&bars->lo_full, 1);
     mbar_init(&bars->tail_done, 1);
     bars->abort_flag = 0;
@@ -804,7 +809,6 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         pa = -1;
         if (!wait_use(&bars->ld_b[qk_buf(i)], qk_use(i), status, ab)) break;
         pb[qk_buf(i)] = -1;
-        if (i >= 1 && !wait_use(&bars->tm_free, i - 1, status, ab)) break;
         tc_fence_after();
         // phase 1a (no S_j): P = q k^T; E^T = v^T
         #pragma unroll
@@ -814,18 +818,22 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + T2_XE, desc_mnmajor(v_s, P64, k), desc_kmajor(id_s, P64, k), ID_EV, k > 0);
         mma_commit(&bars->ph1a);
-        // phase 1b: E^T -= S k^T; dQ = dO S
+        // phase 1b: E^T -= S k^T; dQ = dO S into D[i & 1] (epilogue 3 of tile i-2 has
+        // read it)
+        if (i >= 2 && !wait_use(&bars->d_free[i & 1], (i >> 1) - 1, status, ab)) break;
         tc_fence_after();
         #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + T2_XE, desc_kmajor(s_s, P128, k), desc_kmajor(k_s, P64, k), ID_EK, 1);
         #pragma unroll
         for (int k = 0; k < 8; ++k)
-          mma_bf16(tmem + HI16 + T2_X1, desc_kmajor(g_s, P64, k), desc_mnmajor(s_s, P128, k),
+          mma_bf16(tmem + HI16 + d_tm(i), desc_kmajor(g_s, P64, k), desc_mnmajor(s_s, P128, k),
                    ID_KM, k > 0);
         mma_commit(&bars->ph1);
         if (!wait_use(&bars->ld_sb, i, status, ab)) break;
         ps = -1;
+        // X2 (dE | dWk) is written next: epilogue 3 of tile i-1 has read dWk
+        if (i >= 1 && !wait_use(&bars->x2_free, i - 1, status, ab)) break;
         tc_fence_after();
         if constexpr (RULE != 1) {
           // delta, adam: the k Gb^T part of dE needs no epilogue output (w is applied
@@ -835,6 +843,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             mma_bf16(tmem + T2_X2, desc_kmajor(k_s, P64, k), desc_kmajor(sb_s, P128, k), ID_KK, k > 0);
         }
         if (!wait_use(&bars->ep1, i, status, ab)) break;
+        if (RULE == 1 && i >= 1 && !wait_use(&bars->x2_free, i - 1, status, ab)) break;
         if (RULE == 1 && !wait_use(&bars->wk_full, i, status, ab)) break;
         if (RULE == 1 && !wait_use(&bars->lo_full, i, status, ab)) break;
         if (RULE == 1) pl = -1;
@@ -887,17 +896,17 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         // + dP^T q;  dq += dP k
         #pragma unroll
         for (int k = 0; k < 8; ++k)
-          mma_bf16(tmem + T2_X3, desc_kmajor(de_s, P64, k), desc_mnmajor(s_s, P128, k), ID_KMN,
+          mma_bf16(tmem + d_tm(i), desc_kmajor(de_s, P64, k), desc_mnmajor(s_s, P128, k), ID_KMN,
                    k > 0);
         mma_commit(&bars->s_free);
         if (!wait_use(&bars->ep2, i, status, ab)) break;
         tc_fence_after();
         #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + T2_X3, desc_mnmajor(dp_s, P64, k), desc_mnmajor(q_s, P64, k), ID_MM, 1);
+          mma_bf16(tmem + d_tm(i), desc_mnmajor(dp_s, P64, k), desc_mnmajor(q_s, P64, k), ID_MM, 1);
         #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_bf16(tmem + HI16 + T2_X1, desc_kmajor(dp_s, P64, k), desc_mnmajor(k_s, P64, k), ID_KM,
+          mma_bf16(tmem + HI16 + d_tm(i), desc_kmajor(dp_s, P64, k), desc_mnmajor(k_s, P64, k), ID_KM,
                    1);
         mma_commit(&bars->ph3);
         if (next < tiles) {   // S_j has been read (da of tile i was taken before phase 2 ended)
@@ -1255,26 +1264,26 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         const int c0 = half * 64 + cc * 16;
-        float x1[16], x2[16], x3[16];
-        tmem_ld16(tmem + lb + T2_X1 + c0, x1);   // dq at lanes 16-31
-        tmem_ld16(tmem + lb + T2_X2 + c0, x2);   // dWk at lanes 16-31
-        tmem_ld16(tmem + lb + T2_X3 + c0, x3);   // dK part at lanes 0-15
+        float x13[16], x2[16];
+        tmem_ld16(tmem + lb + d_tm(i) + c0, x13);   // dq at lanes 16-31, dK part at lanes 0-15
+        tmem_ld16(tmem + lb + T2_X2 + c0, x2);      // dWk at lanes 16-31
         tmem_ld_wait();
-        if (cc == 3) {   // the next tile's products may overwrite TMEM now
+        if (cc == 3) {   // later tiles' products may overwrite X2 and D[i & 1] now
           tc_fence_before();
-          mbar_arrive_warp(&bars->tm_free);
+          mbar_arrive_warp(&bars->x2_free);
+          mbar_arrive_warp(&bars->d_free[i & 1]);
         }
         float dwk[16];
 #pragma unroll
         for (int y = 0; y < 16; ++y) dwk[y] = __shfl_xor_sync(0xffffffffu, x2[y], 16);
         if (hi) {
-          st_row8(sm + B2_E, P64, r16, c0 >> 3, x1);
-          st_row8(sm + B2_E, P64, r16, (c0 >> 3) + 1, x1 + 8);
+          st_row8(sm + B2_E, P64, r16, c0 >> 3, x13);
+          st_row8(sm + B2_E, P64, r16, (c0 >> 3) + 1, x13 + 8);
         } else {
 #pragma unroll
-          for (int y = 0; y < 16; ++y) x3[y] = fmaf(w, dwk[y], x3[y]);
-          st_row8(sm + B2_AS, B2_DP - B2_AS, r16, c0 >> 3, x3);
-          st_row8(sm + B2_AS, B2_DP - B2_AS, r16, (c0 >> 3) + 1, x3 + 8);
+          for (int y = 0; y < 16; ++y) x13[y] = fmaf(w, dwk[y], x13[y]);
+          st_row8(sm + B2_AS, B2_DP - B2_AS, r16, c0 >> 3, x13);
+          st_row8(sm + B2_AS, B2_DP - B2_AS, r16, (c0 >> 3) + 1, x13 + 8);
         }
       }
       fence_async_smem();
