@@ -77,6 +77,12 @@ constexpr uint32_t P128 = 16384;  // panel stride of a 128-row tile
 constexpr uint32_t TM_E = 0, TM_G = 64, TM_O = 192, TM_P = 256, TM_SH = 384, TM_SL = 448;
 constexpr uint32_t TM_WEH = 320, TM_WEL = 352;   // w E^T hi / lo, packed bf16 pairs (64 tokens)
 
+// Who drains E: delta, the eight state warps (idle between packing S and G;
+// two warps per TMEM subpartition); adam, the four chunk-local warps (its
+// state warps carry the moment update).
+template <int RULE>
+constexpr int kEWarps = RULE == 0 ? 8 : 4;
+
 struct Bars {
   uint64_t ld_full[2], ld_empty[2];
   uint64_t p_full, as_full, wk_full, e_full, e_smem, g_full, s_full, o_full, o_empty;
@@ -116,12 +122,12 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->ld_full[s], 1);
-      mbar_init(&bars->ld_empty[s], 1 + 4);
+      mbar_init(&bars->ld_empty[s], 1 + kEWarps<RULE>);   // MMA commit, the E-draining warps
     }
     mbar_init(&bars->p_full, 1);
     mbar_init(&bars->as_full, 4);
     mbar_init(&bars->e_full, 1);
-    mbar_init(&bars->e_smem, 4);
+    mbar_init(&bars->e_smem, kEWarps<RULE>);
     mbar_init(&bars->g_full, 1);
     mbar_init(&bars->s_full, 8);
     mbar_init(&bars->o_full, 1);
@@ -272,6 +278,32 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       const float la = logf(fmaxf(__ldg(al + lane), kGateFloor)) +
                        logf(fmaxf(__ldg(al + lane + 32), kGateFloor));
       const float a = expf(warp_sum(la));
+      if constexpr (kEWarps<RULE> == 8) {
+        // -E^T (lanes = value row c, this warp's 32 token columns) -> w E^T hi / lo,
+        // packed bf16 pairs into TMEM, the A operand of G and o2
+        if (!wait_use_w(&bars->e_full, j, status, ab)) break;
+        tc_fence_after();
+        const float* ws = gate_beta + (j & 1) * 64 + half * 32;   // delta: w = beta
+        float x0[16], x1[16];
+        tmem_ld16(tmem + lb + TM_E + half * 32, x0);
+        tmem_ld16(tmem + lb + TM_E + half * 32 + 16, x1);
+        tmem_ld_wait();
+        uint32_t hh[16], ll[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          const float y0 = t < 8 ? x0[2 * t] : x1[2 * t - 16];
+          const float y1 = t < 8 ? x0[2 * t + 1] : x1[2 * t - 15];
+          const float e0 = -y0 * ws[2 * t], e1 = -y1 * ws[2 * t + 1];
+          hh[t] = pack_bf16(e0, e1);
+          ll[t] = pack_bf16(e0 - bf16_lo(hh[t]), e1 - bf16_hi(hh[t]));
+        }
+        tmem_st16(tmem + lb + TM_WEH + half * 16, hh);
+        tmem_st16(tmem + lb + TM_WEL + half * 16, ll);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive_warp(&bars->e_smem);
+        mbar_arrive_warp(&bars->ld_empty[j & 1]);   // done with this stage's gates
+      }
       if constexpr (RULE == 2) {
         const float* be = args.beta + tok0 + j * kC;
         const float* mu = args.mu + tok0 + j * kC;
@@ -427,6 +459,7 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       // E3: -E^T (lanes = value row c, 64 token columns) -> w E^T hi / lo, packed
       // bf16 pairs back into TMEM (the A operand of G and o2)
       if (!wait_use_w(&bars->e_full, j, status, ab)) break;
+      if constexpr (kEWarps<RULE> == 4) {
       tc_fence_after();
       {
         const float* ws = gate_beta + (j & 1) * 64;   // delta: w = beta; adam: w = 1
@@ -456,6 +489,7 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       tc_fence_before();
       mbar_arrive_warp(&bars->e_smem);
       mbar_arrive_warp(&bars->ld_empty[j & 1]);   // done with this stage's gates
+      }
       if (j + 1 < N && !build_as(j + 1)) break;
       // E5: o^T (lanes = value column c, 64 token columns) -> staged o[t][c] -> TMA store
       if (!wait_use_w(&bars->o_full, j, status, ab)) break;
