@@ -92,12 +92,12 @@ constexpr uint32_t B1_SMEM = B1_BAR + 256 + 1024;
 constexpr uint32_t T1_C = 0, T1_DEH = 128, T1_DEL = 160, T1_E = 256, T1_P = 320, T1_SH = 384,
                    T1_SL = 448;
 
-// Who drains dE: delta, the four chunk-local warps; adam, the eight state warps
-// (idle between their Gb pass and W there, and two warps per TMEM subpartition
-// drain in about half the time).  Measured: delta 0.159 vs 0.166 ms, adam
-// 1.82 vs 1.90 ms for the better choice at config 1.
+// Who drains dE: the eight state warps (idle between packing Sb and W; two
+// warps per TMEM subpartition drain in about half the time of one).  Delta's
+// state warps stage the Gb history after the drain, from Sb hi in TMEM, so it
+// overlaps W instead of delaying the drain.
 template <int RULE>
-constexpr int kDeWarps1 = RULE == 2 ? 8 : 4;
+constexpr int kDeWarps1 = 8;
 
 struct Bars1 {
   uint64_t ld_full[kStages1], ld_empty[kStages1];
@@ -417,10 +417,12 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                        logf(fmaxf(__ldg(al + lane + 32), kGateFloor));
       const float a = expf(warp_sum(la));
       if constexpr (kDeWarps1<RULE> == 8) {
-        // dE^T = D (w = 1; lanes = value row c, this warp's 32 token columns) ->
-        // packed bf16 hi / lo pairs into TMEM, the A operand of C -= dE^T k
+        // dE^T = D diag(w) (delta: w = beta; adam: w = 1; lanes = value row c, this
+        // warp's 32 token columns) -> packed bf16 hi / lo pairs into TMEM, the A
+        // operand of C -= dE^T k
         if (!wait_use_w(&bars->de_full, i, status, ab)) break;
         tc_fence_after();
+        const float* ws = gate_beta + (i % kStages1) * 64 + half * 32;
         float x0[16], x1[16];
         tmem_ld16(tmem + lb + T1_E + half * 32, x0);
         tmem_ld16(tmem + lb + T1_E + half * 32 + 16, x1);
@@ -428,8 +430,10 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         uint32_t hh[16], ll[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
-          const float e0 = t < 8 ? x0[2 * t] : x1[2 * t - 16];
-          const float e1 = t < 8 ? x0[2 * t + 1] : x1[2 * t - 15];
+          const float y0 = t < 8 ? x0[2 * t] : x1[2 * t - 16];
+          const float y1 = t < 8 ? x0[2 * t + 1] : x1[2 * t - 15];
+          const float e0 = RULE == 0 ? y0 * ws[2 * t] : y0;
+          const float e1 = RULE == 0 ? y1 * ws[2 * t + 1] : y1;
           hh[t] = pack_bf16(e0, e1);
           ll[t] = pack_bf16(e0 - bf16_lo(hh[t]), e1 - bf16_hi(hh[t]));
         }
@@ -439,6 +443,34 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tc_fence_before();
         mbar_arrive_warp(&bars->de_smem);
         mbar_arrive_warp(&bars->ld_empty[i % kStages1]);   // done with this stage
+      }
+      if constexpr (RULE == 0) {
+        // history for bw2: Gb_j = Sb_{j+1} hi, packed in TMEM since the previous
+        // step, through a staging tile and one TMA store (row N-1 is zero)
+        if (i >= 1) {
+          float f0[16], f1[16];
+          tmem_ld16(tmem + lb + T1_SH + half * 32, f0);
+          tmem_ld16(tmem + lb + T1_SH + half * 32 + 16, f1);
+          tmem_ld_wait();
+          if (threadIdx.x == 0) bulk_wait_read0();
+          named_sync(2, 256);
+          uint8_t* panel = sm + B1_SS + half * P128;
+#pragma unroll
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const float* f = q4 < 4 ? f0 + 4 * q4 : f1 + 4 * (q4 - 4);
+            *reinterpret_cast<uint4*>(panel + sw128_chunk(c, q4)) =
+                make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                           __float_as_uint(f[3]));
+          }
+          fence_async_smem();
+          named_sync(2, 256);
+          if (threadIdx.x == 0) {
+            const int srow = (bh * N + j) * kD;
+            tma_store_2d(&tm_sb, 0, srow, sm + B1_SS);
+            tma_store_2d(&tm_sb, 64, srow, sm + B1_SS + P128);
+            bulk_commit();
+          }
+        }
       }
       if (!wait_use_w(&bars->c_full[0], i, status, ab)) break;
       tc_fence_after();
@@ -465,15 +497,13 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       } else {
       // Sb_j as packed bf16 hi / lo pairs into TMEM (A operand of the next
       // chain product)
-      uint32_t ph[32];
 #pragma unroll
       for (int b = 0; b < 2; ++b) {
         uint32_t pl[16], hh[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
           const float x0 = sb[b * 32 + 2 * t], x1 = sb[b * 32 + 2 * t + 1];
-          ph[b * 16 + t] = pack_bf16(x0, x1);
-          hh[t] = ph[b * 16 + t];
+          hh[t] = pack_bf16(x0, x1);
           pl[t] = pack_bf16(x0 - bf16_lo(hh[t]), x1 - bf16_hi(hh[t]));
         }
         tmem_st16(tmem + lb + T1_SH + half * 32 + b * 16, hh);
@@ -482,25 +512,6 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive_warp(&bars->s_full);
-      // history for bw2: Sb_j hi (= Sb_{(j-1)+1}) through a staging tile and
-      // one TMA store
-      if (j >= 1) {
-        if (threadIdx.x == 0) bulk_wait_read0();
-        named_sync(2, 256);
-        uint8_t* panel = sm + B1_SS + half * P128;
-#pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4)
-          *reinterpret_cast<uint4*>(panel + sw128_chunk(c, q4)) =
-              make_uint4(ph[4 * q4], ph[4 * q4 + 1], ph[4 * q4 + 2], ph[4 * q4 + 3]);
-        fence_async_smem();
-        named_sync(2, 256);
-        if (threadIdx.x == 0) {
-          const int srow = (bh * N + j - 1) * kD;
-          tma_store_2d(&tm_sb, 0, srow, sm + B1_SS);
-          tma_store_2d(&tm_sb, 64, srow, sm + B1_SS + P128);
-          bulk_commit();
-        }
-      }
       }
     }
     // shared memory must outlive the reads of the bulk stores; grid completion
