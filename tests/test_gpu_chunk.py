@@ -142,6 +142,23 @@ def test_config1_full_size_slices(rule, ns):
         compare(pkg, inp, rule, ns, 64, pkg.GMDN_PREC_FAST, torch.bfloat16, TOL_BF16, sl=sl)
 
 
+@pytest.mark.parametrize("B,H,T,rule,ns", [
+    (1, 1, 64, 0, 3), (1, 1, 64, 1, 5), (1, 1, 64, 2, 3),   # one chunk-tile (N = 1)
+    (1, 1, 128, 1, 5),                                       # two tiles
+    (1, 1, 149 * 64, 0, 3),                                  # 149 tiles: one CTA walks two
+    (1, 3, 99 * 64, 2, 3),                                   # 297 tiles: one CTA walks three
+])
+def test_tile_scheduling_edges(B, H, T, rule, ns):
+    """Tile counts around the persistent token-gradient kernel's grid (one CTA
+    per SM, 148 on B200): fewer tiles than CTAs, and CTAs walking one, two or
+    three tiles, which exercises the q/k load-ahead buffers, the S_j / Gb_j
+    tile swap, the per-parity TMEM release and the deferred gate gradients of
+    the last tile."""
+    pkg = load_pkg()
+    inp = pkg.workloads.mixer_inputs(B, H, T, 128, rule=rule, seed=60 + rule)
+    compare(pkg, inp, rule, ns, 64, pkg.GMDN_PREC_FAST, torch.bfloat16, TOL_BF16)
+
+
 def test_precisions_agree_closely():
     pkg = load_pkg()
     inp = pkg.workloads.mixer_inputs(2, 2, 256, 128, rule=0, seed=77)
