@@ -79,9 +79,9 @@ constexpr uint32_t B1_K = 49152;      // k: 3 stages
 constexpr uint32_t B1_G = 98304;      // dO: 3 stages
 constexpr uint32_t B1_AS = 147456;    // A' (bf16), 1 panel x 64 rows
 constexpr uint32_t B1_SS = 155648;    // Gb hi staging for the TMA store, 2 panels x 128 rows
-constexpr uint32_t B1_GATE = 188416;  // beta: 3 stages x 64 floats
-constexpr uint32_t B1_RED = 189184;   // adam: per-warp partial chunk-scalar cotangents [8][4]
-constexpr uint32_t B1_BAR = 189312;
+constexpr uint32_t B1_GATE = 188416;  // beta, alpha, mu, nu: 3 stages x 64 floats each
+constexpr uint32_t B1_RED = 191488;   // adam: per-warp partial chunk-scalar cotangents [8][4]
+constexpr uint32_t B1_BAR = 191616;
 constexpr uint32_t B1_SMEM = B1_BAR + 256 + 1024;
 
 // TMEM: chain accumulator C, dE^T hi / lo (packed bf16 pairs, the A operand of
@@ -118,7 +118,10 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
   Bars1* bars = reinterpret_cast<Bars1*>(sm + B1_BAR);
-  float* gate_beta = reinterpret_cast<float*>(sm + B1_GATE);
+  float* gate_beta = reinterpret_cast<float*>(sm + B1_GATE);   // [3][64] by ring stage
+  float* gate_alpha = gate_beta + 3 * 64;
+  float* gate_mu = gate_beta + 6 * 64;   // adam
+  float* gate_nu = gate_beta + 9 * 64;   // adam
   volatile int* ab = &bars->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.x;
@@ -172,7 +175,7 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         const int j = N - 1 - i, s = i % kStages1;
         const int row = static_cast<int>(tok0) + j * kC;
         if (!wait_free(&bars->ld_empty[s], i / kStages1, status, ab)) return false;
-        mbar_expect_tx(&bars->ld_full[s], 6 * 8192 + 256);
+        mbar_expect_tx(&bars->ld_full[s], 6 * 8192 + 512 + (RULE == 2 ? 512 : 0));
         tma_load_2d(sm + B1_Q + s * 16384, &tm_q, 0, row, &bars->ld_full[s]);
         tma_load_2d(sm + B1_Q + s * 16384 + P64, &tm_q, 64, row, &bars->ld_full[s]);
         tma_load_2d(sm + B1_K + s * 16384, &tm_k, 0, row, &bars->ld_full[s]);
@@ -180,6 +183,11 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tma_load_2d(sm + B1_G + s * 16384, &tm_g, 0, row, &bars->ld_full[s]);
         tma_load_2d(sm + B1_G + s * 16384 + P64, &tm_g, 64, row, &bars->ld_full[s]);
         bulk_load(gate_beta + s * 64, args.beta + tok0 + j * kC, 256, &bars->ld_full[s]);
+        bulk_load(gate_alpha + s * 64, args.alpha + tok0 + j * kC, 256, &bars->ld_full[s]);
+        if (RULE == 2) {
+          bulk_load(gate_mu + s * 64, args.mu + tok0 + j * kC, 256, &bars->ld_full[s]);
+          bulk_load(gate_nu + s * 64, args.nu + tok0 + j * kC, 256, &bars->ld_full[s]);
+        }
         issued = i + 1;
         return true;
       };
@@ -305,16 +313,20 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     // Adam: Gb_jm, Mb, Vb and the chunk-scalar cotangents of chunk jm from
     // sb = Sb_{jm+1}; Gb_jm hi / lo go to TMEM for the next chain product and
     // Gb_jm hi to the history.  Works in 8-column groups to stay in registers.
+    // (chunk jm = N - 1 - (i + 1) is step i + 1's: its gates are in that step's
+    // ring stage, which these warps release only after step i + 1's dE drain)
     auto adam_pass = [&](int jm) -> bool {
       const size_t mm = static_cast<size_t>(bh) * N + jm;
-      const float* be = args.beta + tok0 + jm * kC;
-      const float* mu = args.mu + tok0 + jm * kC;
-      const float* nu = args.nu + tok0 + jm * kC;
-      const float b = warp_sum(__ldg(be + lane) + __ldg(be + lane + 32)) * (1.f / kC);
-      const float mc = expf(warp_sum(logf(fmaxf(__ldg(mu + lane), kGateFloor)) +
-                                     logf(fmaxf(__ldg(mu + lane + 32), kGateFloor))));
-      const float nc = expf(warp_sum(logf(fmaxf(__ldg(nu + lane), kGateFloor)) +
-                                     logf(fmaxf(__ldg(nu + lane + 32), kGateFloor))));
+      const int in = N - 1 - jm;
+      if (!wait_use_w(&bars->ld_full[in % kStages1], in / kStages1, status, ab)) return false;
+      const float* be = gate_beta + (in % kStages1) * 64;
+      const float* mu = gate_mu + (in % kStages1) * 64;
+      const float* nu = gate_nu + (in % kStages1) * 64;
+      const float b = warp_sum(be[lane] + be[lane + 32]) * (1.f / kC);
+      const float mc = expf(warp_sum(logf(fmaxf(mu[lane], kGateFloor)) +
+                                     logf(fmaxf(mu[lane + 32], kGateFloor))));
+      const float nc = expf(warp_sum(logf(fmaxf(nu[lane], kGateFloor)) +
+                                     logf(fmaxf(nu[lane + 32], kGateFloor))));
       const bool have_bar = jm + 2 < N;   // Mb, Vb of chunk jm + 1 exist (else zero)
       const uint4* srow = reinterpret_cast<const uint4*>(args.S_hist + (mm * kD + c) * kD + half * 64);
       float pda = 0.f, pdb = 0.f, pdm = 0.f, pdn = 0.f;
@@ -412,10 +424,12 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     };
     for (int i = 0; i < N; ++i) {
       const int j = N - 1 - i;
-      const float* al = args.alpha + tok0 + j * kC;
-      const float la = logf(fmaxf(__ldg(al + lane), kGateFloor)) +
-                       logf(fmaxf(__ldg(al + lane + 32), kGateFloor));
-      const float a = expf(warp_sum(la));
+      // chunk scalar a_j from the gates the TMA brought into this step's stage (a
+      // global load here stalled the dE drain behind it)
+      if (!wait_use_w(&bars->ld_full[i % kStages1], i / kStages1, status, ab)) break;
+      const float* ga = gate_alpha + (i % kStages1) * 64;
+      const float a = expf(warp_sum(logf(fmaxf(ga[lane], kGateFloor)) +
+                                    logf(fmaxf(ga[lane + 32], kGateFloor))));
       if constexpr (kDeWarps1<RULE> == 8) {
         // dE^T = D diag(w) (delta: w = beta; adam: w = 1; lanes = value row c, this
         // warp's 32 token columns) -> packed bf16 hi / lo pairs into TMEM, the A

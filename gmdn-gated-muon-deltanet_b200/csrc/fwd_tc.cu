@@ -66,8 +66,8 @@ constexpr uint32_t OFF_EL = 139264;       // E_j^T lo
 constexpr uint32_t OFF_I = 155648;        // 64 x 64 identity
 constexpr uint32_t OFF_OS = 163840;       // o_j staging for the TMA store, 2 panels x 64 rows
 constexpr uint32_t OFF_SS = 180224;       // S_{j+1} hi staging for the TMA store, 2 panels x 128 rows
-constexpr uint32_t OFF_GATE = 212992;     // beta: 2 stages x 64 floats
-constexpr uint32_t OFF_BAR = 213504;      // mbarriers and flags
+constexpr uint32_t OFF_GATE = 212992;     // beta, alpha, mu, nu: 2 stages x 64 floats each
+constexpr uint32_t OFF_BAR = 215040;      // mbarriers and flags
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
 
 constexpr uint32_t P64 = 8192;    // panel stride of a 64-row tile
@@ -112,7 +112,10 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
   Bars* bars = reinterpret_cast<Bars*>(sm + OFF_BAR);
-  float* gate_beta = reinterpret_cast<float*>(sm + OFF_GATE);
+  float* gate_beta = reinterpret_cast<float*>(sm + OFF_GATE);   // [2][64]
+  float* gate_alpha = gate_beta + 128;                           // [2][64]
+  float* gate_mu = gate_beta + 256;                              // adam: [2][64]
+  float* gate_nu = gate_beta + 384;                              // adam: [2][64]
   volatile int* ab = &bars->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.x;
@@ -122,7 +125,9 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bars->ld_full[s], 1);
-      mbar_init(&bars->ld_empty[s], 1 + kEWarps<RULE>);   // MMA commit, the E-draining warps
+      // MMA commit, the E-draining warps (adam: and the state warps, which read
+      // the stage's gates for their chunk scalars)
+      mbar_init(&bars->ld_empty[s], 1 + kEWarps<RULE> + (RULE == 2 ? 8 : 0));
     }
     mbar_init(&bars->p_full, 1);
     mbar_init(&bars->as_full, 4);
@@ -156,7 +161,7 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         const int s = j & 1;
         const int row = static_cast<int>(tok0) + j * kC;
         if (!wait_free(&bars->ld_empty[s], j >> 1, status, ab)) break;
-        mbar_expect_tx(&bars->ld_full[s], 6 * 8192 + 256);
+        mbar_expect_tx(&bars->ld_full[s], 6 * 8192 + 512 + (RULE == 2 ? 512 : 0));
         tma_load_2d(sm + OFF_Q + s * 16384, &tm_q, 0, row, &bars->ld_full[s]);
         tma_load_2d(sm + OFF_Q + s * 16384 + P64, &tm_q, 64, row, &bars->ld_full[s]);
         tma_load_2d(sm + OFF_K + s * 16384, &tm_k, 0, row, &bars->ld_full[s]);
@@ -164,6 +169,11 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         tma_load_2d(sm + OFF_V + s * 16384, &tm_v, 0, row, &bars->ld_full[s]);
         tma_load_2d(sm + OFF_V + s * 16384 + P64, &tm_v, 64, row, &bars->ld_full[s]);
         bulk_load(gate_beta + s * 64, args.beta + tok0 + j * kC, 256, &bars->ld_full[s]);
+        bulk_load(gate_alpha + s * 64, args.alpha + tok0 + j * kC, 256, &bars->ld_full[s]);
+        if (RULE == 2) {
+          bulk_load(gate_mu + s * 64, args.mu + tok0 + j * kC, 256, &bars->ld_full[s]);
+          bulk_load(gate_nu + s * 64, args.nu + tok0 + j * kC, 256, &bars->ld_full[s]);
+        }
         issued = j + 1;
       }
       // Never leave with copies in flight (matters only after an abort).
@@ -199,8 +209,9 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + TM_E, desc_mnmajor(v_s, P64, k), desc_kmajor(id_s, P64, k), ID_EV, k > 0);
       };
-      // Issue order per chunk keeps the one-thread issue queue short after G(j),
-      // which the state update waits for: P(j+1) goes in while E(j) is drained.
+      // Issue order per chunk: E(j); o1(j) (runs while E(j) is drained); G(j) as
+      // soon as the drain ends; then o2(j), -v^T I and P of the next chunk, which
+      // run while the state is updated.
       bool ok = N > 0 && issue_P(0);
       if (ok) issue_E1(0);
       for (int j = 0; ok && j < N; ++j) {
@@ -221,9 +232,6 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16_ts(tmem + TM_O, tmem + TM_SH + k * 8, desc_kmajor(q_s, P64, k), ID_ES, k > 0);
-        // P(j+1), once A(j) has read P(j)
-        if (!wait_use(&bars->as_full, j, status, ab)) break;
-        if (j + 1 < N && !issue_P(j + 1)) break;
         // G(j) = (w E)^T_hi k + (w E)^T_lo k   (A from TMEM)
         if (!wait_use(&bars->e_smem, j, status, ab)) break;
         tc_fence_after();
@@ -234,13 +242,19 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int k = 0; k < 4; ++k)
           mma_bf16_ts(tmem + TM_G, tmem + TM_WEL + k * 8, desc_mnmajor(k_s, P64, k), ID_G, 1);
         mma_commit(&bars->g_full);
-        // o2(j): o^T += (w E)^T_hi A'^T
+        // o2(j): o^T += (w E)^T_hi A'^T, once A'(j) is built
+        if (!wait_use(&bars->as_full, j, status, ab)) break;
+        tc_fence_after();
         #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16_ts(tmem + TM_O, tmem + TM_WEH + k * 8, desc_kmajor(as_s, P64, k), ID_O2, 1);
         mma_commit(&bars->o_full);
         mma_commit(&bars->ld_empty[j & 1]);
         if (j + 1 < N) issue_E1(j + 1);   // E(j) has been drained (e_smem)
+        // P(j+1) last: A'(j) has read P(j) (as_full), and an issue blocks this
+        // thread while the pipe is busy, so between o1 and G it kept the thread
+        // from seeing the end of the E drain (~1,000 cycles per chunk)
+        if (j + 1 < N && !issue_P(j + 1)) break;
       }
       // every MMA issued so far has completed before TMEM is released
       mma_commit(&bars->final_mma);
@@ -274,10 +288,12 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     tc_fence_before();
     mbar_arrive_warp(&bars->s_full);
     for (int j = 0; j < N; ++j) {
-      const float* al = args.alpha + tok0 + j * kC;
-      const float la = logf(fmaxf(__ldg(al + lane), kGateFloor)) +
-                       logf(fmaxf(__ldg(al + lane + 32), kGateFloor));
-      const float a = expf(warp_sum(la));
+      // chunk scalars from the gates the TMA brought into this chunk's stage (a
+      // global load here stalled the E drain behind it)
+      if (!wait_use_w(&bars->ld_full[j & 1], j >> 1, status, ab)) break;
+      const float* ga = gate_alpha + (j & 1) * 64;
+      const float a = expf(warp_sum(logf(fmaxf(ga[lane], kGateFloor)) +
+                                    logf(fmaxf(ga[lane + 32], kGateFloor))));
       if constexpr (kEWarps<RULE> == 8) {
         // -E^T (lanes = value row c, this warp's 32 token columns) -> w E^T hi / lo,
         // packed bf16 pairs into TMEM, the A operand of G and o2
@@ -305,14 +321,15 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         mbar_arrive_warp(&bars->ld_empty[j & 1]);   // done with this stage's gates
       }
       if constexpr (RULE == 2) {
-        const float* be = args.beta + tok0 + j * kC;
-        const float* mu = args.mu + tok0 + j * kC;
-        const float* nu = args.nu + tok0 + j * kC;
-        const float b = warp_sum(__ldg(be + lane) + __ldg(be + lane + 32)) * (1.f / kC);
-        const float mc = expf(warp_sum(logf(fmaxf(__ldg(mu + lane), kGateFloor)) +
-                                       logf(fmaxf(__ldg(mu + lane + 32), kGateFloor))));
-        const float nc = expf(warp_sum(logf(fmaxf(__ldg(nu + lane), kGateFloor)) +
-                                       logf(fmaxf(__ldg(nu + lane + 32), kGateFloor))));
+        const float* be = gate_beta + (j & 1) * 64;
+        const float* mu = gate_mu + (j & 1) * 64;
+        const float* nu = gate_nu + (j & 1) * 64;
+        const float b = warp_sum(be[lane] + be[lane + 32]) * (1.f / kC);
+        const float mc = expf(warp_sum(logf(fmaxf(mu[lane], kGateFloor)) +
+                                       logf(fmaxf(mu[lane + 32], kGateFloor))));
+        const float nc = expf(warp_sum(logf(fmaxf(nu[lane], kGateFloor)) +
+                                       logf(fmaxf(nu[lane + 32], kGateFloor))));
+        mbar_arrive_warp(&bars->ld_empty[j & 1]);   // done with this stage's gates
         if (!wait_use_w(&bars->g_full, j, status, ab)) break;
         tc_fence_after();
         const size_t mj = static_cast<size_t>(bh) * N + j;
