@@ -39,6 +39,8 @@ lib.gmdn_last_error_string.restype = ctypes.c_char_p
 lib.gmdn_last_error_string.argtypes = []
 lib.gmdn_kernel_launches.restype = ctypes.c_uint64
 lib.gmdn_kernel_launches.argtypes = []
+lib.gmdn_selftest_wait_timeout.restype = _i
+lib.gmdn_selftest_wait_timeout.argtypes = [_p, ctypes.c_uint64, _p]
 lib.gmdn_prof_enable.restype = None
 lib.gmdn_prof_enable.argtypes = [_i]
 lib.gmdn_prof_report.restype = ctypes.c_char_p

@@ -243,6 +243,16 @@ const char* gmdn_last_error_string(void) { return g_last_error.c_str(); }
 
 uint64_t gmdn_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
+int gmdn_selftest_wait_timeout(uint32_t* status, uint64_t limit_ns, void* stream) {
+  g_last_error.clear();
+  if (!status) return fail(GMDN_ERR_INVALID, "null status pointer");
+  const uint64_t lim = limit_ns < 1000000ull ? 1000000ull
+                                             : (limit_ns > 2000000000ull ? 2000000000ull : limit_ns);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GMDN_LAUNCH(gmdn::wait_timeout_selftest(status, lim, st), "wait_timeout_selftest");
+  return GMDN_OK;
+}
+
 void gmdn_prof_enable(int on) { g_prof_on.store(on ? 1 : 0); }
 
 const char* gmdn_prof_report(void) {

@@ -54,6 +54,10 @@ bool chunk_bwd_tc_supported(const ChunkArgs& p);
 cudaError_t chunk_bwd1_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st);
 cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st);
 
+// Failure-detection self-test (selftest.cu): one CTA's bounded wait on an
+// mbarrier nothing arrives on gives up after limit_ns and sets bit 0 of *status.
+cudaError_t wait_timeout_selftest(uint32_t* status, uint64_t limit_ns, cudaStream_t st);
+
 // rows x 128 bf16 row-major matrix as a TMA map with 64 x box_rows boxes and
 // 128-byte swizzle.
 cudaError_t make_tmap_rows128(CUtensorMap* map, const void* base, uint64_t rows,

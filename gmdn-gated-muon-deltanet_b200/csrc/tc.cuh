@@ -111,22 +111,27 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 }
 
 // Wait for the phase with the given parity to complete.  Gives up after
-// kWaitLimitNs, ORs kStatusWaitTimeout into *status and sets *abort (shared)
-// so that the other warps stop too.  Returns false on give-up or if another
-// warp already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
-                                          volatile int* abort_flag) {
+// limit_ns (kWaitLimitNs in the kernels), ORs kStatusWaitTimeout into *status
+// and sets *abort (shared) so that the other warps stop too.  Returns false on
+// give-up or if another warp already aborted.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint32_t* status,
+                                              volatile int* abort_flag, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
     if (*abort_flag) return false;
-    if (global_ns() - t0 > kWaitLimitNs) {
+    if (global_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       atomicOr(status, kStatusWaitTimeout);
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
+                                          volatile int* abort_flag) {
+  return mbar_wait_for(bar, parity, status, abort_flag, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------------------

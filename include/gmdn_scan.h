@@ -182,6 +182,14 @@ size_t gmdn_chunk_workspace_bytes_ex(int B, int H, int T, int dh, int chunk, int
  * failure reporting). */
 int gmdn_chunk_status(const void* workspace, void* stream);
 
+/* Failure-detection self-test (diagnostic; no reference counterpart): launches
+ * one CTA whose bounded mbarrier wait -- the same wait the kernels use -- can
+ * never complete, with a limit of limit_ns (clamped to [1 ms, 2 s]).  The wait
+ * gives up, ORs 1 into the device word *status and the kernel returns; the
+ * context stays usable.  GMDN_OK when the launch succeeded (read *status after
+ * synchronising `stream`). */
+int gmdn_selftest_wait_timeout(uint32_t* status, uint64_t limit_ns, void* stream);
+
 /* Number of kernels this library has enqueued in this process (diagnostic;
  * no reference counterpart). */
 uint64_t gmdn_kernel_launches(void);
