@@ -202,18 +202,22 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         mma_commit(&bars->p_full);
         return true;
       };
-      // -v_j^T I into the E accumulator (it must be free: E(j-1) drained)
-      auto issue_E1 = [&](int j) {
+      // -v_j^T I into the E accumulator (it must be free: E(j-1) drained); v_j
+      // must have landed in its stage
+      auto issue_E1 = [&](int j) -> bool {
+        if (!wait_use(&bars->ld_full[j & 1], j >> 1, status, ab)) return false;
+        tc_fence_after();
         const uint32_t v_s = stage(OFF_V, j);
         #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + TM_E, desc_mnmajor(v_s, P64, k), desc_kmajor(id_s, P64, k), ID_EV, k > 0);
+        return true;
       };
       // Issue order per chunk: E(j); o1(j) (runs while E(j) is drained); G(j) as
       // soon as the drain ends; then o2(j), -v^T I and P of the next chunk, which
       // run while the state is updated.
       bool ok = N > 0 && issue_P(0);
-      if (ok) issue_E1(0);
+      ok = ok && issue_E1(0);
       for (int j = 0; ok && j < N; ++j) {
         const uint32_t q_s = stage(OFF_Q, j), k_s = stage(OFF_K, j);
         // E(j): D = -v^T I + S_hi k^T + S_lo k^T = -E^T
@@ -250,7 +254,7 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           mma_bf16_ts(tmem + TM_O, tmem + TM_WEH + k * 8, desc_kmajor(as_s, P64, k), ID_O2, 1);
         mma_commit(&bars->o_full);
         mma_commit(&bars->ld_empty[j & 1]);
-        if (j + 1 < N) issue_E1(j + 1);   // E(j) has been drained (e_smem)
+        if (j + 1 < N && !issue_E1(j + 1)) break;   // E(j) has been drained (e_smem)
         // P(j+1) last: A'(j) has read P(j) (as_full), and an issue blocks this
         // thread while the pipe is busy, so between o1 and G it kept the thread
         // from seeing the end of the E drain (~1,000 cycles per chunk)

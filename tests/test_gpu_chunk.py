@@ -168,3 +168,24 @@ def test_precisions_agree_closely():
     assert rel(o1, o0) < 2e-2
     for k in g0:
         assert rel(g1[k], g0[k]) < 2e-2, k
+
+
+@pytest.mark.parametrize("rule,ns", [(0, 3), (2, 3), (1, 5)])
+def test_full_size_runs_are_repeatable(rule, ns):
+    """Repeated fwd+bwd at config-1 size must give bitwise-identical o, dq, dk,
+    dv: every product and reduction is in a fixed order, so a difference means
+    a hand-off race (a product issued before its operands landed).  Gate
+    cotangents are summed with float atomics across CTAs and only have to
+    agree closely."""
+    pkg = load_pkg()
+    inp = pkg.workloads.mixer_inputs(8, 16, 4096, 128, rule=rule, seed=3)
+    o0, g0 = run_kernel(pkg, inp, rule, ns, 64, pkg.GMDN_PREC_FAST, torch.bfloat16)
+    for rep in range(5):
+        o, g = run_kernel(pkg, inp, rule, ns, 64, pkg.GMDN_PREC_FAST, torch.bfloat16)
+        assert torch.equal(o, o0), f"run {rep + 1}: o differs"
+        for n in ("dq", "dk", "dv"):
+            assert torch.equal(g[n], g0[n]), f"run {rep + 1}: {n} differs"
+        for n in ("dalpha", "dbeta", "dmu", "dnu"):
+            if n in g0:
+                scale = g0[n].abs().max().item() + 1e-30
+                assert (g[n] - g0[n]).abs().max().item() <= 1e-5 * scale, f"run {rep + 1}: {n}"
