@@ -246,6 +246,9 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int k = 0; k < 4; ++k)
           mma_bf16_ts(tmem + TM_G, tmem + TM_WEL + k * 8, desc_mnmajor(k_s, P64, k), ID_G, 1);
         mma_commit(&bars->g_full);
+        // G(j) is the stage's last reader (o2 reads A' and TMEM only): release it
+        // now, so the load of chunk j+2 starts an o2 earlier
+        mma_commit(&bars->ld_empty[j & 1]);
         // o2(j): o^T += (w E)^T_hi A'^T, once A'(j) is built
         if (!wait_use(&bars->as_full, j, status, ab)) break;
         tc_fence_after();
@@ -253,7 +256,6 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         for (int k = 0; k < 4; ++k)
           mma_bf16_ts(tmem + TM_O, tmem + TM_WEH + k * 8, desc_kmajor(as_s, P64, k), ID_O2, 1);
         mma_commit(&bars->o_full);
-        mma_commit(&bars->ld_empty[j & 1]);
         if (j + 1 < N && !issue_E1(j + 1)) break;   // E(j) has been drained (e_smem)
         // P(j+1) last: A'(j) has read P(j) (as_full), and an issue blocks this
         // thread while the pipe is busy, so between o1 and G it kept the thread
