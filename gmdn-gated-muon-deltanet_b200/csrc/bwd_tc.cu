@@ -622,12 +622,12 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 // ===========================================================================
 //
 // Warps 0-7 drain accumulators (warp w reads TMEM subpartition w % 4; warps
-// w and w + 4 split the columns), warp 8 issues the TMA loads and the MMAs.
+// w and w + 4 split the columns), warp 8 issues the MMAs, warp 9 the TMA loads.
 // Accumulators: E^T (M=128) feeds dA and dWk through MN-major descriptors;
 // the outputs dq, dk, dv and the small C x C products are M=64 (row-major),
 // paired two per TMEM column range (lanes 0-15 / 16-31).
 
-constexpr int kThreads2 = 288;
+constexpr int kThreads2 = 320;
 constexpr uint32_t B2_Q = 0, B2_K = 16384, B2_V = 32768, B2_G = 49152;
 constexpr uint32_t B2_ST0 = 65536;    // S_j and Gb_j, 2 panels x 128 rows each, in
 constexpr uint32_t B2_ST1 = 98304;    // these two tiles with roles swapped every tile
@@ -650,7 +650,7 @@ constexpr uint32_t T2_X0 = 0, T2_XE = 64, T2_X2 = 128, T2_D0 = 256;
 
 struct Bars2 {
   uint64_t ld_a, ld_b[2], ld_sb, ph1a, ph1, ep1, wk_full, da_done, ph2, de_ready, ep2, s_free, ph3,
-      x2_free, d_free[2], k_free, lo_full, tail_done;
+      x2_free, d_free[2], k_free, lo_full, tail_done, final_mma;
   uint32_t tmem_base;
   int abort_flag;
   float da[2];                 // by local tile parity: a tile's gate gradients are
@@ -734,6 +734,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     mbar_init(&bars->d_free[1], 8);
     mbar_init(&bars->lo_full, 1);
     mbar_init(&bars->tail_done, 1);
+    mbar_init(&bars->final_mma, 1);
     bars->abort_flag = 0;
     bars->da[0] = bars->da[1] = 0.f;
     fence_mbar_init();
@@ -749,8 +750,11 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == 8) {
-    // ------------------------------------------------------------ loads and MMAs (one thread)
+  if (warp == 9) {
+    // ------------------------------------------------------------ TMA loads (one thread)
+    // Each input group of the next tile is issued as soon as the current tile
+    // releases the tiles it goes into, off the MMA thread (a copy issue blocks
+    // its thread for a while, and on the MMA thread that delayed the chain).
     if (lane == 0) {
       // group a: v, dO, S_j and the gates (into tiles the previous tile's phase 2
       // has done with)
@@ -798,19 +802,6 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tma_load_2d(sm + B2_DE, &tm_sbl, 0, srow, &bars->lo_full);
         tma_load_2d(sm + B2_RED, &tm_sbl, 64, srow, &bars->lo_full);
       };
-      const uint32_t v_s = smem_u32(sm + B2_V), g_s = smem_u32(sm + B2_G);
-      const uint32_t as_s = smem_u32(sm + B2_AS), e_s = smem_u32(sm + B2_E);
-      const uint32_t wk_s = smem_u32(sm + B2_WK), de_s = smem_u32(sm + B2_DE);
-      const uint32_t dp_s = smem_u32(sm + B2_DP), id_s = smem_u32(sm + B2_I);
-      constexpr uint32_t ID_P = idesc_bf16(64, 64, false, false);
-      constexpr uint32_t ID_KM = idesc_bf16(64, 128, false, true);        // A K-major, B MN-major
-      constexpr uint32_t ID_KK = idesc_bf16(64, 128, false, false);       // both K-major
-      constexpr uint32_t ID_KMN = idesc_bf16(64, 128, false, true, true);
-      constexpr uint32_t ID_MM = idesc_bf16(64, 128, true, true);         // both MN-major
-      constexpr uint32_t ID_EV = idesc_bf16(128, 64, true, false);        // E^T: v^T I
-      constexpr uint32_t ID_EK = idesc_bf16(128, 64, false, false, true); // E^T: -S k^T
-      constexpr uint32_t ID_DA = idesc_bf16(64, 64, false, true);         // dO E^T
-      int i = 0;
       // local tile of a load group in flight, not yet waited on
       int pa = -1, ps = -1, pl = -1, pb[2] = {-1, -1};
       if (static_cast<int>(blockIdx.x) < tiles) {
@@ -827,13 +818,67 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           pl = 0;
         }
       }
+      int i = 0;
+      for (int tile = blockIdx.x; tile < tiles; tile += G, ++i) {
+        const int next = tile + G;
+        if (next < tiles) {
+          // v, dO and Gb_j have been read (Gb_j also by da): the next tile's v, dO
+          // and S_j
+          if (!wait_use(&bars->ph2, i, status, ab) || !wait_use(&bars->da_done, i, status, ab)) break;
+          issue_a(i + 1, next);
+          pa = i + 1;
+          // S_j has been read by -dE S: the next tile's Gb_j into its tile
+          if (!wait_use(&bars->s_free, i, status, ab)) break;
+          issue_sb(i + 1, next);
+          ps = i + 1;
+        }
+        // q and k have been read (k also by epilogue 2): the q, k of the tile that
+        // uses this buffer next
+        const int nb = tile + kQK * G;
+        if (nb < tiles) {
+          if (!wait_use(&bars->ph3, i, status, ab) || !wait_use(&bars->k_free, i, status, ab)) break;
+          issue_b(i + kQK, nb);
+          pb[qk_buf(i)] = i + kQK;
+        }
+        if (RULE == 1 && next < tiles) {
+          if (!wait_use(&bars->tail_done, i, status, ab)) break;
+          issue_lo(next);
+          pl = i + 1;
+        }
+      }
+      // no copy of ours may still be in flight when the CTA exits
+      int dummy = 0;
+      if (pa >= 0) mbar_wait(&bars->ld_a, pa & 1, status, &dummy);
+      for (int b = 0; b < 2; ++b)
+        if (pb[b] >= 0) mbar_wait(&bars->ld_b[b], qk_use(pb[b]) & 1, status, &dummy);
+      if (ps >= 0) mbar_wait(&bars->ld_sb, ps & 1, status, &dummy);
+      if (pl >= 0) mbar_wait(&bars->lo_full, pl & 1, status, &dummy);
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ MMAs (one thread)
+    if (lane == 0) {
+      const uint32_t v_s = smem_u32(sm + B2_V), g_s = smem_u32(sm + B2_G);
+      const uint32_t as_s = smem_u32(sm + B2_AS), e_s = smem_u32(sm + B2_E);
+      const uint32_t wk_s = smem_u32(sm + B2_WK), de_s = smem_u32(sm + B2_DE);
+      const uint32_t dp_s = smem_u32(sm + B2_DP), id_s = smem_u32(sm + B2_I);
+      constexpr uint32_t ID_P = idesc_bf16(64, 64, false, false);
+      constexpr uint32_t ID_KM = idesc_bf16(64, 128, false, true);        // A K-major, B MN-major
+      constexpr uint32_t ID_KK = idesc_bf16(64, 128, false, false);       // both K-major
+      constexpr uint32_t ID_KMN = idesc_bf16(64, 128, false, true, true);
+      constexpr uint32_t ID_MM = idesc_bf16(64, 128, true, true);         // both MN-major
+      constexpr uint32_t ID_EV = idesc_bf16(128, 64, true, false);        // E^T: v^T I
+      constexpr uint32_t ID_EK = idesc_bf16(128, 64, false, false, true); // E^T: -S k^T
+      constexpr uint32_t ID_DA = idesc_bf16(64, 64, false, true);         // dO E^T
+      int i = 0;
       for (int tile = blockIdx.x; tile < tiles; tile += G, ++i) {
         const uint32_t q_s = smem_u32(sm + q_off(i)), k_s = smem_u32(sm + k_off(i));
         const uint32_t s_s = smem_u32(sm + s_off(i)), sb_s = smem_u32(sm + sb_off(i));
         if (!wait_use(&bars->ld_a, i, status, ab)) break;
-        pa = -1;
         if (!wait_use(&bars->ld_b[qk_buf(i)], qk_use(i), status, ab)) break;
-        pb[qk_buf(i)] = -1;
+        // P overwrites X0: muon and adam read tile i-1's P and dA there for the
+        // dbeta column sums until epilogue 2 arrives on k_free (delta's dbeta
+        // needs no P)
+        if (RULE != 0 && i >= 1 && !wait_use(&bars->k_free, i - 1, status, ab)) break;
         tc_fence_after();
         // phase 1a (no S_j): P = q k^T; E^T = v^T
         #pragma unroll
@@ -856,7 +901,6 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                    ID_KM, k > 0);
         mma_commit(&bars->ph1);
         if (!wait_use(&bars->ld_sb, i, status, ab)) break;
-        ps = -1;
         // X2 (dE | dWk) is written next: epilogue 3 of tile i-1 has read dWk
         if (i >= 1 && !wait_use(&bars->x2_free, i - 1, status, ab)) break;
         tc_fence_after();
@@ -871,7 +915,6 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         if (RULE == 1 && i >= 1 && !wait_use(&bars->x2_free, i - 1, status, ab)) break;
         if (RULE == 1 && !wait_use(&bars->wk_full, i, status, ab)) break;
         if (RULE == 1 && !wait_use(&bars->lo_full, i, status, ab)) break;
-        if (RULE == 1) pl = -1;
         tc_fence_after();
         // phase 2: dE = A^T dO + wk Gb^T;  dA = dO E^T;  dWk = E Gb
         #pragma unroll
@@ -909,12 +952,6 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                      ID_MM, 1);
         }
         mma_commit(&bars->ph2);
-        const int next = tile + G;
-        if (next < tiles) {   // v, dO and Gb_j have been read (also by da): load the next tile's
-          if (!wait_use(&bars->ph2, i, status, ab) || !wait_use(&bars->da_done, i, status, ab)) break;
-          issue_a(i + 1, next);
-          pa = i + 1;
-        }
         if (!wait_use(&bars->de_ready, i, status, ab)) break;
         tc_fence_after();
         // phase 3: dK = -dE S (S_j's last reader, as soon as dE is in shared memory)
@@ -934,34 +971,11 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           mma_bf16(tmem + HI16 + d_tm(i), desc_kmajor(dp_s, P64, k), desc_mnmajor(k_s, P64, k), ID_KM,
                    1);
         mma_commit(&bars->ph3);
-        if (next < tiles) {   // S_j has been read (da of tile i was taken before phase 2 ended)
-          if (!wait_use(&bars->s_free, i, status, ab)) break;
-          issue_sb(i + 1, next);
-          ps = i + 1;
-        }
-        // q and k have been read (k also by epilogue 2's dw): load the next tile's
-        if (!wait_use(&bars->ph3, i, status, ab)) break;
-        if (!wait_use(&bars->k_free, i, status, ab)) break;
-        const int nb = tile + kQK * G;   // the tile whose q, k go into this tile's buffer
-        if (nb < tiles) {
-          issue_b(i + kQK, nb);
-          pb[qk_buf(i)] = i + kQK;
-        }
-        if (next < tiles) {
-          if (RULE == 1) {
-            if (!wait_use(&bars->tail_done, i, status, ab)) break;
-            issue_lo(next);
-            pl = i + 1;
-          }
-        }
       }
-      // no copy of ours may still be in flight when the CTA exits
+      // every MMA issued has completed before TMEM is released
+      mma_commit(&bars->final_mma);
       int dummy = 0;
-      if (pa >= 0) mbar_wait(&bars->ld_a, pa & 1, status, &dummy);
-      for (int b = 0; b < 2; ++b)
-        if (pb[b] >= 0) mbar_wait(&bars->ld_b[b], qk_use(pb[b]) & 1, status, &dummy);
-      if (ps >= 0) mbar_wait(&bars->ld_sb, ps & 1, status, &dummy);
-      if (pl >= 0) mbar_wait(&bars->lo_full, pl & 1, status, &dummy);
+      mbar_wait(&bars->final_mma, 0, status, &dummy);
     }
   } else {
     // ------------------------------------------------------------ epilogue warps 0-7
@@ -1007,7 +1021,9 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       named_sync(1, 256);
       if (tid < kC) {
         const int s = tid;
-        const float db = gpart[s] + gpart[64 + s] + gpart[128 + s] + gpart[192 + s];
+        // column sums of tril(dA) * P (muon, adam; delta's whole dbeta is in gdw)
+        const float db =
+            RULE == 0 ? 0.f : gpart[s] + gpart[64 + s] + gpart[128 + s] + gpart[192 + s];
         const float al = galpha[s];
         const size_t g = tok + s;
         if constexpr (RULE == 1) {
@@ -1228,7 +1244,29 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       // the 16 rows of a warp are summed by a butterfly over lanes 16-31 that
       // leaves each lane two of the warp's 32 column sums.  X0 stays valid until
       // the next tile's phase 1.
-      {
+      if constexpr (RULE == 0) {
+        // Delta: X2 (lanes 0-15) = A^T dO + k Gb^T before the beta scaling, and
+        // dbeta_s = sum_t tril(dA)[t,s] P[t,s] + k_s . (E Gb)_s = <E_s, X2_s>: both
+        // pieces regroup into that row product (E^T from shared memory).  X2 is
+        // intact until epilogue 3 releases it.
+        float dbp = 0.f;
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c0 = half * 64 + cc * 16;
+          float x[16];
+          tmem_ld16(tmem + lb + T2_X2 + c0, x);
+          tmem_ld_wait();
+          if (!hi) {
+#pragma unroll
+            for (int y = 0; y < 16; ++y) {
+              const float e = __bfloat162float(
+                  *reinterpret_cast<const __nv_bfloat16*>(sm + B2_E + sw128_elem(c0 + y, r16)));
+              dbp = fmaf(e, x[y], dbp);
+            }
+          }
+        }
+        if (!hi) gdw[half * 64 + r16] = dbp;
+      } else {
         float v[32];
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
@@ -1260,7 +1298,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           gpart[sp * 64 + col + 1] = v[1];
         }
       }
-      if constexpr (RULE != 2) {
+      if constexpr (RULE == 1) {
         // dw_s = k_s . dWk_s (lanes 16-31 of X2, row s = r16), read before k is reloaded
         float dw = 0.f;
 #pragma unroll
