@@ -21,7 +21,9 @@ synthetic tensors with the distributions the baseline names (no dataset).
 
 Multi-GPU (torchrun, one process per GPU): every rank runs its own config-1
 batch (weak scaling, no data-path collective); the timing barrier and the
-max-over-ranks reduction are the only NCCL traffic.
+max-over-ranks reduction are the only NCCL traffic.  ``--scaling strong``
+instead splits the one global B*H batch into contiguous (b, h) shards, one per
+rank (16 sequences per GPU at N=8), and counts the global B*T tokens per step.
 
 ``--impl reference`` times the reference algorithm on the host cores instead
 (the oracle port; the reference itself is Python and is not present on the
@@ -309,6 +311,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="override B of the workload (small ncu captures)")
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
+                    help="weak: a full batch per rank; strong: the global batch split over ranks")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     if args.batch:
@@ -336,6 +340,13 @@ def main():
     prec = pkg.GMDN_PREC_FAST if args.precision == "fast" else pkg.GMDN_PREC_IEEE
 
     B, H, T, dh, C, rule, ns = (cfg[k] for k in ("B", "H", "T", "dh", "chunk", "rule", "ns"))
+    B_global, H_global = B, H
+    job_cfg = dict(cfg)   # the workload as named (the CPU sample scales against it)
+    if args.scaling == "strong":
+        # this rank's contiguous share of the global (b, h) sequences, as one batch
+        start, end = pkg.sharding.shard_bh(B * H, rank, world)
+        B, H = 1, end - start
+        cfg["B"], cfg["H"] = B, H
     host = pkg.workloads.mixer_inputs(B, H, T, dh, rule, C, seed=rank)
     dev = host.to(device, torch.bfloat16)
     leaves = [dev.q, dev.k, dev.v, dev.alpha, dev.beta, dev.mu] + ([dev.nu] if rule == 2 else [])
@@ -377,7 +388,7 @@ def main():
     elapsed = ev0.elapsed_time(ev1)  # ms
     barrier()
     elapsed = pkg.sharding.max_over_ranks(elapsed, device)
-    tokens_per_step = B * T * world
+    tokens_per_step = B_global * T * (world if args.scaling == "weak" else 1)
     value = tokens_per_step * args.steps / (elapsed / 1e3)
 
     # ---- end to end through the public API from pinned host memory ----
@@ -491,19 +502,23 @@ def main():
     clock_info = clocks.summary()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(pkg, cfg)
+        cpu = cpu_baseline(pkg, job_cfg)
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3),
-            "ms_per_step": elapsed / args.steps, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": elapsed / args.steps, "higher_is_better": True,
+            "scaling": args.scaling,
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": args.config, "model": "mixer core fwd+bwd",
-                       "global_batch": B * world, "seq_len": T, "heads": H, "head_dim": dh,
+                       "global_batch": B_global * (world if args.scaling == "weak" else 1),
+                       "seq_len": T, "heads": H_global, "head_dim": dh,
                        "chunk": C, "rule": RULE_NAMES[rule], "ns": ns,
-                       "precision": args.precision, "parallelism": f"dp{world} (B*H shards)",
-                       "l2": "inputs larger than L2 (q,k,v,dO bf16 = 537 MB per rank)"},
+                       "precision": args.precision,
+                       "parallelism": f"dp{world} (B*H shards, {B * H} sequences per rank)",
+                       "l2": f"inputs larger than L2 (q,k,v,dO bf16 = "
+                             f"{4 * B * H * T * dh * 2 / 1e6:.0f} MB per rank)"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": launches, "clocks": clock_info,
             "kernel_times": kernel_times,

@@ -649,7 +649,7 @@ constexpr uint32_t B2_SMEM = B2_BAR + 256 + 1024;
 constexpr uint32_t T2_X0 = 0, T2_XE = 64, T2_X2 = 128, T2_D0 = 256;
 
 struct Bars2 {
-  uint64_t ld_a, ld_b[2], ld_sb, ph1a, ph1, ep1, wk_full, da_done, ph2, de_ready, ep2, s_free, ph3,
+  uint64_t ld_a, ld_v, ld_b[2], ld_sb, ph1a, ph1, ep1, wk_full, da_done, ph2, de_ready, ep2, s_free, ph3,
       x2_free, d_free[2], k_free, lo_full, tail_done, final_mma;
   uint32_t tmem_base;
   int abort_flag;
@@ -715,6 +715,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 
   if (threadIdx.x == 0) {
     mbar_init(&bars->ld_a, 1);
+    mbar_init(&bars->ld_v, 1);
     mbar_init(&bars->ld_b[0], 1);
     mbar_init(&bars->ld_b[1], 1);
     mbar_init(&bars->ld_sb, 1);
@@ -756,16 +757,19 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     // releases the tiles it goes into, off the MMA thread (a copy issue blocks
     // its thread for a while, and on the MMA thread that delayed the chain).
     if (lane == 0) {
-      // group a: v, dO, S_j and the gates (into tiles the previous tile's phase 2
-      // has done with)
+      // group a: dO, S_j and the gates (into tiles the previous tile's phase 2
+      // has done with); muon also v (its v tile holds E^T lo until phase 2)
       auto issue_a = [&](int i, int tile) {
         const int bh = tile / N, j = tile % N;
         const int tok = bh * args.T + j * kC;
         const int srow = (bh * N + j) * kD;
         float* gt = gates(i);
-        mbar_expect_tx(&bars->ld_a, 4 * 8192 + 2 * 16384 + 512 + (RULE == 1 ? 256 : 0));
-        tma_load_2d(sm + B2_V, &tm_v, 0, tok, &bars->ld_a);
-        tma_load_2d(sm + B2_V + P64, &tm_v, 64, tok, &bars->ld_a);
+        mbar_expect_tx(&bars->ld_a, (RULE == 1 ? 4 : 2) * 8192 + 2 * 16384 + 512 +
+                                        (RULE == 1 ? 256 : 0));
+        if (RULE == 1) {
+          tma_load_2d(sm + B2_V, &tm_v, 0, tok, &bars->ld_a);
+          tma_load_2d(sm + B2_V + P64, &tm_v, 64, tok, &bars->ld_a);
+        }
         tma_load_2d(sm + B2_G, &tm_g, 0, tok, &bars->ld_a);
         tma_load_2d(sm + B2_G + P64, &tm_g, 64, tok, &bars->ld_a);
         tma_load_2d(sm + s_off(i), &tm_s, 0, srow, &bars->ld_a);
@@ -773,6 +777,14 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         bulk_load(gt, args.beta + tok, 256, &bars->ld_a);
         bulk_load(gt + 64, args.alpha + tok, 256, &bars->ld_a);
         if (RULE == 1) bulk_load(gt + 128, args.mu + tok, 256, &bars->ld_a);
+      };
+      // delta, adam: v alone, as soon as the previous tile's phase 1a has read it
+      auto issue_v = [&](int tile) {
+        const int bh = tile / N, j = tile % N;
+        const int tok = bh * args.T + j * kC;
+        mbar_expect_tx(&bars->ld_v, 2 * 8192);
+        tma_load_2d(sm + B2_V, &tm_v, 0, tok, &bars->ld_v);
+        tma_load_2d(sm + B2_V + P64, &tm_v, 64, tok, &bars->ld_v);
       };
       // group sb: Gb_j (into the tile the previous tile's -dE S has done with;
       // first read by k Gb^T after phase 1)
@@ -803,8 +815,12 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tma_load_2d(sm + B2_RED, &tm_sbl, 64, srow, &bars->lo_full);
       };
       // local tile of a load group in flight, not yet waited on
-      int pa = -1, ps = -1, pl = -1, pb[2] = {-1, -1};
+      int pa = -1, ps = -1, pl = -1, pv = -1, pb[2] = {-1, -1};
       if (static_cast<int>(blockIdx.x) < tiles) {
+        if (RULE != 1) {
+          issue_v(blockIdx.x);
+          pv = 0;
+        }
         issue_a(0, blockIdx.x);
         issue_b(0, blockIdx.x);
         issue_sb(0, blockIdx.x);
@@ -821,9 +837,13 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       int i = 0;
       for (int tile = blockIdx.x; tile < tiles; tile += G, ++i) {
         const int next = tile + G;
+        if (RULE != 1 && next < tiles) {   // phase 1a has read v: the next tile's
+          if (!wait_use(&bars->ph1a, i, status, ab)) break;
+          issue_v(next);
+          pv = i + 1;
+        }
         if (next < tiles) {
-          // v, dO and Gb_j have been read (Gb_j also by da): the next tile's v, dO
-          // and S_j
+          // dO and Gb_j have been read (Gb_j also by da): the next tile's dO and S_j
           if (!wait_use(&bars->ph2, i, status, ab) || !wait_use(&bars->da_done, i, status, ab)) break;
           issue_a(i + 1, next);
           pa = i + 1;
@@ -849,6 +869,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       // no copy of ours may still be in flight when the CTA exits
       int dummy = 0;
       if (pa >= 0) mbar_wait(&bars->ld_a, pa & 1, status, &dummy);
+      if (pv >= 0) mbar_wait(&bars->ld_v, pv & 1, status, &dummy);
       for (int b = 0; b < 2; ++b)
         if (pb[b] >= 0) mbar_wait(&bars->ld_b[b], qk_use(pb[b]) & 1, status, &dummy);
       if (ps >= 0) mbar_wait(&bars->ld_sb, ps & 1, status, &dummy);
@@ -873,7 +894,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       for (int tile = blockIdx.x; tile < tiles; tile += G, ++i) {
         const uint32_t q_s = smem_u32(sm + q_off(i)), k_s = smem_u32(sm + k_off(i));
         const uint32_t s_s = smem_u32(sm + s_off(i)), sb_s = smem_u32(sm + sb_off(i));
-        if (!wait_use(&bars->ld_a, i, status, ab)) break;
+        if (RULE == 1 && !wait_use(&bars->ld_a, i, status, ab)) break;
         if (!wait_use(&bars->ld_b[qk_buf(i)], qk_use(i), status, ab)) break;
         // P overwrites X0: muon and adam read tile i-1's P and dA there for the
         // dbeta column sums until epilogue 2 arrives on k_free (delta's dbeta
@@ -884,12 +905,17 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16(tmem + T2_X0, desc_kmajor(q_s, P64, k), desc_kmajor(k_s, P64, k), ID_P, k > 0);
+        if (RULE != 1) {
+          if (!wait_use(&bars->ld_v, i, status, ab)) break;
+          tc_fence_after();
+        }
         #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + T2_XE, desc_mnmajor(v_s, P64, k), desc_kmajor(id_s, P64, k), ID_EV, k > 0);
         mma_commit(&bars->ph1a);
         // phase 1b: E^T -= S k^T; dQ = dO S into D[i & 1] (epilogue 3 of tile i-2 has
         // read it)
+        if (RULE != 1 && !wait_use(&bars->ld_a, i, status, ab)) break;
         if (i >= 2 && !wait_use(&bars->d_free[i & 1], (i >> 1) - 1, status, ab)) break;
         tc_fence_after();
         #pragma unroll
