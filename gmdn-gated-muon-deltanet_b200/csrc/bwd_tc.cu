@@ -1292,6 +1292,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           }
         }
         if (!hi) gdw[half * 64 + r16] = dbp;
+        // epilogue 3 stages dq in the E^T tile: every warp is done reading E^T first
+        named_sync(1, 256);
       } else {
         float v[32];
 #pragma unroll
