@@ -213,9 +213,10 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         return true;
       };
       // Per step i, in the order the inputs are released: P(i+1) once A'(i) has
-      // been built from P(i) and X(i) has left the pipe, the load of step i+3
-      // once step i is done with its stage (W(i), dE drain), Z(i+1) once C(i)
-      // has been drained.
+      // been built from P(i) and X(i) has left the pipe, Z(i+1) once C(i) has
+      // been drained (it runs while Sb is packed), then the load of step i+3
+      // (its stage is free since W(i)).  Issuing the load first held Z(i+1)
+      // back ~1,000 cycles, into the next step's chain products.
       bool ok = true;
       for (int i = 0; ok && i < kStages1 && i < N; ++i) ok = load(i);
       ok = ok && N > 0 && issue_P(0) && issue_Z(0);
@@ -223,8 +224,8 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         if (!wait_use(&bars->as_full, i, status, ab) || !wait_use(&bars->de_full, i, status, ab) ||
             !issue_P(i + 1))
           break;
-        if (i + kStages1 < N && !load(i + kStages1)) break;
         if (!issue_Z(i + 1)) break;
+        if (i + kStages1 < N && !load(i + kStages1)) break;
       }
       // no MMA or copy of this thread may still be in flight when the CTA exits
       mma_commit(&bars->final_tma);
