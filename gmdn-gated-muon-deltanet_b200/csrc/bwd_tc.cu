@@ -534,10 +534,8 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     if (threadIdx.x == 0) bulk_wait_read0();
   } else {
     // ------------------------------------------------------------ chunk-local (warps 8-11)
-    const int tb = threadIdx.x - 256;
     const int sp = warp - 8;
     const uint32_t lb = tmem_lane_base(warp);
-    const int row = sp * 32 + lane;
     const int t16 = sp * 16 + (lane & 15);
     auto build_as = [&](int i) -> bool {
       const float* bs = gate_beta + (i % kStages1) * 64;

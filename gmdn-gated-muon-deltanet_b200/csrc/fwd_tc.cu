@@ -59,15 +59,12 @@ constexpr int kThreadsTc = 448;
 constexpr uint32_t OFF_Q = 0;             // q: 2 stages x 16 KB
 constexpr uint32_t OFF_K = 32768;         // k: 2 stages
 constexpr uint32_t OFF_V = 65536;         // v: 2 stages
-constexpr uint32_t OFF_WK = 98304;        // w * k_j
-constexpr uint32_t OFF_AS = 114688;       // A_j bf16, 1 panel x 64 rows
-constexpr uint32_t OFF_EH = 122880;       // E_j^T hi, 1 panel x 128 rows
-constexpr uint32_t OFF_EL = 139264;       // E_j^T lo
-constexpr uint32_t OFF_I = 155648;        // 64 x 64 identity
-constexpr uint32_t OFF_OS = 163840;       // o_j staging for the TMA store, 2 panels x 64 rows
-constexpr uint32_t OFF_SS = 180224;       // S_{j+1} hi staging for the TMA store, 2 panels x 128 rows
-constexpr uint32_t OFF_GATE = 212992;     // beta, alpha, mu, nu: 2 stages x 64 floats each
-constexpr uint32_t OFF_BAR = 215040;      // mbarriers and flags
+constexpr uint32_t OFF_AS = 98304;        // A_j bf16, 1 panel x 64 rows
+constexpr uint32_t OFF_I = 106496;        // 64 x 64 identity
+constexpr uint32_t OFF_OS = 114688;       // o_j staging for the TMA store, 2 panels x 64 rows
+constexpr uint32_t OFF_SS = 131072;       // S_{j+1} hi staging for the TMA store, 2 panels x 128 rows
+constexpr uint32_t OFF_GATE = 163840;     // beta, alpha, mu, nu: 2 stages x 64 floats each
+constexpr uint32_t OFF_BAR = 165888;      // mbarriers and flags
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
 
 constexpr uint32_t P64 = 8192;    // panel stride of a 64-row tile
