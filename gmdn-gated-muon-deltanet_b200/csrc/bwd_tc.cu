@@ -13,6 +13,7 @@
 //   dq_j     = dO_j S_j + dP_j k_j,            dP = tril(dO E^T) * beta_col
 //   dk_j     = -dE_j S_j + w * (E_j Sb_{j+1}) + dP_j^T q_j
 //   dbeta_s  = sum_t tril(dO E^T)[t][s] P[t][s] + k_s . (E_j Sb_{j+1})_s
+//            = <E_j[s], dE_j[s]> / beta_s         (delta: both terms regroup)
 //   dalpha_s = <Sb_{j+1}, S_j> a_j / alpha_s
 //
 // (identical to the reference's autograd of train_ablation.py:142-187 with
@@ -32,8 +33,8 @@
 //      (hi + lo) operands for Sb and dE; Sb hi/lo live in TMEM as the A
 //      operand of their product, so the recurrence never touches shared
 //      memory.
-// bw2: one CTA per (b, h, chunk) computes every token and gate gradient of
-//      its chunk from q, k, v, dO, S_j and Gb_j.
+// bw2: persistent, one CTA per SM walking the (b, h, chunk) tiles; each tile's
+//      token and gate gradients come from q, k, v, dO, S_j and Gb_j.
 
 #include <cuda.h>
 
@@ -658,24 +659,26 @@ struct Bars2 {
 static_assert(sizeof(Bars2) <= 256, "barrier block");
 
 // Persistent: CTA b handles tiles b, b + G, b + 2G, ... (tile = bh * N + chunk).
-// Each input group of the next tile loads as soon as the current tile is done
-// with it: v, dO and S_j after phase 2 (and delta's da), Gb_j after the first
-// products of phase 3.  S_j and Gb_j swap their two tiles every tile, so the
-// next S_j (needed first, by phase 1) goes into the current Gb_j tile a phase
-// earlier than S_j's own tile frees.  q and k are double-buffered for delta and adam (the
-// w k tile and the reduction array are not needed there), so the q, k of
-// local tile i+2 load once tile i is done with its buffer; muon loads the next
-// tile's q, k after phase 3.  Phase 1 runs the products that need no S_j
-// (P, v^T I) first, so A is built while S_j arrives.  dq is staged in the E^T
-// tile, dk in the A and dP tiles (one 64-column panel each) and dv is stored
-// from the dE tile, so no input tile holds an output; the next tile's
-// epilogue waits for the stores' reads only before it writes A and E^T.
+// Warp 9 issues every load, each input group of the next tile as soon as the
+// current tile is done with the tiles it goes into: v once phase 1a has read
+// it (delta, adam; muon keeps E^T lo in the v tile until phase 2 and loads v
+// with dO), dO and S_j after phase 2 (and delta's da), Gb_j after -dE S.
+// S_j and Gb_j swap their two tiles every tile, so the next S_j (needed first,
+// by phase 1) goes into the current Gb_j tile a phase earlier than S_j's own
+// tile frees.  q and k are double-buffered for delta and adam (the w k tile
+// and the reduction array are not needed there), so the q, k of local tile
+// i+2 load once tile i is done with its buffer; muon loads the next tile's q,
+// k after phase 3.  Phase 1 runs the products that need no S_j (P, v^T I)
+// first, so A is built while S_j arrives.  dq is staged in the E^T tile, dk in
+// the A and dP tiles (one 64-column panel each) and dv is stored from the dE
+// tile, so no input tile holds an output; the next tile's epilogue waits for
+// the stores' reads only before it writes A and E^T.
 // Delta and adam apply the token weight w to the rows of dE in its drain
 // (delta: A = tril(P), dE = diag(beta) (A^T dO + k Gb^T); adam: w = 1), so
 // k Gb^T is issued with phase 1 and runs while epilogue 1 drains; muon builds
 // w * k (w_s = prod_{t>s} mu_t can underflow, so beta / w is no option).
-// The dbeta column sums of tril(dA) * P are reduced across lanes with
-// shuffles (no shared-memory array).
+// dbeta: delta takes it whole as the row product <E_s, dE_s / beta_s>; muon
+// and adam reduce the column sums of tril(dA) * P across lanes with shuffles.
 template <int RULE>
 __global__ void __launch_bounds__(kThreads2, 1)
 chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
