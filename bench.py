@@ -299,6 +299,64 @@ def run_reference_arm(args, cfg: dict) -> None:
 # GPU arm
 # ---------------------------------------------------------------------------
 
+def run_epilogue(args) -> None:
+    """The mixer epilogue alone (train_ablation.py:188-189 up to the output
+    projection): per-head RMSNorm of o (B8 H16 T4096 d128, bf16) into the
+    (B, T, D) layout, forward + backward per step, inputs resident in HBM (larger
+    than L2).  One JSON line; the roofline is HBM bytes per launch of the
+    dominant kernel: forward reads o and writes y, backward reads o and dy and
+    writes do (dweight is 512 B)."""
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    pkg = importlib.import_module(PKG_NAME)
+    L = importlib.import_module(PKG_NAME + "._lib")
+    B, H, T, dh = 8, 16, 4096, 128
+    g = torch.Generator().manual_seed(0)
+    o = torch.randn(B, H, T, dh, generator=g).to(device, torch.bfloat16).requires_grad_(True)
+    w = (1.0 + 0.5 * torch.randn(dh, generator=g)).to(device).requires_grad_(True)
+    dy = torch.randn(B, T, H * dh, generator=g).to(device, torch.bfloat16)
+
+    def step():
+        y = pkg.head_rmsnorm(o, w)
+        return torch.autograd.grad(y, (o, w), dy)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    L.prof_report()
+    L.prof_enable(True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    L.prof_enable(False)
+    kt = L.prof_report()
+    ms = e0.elapsed_time(e1)
+    row_bytes = B * H * T * dh * 2
+    work = {"head_rmsnorm_fwd": 2 * row_bytes, "head_rmsnorm_bwd": 3 * row_bytes}
+    peaks, kind = load_peaks()
+    kernel_times, roof = {}, None
+    for name, (tms, n) in kt.items():
+        kernel_times[name] = {"total_ms": tms, "launches": n, "avg_ms": tms / max(n, 1)}
+    if kt:
+        top = max(kt, key=lambda k: kt[k][0])
+        achieved = work.get(top, 0) / (kt[top][0] / kt[top][1] / 1e3) / 1e9
+        roof = {"kernel": top, "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                "peak_source": ("measured (MEASURED_PEAKS.json hbm_gbs, copy)" if kind == "measured"
+                                else "fallback (6.65 TB/s)")}
+    print(json.dumps({
+        "metric": "epilogue tokens/s fwd+bwd (per-head RMSNorm into (B, T, D)), B8·H16·T4096·d128 bf16",
+        "value": B * T * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "epilogue_config1", "l2": "inputs larger than L2 (o 134 MB)"},
+        "roofline": roof, "kernel_times": kernel_times}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -311,6 +369,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="override B of the workload (small ncu captures)")
+    ap.add_argument("--workload", default="mixer", choices=["mixer", "epilogue"],
+                    help="epilogue: time the per-head RMSNorm epilogue alone (one GPU)")
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                     help="weak: a full batch per rank; strong: the global batch split over ranks")
     args = ap.parse_args()
@@ -320,6 +380,9 @@ def main():
 
     if args.impl == "reference":
         run_reference_arm(args, cfg)
+        return
+    if args.workload == "epilogue":
+        run_epilogue(args)
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -253,6 +253,54 @@ int gmdn_selftest_wait_timeout(uint32_t* status, uint64_t limit_ns, void* stream
   return GMDN_OK;
 }
 
+static int check_rmsnorm(const void* o, const float* weight, const void* out, int B, int H,
+                         int T, int dh) {
+  if (!o || !weight || !out) return fail(GMDN_ERR_INVALID, "null pointer");
+  if (B < 0 || H < 0 || T < 0) return fail(GMDN_ERR_INVALID, "negative size B=%d H=%d T=%d", B, H, T);
+  if (static_cast<long long>(B) * H * T >= (1ll << 31))
+    return fail(GMDN_ERR_UNSUPPORTED, "head_rmsnorm: B*H*T must be below 2^31");
+  if (dh != 32 && dh != 64 && dh != 128)
+    return fail(GMDN_ERR_UNSUPPORTED, "head_rmsnorm: dh must be 32, 64 or 128 (got %d)", dh);
+  for (const void* p : {static_cast<const void*>(o), static_cast<const void*>(weight), out})
+    if (reinterpret_cast<uintptr_t>(p) % 16)
+      return fail(GMDN_ERR_INVALID, "head_rmsnorm: pointers must be 16-byte aligned");
+  return GMDN_OK;
+}
+
+int gmdn_head_rmsnorm_fwd(const void* o, const float* weight, void* y, int B, int H, int T,
+                          int dh, float eps, int in_f32, int out_f32, void* stream) {
+  g_last_error.clear();
+  int rc = check_rmsnorm(o, weight, y, B, H, T, dh);
+  if (rc) return rc;
+  if (static_cast<long long>(B) * H * T == 0) return GMDN_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float e = eps < 0.f ? 1.1920928955078125e-07f : eps;
+  GMDN_LAUNCH(gmdn::head_rmsnorm_fwd(o, weight, y, B, H, T, dh, e, in_f32 != 0, out_f32 != 0, st),
+              "head_rmsnorm_fwd");
+  return GMDN_OK;
+}
+
+int gmdn_head_rmsnorm_bwd(const void* o, const float* weight, const void* dy, void* d_o,
+                          float* dweight, int B, int H, int T, int dh, float eps, int in_f32,
+                          int out_f32, void* stream) {
+  g_last_error.clear();
+  int rc = check_rmsnorm(o, weight, d_o, B, H, T, dh);
+  if (rc) return rc;
+  if (!dy || !dweight) return fail(GMDN_ERR_INVALID, "null pointer");
+  if (reinterpret_cast<uintptr_t>(dy) % 16)
+    return fail(GMDN_ERR_INVALID, "head_rmsnorm: pointers must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float e = eps < 0.f ? 1.1920928955078125e-07f : eps;
+  if (static_cast<long long>(B) * H * T == 0) {
+    cudaError_t ce = cudaMemsetAsync(dweight, 0, sizeof(float) * dh, st);
+    return ce == cudaSuccess ? GMDN_OK : cuda_fail(ce, "head_rmsnorm_bwd");
+  }
+  GMDN_LAUNCH(gmdn::head_rmsnorm_bwd(o, weight, dy, d_o, dweight, B, H, T, dh, e, in_f32 != 0,
+                                     out_f32 != 0, st),
+              "head_rmsnorm_bwd");
+  return GMDN_OK;
+}
+
 void gmdn_prof_enable(int on) { g_prof_on.store(on ? 1 : 0); }
 
 const char* gmdn_prof_report(void) {

@@ -54,6 +54,15 @@ bool chunk_bwd_tc_supported(const ChunkArgs& p);
 cudaError_t chunk_bwd1_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st);
 cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st);
 
+// Mixer epilogue (epilogue.cu): per-head RMSNorm of o (B, H, T, dh) into
+// y (B, T, H*dh), and its backward (dw is zeroed, then accumulated); dh 32, 64
+// or 128, bf16 or fp32 input and output.
+cudaError_t head_rmsnorm_fwd(const void* o, const float* w, void* y, int B, int H, int T, int dh,
+                             float eps, bool in_f32, bool out_f32, cudaStream_t st);
+cudaError_t head_rmsnorm_bwd(const void* o, const float* w, const void* dy, void* d_o, float* dw,
+                             int B, int H, int T, int dh, float eps, bool in_f32, bool out_f32,
+                             cudaStream_t st);
+
 // Failure-detection self-test (selftest.cu): one CTA's bounded wait on an
 // mbarrier nothing arrives on gives up after limit_ns and sets bit 0 of *status.
 cudaError_t wait_timeout_selftest(uint32_t* status, uint64_t limit_ns, cudaStream_t st);

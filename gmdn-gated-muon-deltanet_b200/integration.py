@@ -10,9 +10,11 @@
 
 ``patch_mixer(FastWeightMixer)``
     Replace ``FastWeightMixer.forward`` (train_ablation.py:111-190) with one
-    that keeps the module's own projections, conv, gates, RMSNorm and output
-    projection (lines 124-140 and 188-190, restated) and runs phases 1-3
-    (lines 142-187) as the fused ``chunk_fast_weight`` op.
+    that keeps the module's own projections, conv, gates and output projection
+    (lines 124-140 and 190, restated), runs phases 1-3 (lines 142-187) as the
+    fused ``chunk_fast_weight`` op and the per-head RMSNorm with its (B, T, D)
+    view (lines 188-189) as the fused ``head_rmsnorm`` op (dh 32, 64 or 128;
+    other head sizes keep the module's own norm).
 """
 
 from __future__ import annotations
@@ -62,7 +64,11 @@ def mixer_forward(self, x: torch.Tensor) -> torch.Tensor:
     prec = getattr(self, "b200_precision", ops.GMDN_PREC_FAST)
     o = ops.chunk_fast_weight(q.to(dt), k.to(dt), v.to(dt), g[0], g[1], g[2], nu,
                               _RULES[self.inner], self.ns_steps, C, prec)
-    o = self.norm(o).to(x.dtype)
+    norm = self.norm
+    if (isinstance(norm, torch.nn.RMSNorm) and norm.weight is not None and dh in (32, 64, 128)
+            and x.dtype in (torch.bfloat16, torch.float32)):
+        return self.out(ops.head_rmsnorm(o, norm.weight, norm.eps, x.dtype))
+    o = norm(o).to(x.dtype)
     return self.out(o.transpose(1, 2).reshape(B, T, D))
 
 

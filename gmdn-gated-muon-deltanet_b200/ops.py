@@ -10,6 +10,10 @@ Two ops, matching the two layers of the reference they replace:
     train_ablation.py:142-187 (phases 1-3 of ``FastWeightMixer.forward``):
     o (B, H, T, dh) from q, k, v and the per-token gates.
 
+``head_rmsnorm(o, weight, eps, out_dtype)``
+    train_ablation.py:188-189 up to the output projection: the per-head
+    RMSNorm of o written as (B, T, H * dh).
+
 Both run only on CUDA tensors through ``libgmdn_b200.so``; there is no CPU or
 eager fallback.  The ops are opaque to torch.compile (fake kernels give the
 output shapes), so a compiled trainer can call them.
@@ -26,8 +30,8 @@ from torch import Tensor
 
 from ._lib import GMDN_PREC_FAST, GMDN_PREC_IEEE, check, lib
 
-__all__ = ["state_scan", "chunk_fast_weight", "GMDN_PREC_IEEE", "GMDN_PREC_FAST",
-           "ScanFunction"]
+__all__ = ["state_scan", "chunk_fast_weight", "head_rmsnorm", "GMDN_PREC_IEEE",
+           "GMDN_PREC_FAST", "ScanFunction"]
 
 
 def _ptr(t: Optional[Tensor]):
@@ -294,3 +298,106 @@ def chunk_fast_weight(q: Tensor, k: Tensor, v: Tensor, alpha: Tensor, beta: Tens
     o, _ = torch.ops.gmdn.chunk_fwd(q, k, v, *gates, int(rule), int(ns), int(chunk),
                                     int(precision))
     return o
+
+
+# ---------------------------------------------------------------------------
+# mixer epilogue: per-head RMSNorm into the (B, T, D) layout
+# ---------------------------------------------------------------------------
+
+def _f32_flag(t: Tensor, what: str) -> int:
+    if t.dtype == torch.bfloat16:
+        return 0
+    if t.dtype == torch.float32:
+        return 1
+    raise TypeError(f"{what} must be bfloat16 or float32, got {t.dtype}")
+
+
+def _aligned(t: Tensor) -> Tensor:
+    t = t.contiguous()
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
+@torch.library.custom_op("gmdn::head_rmsnorm_fwd", mutates_args=())
+def _head_rmsnorm_fwd(o: Tensor, weight: Tensor, eps: float, out_f32: bool) -> Tensor:
+    B, H, T, dh = o.shape
+    y = torch.empty(B, T, H * dh, dtype=torch.float32 if out_f32 else torch.bfloat16,
+                    device=o.device)
+    with torch.cuda.device(o.device):
+        rc = lib.gmdn_head_rmsnorm_fwd(_ptr(o), _ptr(weight), _ptr(y), B, H, T, dh, float(eps),
+                                       _f32_flag(o, "o"), int(out_f32), _stream(o))
+    check(rc, "gmdn_head_rmsnorm_fwd")
+    return y
+
+
+@_head_rmsnorm_fwd.register_fake
+def _(o, weight, eps, out_f32):
+    B, H, T, dh = o.shape
+    return o.new_empty(B, T, H * dh, dtype=torch.float32 if out_f32 else torch.bfloat16)
+
+
+@torch.library.custom_op("gmdn::head_rmsnorm_bwd", mutates_args=())
+def _head_rmsnorm_bwd(o: Tensor, weight: Tensor, dy: Tensor, eps: float,
+                      out_f32: bool) -> tuple[Tensor, Tensor]:
+    B, H, T, dh = o.shape
+    d_o = torch.empty_like(o)
+    dw = torch.empty(dh, dtype=torch.float32, device=o.device)
+    with torch.cuda.device(o.device):
+        rc = lib.gmdn_head_rmsnorm_bwd(_ptr(o), _ptr(weight), _ptr(dy), _ptr(d_o), _ptr(dw), B, H,
+                                       T, dh, float(eps), _f32_flag(o, "o"), int(out_f32),
+                                       _stream(o))
+    check(rc, "gmdn_head_rmsnorm_bwd")
+    return d_o, dw
+
+
+@_head_rmsnorm_bwd.register_fake
+def _(o, weight, dy, eps, out_f32):
+    return torch.empty_like(o), weight.new_empty(o.shape[-1], dtype=torch.float32)
+
+
+def _rms_setup(ctx, inputs, output):
+    o, weight, eps, out_f32 = inputs
+    ctx.save_for_backward(o, weight)
+    ctx.cfg = (eps, out_f32)
+    ctx.weight_dtype = weight.dtype
+
+
+def _rms_backward(ctx, dy):
+    o, weight = ctx.saved_tensors
+    eps, out_f32 = ctx.cfg
+    dy = _aligned(dy.to(torch.float32 if out_f32 else torch.bfloat16))
+    d_o, dw = torch.ops.gmdn.head_rmsnorm_bwd(o, weight, dy, eps, out_f32)
+    return d_o, dw, None, None
+
+
+_head_rmsnorm_fwd.register_autograd(_rms_backward, setup_context=_rms_setup)
+
+
+def head_rmsnorm(o: Tensor, weight: Tensor, eps: Optional[float] = None,
+                 out_dtype: Optional[torch.dtype] = None) -> Tensor:
+    """The mixer epilogue before the output projection (train_ablation.py:188-189):
+    ``norm(o).to(out_dtype).transpose(1, 2).reshape(B, T, H * dh)`` with
+    ``norm = nn.RMSNorm(dh)``.
+
+    o: (B, H, T, dh) bf16 or fp32 (the output of ``chunk_fast_weight``);
+    weight: (dh,) the RMSNorm weight; eps: None for torch's default for bf16 /
+    fp32 input (float32 machine epsilon); out_dtype: bf16 or fp32, default the
+    dtype of o.  Each row is normalised in fp32, rounded to o's dtype and stored
+    in out_dtype, as torch's rms_norm followed by ``.to(x.dtype)`` does.
+    Returns (B, T, H * dh); differentiable in o and weight.  dh 32, 64 or 128.
+    """
+    if o.dim() != 4:
+        raise ValueError(f"o must be (B, H, T, dh), got {tuple(o.shape)}")
+    dh = o.shape[-1]
+    if weight.shape != (dh,):
+        raise ValueError(f"weight must be ({dh},), got {tuple(weight.shape)}")
+    if dh not in (32, 64, 128):
+        raise ValueError(f"head_rmsnorm supports dh 32, 64 or 128 (got {dh})")
+    _require_cuda("head_rmsnorm", o, weight)
+    out_dtype = o.dtype if out_dtype is None else out_dtype
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError(f"out_dtype must be bfloat16 or float32, got {out_dtype}")
+    _f32_flag(o, "o")
+    e = -1.0 if eps is None else float(eps)
+    w = weight.float()   # differentiable; the gradient comes back in weight's dtype
+    return torch.ops.gmdn.head_rmsnorm_fwd(_aligned(o), _aligned(w), e,
+                                           out_dtype == torch.float32)

@@ -182,6 +182,21 @@ size_t gmdn_chunk_workspace_bytes_ex(int B, int H, int T, int dh, int chunk, int
  * failure reporting). */
 int gmdn_chunk_status(const void* workspace, void* stream);
 
+/* Mixer epilogue, replaces train_ablation.py:188-189 up to the output
+ * projection: `o = self.norm(o).to(x.dtype)` with norm = nn.RMSNorm(dh), then
+ * `o.transpose(1, 2).reshape(B, T, D)`.  o (B, H, T, dh), weight (dh) fp32,
+ * y (B, T, H * dh).  Per row: upcast to fp32, x * rsqrt(mean(x^2) + eps) *
+ * weight, rounded to the input dtype, stored in the output dtype (torch's
+ * rms_norm for bf16 / fp32 input; eps < 0 selects its default FLT_EPSILON).
+ * in_f32 / out_f32: 1 = fp32, 0 = bf16.  dh must be 32, 64 or 128; pointers
+ * 16-byte aligned.  The backward takes dy in the output dtype and writes
+ * d_o (input dtype) and dweight (fp32; overwritten, not accumulated). */
+int gmdn_head_rmsnorm_fwd(const void* o, const float* weight, void* y, int B, int H, int T,
+                          int dh, float eps, int in_f32, int out_f32, void* stream);
+int gmdn_head_rmsnorm_bwd(const void* o, const float* weight, const void* dy, void* d_o,
+                          float* dweight, int B, int H, int T, int dh, float eps, int in_f32,
+                          int out_f32, void* stream);
+
 /* Failure-detection self-test (diagnostic; no reference counterpart): launches
  * one CTA whose bounded mbarrier wait -- the same wait the kernels use -- can
  * never complete, with a limit of limit_ns (clamped to [1 ms, 2 s]).  The wait

@@ -185,10 +185,45 @@ def mixer_cases(train_ablation, fast_scan):
     return cases
 
 
+def epilogue_cases(train_ablation):
+    """train_ablation.py:188-189 on the reference module's own RMSNorm: the norm,
+    the dtype conversion to x.dtype and the (B, T, D) view, with autograd."""
+    cases = []
+    specs = [
+        # (name, D, heads, B, T, o dtype, x dtype)
+        ("f64_dh32", 64, 2, 2, 8, torch.float64, torch.float64),
+        ("f32_dh64", 128, 2, 2, 16, torch.float32, torch.float32),
+        ("f32_dh128", 256, 2, 2, 16, torch.float32, torch.float32),
+        ("bf16_to_f32_dh128", 256, 2, 2, 16, torch.bfloat16, torch.float32),
+        ("bf16_dh64", 128, 2, 1, 16, torch.bfloat16, torch.bfloat16),
+    ]
+    for idx, (name, D, H, B, T, odt, xdt) in enumerate(specs):
+        torch.manual_seed(4000 + idx)
+        mixer = train_ablation.FastWeightMixer(D, H, "delta", chunk=8)
+        norm = mixer.norm.to(torch.float64 if odt == torch.float64 else torch.float32)
+        dh = D // H
+        gen = torch.Generator().manual_seed(5000 + idx)
+        with torch.no_grad():
+            norm.weight.copy_(1.0 + 0.5 * torch.randn(dh, generator=gen, dtype=norm.weight.dtype))
+        scale = torch.exp(torch.randn(B, H, T, 1, generator=gen, dtype=torch.float64))
+        o = (torch.randn(B, H, T, dh, generator=gen, dtype=torch.float64) * scale).to(odt)
+        o.requires_grad_(True)
+        y = norm(o).to(xdt)                          # train_ablation.py:188
+        y = y.transpose(1, 2).reshape(B, T, D)       # train_ablation.py:189
+        dy = torch.randn(y.shape, generator=gen, dtype=torch.float64).to(xdt)
+        (y.double() * dy.double()).sum().backward()
+        cases.append(dict(name=name, o=o.detach(), weight=norm.weight.detach().clone(),
+                          out_dtype=xdt, y=y.detach(), dy=dy, d_o=o.grad.detach(),
+                          dweight=norm.weight.grad.detach().clone()))
+    return cases
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout")
     ap.add_argument("--out", default=HERE)
+    ap.add_argument("--which", default="all", choices=["all", "epilogue"],
+                    help="epilogue: write only epilogue.pt")
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.ref))
     import fast_scan  # noqa: E402  (the reference's module)
@@ -196,6 +231,13 @@ def main():
 
     torch.set_num_threads(4)
     meta = dict(torch=str(torch.__version__), source="reference fast_scan.py / train_ablation.py, float64 CPU")
+    epi = epilogue_cases(train_ablation)
+    torch.save(dict(meta=dict(torch=str(torch.__version__),
+                              source="reference train_ablation.py:188-189 (its nn.RMSNorm), CPU"),
+                    cases=epi), os.path.join(args.out, "epilogue.pt"))
+    print(f"wrote {len(epi)} epilogue cases to {args.out}")
+    if args.which == "epilogue":
+        return
     scan = scan_cases(fast_scan)
     torch.save(dict(meta=meta, cases=scan), os.path.join(args.out, "scan.pt"))
     mixer = mixer_cases(train_ablation, fast_scan)

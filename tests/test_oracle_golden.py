@@ -96,3 +96,27 @@ def test_mixer_core_matches_reference(case):
             assert g.abs().max().item() == 0.0, name
         else:
             assert rel(g, ref) < 1e-4, name
+
+
+def _epilogue_cases():
+    return torch.load(os.path.join(GOLD, "epilogue.pt"), weights_only=False)["cases"]
+
+
+def _rel(a, b):
+    a, b = a.double(), b.double()
+    return ((a - b).abs().max() / b.abs().max().clamp_min(1e-300)).item()
+
+
+@pytest.mark.parametrize("case", _epilogue_cases(), ids=lambda c: c["name"])
+def test_epilogue_matches_reference(case):
+    """The per-head RMSNorm restatement against train_ablation.py:188-189 run on
+    the reference module's own nn.RMSNorm: output, d_o and dweight."""
+    tol = {torch.float64: 1e-12, torch.float32: 2e-6}.get(case["o"].dtype, 8e-3)
+    o = case["o"].clone().requires_grad_(True)
+    w = case["weight"].clone().requires_grad_(True)
+    y = oracle.head_rmsnorm(o, w, None, case["out_dtype"])
+    assert y.dtype == case["y"].dtype and y.shape == case["y"].shape
+    assert _rel(y, case["y"]) <= tol
+    (y.double() * case["dy"].double()).sum().backward()
+    assert _rel(o.grad, case["d_o"]) <= tol
+    assert _rel(w.grad, case["dweight"]) <= max(tol, 1e-5)
