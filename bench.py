@@ -357,6 +357,68 @@ def run_epilogue(args) -> None:
         "roofline": roof, "kernel_times": kernel_times}), flush=True)
 
 
+def run_prologue(args) -> None:
+    """The mixer prologue alone (train_ablation.py:124-140 after the two
+    projections, which are plain GEMMs and not timed): conv + SiLU + q/k norm +
+    head layout and the gate sigmoids at config-1 size (B8 T4096 D2048, H16,
+    bf16), forward + backward per step, inputs resident in HBM.  Roofline: HBM
+    bytes per launch of the dominant kernel (forward reads u and writes q, k,
+    v; backward reads u, dq, dk, dv and writes du; gates are 2 % of it)."""
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    pkg = importlib.import_module(PKG_NAME)
+    L = importlib.import_module(PKG_NAME + "._lib")
+    B, T, H, dh, nG = 8, 4096, 16, 128, 3
+    D3 = 3 * H * dh
+    g = torch.Generator().manual_seed(0)
+    u = torch.randn(B, T, D3, generator=g).to(device, torch.bfloat16).requires_grad_(True)
+    w = (torch.randn(D3, 1, 4, generator=g) * 0.5).to(device).requires_grad_(True)
+    bb = (torch.randn(D3, generator=g) * 0.1).to(device).requires_grad_(True)
+    gl = torch.randn(B, T, nG * H, generator=g).to(device, torch.bfloat16).requires_grad_(True)
+    cot = [torch.randn(B, H, T, dh, generator=g).to(device, torch.bfloat16) for _ in range(3)]
+    cot.append(torch.randn(nG, B, H, T, generator=g).to(device, torch.bfloat16))
+
+    def step():
+        outs = pkg.mixer_prologue(u, w, bb, gl, H)
+        return torch.autograd.grad(outs, (u, w, bb, gl), cot)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    L.prof_report()
+    L.prof_enable(True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    L.prof_enable(False)
+    kt = L.prof_report()
+    ms = e0.elapsed_time(e1)
+    ub = B * T * D3 * 2
+    work = {"mixer_prologue_fwd": 2 * ub, "mixer_prologue_bwd": 3 * ub}
+    peaks, kind = load_peaks()
+    kernel_times, roof = {}, None
+    for name, (tms, n) in kt.items():
+        kernel_times[name] = {"total_ms": tms, "launches": n, "avg_ms": tms / max(n, 1)}
+    if kt:
+        top = max(kt, key=lambda k: kt[k][0])
+        achieved = work.get(top, 0) / (kt[top][0] / kt[top][1] / 1e3) / 1e9
+        roof = {"kernel": top, "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                "peak_source": ("measured (MEASURED_PEAKS.json hbm_gbs, copy)" if kind == "measured"
+                                else "fallback (6.65 TB/s)")}
+    print(json.dumps({
+        "metric": "prologue tokens/s fwd+bwd (conv + SiLU + q/k norm + gates), B8·T4096·D2048·H16 bf16",
+        "value": B * T * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "prologue_config1", "l2": "inputs larger than L2 (u 403 MB)"},
+        "roofline": roof, "kernel_times": kernel_times}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -369,8 +431,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="override B of the workload (small ncu captures)")
-    ap.add_argument("--workload", default="mixer", choices=["mixer", "epilogue"],
-                    help="epilogue: time the per-head RMSNorm epilogue alone (one GPU)")
+    ap.add_argument("--workload", default="mixer", choices=["mixer", "epilogue", "prologue"],
+                    help="epilogue / prologue: time that part of the mixer alone (one GPU)")
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                     help="weak: a full batch per rank; strong: the global batch split over ranks")
     args = ap.parse_args()
@@ -383,6 +445,9 @@ def main():
         return
     if args.workload == "epilogue":
         run_epilogue(args)
+        return
+    if args.workload == "prologue":
+        run_prologue(args)
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

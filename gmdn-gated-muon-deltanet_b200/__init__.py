@@ -12,10 +12,11 @@ raises if it is missing: there is no fallback implementation.
 """
 
 from ._lib import GMDN_PREC_FAST, GMDN_PREC_IEEE, LIB_PATH, kernel_launches  # noqa: F401
-from .ops import ScanFunction, chunk_fast_weight, head_rmsnorm, state_scan  # noqa: F401
+from .ops import (ScanFunction, chunk_fast_weight, head_rmsnorm, mixer_prologue,  # noqa: F401
+                  state_scan)
 from .integration import patch_mixer, patch_reference  # noqa: F401
 from . import fast_scan, sharding, workloads  # noqa: F401
 
-__all__ = ["state_scan", "chunk_fast_weight", "head_rmsnorm", "ScanFunction", "fast_scan", "workloads",
+__all__ = ["state_scan", "chunk_fast_weight", "head_rmsnorm", "mixer_prologue", "ScanFunction", "fast_scan", "workloads",
            "sharding", "patch_reference", "patch_mixer", "GMDN_PREC_IEEE", "GMDN_PREC_FAST",
            "kernel_launches", "LIB_PATH"]

@@ -76,6 +76,10 @@ lib.gmdn_chunk_fwd_ex.argtypes = [_p] * 10 + [_z] + [_i] * 9 + [_p]
 lib.gmdn_chunk_bwd_ex.restype = _i
 lib.gmdn_chunk_bwd_ex.argtypes = [_p] * 17 + [_z] + [_i] * 9 + [_p]
 
+lib.gmdn_mixer_prologue_fwd.restype = _i
+lib.gmdn_mixer_prologue_fwd.argtypes = [_p] * 8 + [_i] * 6 + [_p]
+lib.gmdn_mixer_prologue_bwd.restype = _i
+lib.gmdn_mixer_prologue_bwd.argtypes = [_p] * 12 + [_i] * 6 + [_p]
 lib.gmdn_head_rmsnorm_fwd.restype = _i
 lib.gmdn_head_rmsnorm_fwd.argtypes = [_p] * 3 + [_i] * 4 + [ctypes.c_float] + [_i] * 2 + [_p]
 lib.gmdn_head_rmsnorm_bwd.restype = _i

@@ -5,6 +5,7 @@
 // nothing synchronises the host.
 
 #include <atomic>
+#include <initializer_list>
 #include <cstdarg>
 #include <cstdio>
 #include <map>
@@ -250,6 +251,57 @@ int gmdn_selftest_wait_timeout(uint32_t* status, uint64_t limit_ns, void* stream
                                              : (limit_ns > 2000000000ull ? 2000000000ull : limit_ns);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   GMDN_LAUNCH(gmdn::wait_timeout_selftest(status, lim, st), "wait_timeout_selftest");
+  return GMDN_OK;
+}
+
+static int check_prologue(std::initializer_list<const void*> ptrs, int B, int T, int H, int dh,
+                          int n_gates) {
+  for (const void* p : ptrs) {
+    if (!p) return fail(GMDN_ERR_INVALID, "mixer_prologue: null pointer");
+    if (reinterpret_cast<uintptr_t>(p) % 16)
+      return fail(GMDN_ERR_INVALID, "mixer_prologue: pointers must be 16-byte aligned");
+  }
+  if (B < 0 || T < 0 || H < 0) return fail(GMDN_ERR_INVALID, "negative size B=%d T=%d H=%d", B, T, H);
+  if (dh != 32 && dh != 64 && dh != 128)
+    return fail(GMDN_ERR_UNSUPPORTED, "mixer_prologue: dh must be 32, 64 or 128 (got %d)", dh);
+  if (n_gates != 3 && n_gates != 4)
+    return fail(GMDN_ERR_INVALID, "mixer_prologue: n_gates must be 3 or 4 (got %d)", n_gates);
+  if (static_cast<long long>(B) * T * 3 * H * dh >= (1ll << 31))
+    return fail(GMDN_ERR_UNSUPPORTED, "mixer_prologue: B*T*3D must be below 2^31");
+  return GMDN_OK;
+}
+
+int gmdn_mixer_prologue_fwd(const void* u, const float* conv_w, const float* conv_b,
+                            const void* gl, void* q, void* k, void* v, void* g, int B, int T,
+                            int H, int dh, int n_gates, int io_f32, void* stream) {
+  g_last_error.clear();
+  int rc = check_prologue({u, conv_w, conv_b, gl, q, k, v, g}, B, T, H, dh, n_gates);
+  if (rc) return rc;
+  if (static_cast<long long>(B) * T * H == 0) return GMDN_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GMDN_LAUNCH(gmdn::mixer_prologue_fwd(u, conv_w, conv_b, gl, q, k, v, g, B, T, H, dh, n_gates,
+                                       io_f32 != 0, st),
+              "mixer_prologue_fwd");
+  return GMDN_OK;
+}
+
+int gmdn_mixer_prologue_bwd(const void* u, const float* conv_w, const float* conv_b,
+                            const void* gl, const void* dq, const void* dk, const void* dv,
+                            const void* dg, void* du, float* dconv_w, float* dconv_b, void* dgl,
+                            int B, int T, int H, int dh, int n_gates, int io_f32, void* stream) {
+  g_last_error.clear();
+  int rc = check_prologue({u, conv_w, conv_b, gl, dq, dk, dv, dg, du, dconv_w, dconv_b, dgl}, B, T,
+                          H, dh, n_gates);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (static_cast<long long>(B) * T * H == 0) {
+    cudaError_t ce = cudaMemsetAsync(dconv_w, 0, sizeof(float) * 3 * H * dh * 4, st);
+    if (ce == cudaSuccess) ce = cudaMemsetAsync(dconv_b, 0, sizeof(float) * 3 * H * dh, st);
+    return ce == cudaSuccess ? GMDN_OK : cuda_fail(ce, "mixer_prologue_bwd");
+  }
+  GMDN_LAUNCH(gmdn::mixer_prologue_bwd(u, conv_w, conv_b, gl, dq, dk, dv, dg, du, dconv_w, dconv_b,
+                                       dgl, B, T, H, dh, n_gates, io_f32 != 0, st),
+              "mixer_prologue_bwd");
   return GMDN_OK;
 }
 

@@ -63,6 +63,18 @@ cudaError_t head_rmsnorm_bwd(const void* o, const float* w, const void* dy, void
                              int B, int H, int T, int dh, float eps, bool in_f32, bool out_f32,
                              cudaStream_t st);
 
+// Mixer prologue (prologue.cu): causal depthwise conv (k=4) + SiLU + q/k L2
+// norm of u (B, T, 3D) into q, k, v (B, H, T, dh), sigmoid of the gate logits
+// (B, T, nG*H) into g (nG, B, H, T); backward (dcw, dcb zeroed, then
+// accumulated).  dh 32, 64 or 128; bf16 or fp32 I/O; conv weight / bias fp32.
+cudaError_t mixer_prologue_fwd(const void* u, const float* cw, const float* cb, const void* gl,
+                               void* q, void* k, void* v, void* g, int B, int T, int H, int dh,
+                               int n_gates, bool io_f32, cudaStream_t st);
+cudaError_t mixer_prologue_bwd(const void* u, const float* cw, const float* cb, const void* gl,
+                               const void* dq, const void* dk, const void* dv, const void* dg,
+                               void* du, float* dcw, float* dcb, void* dgl, int B, int T, int H,
+                               int dh, int n_gates, bool io_f32, cudaStream_t st);
+
 // Failure-detection self-test (selftest.cu): one CTA's bounded wait on an
 // mbarrier nothing arrives on gives up after limit_ns and sets bit 0 of *status.
 cudaError_t wait_timeout_selftest(uint32_t* status, uint64_t limit_ns, cudaStream_t st);

@@ -10,11 +10,13 @@
 
 ``patch_mixer(FastWeightMixer)``
     Replace ``FastWeightMixer.forward`` (train_ablation.py:111-190) with one
-    that keeps the module's own projections, conv, gates and output projection
-    (lines 124-140 and 190, restated), runs phases 1-3 (lines 142-187) as the
-    fused ``chunk_fast_weight`` op and the per-head RMSNorm with its (B, T, D)
-    view (lines 188-189) as the fused ``head_rmsnorm`` op (dh 32, 64 or 128;
-    other head sizes keep the module's own norm).
+    that keeps the module's own projections and output projection (plain
+    GEMMs), runs the conv / SiLU / q-k norm / gate sigmoids (lines 124-140) as
+    the fused ``mixer_prologue`` op, phases 1-3 (lines 142-187) as the fused
+    ``chunk_fast_weight`` op and the per-head RMSNorm with its (B, T, D) view
+    (lines 188-189) as the fused ``head_rmsnorm`` op (dh 32, 64 or 128 and the
+    module's own conv shape; otherwise the module's own layers run those
+    lines).
 """
 
 from __future__ import annotations
@@ -47,12 +49,20 @@ def mixer_forward(self, x: torch.Tensor) -> torch.Tensor:
     C, H, dh = self.chunk, self.h, self.dh
     if T % C:
         raise ValueError("seq_len must be a multiple of chunk size")
-    qkv = self.conv(self.qkv(x).transpose(1, 2))[..., :T].transpose(1, 2)
-    q, k, v = F.silu(qkv).chunk(3, dim=-1)
-    q = F.normalize(q.reshape(B, T, H, dh).transpose(1, 2), dim=-1)
-    k = F.normalize(k.reshape(B, T, H, dh).transpose(1, 2), dim=-1)
-    v = v.reshape(B, T, H, dh).transpose(1, 2)
-    g = torch.sigmoid(self.gates(x)).view(B, T, self.n_gates, H).permute(2, 0, 3, 1)
+    u, gl = self.qkv(x), self.gates(x)
+    conv = self.conv
+    if (dh in (32, 64, 128) and u.dtype in (torch.bfloat16, torch.float32)
+            and tuple(conv.kernel_size) == (4,) and tuple(conv.padding) == (3,)
+            and conv.groups == conv.in_channels == conv.out_channels == 3 * D
+            and conv.bias is not None and self.n_gates in (3, 4)):
+        q, k, v, g = ops.mixer_prologue(u, conv.weight, conv.bias, gl, H)
+    else:
+        qkv = conv(u.transpose(1, 2))[..., :T].transpose(1, 2)
+        q, k, v = F.silu(qkv).chunk(3, dim=-1)
+        q = F.normalize(q.reshape(B, T, H, dh).transpose(1, 2), dim=-1)
+        k = F.normalize(k.reshape(B, T, H, dh).transpose(1, 2), dim=-1)
+        v = v.reshape(B, T, H, dh).transpose(1, 2)
+        g = torch.sigmoid(gl).view(B, T, self.n_gates, H).permute(2, 0, 3, 1)
     nu = g[3] if self.n_gates == 4 else None
     if not torch.compiler.is_compiling():
         self.last_gate_means = {

@@ -10,6 +10,10 @@ Two ops, matching the two layers of the reference they replace:
     train_ablation.py:142-187 (phases 1-3 of ``FastWeightMixer.forward``):
     o (B, H, T, dh) from q, k, v and the per-token gates.
 
+``mixer_prologue(u, conv_weight, conv_bias, gate_logits, n_heads)``
+    train_ablation.py:124-140 after the two projections: q, k, v (B, H, T, dh)
+    and the gates (nG, B, H, T).
+
 ``head_rmsnorm(o, weight, eps, out_dtype)``
     train_ablation.py:188-189 up to the output projection: the per-head
     RMSNorm of o written as (B, T, H * dh).
@@ -30,8 +34,8 @@ from torch import Tensor
 
 from ._lib import GMDN_PREC_FAST, GMDN_PREC_IEEE, check, lib
 
-__all__ = ["state_scan", "chunk_fast_weight", "head_rmsnorm", "GMDN_PREC_IEEE",
-           "GMDN_PREC_FAST", "ScanFunction"]
+__all__ = ["state_scan", "chunk_fast_weight", "head_rmsnorm", "mixer_prologue",
+           "GMDN_PREC_IEEE", "GMDN_PREC_FAST", "ScanFunction"]
 
 
 def _ptr(t: Optional[Tensor]):
@@ -401,3 +405,114 @@ def head_rmsnorm(o: Tensor, weight: Tensor, eps: Optional[float] = None,
     w = weight.float()   # differentiable; the gradient comes back in weight's dtype
     return torch.ops.gmdn.head_rmsnorm_fwd(_aligned(o), _aligned(w), e,
                                            out_dtype == torch.float32)
+
+
+# ---------------------------------------------------------------------------
+# mixer prologue: conv + SiLU + q/k L2 norm + head layout, gate sigmoids
+# ---------------------------------------------------------------------------
+
+@torch.library.custom_op("gmdn::mixer_prologue_fwd", mutates_args=())
+def _prologue_fwd(u: Tensor, conv_w: Tensor, conv_b: Tensor, gl: Tensor,
+                  n_heads: int) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    B, T, D3 = u.shape
+    H = n_heads
+    dh = D3 // 3 // H
+    nG = gl.shape[-1] // H
+    q = u.new_empty(B, H, T, dh)
+    k, v = torch.empty_like(q), torch.empty_like(q)
+    g = gl.new_empty(nG, B, H, T)
+    with torch.cuda.device(u.device):
+        rc = lib.gmdn_mixer_prologue_fwd(_ptr(u), _ptr(conv_w), _ptr(conv_b), _ptr(gl), _ptr(q),
+                                         _ptr(k), _ptr(v), _ptr(g), B, T, H, dh, nG,
+                                         _f32_flag(u, "u"), _stream(u))
+    check(rc, "gmdn_mixer_prologue_fwd")
+    return q, k, v, g
+
+
+@_prologue_fwd.register_fake
+def _(u, conv_w, conv_b, gl, n_heads):
+    B, T, D3 = u.shape
+    dh = D3 // 3 // n_heads
+    q = u.new_empty(B, n_heads, T, dh)
+    return q, torch.empty_like(q), torch.empty_like(q), gl.new_empty(gl.shape[-1] // n_heads, B,
+                                                                      n_heads, T)
+
+
+@torch.library.custom_op("gmdn::mixer_prologue_bwd", mutates_args=())
+def _prologue_bwd(u: Tensor, conv_w: Tensor, conv_b: Tensor, gl: Tensor, dq: Tensor, dk: Tensor,
+                  dv: Tensor, dg: Tensor, n_heads: int) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    B, T, D3 = u.shape
+    H = n_heads
+    dh = D3 // 3 // H
+    nG = gl.shape[-1] // H
+    du, dgl = torch.empty_like(u), torch.empty_like(gl)
+    dcw = torch.empty(D3, 1, 4, dtype=torch.float32, device=u.device)
+    dcb = torch.empty(D3, dtype=torch.float32, device=u.device)
+    with torch.cuda.device(u.device):
+        rc = lib.gmdn_mixer_prologue_bwd(_ptr(u), _ptr(conv_w), _ptr(conv_b), _ptr(gl), _ptr(dq),
+                                         _ptr(dk), _ptr(dv), _ptr(dg), _ptr(du), _ptr(dcw),
+                                         _ptr(dcb), _ptr(dgl), B, T, H, dh, nG,
+                                         _f32_flag(u, "u"), _stream(u))
+    check(rc, "gmdn_mixer_prologue_bwd")
+    return du, dcw, dcb, dgl
+
+
+@_prologue_bwd.register_fake
+def _(u, conv_w, conv_b, gl, dq, dk, dv, dg, n_heads):
+    D3 = u.shape[-1]
+    return (torch.empty_like(u), u.new_empty(D3, 1, 4, dtype=torch.float32),
+            u.new_empty(D3, dtype=torch.float32), torch.empty_like(gl))
+
+
+def _pro_setup(ctx, inputs, output):
+    u, conv_w, conv_b, gl, n_heads = inputs
+    ctx.save_for_backward(u, conv_w, conv_b, gl)
+    ctx.n_heads = n_heads
+
+
+def _pro_backward(ctx, dq, dk, dv, dg):
+    u, conv_w, conv_b, gl = ctx.saved_tensors
+    z = lambda t, like: torch.zeros_like(like) if t is None else _aligned(t.to(like.dtype))
+    B, T, D3 = u.shape
+    H = ctx.n_heads
+    dh = D3 // 3 // H
+    shape = u.new_empty(B, H, T, dh)
+    gshape = gl.new_empty(gl.shape[-1] // H, B, H, T)
+    du, dcw, dcb, dgl = torch.ops.gmdn.mixer_prologue_bwd(
+        u, conv_w, conv_b, gl, z(dq, shape), z(dk, shape), z(dv, shape), z(dg, gshape), H)
+    return du, dcw, dcb, dgl, None
+
+
+_prologue_fwd.register_autograd(_pro_backward, setup_context=_pro_setup)
+
+
+def mixer_prologue(u: Tensor, conv_weight: Tensor, conv_bias: Tensor, gate_logits: Tensor,
+                   n_heads: int) -> tuple[Tensor, Tensor, Tensor, Tensor]:
+    """The mixer prologue after the two projections (train_ablation.py:124-140).
+
+    u = self.qkv(x): (B, T, 3D); conv_weight (3D, 1, 4) and conv_bias (3D,) of
+    the depthwise causal Conv1d (kernel 4, padding 3); gate_logits =
+    self.gates(x): (B, T, nG * H).  Returns q, k (L2-normalised per head, eps
+    1e-12), v, all (B, H, T, dh), and the sigmoid gates (nG, B, H, T) (alpha,
+    beta, mu[, nu] = g[0], g[1], g[2][, g[3]]), all in u's dtype.  Computed in fp32; bf16 or fp32 I/O; dh 32, 64 or 128.
+    Differentiable in u, both conv parameters and gate_logits.
+    """
+    if u.dim() != 3 or gate_logits.dim() != 3:
+        raise ValueError("u must be (B, T, 3D) and gate_logits (B, T, nG*H)")
+    B, T, D3 = u.shape
+    if D3 % (3 * n_heads):
+        raise ValueError(f"3D = {D3} is not divisible by 3 * n_heads = {3 * n_heads}")
+    dh = D3 // 3 // n_heads
+    if dh not in (32, 64, 128):
+        raise ValueError(f"mixer_prologue supports dh 32, 64 or 128 (got {dh})")
+    if gate_logits.shape[:2] != (B, T) or gate_logits.shape[-1] % n_heads or \
+            gate_logits.shape[-1] // n_heads not in (3, 4):
+        raise ValueError(f"gate_logits must be (B, T, 3 or 4 * H), got {tuple(gate_logits.shape)}")
+    if tuple(conv_weight.shape) != (D3, 1, 4) or tuple(conv_bias.shape) != (D3,):
+        raise ValueError("conv must be depthwise with kernel 4: weight (3D, 1, 4), bias (3D,)")
+    _require_cuda("mixer_prologue", u, conv_weight, conv_bias, gate_logits)
+    _f32_flag(u, "u")
+    gl = gate_logits.to(u.dtype)
+    return torch.ops.gmdn.mixer_prologue_fwd(_aligned(u), _aligned(conv_weight.float()),
+                                             _aligned(conv_bias.float()), _aligned(gl),
+                                             int(n_heads))

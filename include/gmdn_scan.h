@@ -182,6 +182,25 @@ size_t gmdn_chunk_workspace_bytes_ex(int B, int H, int T, int dh, int chunk, int
  * failure reporting). */
 int gmdn_chunk_status(const void* workspace, void* stream);
 
+/* Mixer prologue, replaces train_ablation.py:124-140 after the two
+ * projections: qkv = silu(conv(u)) with u = self.qkv(x) (B, T, 3D) and conv
+ * the depthwise causal Conv1d (kernel 4, padding 3, first T outputs; weight
+ * (3D, 1, 4) and bias (3D) fp32); q and k L2-normalised per head over dh
+ * (F.normalize, eps 1e-12), v as is, all (B, H, T, dh); g = sigmoid(gl) with
+ * gl = self.gates(x) (B, T, nG*H) into (nG, B, H, T).  fp32 arithmetic, I/O in
+ * bf16 (io_f32 0) or fp32 (1); dh 32, 64 or 128; n_gates 3 or 4; B*T*3D
+ * below 2^31; tensor pointers 16-byte aligned.  The backward takes dq, dk, dv
+ * (B, H, T, dh) and dg (nG, B, H, T) and writes du (B, T, 3D), dgl
+ * (B, T, nG*H) and the fp32 conv gradients dconv_w (3D*4), dconv_b (3D)
+ * (overwritten, not accumulated). */
+int gmdn_mixer_prologue_fwd(const void* u, const float* conv_w, const float* conv_b,
+                            const void* gl, void* q, void* k, void* v, void* g, int B, int T,
+                            int H, int dh, int n_gates, int io_f32, void* stream);
+int gmdn_mixer_prologue_bwd(const void* u, const float* conv_w, const float* conv_b,
+                            const void* gl, const void* dq, const void* dk, const void* dv,
+                            const void* dg, void* du, float* dconv_w, float* dconv_b, void* dgl,
+                            int B, int T, int H, int dh, int n_gates, int io_f32, void* stream);
+
 /* Mixer epilogue, replaces train_ablation.py:188-189 up to the output
  * projection: `o = self.norm(o).to(x.dtype)` with norm = nn.RMSNorm(dh), then
  * `o.transpose(1, 2).reshape(B, T, D)`.  o (B, H, T, dh), weight (dh) fp32,

@@ -16,9 +16,11 @@ from .scan_oracle import (NS_COEF, EPS_NORM, EPS_ADAM, msign_square,
                           scan_backward)
 from .mixer_oracle import chunk_gate_scalars, token_weights, mixer_core_forward
 from .epilogue_oracle import head_rmsnorm
+from .prologue_oracle import mixer_prologue
 
 __all__ = [
     "NS_COEF", "EPS_NORM", "EPS_ADAM", "msign_square", "msign_square_vjp",
     "scan_forward", "scan_forward_all", "scan_backward",
     "chunk_gate_scalars", "token_weights", "mixer_core_forward", "head_rmsnorm",
+    "mixer_prologue",
 ]

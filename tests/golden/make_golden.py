@@ -218,12 +218,77 @@ def epilogue_cases(train_ablation):
     return cases
 
 
+def prologue_cases(train_ablation, fast_scan):
+    """train_ablation.py:124-140 inside the reference module's own forward: the
+    projections' outputs u = qkv(x) and gl = gates(x) and the conv parameters
+    are recorded with forward hooks, the outputs q, k (F.normalize), the SiLU
+    output (v part) and the sigmoid gates with the attribute proxies, and all
+    their gradients from a backward through the rest of the mixer."""
+    fast_scan.set_backend("eager")
+    cases = []
+    specs = [
+        # (name, inner, D, heads, T, chunk, B, dtype)
+        ("f64_delta_dh32", "delta", 64, 2, 64, 32, 1, torch.float64),
+        ("f32_adam_dh64", "adam", 128, 2, 64, 32, 2, torch.float32),
+        ("f32_delta_dh128", "delta", 256, 2, 64, 64, 1, torch.float32),
+    ]
+    real_F, real_torch = train_ablation.F, train_ablation.torch
+    try:
+        for idx, (name, inner, D, H, T, C, B, dt) in enumerate(specs):
+            torch.manual_seed(6000 + idx)
+            mixer = train_ablation.FastWeightMixer(D, H, inner, chunk=C, ns_steps=3).to(dt)
+            mixer.norm = torch.nn.Identity()
+            mixer.out = torch.nn.Identity()
+            rec = {}
+
+            def hook(name_):
+                def fn(_mod, _inp, out):
+                    out.retain_grad()
+                    rec[name_] = out
+                return fn
+            h1 = mixer.qkv.register_forward_hook(hook("u"))
+            h2 = mixer.gates.register_forward_hook(hook("gl"))
+            gen = torch.Generator().manual_seed(7000 + idx)
+            x = torch.randn(B, T, D, generator=gen, dtype=dt)
+            rf = _Recorder(real_F, ["normalize", "silu"])
+            rt = _Recorder(real_torch, ["sigmoid"])
+            train_ablation.F, train_ablation.torch = rf, rt
+            y = mixer(x)
+            train_ablation.F, train_ablation.torch = real_F, real_torch
+            h1.remove()
+            h2.remove()
+            dy = torch.randn(y.shape, generator=gen, dtype=dt)
+            (y * dy).sum().backward()
+            dh = D // H
+            q, k = rf.records["normalize"]
+            s = rf.records["silu"][0]
+            g = rt.records["sigmoid"][0]
+            nG = mixer.n_gates
+            v = s.chunk(3, dim=-1)[2].reshape(B, T, H, dh).transpose(1, 2)
+            dv = s.grad.chunk(3, dim=-1)[2].reshape(B, T, H, dh).transpose(1, 2)
+            cases.append(dict(
+                name=name, n_heads=H,
+                u=rec["u"].detach(), gl=rec["gl"].detach(),
+                conv_w=mixer.conv.weight.detach().clone(), conv_b=mixer.conv.bias.detach().clone(),
+                q=q.detach().contiguous(), k=k.detach().contiguous(), v=v.detach().contiguous(),
+                g=g.detach().view(B, T, nG, H).permute(2, 0, 3, 1).contiguous(),
+                dq=q.grad.contiguous(), dk=k.grad.contiguous(), dv=dv.contiguous(),
+                dg=g.grad.view(B, T, nG, H).permute(2, 0, 3, 1).contiguous(),
+                du=rec["u"].grad.detach(), dgl=rec["gl"].grad.detach(),
+                dconv_w=mixer.conv.weight.grad.detach().clone(),
+                dconv_b=mixer.conv.bias.grad.detach().clone(),
+            ))
+    finally:
+        train_ablation.F, train_ablation.torch = real_F, real_torch
+    return cases
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout")
     ap.add_argument("--out", default=HERE)
-    ap.add_argument("--which", default="all", choices=["all", "epilogue"],
-                    help="epilogue: write only epilogue.pt")
+    ap.add_argument("--which", default="all", choices=["all", "epilogue", "prologue"],
+                    help="epilogue / prologue: write only that fixture file")
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.ref))
     import fast_scan  # noqa: E402  (the reference's module)
@@ -231,6 +296,14 @@ def main():
 
     torch.set_num_threads(4)
     meta = dict(torch=str(torch.__version__), source="reference fast_scan.py / train_ablation.py, float64 CPU")
+    if args.which in ("all", "prologue"):
+        pro = prologue_cases(train_ablation, fast_scan)
+        torch.save(dict(meta=dict(torch=str(torch.__version__),
+                                  source="reference train_ablation.py:124-140 (its own forward), CPU"),
+                        cases=pro), os.path.join(args.out, "prologue.pt"))
+        print(f"wrote {len(pro)} prologue cases to {args.out}")
+        if args.which == "prologue":
+            return
     epi = epilogue_cases(train_ablation)
     torch.save(dict(meta=dict(torch=str(torch.__version__),
                               source="reference train_ablation.py:188-189 (its nn.RMSNorm), CPU"),

@@ -120,3 +120,25 @@ def test_epilogue_matches_reference(case):
     (y.double() * case["dy"].double()).sum().backward()
     assert _rel(o.grad, case["d_o"]) <= tol
     assert _rel(w.grad, case["dweight"]) <= max(tol, 1e-5)
+
+
+def _prologue_cases():
+    return torch.load(os.path.join(GOLD, "prologue.pt"), weights_only=False)["cases"]
+
+
+@pytest.mark.parametrize("case", _prologue_cases(), ids=lambda c: c["name"])
+def test_prologue_matches_reference(case):
+    """The prologue restatement against train_ablation.py:124-140 recorded in the
+    reference module's own forward: q, k, v, gates and every input gradient."""
+    tol = 1e-12 if case["u"].dtype == torch.float64 else 5e-6
+    u = case["u"].clone().requires_grad_(True)
+    gl = case["gl"].clone().requires_grad_(True)
+    w = case["conv_w"].clone().requires_grad_(True)
+    b = case["conv_b"].clone().requires_grad_(True)
+    q, k, v, g = oracle.mixer_prologue(u, w, b, gl, case["n_heads"])
+    for name, got in (("q", q), ("k", k), ("v", v), ("g", g)):
+        assert _rel(got, case[name]) <= tol, name
+    loss = sum((t * case["d" + n]).sum() for n, t in (("q", q), ("k", k), ("v", v), ("g", g)))
+    loss.backward()
+    for name, got in (("du", u.grad), ("dgl", gl.grad), ("dconv_w", w.grad), ("dconv_b", b.grad)):
+        assert _rel(got, case[name]) <= max(tol, 2e-5), name
