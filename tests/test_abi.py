@@ -141,3 +141,52 @@ def test_patch_reference_swaps_only_the_kernel_class():
     pkg.patch_reference(mod)
     assert mod.HAS_TRITON is True and mod.scan_eager is sentinel
     assert hasattr(mod._TritonScan, "apply")
+
+
+def _aligned_addr():
+    # a 16-byte aligned host address: the checks below return before any
+    # device access, so the pointer is never dereferenced
+    buf = (ctypes.c_char * 64)()
+    return buf, ctypes.c_void_p((ctypes.addressof(buf) + 15) // 16 * 16)
+
+
+def test_epilogue_and_prologue_reject_bad_arguments():
+    from importlib import import_module
+    lib = import_module("gmdn-gated-muon-deltanet_b200._lib").lib
+    _keep, p = _aligned_addr()
+    null = ctypes.c_void_p(None)
+    stream = ctypes.c_void_p(None)
+    # head_rmsnorm: unsupported dh, null pointer, misaligned pointer, negative size
+    assert lib.gmdn_head_rmsnorm_fwd(p, p, p, 1, 2, 8, 48, -1.0, 1, 1, stream) == 2
+    assert lib.gmdn_head_rmsnorm_fwd(p, null, p, 1, 2, 8, 64, -1.0, 1, 1, stream) == 1
+    bad = ctypes.c_void_p(p.value + 2)
+    assert lib.gmdn_head_rmsnorm_fwd(bad, p, p, 1, 2, 8, 64, -1.0, 1, 1, stream) == 1
+    assert lib.gmdn_head_rmsnorm_bwd(p, p, null, p, p, 1, 2, 8, 64, -1.0, 1, 1, stream) == 1
+    assert lib.gmdn_head_rmsnorm_fwd(p, p, p, -1, 2, 8, 64, -1.0, 1, 1, stream) == 1
+    # mixer_prologue: bad n_gates, unsupported dh, null pointer, too large
+    assert lib.gmdn_mixer_prologue_fwd(p, p, p, p, p, p, p, p, 1, 8, 2, 64, 5, 1, stream) == 1
+    assert lib.gmdn_mixer_prologue_fwd(p, p, p, p, p, p, p, p, 1, 8, 2, 48, 3, 1, stream) == 2
+    assert lib.gmdn_mixer_prologue_fwd(p, p, null, p, p, p, p, p, 1, 8, 2, 64, 3, 1, stream) == 1
+    assert lib.gmdn_mixer_prologue_bwd(p, p, p, p, p, p, p, p, p, p, p, null, 1, 8, 2, 64, 3, 1,
+                                       stream) == 1
+    assert lib.gmdn_mixer_prologue_fwd(p, p, p, p, p, p, p, p, 4096, 65536, 16, 128, 3, 0,
+                                       stream) == 2
+    assert b"2^31" in lib.gmdn_last_error_string()
+
+
+def test_epilogue_and_prologue_ops_validate_on_cpu():
+    pkg = load_pkg()
+    o = torch.zeros(1, 2, 8, 64)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        pkg.head_rmsnorm(o, torch.ones(64))
+    with pytest.raises(ValueError):
+        pkg.head_rmsnorm(o, torch.ones(32))
+    u = torch.zeros(1, 8, 3 * 2 * 64)
+    gl = torch.zeros(1, 8, 3 * 2)
+    w, b = torch.zeros(3 * 2 * 64, 1, 4), torch.zeros(3 * 2 * 64)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        pkg.mixer_prologue(u, w, b, gl, 2)
+    with pytest.raises(ValueError):
+        pkg.mixer_prologue(u, w, b, torch.zeros(1, 8, 5 * 2), 2)
+    with pytest.raises(ValueError):
+        pkg.mixer_prologue(u, torch.zeros(3 * 2 * 64, 1, 3), b, gl, 2)
