@@ -34,8 +34,8 @@ constexpr int kWarpsP = 8;       // warps per block (forward)
 constexpr int kWarpsB = 2;       // warps per block (backward: ~160 registers a thread, so
                                  // small blocks let six of them share an SM)
 constexpr float kNormEps = 1e-12f;
-constexpr int kPF = 4;           // rows a forward warp loads ahead of its arithmetic
-constexpr int kPB = 4;           // rows (and cotangent rows) a backward warp loads ahead
+constexpr int kPF = 2;           // rows a forward warp loads ahead of its arithmetic
+constexpr int kPB = 2;           // rows (and cotangent rows) a backward warp loads ahead
 
 __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
@@ -104,7 +104,7 @@ __device__ __forceinline__ Strip strip_of(int w, int H, int T) {
 }
 
 template <int VEC, typename TT>
-__global__ void __launch_bounds__(kWarpsP * 32)
+__global__ void __launch_bounds__(kWarpsP * 32, 4)   // 64 registers: 32 warps an SM
 prologue_fwd_kernel(const TT* __restrict__ u, const float* __restrict__ cw,
                     const float* __restrict__ cb, TT* __restrict__ q, TT* __restrict__ k,
                     TT* __restrict__ v, int B, int T, int H, int strips) {
