@@ -419,6 +419,66 @@ def run_prologue(args) -> None:
         "roofline": roof, "kernel_times": kernel_times}), flush=True)
 
 
+def run_scan(args) -> None:
+    """The scan-only drop-in (fast_state_scan / _TritonScan, fast_scan.py:334-414)
+    at config-1 shapes: fp32 U, K (B8 H16 N64 128x128), delta rule, forward +
+    backward per step through ``state_scan``, inputs resident in HBM.  Roofline:
+    the algorithmic HBM bytes of each launch (forward reads U, K and writes S,
+    1.61 GB; backward reads U, K, S, gS and writes dU, dK, 3.22 GB)."""
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    pkg = importlib.import_module(PKG_NAME)
+    L = importlib.import_module(PKG_NAME + "._lib")
+    B, H, N, dh = 8, 16, 64, 128
+    g = torch.Generator().manual_seed(0)
+    mk = lambda *sh, sc=1.0: (torch.randn(*sh, generator=g) * sc).to(device)
+    U = mk(B, H, N, dh, dh, sc=0.1).requires_grad_(True)
+    K = mk(B, H, N, dh, dh, sc=0.01).requires_grad_(True)
+    gate = lambda: torch.full((B, H, N), 0.9, device=device).requires_grad_(True)
+    a, b, m, n = gate(), gate(), gate(), gate()
+    gS = mk(B, H, N, dh, dh)
+
+    def step():
+        S = pkg.state_scan(U, K, a, b, m, n, 0, 5)
+        return torch.autograd.grad(S, (U, K, a, b, m, n), gS)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    L.prof_report()
+    L.prof_enable(True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    L.prof_enable(False)
+    kt = L.prof_report()
+    ms = e0.elapsed_time(e1)
+    mat = B * H * N * dh * dh * 4
+    work = {"scan_fwd_ieee": 3 * mat, "scan_bwd_ieee": 6 * mat}
+    peaks, kind = load_peaks()
+    kernel_times, roof = {}, None
+    for name, (tms, cnt) in kt.items():
+        kernel_times[name] = {"total_ms": tms, "launches": cnt, "avg_ms": tms / max(cnt, 1)}
+    if kt:
+        top = max(kt, key=lambda k: kt[k][0])
+        achieved = work.get(top, 0) / (kt[top][0] / kt[top][1] / 1e3) / 1e9
+        roof = {"kernel": top, "bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                "peak_source": ("measured (MEASURED_PEAKS.json hbm_gbs, copy)" if kind == "measured"
+                                else "fallback (6.65 TB/s)")}
+    print(json.dumps({
+        "metric": "scan-only tokens/s fwd+bwd (fast_state_scan, fp32 U/K), B8·H16·N64·d128 delta",
+        "value": B * N * 64 * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps,
+        "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "scan_config1", "l2": "inputs larger than L2 (U, K 537 MB each)"},
+        "roofline": roof, "kernel_times": kernel_times}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -431,8 +491,10 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="override B of the workload (small ncu captures)")
-    ap.add_argument("--workload", default="mixer", choices=["mixer", "epilogue", "prologue"],
-                    help="epilogue / prologue: time that part of the mixer alone (one GPU)")
+    ap.add_argument("--workload", default="mixer",
+                    choices=["mixer", "epilogue", "prologue", "scan"],
+                    help="epilogue / prologue: that part of the mixer alone; scan: the "
+                         "scan-only drop-in (fast_state_scan) on fp32 U, K; one GPU each")
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
                     help="weak: a full batch per rank; strong: the global batch split over ranks")
     args = ap.parse_args()
@@ -448,6 +510,9 @@ def main():
         return
     if args.workload == "prologue":
         run_prologue(args)
+        return
+    if args.workload == "scan":
+        run_scan(args)
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
