@@ -34,20 +34,21 @@ def _fro(x: torch.Tensor) -> torch.Tensor:
     return x.square().sum(dim=(-2, -1), keepdim=True).sqrt()
 
 
-def _ns_iter(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+def _ns_iter(x: torch.Tensor, mm=torch.matmul) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """One quintic NS step; returns (x_next, gram, poly) where gram = x x^T and
-    poly = c1*gram + c2*gram^2 (fast_scan.py:67-68)."""
+    poly = c1*gram + c2*gram^2 (fast_scan.py:67-68).  ``mm`` is the matrix
+    product (a rounding emulation may replace it)."""
     c0, c1, c2 = NS_COEF
-    gram = x @ x.transpose(-1, -2)
-    poly = c1 * gram + c2 * (gram @ gram)
-    return c0 * x + poly @ x, gram, poly
+    gram = mm(x, x.transpose(-1, -2))
+    poly = c1 * gram + c2 * mm(gram, gram)
+    return c0 * x + mm(poly, x), gram, poly
 
 
-def msign_square(M: torch.Tensor, ns: int) -> torch.Tensor:
+def msign_square(M: torch.Tensor, ns: int, mm=torch.matmul) -> torch.Tensor:
     """Frobenius-normalise, then ``ns`` NS steps (fast_scan.py:63-69)."""
     x = M / (_fro(M) + EPS_NORM)
     for _ in range(ns):
-        x, _, _ = _ns_iter(x)
+        x, _, _ = _ns_iter(x, mm)
     return x
 
 
@@ -83,20 +84,20 @@ def _gate(t: torch.Tensor, i: int) -> torch.Tensor:
     return t[:, :, i, None, None]
 
 
-def _step(rule: int, ns: int, S, M, V, Ui, Ki, ai, bi, mi, ni):
+def _step(rule: int, ns: int, S, M, V, Ui, Ki, ai, bi, mi, ni, mm=torch.matmul):
     """One chunk of the recurrence (fast_scan.py:82-94). Returns (S', M', V')."""
-    G = Ui - S @ Ki
+    G = Ui - mm(S, Ki)
     if rule == 0:
         return ai * S + G, M, V
     if rule == 1:
         M1 = mi * M + G
-        return ai * S + bi * msign_square(M1, ns), M1, V
+        return ai * S + bi * msign_square(M1, ns, mm), M1, V
     M1 = mi * M + (1 - mi) * G
     V1 = ni * V + (1 - ni) * G.square()
     return ai * S + bi * M1 / (V1.sqrt() + EPS_ADAM), M1, V1
 
 
-def scan_forward_all(U, K, a, b, m, n, rule: int, ns: int):
+def scan_forward_all(U, K, a, b, m, n, rule: int, ns: int, mm=torch.matmul):
     """Pre-update S, M, V for every chunk, each (B, H, N, dh, dh)."""
     if rule not in (0, 1, 2):
         raise ValueError(f"rule must be 0 (delta), 1 (muon) or 2 (adam), got {rule}")
@@ -110,13 +111,13 @@ def scan_forward_all(U, K, a, b, m, n, rule: int, ns: int):
         m_hist.append(M)
         v_hist.append(V)
         S, M, V = _step(rule, ns, S, M, V, U[:, :, i], K[:, :, i], _gate(a, i),
-                        _gate(b, i), _gate(m, i), _gate(n, i))
+                        _gate(b, i), _gate(m, i), _gate(n, i), mm)
     return (torch.stack(s_hist, 2), torch.stack(m_hist, 2), torch.stack(v_hist, 2))
 
 
-def scan_forward(U, K, a, b, m, n, rule: int, ns: int) -> torch.Tensor:
+def scan_forward(U, K, a, b, m, n, rule: int, ns: int, mm=torch.matmul) -> torch.Tensor:
     """Pre-update state stack (B, H, N, dh, dh); differentiable by autograd."""
-    return scan_forward_all(U, K, a, b, m, n, rule, ns)[0]
+    return scan_forward_all(U, K, a, b, m, n, rule, ns, mm)[0]
 
 
 def scan_final_state(U, K, a, b, m, n, rule: int, ns: int) -> torch.Tensor:

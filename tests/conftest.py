@@ -27,3 +27,16 @@ def load_pkg():
 @pytest.fixture(scope="session")
 def pkg():
     return load_pkg()
+
+
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    """List every parity case that passed only on a widened (conditioning-floor)
+    bound, so that none passes silently above the flat bar."""
+    import parity
+    if not parity.WIDENED:
+        return
+    tr = terminalreporter
+    tr.section("parity cases on a widened bound (fp32 adam / muon)")
+    for name, err, bound, e64, floor in parity.WIDENED:
+        tr.write_line(f"{name}: err {err:.3e} <= bound {bound:.3e} "
+                      f"(floor {floor:.3e}, kernel-vs-fp64 {e64:.3e})")

@@ -2,18 +2,22 @@
 
 For every output and gradient x of the kernel:
 
-    err(x, fp32 oracle) <= max(tol, 4 * floor)
+    err(x, fp32 oracle) <= bound
 
-with err = max|x - y| / max|y| (the metric of the reference's test.py:24-25),
-tol = 1e-4 for fp32 inputs and 2e-2 for bf16 inputs, and floor the
-conditioning floor of the problem: how far an fp32 evaluation of the
-reference recurrence lands from the fp64 one.  The floor is first taken from
-the plain fp32 oracle; where the kernel exceeds that bound, the floor becomes
-the envelope over that run and three more fp32 runs on inputs perturbed by
-half an ulp (every one an equally valid fp32 evaluation).  For adam (the
-1/(2 sqrt V) term, sign-like updates when V ~ 0) and deep muon NS chains that
-envelope spans several x, so a single sample is not a usable floor; for delta
-it stays far below tol and the bar is the plain 1e-4 / 2e-2.
+with err = max|x - y| / max|y| (the metric of the reference's test.py:24-25)
+and tol = 1e-4 for fp32 inputs, 2e-2 for bf16 inputs.
+
+* bf16 runs and fp32 delta runs: bound = tol, flat.  These are the bars the
+  port is held to; no conditioning allowance widens them.
+* fp32 adam and muon runs (``widen=True``): bound = max(tol, 4 * floor), where
+  floor is how far an fp32 evaluation of the reference recurrence lands from
+  the fp64 one: first the plain fp32 oracle, and, where the kernel exceeds
+  that bound, the envelope over that run and three more fp32 runs on inputs
+  perturbed by half an ulp (every one an equally valid fp32 evaluation).  For
+  adam (the 1/(2 sqrt V) term, sign-like updates when V ~ 0) and deep muon NS
+  chains that envelope spans several x, so a single sample is not a usable
+  floor.  Every case that passes only on a widened bound is recorded in
+  ``WIDENED`` and listed at the end of the pytest run.
 
 Gradients that are exactly zero in the oracle (gates a rule never reads) must
 be exactly zero in the kernel.
@@ -39,10 +43,16 @@ def perturb(t: torch.Tensor | None, seed: int) -> torch.Tensor | None:
     return (t.double() * (1.0 + noise)).to(t.dtype)
 
 
+# (case, err, widened bound, kernel-vs-fp64, floor) of every case that passed
+# only because the conditioning allowance widened its bound
+WIDENED: list = []
+
+
 def check_outputs(got: dict, ref_fn, tol: float, report: list | None = None,
-                  prefix: str = "") -> None:
+                  prefix: str = "", widen: bool = False) -> None:
     """got: name -> kernel tensor.  ref_fn(dtype, seed) -> name -> oracle tensor
-    (seed None = unperturbed inputs)."""
+    (seed None = unperturbed inputs).  widen: allow the conditioning floor
+    (fp32 adam / muon only)."""
     r64 = ref_fn(torch.float64, None)
     r32 = ref_fn(torch.float32, None)
     envelope = None
@@ -53,16 +63,19 @@ def check_outputs(got: dict, ref_fn, tol: float, report: list | None = None,
             assert x.abs().max().item() == 0.0, f"{prefix}{name}: expected exact zeros"
             continue
         assert torch.isfinite(x).all(), f"{prefix}{name}: non-finite values"
-        floor = rel(r32[name], y64)
         err = rel(x, r32[name])
-        bound = max(tol, 4.0 * floor)
-        if err > bound:
-            if envelope is None:
-                envelope = [ref_fn(torch.float32, s) for s in (1, 2, 3)]
-            floor = max([floor] + [rel(e[name], y64) for e in envelope])
+        bound, floor = tol, rel(r32[name], y64)
+        if err > tol and widen:
             bound = max(tol, 4.0 * floor)
+            if err > bound:
+                if envelope is None:
+                    envelope = [ref_fn(torch.float32, s) for s in (1, 2, 3)]
+                floor = max([floor] + [rel(e[name], y64) for e in envelope])
+                bound = max(tol, 4.0 * floor)
+            if err <= bound:
+                WIDENED.append((prefix + name, err, bound, rel(x, y64), floor))
         if report is not None:
             report.append((prefix + name, err, bound, rel(x, y64), floor))
         assert err <= bound, (f"{prefix}{name}: rel err {err:.3e} vs fp32 oracle > bound "
-                              f"{bound:.3e} (fp32-vs-fp64 envelope {floor:.3e}, "
+                              f"{bound:.3e} (fp32-vs-fp64 floor {floor:.3e}, "
                               f"kernel-vs-fp64 {rel(x, y64):.3e})")
