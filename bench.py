@@ -77,9 +77,12 @@ def kernel_work(name: str, cfg: dict) -> tuple[str, float, float]:
                           (2 x 2Cd^2) = 8.39 MFLOP (delta, adam)
       chunk_bwd1_muon_tc  the same + 8 ns mm: the msign VJP, 3 recomputed and 5
                           cotangent products per step (fp32 state)
-      chunk_bwd2_tc       bytes: q, k, v, dO in (4 C d 2), S_j and Gb_j in (2 d^2 2),
-                          gates in (2 C 4), dq, dk, dv out (3 C d 2), gate cotangents
-                          out (3 C 4) = 181,504 B; muon adds Gb_j lo (d^2 2) and mu (C 4)
+      chunk_bwd2_tc       bytes, the backward's algorithmic HBM traffic of the
+                          survey's definition: q, k, v, dO in (4 C d 2), dq, dk, dv out
+                          (3 C d 2), every gate of the rule in and its cotangent out
+                          (2 n_g C 4; n_g = 2 delta, 3 muon, 4 adam) = 115,712 B for delta.
+                          The S_j and Gb_j histories it also reads by design (2 d^2 2, muon
+                          + Gb_j lo d^2 2) are reported apart as design bytes.
     Newton-Schulz counts the algorithmic products once (the kernels spend three
     split-bf16 MMAs on each).  The exact-fp32 kernels count their products.
     """
@@ -102,9 +105,8 @@ def kernel_work(name: str, cfg: dict) -> tuple[str, float, float]:
         "scan_fwd_ieee": (0.0, mm * (1 + 3 * ns)),
         "scan_bwd_ieee": (0.0, mm * (3 + 8 * ns)),
     }
-    bw2 = 4 * C * d * 2 + 2 * d * d * 2 + 2 * C * 4 + 3 * C * d * 2 + 3 * C * 4
-    if cfg["rule"] == 1:
-        bw2 += d * d * 2 + C * 4
+    n_g = {0: 2, 1: 3, 2: 4}[cfg["rule"]]
+    bw2 = 7 * C * d * 2 + 2 * n_g * C * 4
     nbytes = {"chunk_bwd2_tc": bw2}
     if name in nbytes:
         return "hbm", float(nbytes[name] * units), 0.0
@@ -112,6 +114,51 @@ def kernel_work(name: str, cfg: dict) -> tuple[str, float, float]:
         f16, f32 = flops[name]
         return "tensor", float(f16 * units), float(f32 * units)
     return "tensor", float("nan"), 0.0
+
+
+def design_bytes(name: str, cfg: dict) -> float | None:
+    """Bytes a launch moves by design beyond the algorithmic ones: the state
+    histories the token-gradient kernel reads (S_j and Gb_j bf16, muon also the
+    bf16 remainder of Gb_j), per launch."""
+    if name != "chunk_bwd2_tc":
+        return None
+    B, H, T, d, C = cfg["B"], cfg["H"], cfg["T"], cfg["dh"], cfg["chunk"]
+    per = 2 * d * d * 2 + (d * d * 2 if cfg["rule"] == 1 else 0)
+    return float(kernel_work(name, cfg)[1] + per * B * H * (T // C))
+
+
+def step_work(cfg: dict) -> tuple[float, float, float]:
+    """(bf16 flops, fp32-state flops, HBM bytes) of one mixer-core fwd+bwd, the
+    survey's algorithmic definition: phases 1 and 3 forward 2C^2d + 4Cd^2 +
+    4C^2d + 2Cd^2 per chunk-head and twice that backward; the state products
+    4 mm(d^3) (muon + 11 ns mm); q, k, v, o, dO, dq, dk, dv (bf16) and three
+    passes over the rule's gates (fp32)."""
+    B, H, T, d, C = cfg["B"], cfg["H"], cfg["T"], cfg["dh"], cfg["chunk"]
+    units = B * H * (T // C)
+    fwd = 2 * C * C * d + 4 * C * d * d + 4 * C * C * d + 2 * C * d * d
+    mm = 2.0 * d ** 3
+    ns = cfg["ns"] if cfg["rule"] == 1 else 0
+    n_g = {0: 2, 1: 3, 2: 4}[cfg["rule"]]
+    nbytes = 11 * B * H * T * d * 2 + 3 * n_g * B * H * T * 4
+    return 3.0 * fwd * units, (4 + 11 * ns) * mm * units, float(nbytes)
+
+
+def step_roofline(cfg: dict, ms_per_step: float, peaks: dict, kind: str) -> dict:
+    """The whole step against the survey's roofline: the slower of the tensor
+    time (bf16 products at the bf16 peak, fp32-state products at TF32 = half
+    of it) and the HBM time, at the nominal peaks (2.25 PFLOP/s, 8 TB/s) and at
+    the measured ones."""
+    f16, f32, nbytes = step_work(cfg)
+    spec = max(f16 / 2.25e15 + f32 / 1.125e15, nbytes / 8e12)
+    bf = peaks["bf16_tflops"] * 1e12
+    meas = max(f16 / bf + f32 / (bf / 2), nbytes / (peaks["hbm_gbs"] * 1e9))
+    t = ms_per_step / 1e3
+    return {"spec_us": spec * 1e6, "measured_us": meas * 1e6, "step_us": t * 1e6,
+            "frac_spec": spec / t, "frac_measured": meas / t,
+            "bf16_gflop": f16 / 1e9, "fp32_state_gflop": f32 / 1e9, "hbm_gb": nbytes / 1e9,
+            "peaks": ("nominal 2.25 PFLOP/s bf16, 1.125 TF32, 8 TB/s; measured "
+                      + ("MEASURED_PEAKS.json" if kind == "measured" else "fallback")
+                      + " bf16 burst and HBM copy, TF32 = bf16 / 2 (assumed)")}
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -259,34 +306,75 @@ def cpu_baseline(pkg, cfg: dict, reps: int = 3) -> dict:
                        f"heads covered ({scfg['H']}/{cfg['H']})")}
 
 
+def load_workloads():
+    """The seeded input generator, loaded by file path: importing it as a
+    submodule would import the package, which maps libgmdn_b200.so, and the
+    reference arm must run without the product's native code."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "gmdn_b200_workloads", os.path.join(ROOT, PKG_NAME, "workloads.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def job_config(args, cfg: dict, world: int) -> dict:
+    """The `config` object of the JSON line, identical for both arms at the
+    same N (cfg is the workload as named, before any per-rank sharding)."""
+    B, H, T, dh, C = (cfg[k] for k in ("B", "H", "T", "dh", "chunk"))
+    strong = args.scaling == "strong"
+    per_rank = B * H // world if strong else B * H
+    return {"workload": args.config, "model": "mixer core fwd+bwd",
+            "global_batch": B * (1 if strong else world), "seq_len": T, "heads": H,
+            "head_dim": dh, "chunk": C, "rule": RULE_NAMES[cfg["rule"]], "ns": cfg["ns"],
+            "precision": args.precision,
+            "parallelism": f"dp{world} (B*H shards, {per_rank} sequences per rank)",
+            "l2": f"inputs larger than L2 (q,k,v,dO bf16 = "
+                  f"{4 * per_rank * T * dh * 2 / 1e6:.0f} MB per rank)"}
+
+
+def reference_sample_cfg(cfg: dict) -> dict:
+    """What one reference-arm step computes: the whole workload when one CPU
+    step of it takes seconds (delta: ~5-6 s at config 1 on 16 cores), else the
+    bounded CPU sample (adam / muon steps take minutes at full size)."""
+    return dict(cfg) if cfg["rule"] == 0 else cpu_sample_cfg(cfg)
+
+
 def run_reference_arm(args, cfg: dict) -> None:
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    pkg = importlib.import_module(PKG_NAME + ".workloads")
+    wl = load_workloads()
     import oracle as oracle_mod
 
     class _P:
-        workloads = pkg
+        workloads = wl
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    scfg = cpu_sample_cfg(cfg)
-    inp = pkg.mixer_inputs(scfg["B"], scfg["H"], scfg["T"], scfg["dh"], scfg["rule"],
-                           scfg["chunk"], seed=0)
+    scfg = reference_sample_cfg(cfg)
+    inp = wl.mixer_inputs(scfg["B"], scfg["H"], scfg["T"], scfg["dh"], scfg["rule"],
+                          scfg["chunk"], seed=0)
+    # activations as the GPU arm's kernels see them (bf16), computed in fp32
+    for n in ("q", "k", "v", "dO"):
+        setattr(inp, n, getattr(inp, n).to(torch.bfloat16).float())
     for _ in range(args.warmup):
         cpu_oracle_step(_P, oracle_mod, scfg, inp)
     times = [cpu_oracle_step(_P, oracle_mod, scfg, inp) for _ in range(args.steps)]
     total = sum(times)
     value = cpu_tokens(cfg, scfg) * args.steps / total
+    full = scfg == cfg
     sample = (f"oracle port of the reference eager path (fast_scan.py:72-95 + "
-              f"train_ablation.py:142-187), fp32 autograd, B{scfg['B']} H{scfg['H']} "
-              f"T{scfg['T']} dh{scfg['dh']} per step; tokens scaled by heads covered")
+              f"train_ablation.py:142-187), fp32 autograd on {threads} threads, "
+              f"B{scfg['B']} H{scfg['H']} T{scfg['T']} dh{scfg['dh']} per step" +
+              ("" if full else "; tokens scaled by heads covered"))
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.config, **cfg, "rule": RULE_NAMES[cfg["rule"]]},
+        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": job_config(args, cfg, world),
+        "workload_per_step": "full" if full else "sample",
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -687,9 +775,21 @@ def main():
             peak = peaks["hbm_gbs"]
             unit = "GB/s"
         tr = traffic.get(args.config, {}).get(top)
+        if tr is not None and args.batch:
+            tr = None   # the committed figure is for the named workload, not a resized one
         roofline = {"kernel": top, "bound": bound, "achieved": achieved, "peak": peak,
                     "unit": unit, "frac": achieved / peak, "traffic": tr,
                     "peak_source": source}
+        if bound == "hbm":
+            roofline["algorithmic_bytes"] = work
+            dbytes = design_bytes(top, cfg)
+            if dbytes is not None:
+                roofline["design_bytes"] = dbytes
+                roofline["design_frac"] = dbytes / avg_s / 1e9 / peak
+                if tr is not None:
+                    roofline["traffic_over_design"] = tr / dbytes
+            if tr is not None:
+                roofline["traffic_over_algorithmic"] = tr / work
 
     clocks.stop()
     clock_info = clocks.summary()
@@ -704,15 +804,10 @@ def main():
             "ms_per_step": elapsed / args.steps, "higher_is_better": True,
             "scaling": args.scaling,
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": args.config, "model": "mixer core fwd+bwd",
-                       "global_batch": B_global * (world if args.scaling == "weak" else 1),
-                       "seq_len": T, "heads": H_global, "head_dim": dh,
-                       "chunk": C, "rule": RULE_NAMES[rule], "ns": ns,
-                       "precision": args.precision,
-                       "parallelism": f"dp{world} (B*H shards, {B * H} sequences per rank)",
-                       "l2": f"inputs larger than L2 (q,k,v,dO bf16 = "
-                             f"{4 * B * H * T * dh * 2 / 1e6:.0f} MB per rank)"},
-            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "config": job_config(args, job_cfg, world),
+            "roofline": roofline,
+            "step_roofline": step_roofline(cfg, elapsed / args.steps, peaks, peak_kind),
+            "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": launches, "clocks": clock_info,
             "kernel_times": kernel_times,
         }

@@ -113,7 +113,11 @@ int gmdn_scan_bwd(const float* U, const float* K, const float* a, const float* b
  * before any stream capture.  Every call on a device shares the one array,
  * which keeps the last call's contents (the kernel clears what must start at
  * zero): calls that overlap on the GPU, from two streams or two host threads,
- * race on it and give wrong results, so keep them in order on one stream. */
+ * race on it and give wrong results, so keep them in order on one stream.
+ * The looked-up address lives as long as the device's context: a reset of the
+ * device (cudaDeviceReset, or a primary-context reset) unloads this library's
+ * device code and leaves the address stale, so do not call this entry point
+ * on a device after resetting it in the same process. */
 int gmdn_scan_fwd_noalloc(const float* U, const float* K, const float* a,
                           const float* b, const float* m, const float* n,
                           float* S_out, void* saved, int B, int H, int N, int dh,
