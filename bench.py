@@ -19,11 +19,14 @@ synthetic tensors with the distributions the baseline names (no dataset).
   cpu_baseline  the CPU oracle (a port of the reference's eager path) on a
             bounded sample of the same workload, rank 0, N=1 only.
 
-Multi-GPU (torchrun, one process per GPU): every rank runs its own config-1
-batch (weak scaling, no data-path collective); the timing barrier and the
-max-over-ranks reduction are the only NCCL traffic.  ``--scaling strong``
-instead splits the one global B*H batch into contiguous (b, h) shards, one per
-rank (16 sequences per GPU at N=8), and counts the global B*T tokens per step.
+Multi-GPU (torchrun, one process per GPU): the default ``--scaling strong``
+splits the one global B8*H16 batch the metric names into contiguous (b, h)
+shards, one per rank (16 sequences per GPU at N=8), and counts the global B*T
+tokens per step; ``--scaling weak`` runs a full config-1 batch per rank.  At
+N > 1 the other mode is timed briefly as well (``other_scaling``), and every
+rank's step and kernel times are gathered (``per_rank``).  The scan has no
+data-path collective: the timing barrier, the max-over-ranks reduction and the
+per-rank gather are the only NCCL traffic.
 
 ``--impl reference`` times the reference algorithm on the host cores instead
 (the oracle port; the reference itself is Python and is not present on the
@@ -510,9 +513,13 @@ def run_prologue(args) -> None:
 def run_scan(args) -> None:
     """The scan-only drop-in (fast_state_scan / _TritonScan, fast_scan.py:334-414)
     at config-1 shapes: fp32 U, K (B8 H16 N64 128x128), delta rule, forward +
-    backward per step through ``state_scan``, inputs resident in HBM.  Roofline:
-    the algorithmic HBM bytes of each launch (forward reads U, K and writes S,
-    1.61 GB; backward reads U, K, S, gS and writes dU, dK, 3.22 GB)."""
+    backward per step through ``state_scan`` at the reference's default
+    precision (tf32 -> GMDN_PREC_FAST: the tensor-core scan), inputs resident in
+    HBM.  Roofline: the algorithmic HBM bytes of each launch (forward reads U,
+    K and writes S, 1.61 GB; the backward's chain reads K, gS and writes dU, its
+    dK kernel reads S, dU and writes dK, 1.61 GB each; the exact backward reads
+    U, K, S, gS and writes dU, dK, 3.22 GB).  ``--precision ieee`` times the
+    exact kernels."""
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     pkg = importlib.import_module(PKG_NAME)
@@ -526,8 +533,10 @@ def run_scan(args) -> None:
     a, b, m, n = gate(), gate(), gate(), gate()
     gS = mk(B, H, N, dh, dh)
 
+    prec = pkg.GMDN_PREC_FAST if args.precision == "fast" else pkg.GMDN_PREC_IEEE
+
     def step():
-        S = pkg.state_scan(U, K, a, b, m, n, 0, 5)
+        S = pkg.state_scan(U, K, a, b, m, n, 0, 5, prec)
         return torch.autograd.grad(S, (U, K, a, b, m, n), gS)
 
     for _ in range(max(args.warmup, 3)):
@@ -546,7 +555,11 @@ def run_scan(args) -> None:
     kt = L.prof_report()
     ms = e0.elapsed_time(e1)
     mat = B * H * N * dh * dh * 4
-    work = {"scan_fwd_ieee": 3 * mat, "scan_bwd_ieee": 6 * mat}
+    # algorithmic HBM bytes per launch: forward U, K in and S out; exact
+    # backward U, K, S, gS in and dU, dK out; tensor-core backward: the chain
+    # reads K, gS and writes dU, then dK reads S, dU and writes dK
+    work = {"scan_fwd_ieee": 3 * mat, "scan_bwd_ieee": 6 * mat, "scan_fwd_tc": 3 * mat,
+            "scan_bwd_chain_tc": 3 * mat, "scan_bwd_dk_tc": 3 * mat}
     peaks, kind = load_peaks()
     kernel_times, roof = {}, None
     for name, (tms, cnt) in kt.items():
@@ -563,8 +576,49 @@ def run_scan(args) -> None:
         "value": B * N * 64 * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps,
         "higher_is_better": True, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "scan_config1", "l2": "inputs larger than L2 (U, K 537 MB each)"},
+        "config": {"workload": "scan_config1", "precision": args.precision,
+                   "l2": "inputs larger than L2 (U, K 537 MB each)"},
         "roofline": roof, "kernel_times": kernel_times}), flush=True)
+
+
+def time_config(pkg, L, name: str, prec: int, steps: int, warmup: int, peaks: dict,
+                peak_kind: str) -> dict:
+    """One GPU, another configuration of the baseline on the same box and
+    clocks: mixer-core fwd+bwd per step, inputs resident in HBM, CUDA events,
+    kernel times from the library's own per-launch events, and the step
+    against the survey's roofline."""
+    cfg = dict(CONFIGS[name])
+    B, H, T, dh, C, rule, ns = (cfg[k] for k in ("B", "H", "T", "dh", "chunk", "rule", "ns"))
+    dev = pkg.workloads.mixer_inputs(B, H, T, dh, rule, C, seed=0).to("cuda", torch.bfloat16)
+    leaves = [dev.q, dev.k, dev.v, dev.alpha, dev.beta, dev.mu] + ([dev.nu] if rule == 2 else [])
+    for t in leaves:
+        t.requires_grad_(True)
+
+    def step():
+        o = pkg.chunk_fast_weight(dev.q, dev.k, dev.v, dev.alpha, dev.beta, dev.mu,
+                                  dev.nu if rule == 2 else None, rule, ns, C, prec)
+        return torch.autograd.grad(o, leaves, dev.dO)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    L.prof_report()
+    L.prof_enable(True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    L.prof_enable(False)
+    kt = L.prof_report()
+    ms = e0.elapsed_time(e1) / steps
+    return {"config": name, "rule": RULE_NAMES[rule], "B": B, "H": H, "T": T, "ns": ns,
+            "ms_per_step": ms, "value": B * T / (ms / 1e3), "unit": "tokens/s", "steps": steps,
+            "step_roofline": step_roofline(cfg, ms, peaks, peak_kind),
+            "kernel_times": {k: {"avg_ms": v[0] / max(v[1], 1), "launches": v[1]}
+                             for k, v in kt.items()}}
 
 
 def main():
@@ -577,14 +631,18 @@ def main():
     ap.add_argument("--precision", default="fast", choices=["fast", "ieee"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-others", action="store_true",
+                    help="skip the one-GPU lines of configs 2, 3 and 3-long in the default run")
     ap.add_argument("--batch", type=int, default=None,
                     help="override B of the workload (small ncu captures)")
     ap.add_argument("--workload", default="mixer",
                     choices=["mixer", "epilogue", "prologue", "scan"],
                     help="epilogue / prologue: that part of the mixer alone; scan: the "
                          "scan-only drop-in (fast_state_scan) on fp32 U, K; one GPU each")
-    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"],
-                    help="weak: a full batch per rank; strong: the global batch split over ranks")
+    ap.add_argument("--scaling", default="strong", choices=["weak", "strong"],
+                    help="strong (default): the one global batch the metric names split into "
+                         "(b, h) shards over the ranks; weak: a full batch per rank.  At N > 1 "
+                         "the other mode is also timed briefly and reported as an extra key")
     args = ap.parse_args()
     cfg = dict(CONFIGS[args.config])
     if args.batch:
@@ -667,10 +725,62 @@ def main():
     kt = L.prof_report()
     launches = L.kernel_launches() - launches0
     elapsed = ev0.elapsed_time(ev1)  # ms
+    own_ms = elapsed
     barrier()
     elapsed = pkg.sharding.max_over_ranks(elapsed, device)
     tokens_per_step = B_global * T * (world if args.scaling == "weak" else 1)
     value = tokens_per_step * args.steps / (elapsed / 1e3)
+
+    # ---- per-rank step times and kernel times (names the limiting rank) ----
+    per_rank = None
+    mine = {"rank": rank, "ms_per_step": own_ms / args.steps,
+            "sequences": B * H,
+            "kernels_ms": {k: round(v[0] / max(v[1], 1), 5) for k, v in kt.items()}}
+    if dist is not None:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, mine)
+        per_rank = gathered
+    else:
+        per_rank = [mine]
+
+    # ---- the other scaling mode, briefly (N > 1): weak = a full batch per rank ----
+    other = None
+    if world > 1:
+        mode = "weak" if args.scaling == "strong" else "strong"
+        if mode == "weak":
+            oB, oH = B_global, H_global
+        else:
+            s0, s1 = pkg.sharding.shard_bh(B_global * H_global, rank, world)
+            oB, oH = 1, s1 - s0
+        oh = pkg.workloads.mixer_inputs(oB, oH, T, dh, rule, C, seed=100 + rank).to(
+            device, torch.bfloat16)
+        oleaves = [oh.q, oh.k, oh.v, oh.alpha, oh.beta, oh.mu] + ([oh.nu] if rule == 2 else [])
+        for t in oleaves:
+            t.requires_grad_(True)
+
+        def ostep():
+            o = pkg.chunk_fast_weight(oh.q, oh.k, oh.v, oh.alpha, oh.beta, oh.mu,
+                                      oh.nu if rule == 2 else None, rule, ns, C, prec)
+            return torch.autograd.grad(o, oleaves, oh.dO)
+
+        for _ in range(3):
+            ostep()
+        osteps = max(3, min(args.steps, 10))
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(osteps):
+            ostep()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        oms = pkg.sharding.max_over_ranks(e0.elapsed_time(e1), device)
+        otok = B_global * T * (world if mode == "weak" else 1)
+        other = {"scaling": mode, "value": otok * osteps / (oms / 1e3), "unit": "tokens/s",
+                 "ms_per_step": oms / osteps, "steps": osteps, "tokens_per_step": otok,
+                 "sequences_per_rank": oB * oH}
+        del oh, oleaves
 
     # ---- end to end through the public API from pinned host memory ----
     # Every step copies its inputs host->device and o plus every gradient
@@ -791,6 +901,12 @@ def main():
             if tr is not None:
                 roofline["traffic_over_algorithmic"] = tr / work
 
+    # ---- the other baseline configurations on the same box and clocks (one GPU) ----
+    other_configs = None
+    if world == 1 and args.config == "config1_delta" and not args.batch and not args.no_others:
+        other_configs = [time_config(pkg, L, name, prec, 5, 3, peaks, peak_kind)
+                         for name in ("config2_muon", "config3_adam", "config3_adam_long")]
+
     clocks.stop()
     clock_info = clocks.summary()
     cpu = None
@@ -809,7 +925,8 @@ def main():
             "step_roofline": step_roofline(cfg, elapsed / args.steps, peaks, peak_kind),
             "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": launches, "clocks": clock_info,
-            "kernel_times": kernel_times,
+            "kernel_times": kernel_times, "per_rank": per_rank, "other_scaling": other,
+            "other_configs": other_configs,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:

@@ -108,12 +108,15 @@ struct ChunkBufs {
 ChunkBufs carve_chunk(void* saved, void* ws, int BH, int N, int dh, int rule, int ns,
                       bool fast) {
   ChunkBufs b{};
-  const size_t per = mats(static_cast<size_t>(BH) * N, dh);
   const size_t sc = static_cast<size_t>(BH) * N;
   Carver cs(saved);
   Carver cw(ws);
   b.status = reinterpret_cast<uint32_t*>(cw.take(64));
   if (fast) {
+    // the tensor-core kernels keep every state as 128 x 128 (a dh-64 head is
+    // the leading 64 x 64 block, the rest zero)
+    dh = 128;
+    const size_t per = mats(static_cast<size_t>(BH) * N, dh);
     auto half_mats = [&](Carver& c) { return reinterpret_cast<uint16_t*>(c.take((per + 1) / 2)); };
     b.tc.status = b.status;
     b.tc.S_hist = half_mats(cs);
@@ -123,6 +126,7 @@ ChunkBufs carve_chunk(void* saved, void* ws, int BH, int N, int dh, int rule, in
       b.tc.Vp_hist = half_mats(cs);
     }
     if (rule == 1) {
+      b.tc.S_lo_hist = half_mats(cs);
       b.tc.M_hist = cs.take(per);
       b.tc.X_hist = reinterpret_cast<uint8_t*>(cs.take(per * static_cast<size_t>(ns)));
     }
@@ -140,6 +144,7 @@ ChunkBufs carve_chunk(void* saved, void* ws, int BH, int N, int dh, int rule, in
     b.ws_bytes = cw.used;
     return b;
   }
+  const size_t per = mats(static_cast<size_t>(BH) * N, dh);
   b.S = cs.take(per);
   b.M_hist = rule != 0 ? cs.take(per) : nullptr;
   b.V_hist = rule == 2 ? cs.take(per) : nullptr;
@@ -389,12 +394,16 @@ size_t gmdn_scan_saved_bytes(int B, int H, int N, int dh, int rule) {
   return carve_scan_saved(nullptr, B * H, N, dh, rule).bytes;
 }
 
+// The scan workspace: the device status word (first 256 bytes, read by
+// gmdn_chunk_status), then the exact-fp32 kernels' per-(b,h) scratch.
+constexpr size_t kScanStatusBytes = 256;
+
 size_t gmdn_scan_workspace_bytes(int B, int H, int N, int dh, int rule, int ns, int precision) {
   (void)N;
   (void)rule;
   (void)precision;
   if (B < 0 || H < 0 || !dh_ok(dh) || ns < 0) return 0;
-  return align_up(scan_scratch_floats(B * H, dh, ns) * sizeof(float));
+  return kScanStatusBytes + align_up(scan_scratch_floats(B * H, dh, ns) * sizeof(float));
 }
 
 int gmdn_scan_fwd(const float* U, const float* K, const float* a, const float* b,
@@ -415,10 +424,19 @@ int gmdn_scan_fwd(const float* U, const float* K, const float* a, const float* b
   gmdn::ScanArgs p{};
   p.U = U; p.K = K; p.a = a; p.b = b; p.m = m; p.n = n;
   p.S = S_out; p.M_hist = sv.M_hist; p.V_hist = sv.V_hist;
-  p.scratch = static_cast<float*>(workspace);
+  p.scratch = reinterpret_cast<float*>(static_cast<char*>(workspace) + kScanStatusBytes);
   p.BH = B * H; p.N = N; p.dh = dh; p.rule = rule; p.ns = ns;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // Both precisions run the exact-fp32 kernels for the phase-2-only scan.
+  uint32_t* status = static_cast<uint32_t*>(workspace);
+  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(uint32_t), st);
+  if (e != cudaSuccess) return cuda_fail(e, "status reset");
+  // GMDN_PREC_FAST, delta / adam at dh 128: the tensor-core scan (its bounded
+  // waits report through the status word); everything else runs the
+  // exact-fp32 kernels.
+  if (precision == GMDN_PREC_FAST && gmdn::scan_fwd_tc_supported(p)) {
+    GMDN_LAUNCH(gmdn::scan_fwd_tc(p, status, st), "scan_fwd_tc");
+    return GMDN_OK;
+  }
   GMDN_LAUNCH(gmdn::scan_fwd_ieee(p, st), "scan_fwd_ieee");
   return GMDN_OK;
 }
@@ -444,9 +462,19 @@ int gmdn_scan_bwd(const float* U, const float* K, const float* a, const float* b
   p.U = U; p.K = K; p.a = a; p.b = b; p.m = m; p.n = n;
   p.S = const_cast<float*>(S_all); p.M_hist = sv.M_hist; p.V_hist = sv.V_hist;
   p.gS = gS; p.dU = dU; p.dK = dK; p.da = da; p.db = db; p.dm = dm; p.dn = dn;
-  p.scratch = static_cast<float*>(workspace);
+  p.scratch = reinterpret_cast<float*>(static_cast<char*>(workspace) + kScanStatusBytes);
   p.BH = B * H; p.N = N; p.dh = dh; p.rule = rule; p.ns = ns;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint32_t* status = static_cast<uint32_t*>(workspace);
+  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(uint32_t), st);
+  if (e != cudaSuccess) return cuda_fail(e, "status reset");
+  // GMDN_PREC_FAST, delta at dh 128: the reverse chain on the tensor cores,
+  // then dK and da for every matrix
+  if (precision == GMDN_PREC_FAST && gmdn::scan_bwd_tc_supported(p)) {
+    GMDN_LAUNCH(gmdn::scan_bwd_chain_tc(p, status, st), "scan_bwd_chain_tc");
+    GMDN_LAUNCH(gmdn::scan_bwd_dk_tc(p, status, st), "scan_bwd_dk_tc");
+    return GMDN_OK;
+  }
   GMDN_LAUNCH(gmdn::scan_bwd_ieee(p, st), "scan_bwd_ieee");
   return GMDN_OK;
 }

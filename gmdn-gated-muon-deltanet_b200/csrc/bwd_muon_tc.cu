@@ -20,7 +20,7 @@
 // Gs by 1/den.
 //
 // Phase A, the chain step (as the delta kernel, with Gb_j for Sb_{j+1}):
-//   dE_j^T = Gb_j (w k_j)^T + dO_j^T A_j
+//   dE_j^T = (Gb_j k_j^T + dO_j^T A'_j) diag(w),  A' = A / w (w applied in the drain)
 //   Sb_j   = a_c Sb_{j+1} + dO_j^T q_j - dE_j^T k_j
 // and Gb_j (bf16) goes to the history for the token-gradient kernel.
 //
@@ -45,6 +45,10 @@ using namespace tc;
 constexpr int kC = 64;
 constexpr int kD = 128;
 constexpr int kThreadsMB = 448;
+// Token weights w_s = prod_{t>s} mu_t can underflow; A' = A / w and the dE^T
+// drain both use max(w, kMuonWFloor) (the error, (w_eff - w) Gb k^T, is below
+// 1e-28 |Gb k^T|).
+constexpr float kMuonWFloor = 1e-30f;
 constexpr uint32_t P64 = 8192;
 constexpr uint32_t P128 = 16384;
 
@@ -52,7 +56,7 @@ constexpr uint32_t P128 = 16384;
 constexpr uint32_t U_X = 0;          // X_k hi (32 KB), lo (32 KB)
 constexpr uint32_t U_Y = 65536;      // Y hi, lo
 constexpr uint32_t U_Z = 131072;     // G hi, lo
-constexpr uint32_t A_WK = 0;         // phase A, in X: w*k (16 KB)
+constexpr uint32_t A_WK = 0;         // phase A, in X: unused (16 KB)
 constexpr uint32_t A_AS = 16384;     //                A (8 KB)
 constexpr uint32_t A_DEH = 32768;    //                dE^T hi (16 KB)
 constexpr uint32_t A_DEL = 49152;    //                dE^T lo (16 KB)
@@ -81,6 +85,7 @@ static_assert(sizeof(BarsMB) <= 256, "barrier block");
 struct MuonBwArgs {
   const float *alpha, *beta, *mu;
   const uint16_t* S_hist;
+  const uint16_t* S_lo_hist;
   const float* M_hist;
   const uint8_t* X_hist;
   float* Mb_ws;
@@ -185,7 +190,7 @@ chunk_bwd1_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       const uint32_t y_h = smem_u32(sm + U_Y), y_l = y_h + 32768;
       const uint32_t z_h = smem_u32(sm + U_Z), z_l = z_h + 32768;
       const uint32_t q_s = smem_u32(sm + A_Q), k_s = smem_u32(sm + A_K), g_s = smem_u32(sm + A_G);
-      const uint32_t wk_s = smem_u32(sm + A_WK), as_s = smem_u32(sm + A_AS);
+      const uint32_t as_s = smem_u32(sm + A_AS);
       const uint32_t deh_s = smem_u32(sm + A_DEH), del_s = smem_u32(sm + A_DEL);
       constexpr uint32_t ID_KK = idesc_bf16(128, 128, false, false);
       constexpr uint32_t ID_KM = idesc_bf16(128, 128, false, true);
@@ -281,10 +286,10 @@ chunk_bwd1_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          mma_bf16_ts(tmem + R2_E, tmem + R3 + k * 8, desc_kmajor(wk_s, P64, k), ID_Y, k > 0);
+          mma_bf16_ts(tmem + R2_E, tmem + R3 + k * 8, desc_kmajor(k_s, P64, k), ID_Y, k > 0);
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          mma_bf16_ts(tmem + R2_E, tmem + R3 + 64 + k * 8, desc_kmajor(wk_s, P64, k), ID_Y, 1);
+          mma_bf16_ts(tmem + R2_E, tmem + R3 + 64 + k * 8, desc_kmajor(k_s, P64, k), ID_Y, 1);
         if (!wait_use(&bars->as_full, i, status, ab)) break;
         tc_fence_after();
 #pragma unroll
@@ -362,12 +367,18 @@ chunk_bwd1_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
       {
         const float* mi = args.M_hist;
         const uint4* srow = reinterpret_cast<const uint4*>(args.S_hist + (mj * kD + c) * kD + half * 64);
+        const uint4* slrow =
+            reinterpret_cast<const uint4*>(args.S_lo_hist + (mj * kD + c) * kD + half * 64);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          float m[16], s8[16];
+          float m[16], s8[16], sl8[16];
           ld_f16x4(reinterpret_cast<const float*>(slab_f32(const_cast<float*>(mi), static_cast<int>(mj), half, 4 * q, c)), m);
           unpack8(srow[2 * q], s8);
           unpack8(srow[2 * q + 1], s8 + 8);
+          unpack8(slrow[2 * q], sl8);
+          unpack8(slrow[2 * q + 1], sl8 + 8);
+#pragma unroll
+          for (int t = 0; t < 16; ++t) s8[t] += sl8[t];   // S_j to ~16 bits
 #pragma unroll
           for (int t = 0; t < 16; ++t) {
             red4[0] = fmaf(m[t], m[t], red4[0]);
@@ -631,20 +642,10 @@ chunk_bwd1_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         gate_w[2 * lane + 1] = expf(s - l0 - l1);
       }
       named_sync(1, 128);
-#pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        const int id = tb + 128 * m;
-        const uint32_t off = static_cast<uint32_t>(id) * 16u;
-        const float w = gate_w[(id & 511) >> 3];
-        const uint4 x = *reinterpret_cast<const uint4*>(sm + A_K + off);
-        uint4 y;
-        y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
-        y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
-        y.z = pack_bf16(bf16_lo(x.z) * w, bf16_hi(x.z) * w);
-        y.w = pack_bf16(bf16_lo(x.w) * w, bf16_hi(x.w) * w);
-        *reinterpret_cast<uint4*>(sm + A_WK + off) = y;
-      }
-      fence_async_smem();
+      // w is applied to the columns of dE^T in its drain (dE^T = (Gb k^T +
+      // dO^T A') diag(w), A' = A / w) instead of being multiplied into k: w k
+      // rounded to bf16 would break the cancellation in Gb (w k)^T against the
+      // forward's G, whose w k keeps ~16 bits
       mbar_arrive(&bars->wk_full);
       // A = tril(P) * beta
       if (!wait_use(&bars->p_full, i, status, ab)) break;
@@ -663,7 +664,8 @@ chunk_bwd1_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
 #pragma unroll
             for (int x = 0; x < 8; ++x) {
               const int sc = cc * 16 + h * 8 + x;
-              v8[x] = (sc <= t16) ? src[x] * gate_beta[sc] : 0.f;
+              v8[x] = (sc <= t16) ? src[x] * gate_beta[sc] / fmaxf(gate_w[sc], kMuonWFloor)
+                                  : 0.f;
             }
             st_row8(sm + A_AS, P64, t16, cc * 2 + h, v8);
           }
@@ -688,8 +690,9 @@ chunk_bwd1_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
           float hi[8], lo[8];
 #pragma unroll
           for (int x = 0; x < 8; ++x) {
-            hi[x] = __bfloat162float(__float2bfloat16_rn(src[x]));
-            lo[x] = src[x] - hi[x];
+            const float d = src[x] * fmaxf(gate_w[h * 8 + x], kMuonWFloor);
+            hi[x] = __bfloat162float(__float2bfloat16_rn(d));
+            lo[x] = d - hi[x];
           }
           st_row8(sm + A_DEH, P128, row, h, hi);
           st_row8(sm + A_DEL, P128, row, h, lo);
@@ -713,14 +716,15 @@ chunk_bwd1_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
 
 cudaError_t chunk_bwd1_muon_tc(const ChunkArgs& p, const TcBufs& b, int ns, cudaStream_t st) {
   if (!b.M_hist || (ns > 0 && !b.X_hist) || !b.M_ws || !b.dac || !b.dbc || !b.dmc || !b.dnc ||
-      !b.Gbar_lo_hist)
+      !b.Gbar_lo_hist || !b.S_lo_hist)
     return cudaErrorInvalidValue;
   CUtensorMap mq, mk, mg, mgb, mgbl;
   const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
   cudaError_t e;
-  if ((e = make_tmap_rows128(&mq, p.q, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mk, p.k, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mg, p.dO, rows, 64)) != cudaSuccess) return e;
+  const uint32_t w = static_cast<uint32_t>(p.dh);
+  if ((e = make_tmap_rows128(&mq, p.q, rows, 64, w)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mk, p.k, rows, 64, w)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mg, p.dO, rows, 64, w)) != cudaSuccess) return e;
   if ((e = make_tmap_rows128(&mgb, b.Gbar_hist, static_cast<uint64_t>(p.BH) * p.N * kD, 128)) !=
       cudaSuccess)
     return e;
@@ -732,6 +736,7 @@ cudaError_t chunk_bwd1_muon_tc(const ChunkArgs& p, const TcBufs& b, int ns, cuda
   a.beta = p.beta;
   a.mu = p.mu;
   a.S_hist = b.S_hist;
+  a.S_lo_hist = b.S_lo_hist;
   a.M_hist = b.M_hist;
   a.X_hist = b.X_hist;
   a.Mb_ws = b.M_ws;

@@ -66,7 +66,8 @@ struct BwArgs {
   float *dalpha, *dbeta, *dmu, *dnu;
   uint32_t* status;
   int N, T;
-  int tiles;   // bw2: B * H * N
+  int tiles;      // bw2: B * H * N
+  int store_hi;   // dh 128: store the upper 64 columns of dq, dk, dv (dh 64: zero padding)
 };
 
 // ===========================================================================
@@ -628,12 +629,16 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 // paired two per TMEM column range (lanes 0-15 / 16-31).
 
 constexpr int kThreads2 = 320;
+// Muon token weights w_s = prod_{t>s} mu_t can underflow; A' = A / w uses
+// max(w, kMuonWFloor), and the drain multiplies by the same value, so dE is
+// exact up to (w_eff - w) k Gb^T, below 1e-28 |k Gb^T|.
+constexpr float kMuonWFloor = 1e-30f;
 constexpr uint32_t B2_Q = 0, B2_K = 16384, B2_V = 32768, B2_G = 49152;
 constexpr uint32_t B2_ST0 = 65536;    // S_j and Gb_j, 2 panels x 128 rows each, in
 constexpr uint32_t B2_ST1 = 98304;    // these two tiles with roles swapped every tile
 constexpr uint32_t B2_AS = 131072;    // A bf16 [t][s]; then dk staging, panel 0
 constexpr uint32_t B2_E = 139264;     // E^T bf16 [c][s], 1 panel x 128 rows; then dq staging
-constexpr uint32_t B2_WK = 155648;    // muon: w * k; delta, adam: q of odd local tiles
+constexpr uint32_t B2_WK = 155648;    // delta, adam: q of odd local tiles (muon: unused)
 constexpr uint32_t B2_DE = 172032;    // dE bf16 [s][c] (= dv, stored from here)
 constexpr uint32_t B2_DP = 188416;    // dP bf16 [t][s]; then dk staging, panel 1
 constexpr uint32_t B2_I = 196608;     // identity
@@ -882,7 +887,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     if (lane == 0) {
       const uint32_t v_s = smem_u32(sm + B2_V), g_s = smem_u32(sm + B2_G);
       const uint32_t as_s = smem_u32(sm + B2_AS), e_s = smem_u32(sm + B2_E);
-      const uint32_t wk_s = smem_u32(sm + B2_WK), de_s = smem_u32(sm + B2_DE);
+      const uint32_t de_s = smem_u32(sm + B2_DE);
       const uint32_t dp_s = smem_u32(sm + B2_DP), id_s = smem_u32(sm + B2_I);
       constexpr uint32_t ID_P = idesc_bf16(64, 64, false, false);
       constexpr uint32_t ID_KM = idesc_bf16(64, 128, false, true);        // A K-major, B MN-major
@@ -944,7 +949,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         if (RULE == 1 && !wait_use(&bars->wk_full, i, status, ab)) break;
         if (RULE == 1 && !wait_use(&bars->lo_full, i, status, ab)) break;
         tc_fence_after();
-        // phase 2: dE = A^T dO + wk Gb^T;  dA = dO E^T;  dWk = E Gb
+        // phase 2: dE = diag(w) (A'^T dO + k Gb^T);  dA = dO E^T;  dWk = E Gb
         #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + T2_X2, desc_mnmajor(as_s, P64, k), desc_mnmajor(g_s, P64, k), ID_MM,
@@ -953,10 +958,10 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           const uint32_t sbl_s = smem_u32(sm + B2_DE);   // panels 32 KB apart (dE tile, B2_RED)
           #pragma unroll
           for (int k = 0; k < 8; ++k)
-            mma_bf16(tmem + T2_X2, desc_kmajor(wk_s, P64, k), desc_kmajor(sb_s, P128, k), ID_KK, 1);
+            mma_bf16(tmem + T2_X2, desc_kmajor(k_s, P64, k), desc_kmajor(sb_s, P128, k), ID_KK, 1);
           #pragma unroll
           for (int k = 0; k < 8; ++k)
-            mma_bf16(tmem + T2_X2, desc_kmajor(wk_s, P64, k), desc_kmajor(sbl_s, B2_RED - B2_DE, k),
+            mma_bf16(tmem + T2_X2, desc_kmajor(k_s, P64, k), desc_kmajor(sbl_s, B2_RED - B2_DE, k),
                      ID_KK, 1);
         }
         #pragma unroll
@@ -1118,21 +1123,9 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         named_sync(1, 256);
       }
       if constexpr (RULE == 1) {
-        // w * k, w = suffix product of mu (delta and adam apply w to the rows of dE)
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          const int id = tid + 256 * m;
-          const uint32_t off = static_cast<uint32_t>(id) * 16u;
-          const uint4 x = *reinterpret_cast<const uint4*>(sm + k_tile + off);
-          const float w = gw[(id & 511) >> 3];
-          uint4 y;
-          y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
-          y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
-          y.z = pack_bf16(bf16_lo(x.z) * w, bf16_hi(x.z) * w);
-          y.w = pack_bf16(bf16_lo(x.w) * w, bf16_hi(x.w) * w);
-          *reinterpret_cast<uint4*>(sm + B2_WK + off) = y;
-        }
-        fence_async_smem();
+        // w is ready for epilogues 1 and 2 (every rule applies w to the rows of dE
+        // in its drain instead of multiplying it into k: w k rounded to bf16 would
+        // break the cancellation in w k Gb^T, |Gb| ~ 50 against ~0.1)
         mbar_arrive_warp(&bars->wk_full);
       }
       if (warp == 0) {  // chunk decay product a_c = prod clamp(alpha)
@@ -1168,7 +1161,13 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 #pragma unroll
             for (int x = 0; x < 8; ++x) {
               const int sc = c0 + h * 8 + x;
-              v8[x] = (sc <= r16) ? (RULE == 0 ? p[h * 8 + x] : p[h * 8 + x] * gbeta[sc]) : 0.f;
+              // A' = tril(P) beta / w: delta (w = beta) tril(P); muon tril(P) beta / w
+              // (w floored, see kMuonWFloor); adam (w = 1) tril(P) beta
+              v8[x] = (sc <= r16) ? (RULE == 0   ? p[h * 8 + x]
+                                     : RULE == 1 ? p[h * 8 + x] * gbeta[sc] /
+                                                       fmaxf(gw[sc], kMuonWFloor)
+                                                 : p[h * 8 + x] * gbeta[sc])
+                                  : 0.f;
             }
             st_row8(sm + B2_AS, P64, r16, (c0 >> 3) + h, v8);
           }
@@ -1218,8 +1217,9 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       // ---- epilogue 2: dE -> bf16 (also dv), then dP = tril(dA) beta; dbeta pieces; dw
       if (!wait_use_w(&bars->ph2, i, status, ab)) break;
       tc_fence_after();
-      // X2: dE (lanes 0-15; delta: times beta_s), row s = r16, 64 columns
-      const float wde = RULE == 0 ? gbeta[r16] : 1.f;
+      // X2: dE (lanes 0-15; delta: times beta_s, muon: times w_s), row s = r16,
+      // 64 columns
+      const float wde = RULE == 0 ? gbeta[r16] : RULE == 1 ? fmaxf(gw[r16], kMuonWFloor) : 1.f;
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         const int c0 = half * 64 + cc * 16;
@@ -1227,7 +1227,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tmem_ld16(tmem + lb + T2_X2 + c0, x);
         tmem_ld_wait();
         if (!hi) {
-          if constexpr (RULE == 0) {
+          if constexpr (RULE != 2) {
 #pragma unroll
             for (int y = 0; y < 16; ++y) x[y] *= wde;
           }
@@ -1264,7 +1264,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       named_sync(1, 256);
       if (tid == 0) {   // dv = dE, straight from the dE tile
         tma_store_2d(&tm_dv, 0, static_cast<int>(tok), sm + B2_DE);
-        tma_store_2d(&tm_dv, 64, static_cast<int>(tok), sm + B2_DE + P64);
+        if (args.store_hi) tma_store_2d(&tm_dv, 64, static_cast<int>(tok), sm + B2_DE + P64);
         bulk_commit();
       }
       // dbeta's A part: column sums over t of tril(dA) * P, off the critical path
@@ -1383,9 +1383,9 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       named_sync(1, 256);
       if (tid == 0) {
         tma_store_2d(&tm_dq, 0, static_cast<int>(tok), sm + B2_E);
-        tma_store_2d(&tm_dq, 64, static_cast<int>(tok), sm + B2_E + P64);
+        if (args.store_hi) tma_store_2d(&tm_dq, 64, static_cast<int>(tok), sm + B2_E + P64);
         tma_store_2d(&tm_dk, 0, static_cast<int>(tok), sm + B2_AS);
-        tma_store_2d(&tm_dk, 64, static_cast<int>(tok), sm + B2_DP);
+        if (args.store_hi) tma_store_2d(&tm_dk, 64, static_cast<int>(tok), sm + B2_DP);
         bulk_commit();
       }
       if constexpr (RULE == 1) {
@@ -1444,6 +1444,7 @@ BwArgs bw_args(const ChunkArgs& p, const TcBufs& b) {
   a.status = b.status;
   a.N = p.N;
   a.T = p.T;
+  a.store_hi = p.dh == kD;
   return a;
 }
 
@@ -1486,9 +1487,10 @@ cudaError_t chunk_bwd1_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st) 
   CUtensorMap mq, mk, mg, msb;
   const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
   cudaError_t e;
-  if ((e = make_tmap_rows128(&mq, p.q, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mk, p.k, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mg, p.dO, rows, 64)) != cudaSuccess) return e;
+  const uint32_t w = static_cast<uint32_t>(p.dh);
+  if ((e = make_tmap_rows128(&mq, p.q, rows, 64, w)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mk, p.k, rows, 64, w)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mg, p.dO, rows, 64, w)) != cudaSuccess) return e;
   if ((e = make_tmap_rows128(&msb, b.Gbar_hist, static_cast<uint64_t>(p.BH) * p.N * kD, 128)) !=
       cudaSuccess)
     return e;
@@ -1509,7 +1511,8 @@ cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st) 
   const void* base[10] = {p.q, p.k, p.v, p.dO, b.S_hist, b.Gbar_hist, lo, p.dq, p.dk, p.dv};
   for (int i = 0; i < 10; ++i) {
     const bool hist = i >= 4 && i <= 6;
-    cudaError_t e = make_tmap_rows128(&m[i], base[i], hist ? srows : rows, hist ? 128 : 64);
+    cudaError_t e = make_tmap_rows128(&m[i], base[i], hist ? srows : rows, hist ? 128 : 64,
+                                      hist ? 128u : static_cast<uint32_t>(p.dh));
     if (e != cudaSuccess) return e;
   }
   const BwArgs a = bw_args(p, b);

@@ -19,6 +19,7 @@ namespace gmdn {
 struct TcBufs {
   uint32_t* status;       // device status word (workspace)
   uint16_t* S_hist;       // saved: S_j, bf16 row-major (every rule)
+  uint16_t* S_lo_hist;    // saved, muon: S_j - bf16(S_j), bf16 row-major
   uint16_t* G_hist;       // saved, adam: G_j, bf16 slab
   uint16_t* Mp_hist;      // saved, adam: pre-update M_j, bf16 slab
   uint16_t* Vp_hist;      // saved, adam: pre-update V_j, bf16 slab
@@ -33,7 +34,11 @@ struct TcBufs {
   float *dac, *dbc, *dmc, *dnc;  // workspace, adam: cotangents of a_c, b_c, mu_c, nu_c
 };
 
-// Fused mixer core forward (phases 1-3), delta and adam rules, dh 128,
+// True when the driver's cuTensorMapEncodeTiled could be resolved (every
+// tensor-core path needs it).
+bool tma_encode_available();
+
+// Fused mixer core forward (phases 1-3), delta and adam rules, dh 128 or 64,
 // chunk 64, bf16.
 bool chunk_fwd_tc_supported(const ChunkArgs& p);
 cudaError_t chunk_fwd_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st);
@@ -53,6 +58,17 @@ cudaError_t chunk_bwd1_muon_tc(const ChunkArgs& p, const TcBufs& b, int ns, cuda
 bool chunk_bwd_tc_supported(const ChunkArgs& p);
 cudaError_t chunk_bwd1_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st);
 cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st);
+
+// Phase-2 state scan on the tensor cores (scan_tc.cu): gmdn_scan_fwd with
+// GMDN_PREC_FAST, delta and adam, dh 128; split-bf16 products.  `status` is
+// the device status word (bounded waits).
+bool scan_fwd_tc_supported(const ScanArgs& p);
+cudaError_t scan_fwd_tc(const ScanArgs& p, uint32_t* status, cudaStream_t st);
+// Its backward, delta at dh 128: the reverse chain (dU) on the tensor cores,
+// then dK = -S^T dU and da = <dU, S> for every matrix in a second kernel.
+bool scan_bwd_tc_supported(const ScanArgs& p);
+cudaError_t scan_bwd_chain_tc(const ScanArgs& p, uint32_t* status, cudaStream_t st);
+cudaError_t scan_bwd_dk_tc(const ScanArgs& p, uint32_t* status, cudaStream_t st);
 
 // Mixer epilogue (epilogue.cu): per-head RMSNorm of o (B, H, T, dh) into
 // y (B, T, H*dh), and its backward (dw is zeroed, then accumulated); dh 32, 64
@@ -79,9 +95,12 @@ cudaError_t mixer_prologue_bwd(const void* u, const float* cw, const float* cb, 
 // mbarrier nothing arrives on gives up after limit_ns and sets bit 0 of *status.
 cudaError_t wait_timeout_selftest(uint32_t* status, uint64_t limit_ns, cudaStream_t st);
 
-// rows x 128 bf16 row-major matrix as a TMA map with 64 x box_rows boxes and
-// 128-byte swizzle.
+// rows x width bf16 row-major matrix (width 64 or 128) as a TMA map with
+// 64 x box_rows boxes and 128-byte swizzle.  With width 64 the box at column
+// 64 lies wholly outside the matrix and a load of it fills the shared-memory
+// panel with zeros: the dh-128 kernels read a dh-64 head as one whose upper
+// 64 features are zero.
 cudaError_t make_tmap_rows128(CUtensorMap* map, const void* base, uint64_t rows,
-                              uint32_t box_rows);
+                              uint32_t box_rows, uint32_t width = 128);
 
 }  // namespace gmdn

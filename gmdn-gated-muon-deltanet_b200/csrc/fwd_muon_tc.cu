@@ -1,10 +1,12 @@
-// Fused tensor-core forward of the mixer core, muon rule, dh = 128, C = 64.
+// Fused tensor-core forward of the mixer core, muon rule, dh = 128 (or 64,
+// as a dh-128 head with zero upper features, see fwd_tc.cu), C = 64.
 //
 // Same residual form of the chunk as the delta kernel (fwd_tc.cu): with
 // E_j = v_j - k_j S_j^T and token weights w_s = prod_{t>s} mu_t
 // (train_ablation.py:151-158),
 //
 //   G_j     = E_j^T (w k_j)                              (train_ablation.py:164-165)
+//             (E^T and w k both as bf16 hi + lo: hi.hi + lo.hi + hi.lo)
 //   o_j     = q_j S_j^T + A_j E_j                        (train_ablation.py:166-167, 186)
 //   M_{j+1} = mu_c M_j + G_j
 //   X       = msign(M_{j+1}): X_0 = M / (|M|_F + 1e-7), then ns quintic
@@ -23,7 +25,7 @@
 // The first step takes X_0 = M unnormalised and folds 1/den into the Gram
 // drain (1/den^2) and into P' (1/den).
 //
-// For the backward the kernel keeps S_j (bf16), M_{j+1} (fp32 slab) and the
+// For the backward the kernel keeps S_j (bf16 hi and lo), M_{j+1} (fp32 slab) and the
 // Newton-Schulz inputs X_0 (= M_{j+1} unnormalised), X_1 .. X_{ns-1} as the
 // split bf16 tiles the MMAs read, copied out with bulk stores while the
 // products run.
@@ -70,9 +72,10 @@ constexpr uint32_t M_EH = 131072;
 constexpr uint32_t M_EL = 147456;
 constexpr uint32_t M_WK = 163840;
 constexpr uint32_t M_OS = 180224;
-constexpr uint32_t M_GATE = 196608;  // beta[64], mu[64], w[64]
-constexpr uint32_t M_RED = 197376;   // per-warp partial sums [8]
-constexpr uint32_t M_BAR = 197632;
+constexpr uint32_t M_WKL = 196608;   // w*k bf16 remainder (16 KB), outside the Gram tiles
+constexpr uint32_t M_GATE = 212992;  // beta[64], mu[64], w[64]
+constexpr uint32_t M_RED = 213760;   // per-warp partial sums [8]
+constexpr uint32_t M_BAR = 214016;
 constexpr uint32_t M_SMEM = M_BAR + 256 + 1024;
 
 // TMEM columns
@@ -96,10 +99,12 @@ static_assert(sizeof(BarsM) <= 256, "barrier block");
 struct MuonArgs {
   const float *alpha, *beta, *mu;
   uint16_t* S_hist;
+  uint16_t* S_lo_hist;   // S_j - bf16(S_j), bf16
   float* M_hist;      // fp32 slab per chunk: M_{j+1}
   uint8_t* X_hist;    // per chunk ns slots of 64 KB: X_k hi tile, X_k lo tile
   uint32_t* status;
   int N, T, ns;
+  int store_hi;   // dh 128: store o's upper 64 columns (dh 64: they are the zero padding)
 };
 
 // Split x into bf16 hi + lo and store 8 values of row `row` at column group
@@ -131,7 +136,8 @@ __device__ __forceinline__ void tmem_split16(uint32_t th, uint32_t tl, const flo
 __global__ void __launch_bounds__(kThreadsM, 1)
 chunk_fwd_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                  const __grid_constant__ CUtensorMap tm_sh, MuonArgs args) {
+                  const __grid_constant__ CUtensorMap tm_sh, const __grid_constant__ CUtensorMap tm_sl,
+                  MuonArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
@@ -207,6 +213,7 @@ chunk_fwd_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
     if (lane == 0) {
       const uint32_t q_s = smem_u32(sm + M_Q), k_s = smem_u32(sm + M_K), v_s = smem_u32(sm + M_V);
       const uint32_t wk_s = smem_u32(sm + M_WK), as_s = smem_u32(sm + M_AS);
+      const uint32_t wkl_s = smem_u32(sm + M_WKL);
       const uint32_t eh_s = smem_u32(sm + M_EH), el_s = smem_u32(sm + M_EL);
       const uint32_t id_s = smem_u32(sm + M_I);
       const uint32_t xh_s = smem_u32(sm + M_XH), xl_s = smem_u32(sm + M_XL);
@@ -262,7 +269,7 @@ chunk_fwd_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16_ts(tmem + TM_O, tmem + TM_SH + k * 8, desc_kmajor(q_s, P64, k), ID_ES, k > 0);
-        // G(j) = E^T_hi wk + E^T_lo wk -> A1
+        // G(j) = E^T_hi wk_hi + E^T_lo wk_hi + E^T_hi wk_lo -> A1
         if (!wait_use(&bars->e_smem, j, status, ab)) break;
         if (!wait_use(&bars->wk_full, j, status, ab)) break;
         tc_fence_after();
@@ -272,6 +279,9 @@ chunk_fwd_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_bf16(tmem + TM_A1, desc_kmajor(el_s, P128, k), desc_mnmajor(wk_s, P64, k), ID_G, 1);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_bf16(tmem + TM_A1, desc_kmajor(eh_s, P128, k), desc_mnmajor(wkl_s, P64, k), ID_G, 1);
         mma_commit(&bars->g_full);
         // o2(j): o^T += E^T_hi A^T
 #pragma unroll
@@ -329,11 +339,12 @@ chunk_fwd_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         tmem_st16(tmem + lb + TM_SL + half * 32 + b * 16, zr);
       }
       tmem_st_wait();
-      uint4* g = reinterpret_cast<uint4*>(args.S_hist + (static_cast<size_t>(bh) * N) * kD * kD +
-                                          static_cast<size_t>(c) * kD + half * 64);
+      const size_t s0 = (static_cast<size_t>(bh) * N) * kD * kD + static_cast<size_t>(c) * kD + half * 64;
+      uint4* g = reinterpret_cast<uint4*>(args.S_hist + s0);
+      uint4* gl = reinterpret_cast<uint4*>(args.S_lo_hist + s0);
       const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) g[i] = z;
+      for (int i = 0; i < 8; ++i) g[i] = gl[i] = z;
     }
     tc_fence_before();
     mbar_arrive(&bars->s_full);
@@ -376,11 +387,20 @@ chunk_fwd_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       if (j + 1 < N) {
         if (tid == 0) bulk_wait_read0();   // X tile copies out have read the tile
         named_sync(2, 256);
+        // and its bf16 remainder through the X lo tile: the alpha cotangent
+        // <Sb_{j+1}, S_j> is a cancelling sum that bf16 S alone moves by ~2e-2
         uint8_t* panel = sm + M_XH + half * P128;
+        uint8_t* panel_lo = sm + M_XL + half * P128;
 #pragma unroll
         for (int q4 = 0; q4 < 8; ++q4) {
           const float* v = st + 8 * q4;
-          *reinterpret_cast<uint4*>(panel + sw128_chunk(c, q4)) = pack8(v);
+          const uint4 hi4 = pack8(v);
+          float lo8[8];
+          unpack8(hi4, lo8);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) lo8[t] = v[t] - lo8[t];
+          *reinterpret_cast<uint4*>(panel + sw128_chunk(c, q4)) = hi4;
+          *reinterpret_cast<uint4*>(panel_lo + sw128_chunk(c, q4)) = pack8(lo8);
         }
         fence_async_smem();
         named_sync(2, 256);
@@ -388,6 +408,8 @@ chunk_fwd_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
           const int srow = (bh * N + j + 1) * kD;
           tma_store_2d(&tm_sh, 0, srow, sm + M_XH);
           tma_store_2d(&tm_sh, 64, srow, sm + M_XH + P128);
+          tma_store_2d(&tm_sl, 0, srow, sm + M_XL);
+          tma_store_2d(&tm_sl, 64, srow, sm + M_XL + P128);
           bulk_commit();
         }
       }
@@ -548,12 +570,19 @@ chunk_fwd_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
         const uint32_t off = static_cast<uint32_t>(id) * 16u;
         const float w = gate_w[(id & 511) >> 3];
         const uint4 x = *reinterpret_cast<const uint4*>(sm + M_K + off);
-        uint4 y;
-        y.x = pack_bf16(bf16_lo(x.x) * w, bf16_hi(x.x) * w);
-        y.y = pack_bf16(bf16_lo(x.y) * w, bf16_hi(x.y) * w);
-        y.z = pack_bf16(bf16_lo(x.z) * w, bf16_hi(x.z) * w);
-        y.w = pack_bf16(bf16_lo(x.w) * w, bf16_hi(x.w) * w);
-        *reinterpret_cast<uint4*>(sm + M_WK + off) = y;
+        // w k as bf16 hi + lo: the muon weights are long products of gates,
+        // and a single bf16 rounding of w k in G perturbs the state enough to
+        // move the mu cotangent (a cancelling sum over the chunk) by ~3e-2
+        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+        uint32_t yh[4], yl[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = bf16_lo(xs[e]) * w, p1 = bf16_hi(xs[e]) * w;
+          yh[e] = pack_bf16(p0, p1);
+          yl[e] = pack_bf16(p0 - bf16_lo(yh[e]), p1 - bf16_hi(yh[e]));
+        }
+        *reinterpret_cast<uint4*>(sm + M_WK + off) = make_uint4(yh[0], yh[1], yh[2], yh[3]);
+        *reinterpret_cast<uint4*>(sm + M_WKL + off) = make_uint4(yl[0], yl[1], yl[2], yl[3]);
       }
       fence_async_smem();
       mbar_arrive(&bars->wk_full);
@@ -648,7 +677,7 @@ chunk_fwd_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
       if (tb == 0) {
         const int orow = static_cast<int>(tok0) + j * kC;
         tma_store_2d(&tm_o, 0, orow, sm + M_OS);
-        tma_store_2d(&tm_o, 64, orow, sm + M_OS + P64);
+        if (args.store_hi) tma_store_2d(&tm_o, 64, orow, sm + M_OS + P64);
         bulk_commit();
         bulk_wait_read0();          // the staging tile is free for the Gram tiles
         mbar_arrive(&bars->os_free);
@@ -671,26 +700,34 @@ chunk_fwd_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_constan
 }  // namespace
 
 bool chunk_fwd_muon_tc_supported(const ChunkArgs& p) {
-  return p.rule == 1 && p.dh == kD && p.C == kC && !p.io_f32 && p.N >= 1;
+  return p.rule == 1 && (p.dh == kD || p.dh == 64) && p.C == kC && !p.io_f32 && p.N >= 1 &&
+         tma_encode_available();
 }
 
 cudaError_t chunk_fwd_muon_tc(const ChunkArgs& p, const TcBufs& b, int ns, cudaStream_t st) {
   if (!b.M_hist || (ns > 0 && !b.X_hist)) return cudaErrorInvalidValue;
-  CUtensorMap mq, mk, mv, mo, msh;
+  if (!b.S_lo_hist) return cudaErrorInvalidValue;
+  CUtensorMap mq, mk, mv, mo, msh, msl;
   const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
   cudaError_t e;
   if ((e = make_tmap_rows128(&msh, b.S_hist, static_cast<uint64_t>(p.BH) * p.N * kD, 128)) !=
       cudaSuccess)
     return e;
-  if ((e = make_tmap_rows128(&mq, p.q, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mk, p.k, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mv, p.v, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mo, p.o, rows, 64)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&msl, b.S_lo_hist, static_cast<uint64_t>(p.BH) * p.N * kD, 128)) !=
+      cudaSuccess)
+    return e;
+  const uint32_t w = static_cast<uint32_t>(p.dh);
+  if ((e = make_tmap_rows128(&mq, p.q, rows, 64, w)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mk, p.k, rows, 64, w)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mv, p.v, rows, 64, w)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mo, p.o, rows, 64, w)) != cudaSuccess) return e;
   MuonArgs a{};
+  a.store_hi = p.dh == kD;
   a.alpha = p.alpha;
   a.beta = p.beta;
   a.mu = p.mu;
   a.S_hist = b.S_hist;
+  a.S_lo_hist = b.S_lo_hist;
   a.M_hist = b.M_hist;
   a.X_hist = b.X_hist;
   a.status = b.status;
@@ -699,7 +736,7 @@ cudaError_t chunk_fwd_muon_tc(const ChunkArgs& p, const TcBufs& b, int ns, cudaS
   a.ns = ns;
   e = cudaFuncSetAttribute(chunk_fwd_tc_muon, cudaFuncAttributeMaxDynamicSharedMemorySize, M_SMEM);
   if (e != cudaSuccess) return e;
-  chunk_fwd_tc_muon<<<p.BH, kThreadsM, M_SMEM, st>>>(mq, mk, mv, mo, msh, a);
+  chunk_fwd_tc_muon<<<p.BH, kThreadsM, M_SMEM, st>>>(mq, mk, mv, mo, msh, msl, a);
   return cudaGetLastError();
 }
 

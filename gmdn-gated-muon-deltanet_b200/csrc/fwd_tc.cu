@@ -1,5 +1,8 @@
 // Fused tensor-core forward of the mixer core, delta and adam rules,
-// dh = 128, C = 64.
+// dh = 128 (or 64), C = 64.  A dh-64 head runs as a dh-128 one whose upper 64
+// features are zero: its TMA maps are 64 columns wide, so the load of the
+// upper panel fills shared memory with zeros, and the store of o's upper panel
+// is skipped.  The state then stays zero outside its leading 64 x 64 block.
 //
 // One CTA per (batch, head) walks the N chunks in order.  The chunk update
 // of the reference (fast_scan.py:82-85 on the products of
@@ -98,6 +101,7 @@ struct FwdArgs {
   float *M_ws, *V_ws;                    // adam
   uint32_t* status;
   int N, T;
+  int store_hi;   // dh 128: store o's upper 64 columns (dh 64: they are the zero padding)
 };
 
 template <int RULE>
@@ -540,7 +544,7 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       if (tb == 0) {
         const int orow = static_cast<int>(tok0) + j * kC;
         tma_store_2d(&tm_o, 0, orow, sm + OFF_OS);
-        tma_store_2d(&tm_o, 64, orow, sm + OFF_OS + P64);
+        if (args.store_hi) tma_store_2d(&tm_o, 64, orow, sm + OFF_OS + P64);
         bulk_commit();
       }
     }
@@ -580,13 +584,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace
 
-// rows x 128 bf16 matrix, 64 x 64 boxes, 128-byte swizzle.
+// rows x width bf16 matrix, 64 x box_rows boxes, 128-byte swizzle.
 cudaError_t make_tmap_rows128(CUtensorMap* map, const void* base, uint64_t rows,
-                              uint32_t box_rows) {
+                              uint32_t box_rows, uint32_t width) {
   auto fn = encode_fn();
   if (!fn) return cudaErrorNotSupported;
-  cuuint64_t dims[2] = {128, rows};
-  cuuint64_t strides[1] = {256};
+  if (width != 64 && width != 128) return cudaErrorInvalidValue;
+  cuuint64_t dims[2] = {width, rows};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(width) * 2};
   cuuint32_t box[2] = {64, box_rows};
   cuuint32_t es[2] = {1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
@@ -595,9 +600,11 @@ cudaError_t make_tmap_rows128(CUtensorMap* map, const void* base, uint64_t rows,
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+bool tma_encode_available() { return encode_fn() != nullptr; }
+
 bool chunk_fwd_tc_supported(const ChunkArgs& p) {
-  return (p.rule == 0 || p.rule == 2) && p.dh == kD && p.C == kC && !p.io_f32 && p.N >= 1 &&
-         encode_fn();
+  return (p.rule == 0 || p.rule == 2) && (p.dh == kD || p.dh == 64) && p.C == kC && !p.io_f32 &&
+         p.N >= 1 && encode_fn();
 }
 
 template <int RULE>
@@ -618,11 +625,13 @@ cudaError_t chunk_fwd_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st) {
   if ((e = make_tmap_rows128(&msh, b.S_hist, static_cast<uint64_t>(p.BH) * p.N * kD, 128)) !=
       cudaSuccess)
     return e;
-  if ((e = make_tmap_rows128(&mq, p.q, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mk, p.k, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mv, p.v, rows, 64)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&mo, p.o, rows, 64)) != cudaSuccess) return e;
+  const uint32_t w = static_cast<uint32_t>(p.dh);
+  if ((e = make_tmap_rows128(&mq, p.q, rows, 64, w)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mk, p.k, rows, 64, w)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mv, p.v, rows, 64, w)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&mo, p.o, rows, 64, w)) != cudaSuccess) return e;
   FwdArgs a{};
+  a.store_hi = p.dh == kD;
   a.beta = p.beta;
   a.alpha = p.alpha;
   a.mu = p.mu;

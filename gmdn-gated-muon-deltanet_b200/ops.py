@@ -85,6 +85,8 @@ def _state_scan_fwd(U: Tensor, K: Tensor, a: Tensor, b: Tensor, m: Tensor, n: Te
                                _ptr(saved), _ptr(ws), ws_bytes, B, H, N, dh, rule, ns,
                                precision, _stream(U))
     check(rc, "gmdn_scan_fwd")
+    if S.numel():
+        _check_status(ws, "gmdn_scan_fwd (device)")
     return S, saved
 
 
@@ -110,6 +112,8 @@ def _state_scan_bwd(U: Tensor, K: Tensor, a: Tensor, b: Tensor, m: Tensor, n: Te
                                _ptr(dm), _ptr(dn), _ptr(ws), ws_bytes, B, H, N, dh, rule, ns,
                                precision, _stream(U))
     check(rc, "gmdn_scan_bwd")
+    if dU.numel():
+        _check_status(ws, "gmdn_scan_bwd (device)")
     return dU, dK, da, db, dm, dn
 
 

@@ -64,12 +64,17 @@ const char* gmdn_last_error_string(void);
  * fast_scan.py:367-368 allocates). */
 size_t gmdn_scan_saved_bytes(int B, int H, int N, int dh, int rule);
 
-/* Scratch bytes for gmdn_scan_fwd / gmdn_scan_bwd. */
+/* Scratch bytes for gmdn_scan_fwd / gmdn_scan_bwd.  The first 256 bytes hold
+ * the device status word that gmdn_chunk_status reads after a call. */
 size_t gmdn_scan_workspace_bytes(int B, int H, int N, int dh, int rule, int ns,
                                  int precision);
 
 /* Forward: S_out <- pre-update states.  Replaces _TritonScan.forward
- * (fast_scan.py:360-377) and _scan_fwd_kernel (fast_scan.py:206-248). */
+ * (fast_scan.py:360-377) and _scan_fwd_kernel (fast_scan.py:206-248).
+ * precision GMDN_PREC_FAST (the reference's tf32 default) with rule 0 (delta)
+ * at dh 128 runs the tensor-core scan (split-bf16 products, ~16 significant
+ * bits per operand, within 1e-4 of the fp32 recurrence); every other case, and
+ * GMDN_PREC_IEEE, runs exact fp32 FMAs.  gmdn_scan_bwd follows the same rule. */
 int gmdn_scan_fwd(const float* U, const float* K, const float* a, const float* b,
                   const float* m, const float* n, float* S_out, void* saved,
                   void* workspace, size_t workspace_bytes, int B, int H, int N,
@@ -91,10 +96,11 @@ int gmdn_scan_bwd(const float* U, const float* K, const float* a, const float* b
  * by every GPU that loads this library until the process exits. */
 #define GMDN_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 
-/* gmdn_scan_fwd without a workspace: same arguments, results and precision,
- * but its scratch is a fixed device array inside this library, so the call
- * allocates nothing.  No counterpart in the reference (its Triton wrapper
- * allocates with torch, fast_scan.py:366-368).
+/* gmdn_scan_fwd without a workspace: same arguments and results, but its
+ * scratch is a fixed device array inside this library, so the call allocates
+ * nothing.  It always runs the exact-fp32 scan (the kernel that needs the
+ * scratch), for either `precision`.  No counterpart in the reference (its
+ * Triton wrapper allocates with torch, fast_scan.py:366-368).
  *
  * For callers that cannot allocate device memory: a runtime that owns every
  * device buffer and hands a foreign call only its operands and results (a
@@ -180,9 +186,9 @@ size_t gmdn_chunk_saved_bytes_ex(int B, int H, int T, int dh, int chunk, int rul
 size_t gmdn_chunk_workspace_bytes_ex(int B, int H, int T, int dh, int chunk, int rule,
                                      int ns, int precision, int io_f32);
 
-/* Reads the device status word the last chunk call on this workspace left
- * (synchronises `stream`): GMDN_OK, or GMDN_ERR_DEVICE when a kernel gave up
- * a bounded wait.  No reference counterpart (the reference has no device-side
+/* Reads the device status word the last chunk or scan call on this workspace
+ * left (synchronises `stream`): GMDN_OK, or GMDN_ERR_DEVICE when a kernel gave
+ * up a bounded wait.  No reference counterpart (the reference has no device-side
  * failure reporting). */
 int gmdn_chunk_status(const void* workspace, void* stream);
 

@@ -147,3 +147,50 @@ def test_empty_chunk_axis():
     g = torch.zeros(2, 3, 0, device="cuda")
     S = pkg.state_scan(U, U, g, g, g, g, 1, 3)
     assert S.shape == (2, 3, 0, 16, 16)
+
+
+def _launched(pkg, fn):
+    L = pkg._lib
+    L.prof_report()
+    L.prof_enable(True)
+    try:
+        fn()
+        torch.cuda.synchronize()
+    finally:
+        L.prof_enable(False)
+    return set(L.prof_report())
+
+
+@pytest.mark.parametrize("rule,ns", [(0, 3)])
+@pytest.mark.parametrize("N", [1, 2, 9, 64])
+def test_tensor_core_scan(rule, N, ns):
+    """GMDN_PREC_FAST at dh 128, delta: the forward runs scan_fwd_tc, the
+    split-bf16 tcgen05 scan, and the backward its reverse chain and the dK / da
+    kernel on the tensor cores; states and every gradient against the oracle
+    at the fp32 bar, on the reference fixture's input family (test.py:28-38)."""
+    pkg = load_pkg()
+    base = pkg.workloads.scan_inputs(2, 3, N, 128, C=64, seed=500 + 10 * rule + N)
+    gS = torch.randn(base[0].shape, generator=torch.Generator().manual_seed(5))
+    names = _launched(pkg, lambda: run_kernel(pkg, base, gS, rule, ns, pkg.GMDN_PREC_FAST))
+    assert "scan_fwd_tc" in names, names
+    if rule == 0:
+        assert {"scan_bwd_chain_tc", "scan_bwd_dk_tc"} <= names, names
+    S, g = run_kernel(pkg, base, gS, rule, ns, pkg.GMDN_PREC_FAST)
+    check_outputs(dict(zip(["S"] + NAMES, [S] + g)), scan_ref_fn(base, gS, rule, ns), TOL_FP32,
+                  widen=rule != 0)
+
+
+@pytest.mark.parametrize("rule,ns", [(0, 3)])
+def test_tensor_core_scan_config1_slices(rule, ns):
+    """Config-1 scan size (B8 H16 N64 dh128) on the tensor-core scan: slices
+    against the oracle on the same slice."""
+    pkg = load_pkg()
+    B, H, N, dh = 8, 16, 64, 128
+    base = pkg.workloads.scan_inputs(B, H, N, dh, C=64, seed=21 + rule)
+    gS = torch.randn(base[0].shape, generator=torch.Generator().manual_seed(4))
+    S, g = run_kernel(pkg, base, gS, rule, ns, pkg.GMDN_PREC_FAST)
+    for (b, h) in ((0, 0), (7, 15)):
+        sl = [t[b:b + 1, h:h + 1] for t in base]
+        got = dict(zip(["S"] + NAMES, [S[b:b + 1, h:h + 1]] + [a[b:b + 1, h:h + 1] for a in g]))
+        check_outputs(got, scan_ref_fn(sl, gS[b:b + 1, h:h + 1], rule, ns), TOL_FP32,
+                      prefix=f"({b},{h}):", widen=rule != 0)
