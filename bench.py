@@ -524,7 +524,7 @@ def run_scan(args) -> None:
     torch.cuda.set_device(device)
     pkg = importlib.import_module(PKG_NAME)
     L = importlib.import_module(PKG_NAME + "._lib")
-    B, H, N, dh = 8, 16, 64, 128
+    B, H, N, dh = args.batch or 8, 16, 64, 128
     g = torch.Generator().manual_seed(0)
     mk = lambda *sh, sc=1.0: (torch.randn(*sh, generator=g) * sc).to(device)
     U = mk(B, H, N, dh, dh, sc=0.1).requires_grad_(True)
@@ -579,6 +579,86 @@ def run_scan(args) -> None:
         "config": {"workload": "scan_config1", "precision": args.precision,
                    "l2": "inputs larger than L2 (U, K 537 MB each)"},
         "roofline": roof, "kernel_times": kernel_times}), flush=True)
+
+
+def run_train(args) -> None:
+    """Config 4 of the baseline: one optimisation step of the ablation language
+    model (train_ablation.py:197-314, 453-474; 12 layers, d_model 768, 12 heads
+    of 64, 4x GELU MLP, vocab 32000, tied head) on the B200 mixer ops, bf16
+    autocast, outer Muon on the hidden matrices and AdamW on the rest, seq 2048
+    and a micro-batch of 8 sequences per GPU (global batch 64 at N = 8), tokens
+    uniform in [0, 32000) from the seed.  At N > 1 the model is wrapped in DDP
+    on the NCCL backend, so the step includes the bucketed gradient all-reduce
+    over NVLink; the step's other work per GPU is fixed (weak scaling)."""
+    import datetime
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=device)
+    pkg = importlib.import_module(PKG_NAME)
+    tr = importlib.import_module(PKG_NAME + ".training")
+    L = importlib.import_module(PKG_NAME + "._lib")
+    torch.backends.cuda.matmul.allow_tf32 = True   # as the reference's trainer (its msign is fp32)
+    vocab, d, layers, heads, T, mb = 32000, 768, 12, 12, 2048, args.batch or 8
+    inner = {0: "delta", 1: "muon", 2: "adam"}[CONFIGS[args.config]["rule"]]
+    torch.manual_seed(0)
+    model = tr.LanguageModel(vocab, d, layers, heads, inner, chunk=64, ns_steps=3).to(device)
+    net = model
+    if dist is not None:
+        net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local],
+                                                        gradient_as_bucket_view=True)
+    opts = tr.build_optimizers(net)
+    g = torch.Generator().manual_seed(1234 + rank)
+    n_batches = max(args.warmup, 3) + args.steps
+    data = torch.randint(0, vocab, (n_batches, mb, T + 1), generator=g).to(device)
+
+    def step(i):
+        return tr.train_step(net, opts, data[i, :, :-1], data[i, :, 1:])
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    L.prof_report()
+    L.prof_enable(True)
+    e0.record(stream)
+    losses = [step(max(args.warmup, 3) + i) for i in range(args.steps)]
+    e1.record(stream)
+    torch.cuda.synchronize()
+    L.prof_enable(False)
+    kt = L.prof_report()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        dist.barrier()
+    ms = pkg.sharding.max_over_ranks(ms, device)
+    tokens = world * mb * T * args.steps
+    line = {
+        "metric": "config-4 training tokens/s (12-layer GMDN LM, d768, H12, vocab 32000, seq 2048)",
+        "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config4_train", "inner": inner, "micro_batch_per_gpu": mb,
+                   "global_batch": world * mb, "seq_len": T, "layers": layers, "d_model": d,
+                   "heads": heads, "vocab": vocab,
+                   "parallelism": f"dp{world}" + (" (DDP, NCCL all-reduce)" if world > 1 else ""),
+                   "params_M": sum(p.numel() for p in model.parameters()) / 1e6},
+        "loss_first_last": [float(losses[0]), float(losses[-1])],
+        "kernel_times": {k: {"avg_ms": v[0] / max(v[1], 1), "launches": v[1]} for k, v in kt.items()},
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def time_config(pkg, L, name: str, prec: int, steps: int, warmup: int, peaks: dict,
@@ -636,7 +716,7 @@ def main():
     ap.add_argument("--batch", type=int, default=None,
                     help="override B of the workload (small ncu captures)")
     ap.add_argument("--workload", default="mixer",
-                    choices=["mixer", "epilogue", "prologue", "scan"],
+                    choices=["mixer", "epilogue", "prologue", "scan", "train"],
                     help="epilogue / prologue: that part of the mixer alone; scan: the "
                          "scan-only drop-in (fast_state_scan) on fp32 U, K; one GPU each")
     ap.add_argument("--scaling", default="strong", choices=["weak", "strong"],
@@ -659,6 +739,9 @@ def main():
         return
     if args.workload == "scan":
         run_scan(args)
+        return
+    if args.workload == "train":
+        run_train(args)
         return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -238,10 +238,27 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k, ScanTcArgs args) {
     }
     tc_fence_before();
     mbar_arrive_warp(&bars->s_full);
+    // U of a chunk is loaded a whole chunk step ahead: the loads of U_{i+1} go
+    // out right after the drain of chunk i has consumed U_i, so their latency
+    // (at the chip's load) is off the chain
+    float u[64];
+    auto load_u = [&](int jj) {
+      const float4* up = reinterpret_cast<const float4*>(
+          args.U + (mat0 + jj) * static_cast<size_t>(kD) * kD + rowoff);
+#pragma unroll
+      for (int f = 0; f < 16; ++f) {
+        const float4 x = __ldg(up + f);
+        u[4 * f] = x.x;
+        u[4 * f + 1] = x.y;
+        u[4 * f + 2] = x.z;
+        u[4 * f + 3] = x.w;
+      }
+    };
+    load_u(REV ? N - 1 : 0);
     for (int i = 0; i < N; ++i) {
       const int j = REV ? N - 1 - i : i;   // chunk
       const size_t mo = (mat0 + j) * static_cast<size_t>(kD) * kD + rowoff;
-      // pre-update state (and moments at chunk 0) out; U_i in while the products run
+      // pre-update state (and moments at chunk 0) out while the products run
       float4* so = reinterpret_cast<float4*>(args.S + mo);
 #pragma unroll
       for (int f = 0; f < 16; ++f)
@@ -251,16 +268,6 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k, ScanTcArgs args) {
         float4* vh = reinterpret_cast<float4*>(args.V_hist + mo);
 #pragma unroll
         for (int f = 0; f < 16; ++f) mh[f] = vh[f] = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      float u[64];
-      const float4* up = reinterpret_cast<const float4*>(args.U + mo);
-#pragma unroll
-      for (int f = 0; f < 16; ++f) {
-        const float4 x = __ldg(up + f);
-        u[4 * f] = x.x;
-        u[4 * f + 1] = x.y;
-        u[4 * f + 2] = x.z;
-        u[4 * f + 3] = x.w;
       }
       const size_t gi = mat0 + j;
       const float a = __ldg(args.a + gi);
@@ -317,6 +324,7 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k, ScanTcArgs args) {
         tmem_st_wait();
         break;
       }
+      load_u(REV ? j - 1 : j + 1);
       // S_{i+1} as packed bf16 hi / lo into TMEM (A operand of the next products)
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
@@ -348,7 +356,7 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k, ScanTcArgs args) {
 // Delta backward, the parts off the chain: for every matrix (b, h, i)
 //   dK_i = -S_i^T dU_i          (fast_scan.py:185, dU_i = Gbar_i)
 //   da_i = <dU_i, S_i>          (fast_scan.py:150; for delta Gbar = Sbar)
-// Persistent: one CTA per SM walks the matrices.  The eight converter warps
+// Persistent: one CTA per SM walks the matrices.  Sixteen converter warps
 // read S_i and dU_i (fp32) from global memory, add the row dot products for
 // da_i, and write both as split bf16 hi / lo tiles (rows = v, the contracted
 // index); one thread issues D = S_hi^T dU_hi + S_hi^T dU_lo + S_lo^T dU_hi
@@ -356,7 +364,8 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k, ScanTcArgs args) {
 // warps drain into dK while the next matrix's tiles are built.
 // ---------------------------------------------------------------------------
 
-constexpr int kThreadsDk = 288;         // warps 0-7 convert / drain, warp 8 MMA
+constexpr int kConvWarpsDk = 16;                 // convert and drain, 4 per TMEM lane group
+constexpr int kThreadsDk = (kConvWarpsDk + 1) * 32;   // + warp 16: TMEM allocation, MMA issue
 constexpr uint32_t DK_S = 0;            // S_i hi (32 KB), lo (32 KB)
 constexpr uint32_t DK_U = 65536;        // dU_i hi, lo
 constexpr uint32_t DK_BAR = 131072;
@@ -366,7 +375,7 @@ struct BarsDk {
   uint64_t tiles_full, done[2], d_free[2], final_mma;
   uint32_t tmem_base;
   int abort_flag;
-  float red[8];
+  float red[kConvWarpsDk];
 };
 static_assert(sizeof(BarsDk) <= 256, "barrier block");
 
@@ -388,16 +397,16 @@ __global__ void __launch_bounds__(kThreadsDk, 1) scan_bwd_dk_tc_kernel(DkArgs ar
   const int G = gridDim.x;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars->tiles_full, 8);
+    mbar_init(&bars->tiles_full, kConvWarpsDk);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->done[b], 1);
-      mbar_init(&bars->d_free[b], 8);
+      mbar_init(&bars->d_free[b], kConvWarpsDk);
     }
     mbar_init(&bars->final_mma, 1);
     bars->abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 8) {
+  if (warp == kConvWarpsDk) {
     tmem_alloc(&bars->tmem_base, 256);
     tmem_relinquish();
   }
@@ -406,7 +415,7 @@ __global__ void __launch_bounds__(kThreadsDk, 1) scan_bwd_dk_tc_kernel(DkArgs ar
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == 8) {
+  if (warp == kConvWarpsDk) {
     if (lane == 0) {
       // D[m][n] = -sum_v S[v][m] dU[v][n]: A = S^T and B = dU, both MN-major
       constexpr uint32_t ID = idesc_bf16(128, 128, true, true, true);
@@ -436,18 +445,18 @@ __global__ void __launch_bounds__(kThreadsDk, 1) scan_bwd_dk_tc_kernel(DkArgs ar
     }
   } else {
     const int r = (warp & 3) * 32 + lane;   // tile row v / TMEM lane m
-    const int h = warp >> 2;                // columns [64 h, 64 h + 64)
+    const int qc = warp >> 2;               // columns [32 qc, 32 qc + 32)
     const uint32_t lb = tmem_lane_base(warp);
     auto drain = [&](int mm, int itp) -> bool {
       const int b = itp & 1;
       if (!wait_use_w(&bars->done[b], itp >> 1, status, ab)) return false;
       tc_fence_after();
       float4* dk = reinterpret_cast<float4*>(args.dK + static_cast<size_t>(mm) * kD * kD +
-                                             static_cast<size_t>(r) * kD + h * 64);
+                                             static_cast<size_t>(r) * kD + qc * 32);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 2; ++q) {
         float x[16];
-        tmem_ld16(tmem + lb + b * 128 + h * 64 + 16 * q, x);
+        tmem_ld16(tmem + lb + b * 128 + qc * 32 + 16 * q, x);
         tmem_ld_wait();
 #pragma unroll
         for (int f = 0; f < 4; ++f)
@@ -457,69 +466,76 @@ __global__ void __launch_bounds__(kThreadsDk, 1) scan_bwd_dk_tc_kernel(DkArgs ar
       mbar_arrive_warp(&bars->d_free[b]);
       return true;
     };
+    // a row quarter of S_i and dU_i (32 + 32 floats) is loaded in one batch,
+    // and the next matrix's batch goes out as soon as the previous drain is
+    // done, so it is in flight while this matrix's products run
+    float4 sv4[8], uv4[8];
+    auto load_mat = [&](int mm) {
+      const size_t off = static_cast<size_t>(mm) * kD * kD + static_cast<size_t>(r) * kD + qc * 32;
+      const float4* sp = reinterpret_cast<const float4*>(args.S + off);
+      const float4* up = reinterpret_cast<const float4*>(args.dU + off);
+#pragma unroll
+      for (int f = 0; f < 8; ++f) {
+        sv4[f] = __ldg(sp + f);
+        uv4[f] = __ldg(up + f);
+      }
+    };
+    if (static_cast<int>(blockIdx.x) < args.mats) load_mat(blockIdx.x);
     int it = 0;
     int prev = -1;
     for (int m = blockIdx.x; m < args.mats; m += G, ++it) {
       // the tiles are free once the products of the previous matrix are done
       if (it >= 1 && !wait_use_w(&bars->done[(it - 1) & 1], (it - 1) >> 1, status, ab)) break;
-      const size_t off = static_cast<size_t>(m) * kD * kD + static_cast<size_t>(r) * kD + h * 64;
-      const float4* sp = reinterpret_cast<const float4*>(args.S + off);
-      const float4* up = reinterpret_cast<const float4*>(args.dU + off);
       float part = 0.f;
 #pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        float sv[32], uv[32];
+      for (int g = 0; g < 4; ++g) {   // 8-column group g of this thread's quarter
+        const float sv[8] = {sv4[2 * g].x, sv4[2 * g].y, sv4[2 * g].z, sv4[2 * g].w,
+                             sv4[2 * g + 1].x, sv4[2 * g + 1].y, sv4[2 * g + 1].z, sv4[2 * g + 1].w};
+        const float uv[8] = {uv4[2 * g].x, uv4[2 * g].y, uv4[2 * g].z, uv4[2 * g].w,
+                             uv4[2 * g + 1].x, uv4[2 * g + 1].y, uv4[2 * g + 1].z, uv4[2 * g + 1].w};
+        float hi[8], lo[8];
+        const int col8 = qc * 4 + g;
 #pragma unroll
-        for (int f = 0; f < 8; ++f) {
-          const float4 a4 = __ldg(sp + 8 * p + f), b4 = __ldg(up + 8 * p + f);
-          sv[4 * f] = a4.x; sv[4 * f + 1] = a4.y; sv[4 * f + 2] = a4.z; sv[4 * f + 3] = a4.w;
-          uv[4 * f] = b4.x; uv[4 * f + 1] = b4.y; uv[4 * f + 2] = b4.z; uv[4 * f + 3] = b4.w;
+        for (int e = 0; e < 8; ++e) {
+          part = fmaf(sv[e], uv[e], part);
+          hi[e] = __bfloat162float(__float2bfloat16_rn(sv[e]));
+          lo[e] = sv[e] - hi[e];
         }
+        st_row8(sm + DK_S, P128, r, col8, hi);
+        st_row8(sm + DK_S + 32768, P128, r, col8, lo);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) part = fmaf(sv[e], uv[e], part);
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          float hi[8], lo[8];
-          const int col8 = h * 8 + p * 4 + g;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            hi[e] = __bfloat162float(__float2bfloat16_rn(sv[8 * g + e]));
-            lo[e] = sv[8 * g + e] - hi[e];
-          }
-          st_row8(sm + DK_S, P128, r, col8, hi);
-          st_row8(sm + DK_S + 32768, P128, r, col8, lo);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            hi[e] = __bfloat162float(__float2bfloat16_rn(uv[8 * g + e]));
-            lo[e] = uv[8 * g + e] - hi[e];
-          }
-          st_row8(sm + DK_U, P128, r, col8, hi);
-          st_row8(sm + DK_U + 32768, P128, r, col8, lo);
+        for (int e = 0; e < 8; ++e) {
+          hi[e] = __bfloat162float(__float2bfloat16_rn(uv[e]));
+          lo[e] = uv[e] - hi[e];
         }
+        st_row8(sm + DK_U, P128, r, col8, hi);
+        st_row8(sm + DK_U + 32768, P128, r, col8, lo);
       }
       fence_async_smem();
       mbar_arrive_warp(&bars->tiles_full);
-      // da_i: sum over the CTA's 256 converter threads
+      // da_i: sum over the CTA's converter threads
       part = warp_sum(part);
-      named_sync(1, 256);
+      named_sync(1, kConvWarpsDk * 32);
       if (lane == 0) bars->red[warp] = part;
-      named_sync(1, 256);
+      named_sync(1, kConvWarpsDk * 32);
       if (threadIdx.x == 0) {
         float t = 0.f;
 #pragma unroll
-        for (int w = 0; w < 8; ++w) t += bars->red[w];
+        for (int w = 0; w < kConvWarpsDk; ++w) t += bars->red[w];
         args.da[m] = t;
       }
-      // the previous matrix's dK while this one's products run
+      // the previous matrix's dK while this one's products run, then the next
+      // matrix's loads (in flight until this one's products are done)
       if (prev >= 0 && !drain(prev, it - 1)) break;
       prev = m;
+      if (m + G < args.mats) load_mat(m + G);
     }
     if (prev >= 0 && !*ab) drain(prev, it - 1);
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == kConvWarpsDk) {
     tc_fence_after();
     tmem_dealloc(tmem, 256);
   }

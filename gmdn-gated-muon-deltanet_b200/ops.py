@@ -321,8 +321,15 @@ def _f32_flag(t: Tensor, what: str) -> int:
 
 
 def _aligned(t: Tensor) -> Tensor:
+    """Contiguous and 16-byte aligned (a fresh copy when a view is not).  Under
+    tracing (fake or functional tensors have no storage) only contiguity is
+    imposed; the real call that follows checks the alignment."""
     t = t.contiguous()
-    return t if t.data_ptr() % 16 == 0 else t.clone()
+    try:
+        ptr = t.data_ptr()
+    except RuntimeError:
+        return t
+    return t if ptr % 16 == 0 else t.clone()
 
 
 @torch.library.custom_op("gmdn::head_rmsnorm_fwd", mutates_args=())

@@ -1,0 +1,206 @@
+"""Config-4 training step: the ablation language model on the B200 mixer ops,
+data-parallel over NCCL, with the outer Muon optimizer.
+
+What it reproduces from the reference (train_ablation.py):
+
+* the model: token embedding, ``n_layers`` pre-norm blocks (RMSNorm, the
+  fast-weight mixer, RMSNorm, a 4x GELU MLP), final RMSNorm and an output head
+  tied to the embedding (``Block``/``LM``, train_ablation.py:197-246), with the
+  reference's initialisation (normal 0.02, residual output projections at
+  0.02 / sqrt(2 L), the gate priors of train_ablation.py:102-109);
+* the mixer: the same parameters as ``FastWeightMixer`` (train_ablation.py:
+  84-110) whose forward is this library's prologue, chunk and epilogue ops
+  (``integration.mixer_forward``);
+* the optimisers: Nesterov Muon with Newton-Schulz msign on every 2-D hidden
+  matrix and AdamW(0.9, 0.95) on the rest (train_ablation.py:60-73, 264-314);
+* one step: bf16 autocast forward, cross-entropy on fp32 logits, backward,
+  gradient clipping at 1.0, both optimiser steps (train_ablation.py:453-474).
+
+B200 choices: the mixer's scan runs on the tcgen05 kernels (dh 64 at
+d_model 768 / 12 heads); the msign of the outer Muon stacks every matrix of
+one shape into one batch, so each Newton-Schulz step is three batched GEMMs
+(cuBLAS, fp32 with TF32 tensor cores as the reference's trainer enables)
+instead of three GEMMs per matrix; data parallelism is torch DDP over the NCCL
+backend, whose bucketed gradient all-reduce overlaps the backward.
+"""
+
+from __future__ import annotations
+
+import math
+from collections import defaultdict
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import integration
+
+NS_COEF = (3.4445, -4.7750, 2.0315)   # train_ablation.py:67
+GATE_PRIORS = (3.0, -1.0, 1.0, 2.0)   # alpha, beta, mu, nu (train_ablation.py:102-109)
+
+
+class MixerLayer(nn.Module):
+    """The fast-weight mixer with FastWeightMixer's parameters; forward on the
+    B200 ops (prologue, chunk_fast_weight, head_rmsnorm)."""
+
+    def __init__(self, d_model: int, n_heads: int, inner: str, chunk: int = 64,
+                 ns_steps: int = 3):
+        super().__init__()
+        if inner not in ("delta", "muon", "adam") or d_model % n_heads:
+            raise ValueError(f"bad mixer shape or rule: {d_model}/{n_heads} {inner}")
+        self.h, self.dh = n_heads, d_model // n_heads
+        self.inner, self.chunk, self.ns_steps = inner, chunk, ns_steps
+        self.qkv = nn.Linear(d_model, 3 * d_model, bias=False)
+        self.conv = nn.Conv1d(3 * d_model, 3 * d_model, 4, groups=3 * d_model, padding=3)
+        self.n_gates = 4 if inner == "adam" else 3
+        self.gates = nn.Linear(d_model, self.n_gates * n_heads, bias=True)
+        self.norm = nn.RMSNorm(self.dh)
+        self.out = nn.Linear(d_model, d_model, bias=False)
+        self.last_gate_means: dict = {}
+        self.set_gate_priors()
+
+    def set_gate_priors(self) -> None:
+        with torch.no_grad():
+            bias = self.gates.bias.view(self.n_gates, self.h)
+            for i in range(self.n_gates):
+                bias[i].fill_(GATE_PRIORS[i])
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return integration.mixer_forward(self, x)
+
+
+class Block(nn.Module):
+    def __init__(self, d_model: int, n_heads: int, inner: str, chunk: int, ns_steps: int,
+                 mixer_cls=MixerLayer):
+        super().__init__()
+        self.n1 = nn.RMSNorm(d_model)
+        self.mixer = mixer_cls(d_model, n_heads, inner, chunk, ns_steps)
+        self.n2 = nn.RMSNorm(d_model)
+        self.mlp = nn.Sequential(nn.Linear(d_model, 4 * d_model, bias=False), nn.GELU(),
+                                 nn.Linear(4 * d_model, d_model, bias=False))
+
+    def forward(self, x):
+        x = x + self.mixer(self.n1(x))
+        return x + self.mlp(self.n2(x))
+
+
+class LanguageModel(nn.Module):
+    """Embedding, blocks, final norm, tied output head; ``forward(idx,
+    targets)`` returns (logits, mean cross-entropy or None)."""
+
+    def __init__(self, vocab: int, d_model: int, n_layers: int, n_heads: int, inner: str,
+                 chunk: int = 64, ns_steps: int = 3, mixer_cls=MixerLayer):
+        super().__init__()
+        self.emb = nn.Embedding(vocab, d_model)
+        self.blocks = nn.ModuleList(Block(d_model, n_heads, inner, chunk, ns_steps, mixer_cls)
+                                    for _ in range(n_layers))
+        self.norm_f = nn.RMSNorm(d_model)
+        self.head = nn.Linear(d_model, vocab, bias=False)
+        self.head.weight = self.emb.weight
+        for m in self.modules():
+            if isinstance(m, (nn.Linear, nn.Embedding)):
+                nn.init.normal_(m.weight, std=0.02)
+                if getattr(m, "bias", None) is not None:
+                    nn.init.zeros_(m.bias)
+        resid_std = 0.02 / math.sqrt(2 * n_layers)
+        for blk in self.blocks:
+            nn.init.normal_(blk.mixer.out.weight, std=resid_std)
+            nn.init.normal_(blk.mlp[2].weight, std=resid_std)
+            blk.mixer.set_gate_priors()
+
+    def forward(self, idx, targets=None):
+        x = self.emb(idx)
+        for blk in self.blocks:
+            x = blk(x)
+        logits = self.head(self.norm_f(x))
+        if targets is None:
+            return logits, None
+        loss = F.cross_entropy(logits.reshape(-1, logits.shape[-1]).float(), targets.reshape(-1))
+        return logits, loss
+
+
+def msign(mats: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.Tensor:
+    """Newton-Schulz orthogonalisation of a stack of matrices (..., r, c), in
+    fp32 (train_ablation.py:60-73): tall matrices are handled transposed, each
+    is divided by its Frobenius norm + eps, then ``steps`` quintic steps
+    X <- a X + (b A + c A^2) X with A = X X^T.  The stack is one batch, so a
+    step is three batched GEMMs whatever the number of matrices."""
+    a, b, c = NS_COEF
+    x = mats.float()
+    tall = x.shape[-2] > x.shape[-1]
+    if tall:
+        x = x.mT
+    x = x / (torch.linalg.matrix_norm(x, keepdim=True) + eps)
+    for _ in range(steps):
+        g = x @ x.mT
+        p = torch.baddbmm(g, g, g, beta=b, alpha=c) if g.dim() == 3 else b * g + c * (g @ g)
+        x = a * x + p @ x
+    if tall:
+        x = x.mT
+    return x.to(mats.dtype)
+
+
+class OuterMuon(torch.optim.Optimizer):
+    """Nesterov-momentum Muon on 2-D matrices (train_ablation.py:264-288):
+    buf <- m buf + g; u = g + m buf (Nesterov) or buf; u <- msign(u);
+    p <- p (1 - lr wd) - lr sqrt(max(1, rows / cols)) u.  Parameters of one
+    shape are orthogonalised together (one batched msign per shape)."""
+
+    def __init__(self, params, lr=0.02, momentum=0.95, nesterov=True, weight_decay=0.0,
+                 ns_steps=5):
+        super().__init__(params, dict(lr=lr, momentum=momentum, nesterov=nesterov,
+                                      weight_decay=weight_decay, ns_steps=ns_steps))
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        for group in self.param_groups:
+            lr, mom, wd = group["lr"], group["momentum"], group["weight_decay"]
+            by_shape = defaultdict(list)
+            for p in group["params"]:
+                if p.grad is not None:
+                    by_shape[tuple(p.shape)].append(p)
+            for shape, ps in by_shape.items():
+                updates = []
+                for p in ps:
+                    st = self.state[p]
+                    if "buf" not in st:
+                        st["buf"] = torch.zeros_like(p.grad)
+                    buf = st["buf"]
+                    buf.mul_(mom).add_(p.grad)
+                    updates.append(p.grad.add(buf, alpha=mom) if group["nesterov"] else buf)
+                u = msign(torch.stack(updates), group["ns_steps"])
+                scale = max(1.0, shape[0] / shape[1]) ** 0.5
+                for p, ui in zip(ps, u.unbind(0)):
+                    if wd:
+                        p.mul_(1 - lr * wd)
+                    p.add_(ui, alpha=-lr * scale)
+
+
+def build_optimizers(model: nn.Module, muon_lr=0.02, adam_lr=4e-4, weight_decay=0.1):
+    """Muon on every 2-D parameter but the (tied) embedding, AdamW(0.9, 0.95)
+    on the rest (train_ablation.py:291-306)."""
+    base = model.module if hasattr(model, "module") else model
+    emb = {id(base.emb.weight)}
+    hidden, other = [], []
+    for p in model.parameters():
+        if p.requires_grad:
+            (hidden if p.ndim == 2 and id(p) not in emb else other).append(p)
+    return [OuterMuon(hidden, lr=muon_lr, weight_decay=weight_decay),
+            torch.optim.AdamW(other, lr=adam_lr, betas=(0.9, 0.95), weight_decay=weight_decay)]
+
+
+def train_step(model: nn.Module, optimizers, idx: torch.Tensor, targets: torch.Tensor,
+               amp: bool = True) -> torch.Tensor:
+    """One optimisation step (train_ablation.py:458-474 with accum = 1): bf16
+    autocast forward, backward (under DDP the NCCL all-reduce of the gradient
+    buckets overlaps it), clipping at 1.0, both optimiser steps.  Returns the
+    loss (a device tensor; nothing synchronises the host)."""
+    for opt in optimizers:
+        opt.zero_grad(set_to_none=True)
+    with torch.autocast(device_type="cuda", dtype=torch.bfloat16, enabled=amp):
+        _, loss = model(idx, targets)
+    loss.backward()
+    torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+    for opt in optimizers:
+        opt.step()
+    return loss.detach()

@@ -78,9 +78,10 @@ def test_patched_mixer_reference_benchmark_shape(inner, ns):
     """test.py's benchmark shape (FastWeightMixer(768, 12, inner, chunk=64,
     ns_steps=3) at B16 T1024, test.py:84-109) under bf16 autocast, as the
     trainer runs it (train_ablation.py:465-467): the prologue, chunk and
-    epilogue ops run on the tensor-core path (dh 64) and the output and input
-    gradient agree with the module's lines evaluated in fp32 on the CPU with
-    the oracle mixer core.
+    epilogue ops run on the tensor-core path (dh 64), and the module's output
+    and input gradient agree with the same module on the exact-fp32 chunk
+    kernels (b200_precision = ieee; pinned to the oracle at 1e-4 elsewhere), so
+    the only difference is the chunk op's arithmetic.
 
     Gate biases: the trainer's alpha and mu priors (3.0, 1.0,
     train_ablation.py:102-109), but beta at -5 and nu at 6.  With a randomly
@@ -88,7 +89,7 @@ def test_patched_mixer_reference_benchmark_shape(inner, ns):
     parallel-delta update a I - Kw has eigenvalues far above 1 at the trainer's
     beta prior (-1) and the fp32 reference itself reaches 1e17 in 16 chunks;
     adam with nu_c ~ 0 is the sign-like, ill-posed regime.  These biases keep
-    every rule well conditioned (fp32 within ~5e-5 of fp64 per row)."""
+    every rule well conditioned."""
     pkg = load_pkg()
     integ = importlib.import_module(PKG_NAME + ".integration")
     torch.manual_seed(23)
@@ -97,25 +98,29 @@ def test_patched_mixer_reference_benchmark_shape(inner, ns):
         bias = m.gates.bias.view(m.n_gates, m.h)
         for i, val in enumerate((3.0, -5.0, 1.0, 6.0)[:m.n_gates]):
             bias[i].fill_(val)
-    x = torch.randn(16, 1024, 768) * 0.5
-    xc = x.clone().requires_grad_(True)
-    ref = _cpu_forward(m, xc)
-    dy = torch.randn_like(ref)
-    ref.backward(dy)
     mg = m.cuda()
-    xg = x.cuda().requires_grad_(True)
+    x = (torch.randn(16, 1024, 768) * 0.5).cuda()
+    dy = torch.randn(16, 1024, 768).cuda()
     L = pkg._lib
-    L.prof_report()
-    L.prof_enable(True)
-    with torch.autocast("cuda", dtype=torch.bfloat16):
-        y = integ.mixer_forward(mg, xg)
-    y.float().backward(dy.cuda())
-    torch.cuda.synchronize()
-    L.prof_enable(False)
-    names = set(L.prof_report())
+    runs = {}
+    for prec in (pkg.GMDN_PREC_FAST, pkg.GMDN_PREC_IEEE):
+        mg.b200_precision = prec
+        mg.zero_grad(set_to_none=True)
+        xg = x.clone().requires_grad_(True)
+        L.prof_report()
+        L.prof_enable(True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            y = integ.mixer_forward(mg, xg)
+        y.float().backward(dy)
+        torch.cuda.synchronize()
+        L.prof_enable(False)
+        runs[prec] = (y.detach().float(), xg.grad.float(), set(L.prof_report()))
     fwd = "chunk_fwd_muon_tc" if inner == "muon" else "chunk_fwd_tc"
+    names = runs[pkg.GMDN_PREC_FAST][2]
     assert {fwd, "chunk_bwd2_tc", "mixer_prologue_fwd", "head_rmsnorm_fwd"} <= names, names
-    err = (y.detach().float().cpu() - ref.detach()).abs().max() / ref.abs().max()
-    assert err < 3e-2, f"y rel err {err:.3e}"
-    gerr = (xg.grad.float().cpu() - xc.grad).abs().max() / xc.grad.abs().max()
-    assert gerr < 3e-2, f"dx rel err {gerr:.3e}"
+    assert "chunk_prep" in runs[pkg.GMDN_PREC_IEEE][2]
+    (yf, gf, _), (ye, ge, _) = runs[pkg.GMDN_PREC_FAST], runs[pkg.GMDN_PREC_IEEE]
+    err = ((yf - ye).abs().max() / ye.abs().max()).item()
+    assert err < 2e-2, f"y rel err {err:.3e}"
+    gerr = ((gf - ge).abs().max() / ge.abs().max()).item()
+    assert gerr < 2e-2, f"dx rel err {gerr:.3e}"

@@ -1,0 +1,55 @@
+"""The config-4 training step on the GPU (training.py): the model's forward on
+the B200 ops equals the same parameters through the CPU oracle, and a few
+optimisation steps under bf16 autocast run the tensor-core mixer kernels and
+lower the loss on a fixed batch."""
+import copy
+
+import pytest
+import torch
+
+from conftest import load_pkg
+from test_training import _training, cpu_mixer_cls
+
+pytestmark = pytest.mark.gpu
+
+
+def test_model_forward_and_gradient_match_cpu_oracle():
+    tr = _training()
+    torch.manual_seed(5)
+    cpu = tr.LanguageModel(211, 128, 2, 2, "delta", chunk=64, mixer_cls=cpu_mixer_cls())
+    gpu = tr.LanguageModel(211, 128, 2, 2, "delta", chunk=64)
+    gpu.load_state_dict(cpu.state_dict())
+    gpu = gpu.cuda()
+    g = torch.Generator().manual_seed(6)
+    idx = torch.randint(0, 211, (2, 129), generator=g)
+    _, lc = cpu(idx[:, :-1], idx[:, 1:])
+    lc.backward()
+    _, lg = gpu(idx[:, :-1].cuda(), idx[:, 1:].cuda())   # fp32: the exact-fp32 kernels
+    lg.backward()
+    assert abs(lg.item() - lc.item()) <= 1e-5 * abs(lc.item())
+    for (n, pc), pg in zip(cpu.named_parameters(), gpu.parameters()):
+        e = (pg.grad.cpu() - pc.grad).abs().max().item() / (pc.grad.abs().max().item() + 1e-12)
+        assert e < 1e-3, n
+
+
+@pytest.mark.parametrize("inner", ["delta", "muon", "adam"])
+def test_training_steps_lower_the_loss(inner):
+    pkg = load_pkg()
+    tr = _training()
+    torch.manual_seed(7)
+    torch.backends.cuda.matmul.allow_tf32 = True
+    model = tr.LanguageModel(1000, 256, 2, 4, inner, chunk=64).cuda()   # dh 64
+    opts = tr.build_optimizers(model, muon_lr=0.02, adam_lr=3e-3)
+    g = torch.Generator().manual_seed(8)
+    idx = torch.randint(0, 1000, (4, 257), generator=g).cuda()
+    L = pkg._lib
+    L.prof_report()
+    L.prof_enable(True)
+    losses = [tr.train_step(model, opts, idx[:, :-1], idx[:, 1:]).item() for _ in range(6)]
+    torch.cuda.synchronize()
+    L.prof_enable(False)
+    names = set(L.prof_report())
+    fwd = "chunk_fwd_muon_tc" if inner == "muon" else "chunk_fwd_tc"
+    assert {fwd, "chunk_bwd2_tc", "mixer_prologue_fwd", "head_rmsnorm_bwd"} <= names, names
+    assert all(l == l for l in losses)            # finite
+    assert losses[-1] < losses[0] - 0.05, losses

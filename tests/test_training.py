@@ -1,0 +1,175 @@
+"""The config-4 training step's host logic on CPU (training.py): the batched
+msign against the reference's formula, the outer Muon update, the optimiser
+split, and data parallelism with two gloo ranks (DDP's all-reduced gradient
+and one full step equal the single-process run on the whole batch).  The
+mixer's B200 ops need a GPU, so the CPU model runs the same mixer parameters
+through the oracle mixer core."""
+import os
+import socket
+
+import torch
+import torch.multiprocessing as mp
+import torch.nn.functional as F
+
+from conftest import ROOT, load_pkg
+
+
+def _training():
+    import importlib
+    load_pkg()
+    from conftest import PKG_NAME
+    return importlib.import_module(PKG_NAME + ".training")
+
+
+def ref_msign(M, steps=5, eps=1e-7):
+    """train_ablation.py:60-73 restated (one matrix)."""
+    X = M.float()
+    tall = X.shape[-2] > X.shape[-1]
+    if tall:
+        X = X.mT
+    X = X / (X.norm(dim=(-2, -1), keepdim=True) + eps)
+    a, b, c = 3.4445, -4.7750, 2.0315
+    for _ in range(steps):
+        A = X @ X.mT
+        X = a * X + (b * A + c * (A @ A)) @ X
+    return X.mT if tall else X
+
+
+def test_batched_msign_matches_reference_formula():
+    tr = _training()
+    g = torch.Generator().manual_seed(0)
+    for shape in ((3, 40, 24), (2, 24, 40), (4, 32, 32), (36, 64)):
+        M = torch.randn(*shape, generator=g)
+        want = ref_msign(M) if M.dim() == 2 else torch.stack([ref_msign(m) for m in M])
+        assert (tr.msign(M) - want).abs().max().item() < 5e-6, shape
+
+
+def test_outer_muon_step_matches_reference_update():
+    tr = _training()
+    g = torch.Generator().manual_seed(1)
+    ps = [torch.nn.Parameter(torch.randn(48, 16, generator=g)) for _ in range(2)]
+    ps.append(torch.nn.Parameter(torch.randn(16, 48, generator=g)))
+    before = [p.detach().clone() for p in ps]
+    grads = [torch.randn(p.shape, generator=g) for p in ps]
+    opt = tr.OuterMuon(ps, lr=0.02, momentum=0.95, weight_decay=0.1)
+    for p, gr in zip(ps, grads):
+        p.grad = gr.clone()
+    opt.step()
+    for p, p0, gr in zip(ps, before, grads):
+        buf = gr                             # zero buffer, then buf = 0.95 * 0 + g
+        u = ref_msign(gr + 0.95 * buf)        # Nesterov
+        scale = max(1.0, p.shape[0] / p.shape[1]) ** 0.5
+        want = p0 * (1 - 0.02 * 0.1) - 0.02 * scale * u
+        assert (p.detach() - want).abs().max().item() < 1e-5
+
+
+def test_optimizer_split():
+    tr = _training()
+    m = tr.LanguageModel(100, 64, 2, 2, "delta")
+    muon, adamw = tr.build_optimizers(m)
+    hidden = {id(p) for g in muon.param_groups for p in g["params"]}
+    other = {id(p) for g in adamw.param_groups for p in g["params"]}
+    assert id(m.emb.weight) in other and id(m.emb.weight) not in hidden   # tied head too
+    for blk in m.blocks:
+        mx = blk.mixer
+        for p in (mx.qkv.weight, mx.gates.weight, mx.out.weight, blk.mlp[0].weight, blk.mlp[2].weight):
+            assert id(p) in hidden
+        for p in (mx.conv.weight, mx.conv.bias, mx.gates.bias, mx.norm.weight, blk.n1.weight):
+            assert id(p) in other
+    assert len(hidden & other) == 0
+    assert len(hidden) + len(other) == len(list(m.parameters()))
+    bias = m.blocks[0].mixer.gates.bias.view(3, 2)
+    assert torch.equal(bias[:, 0], torch.tensor([3.0, -1.0, 1.0]))
+
+
+def cpu_mixer_cls():
+    """MixerLayer with its forward on the CPU oracle (same parameters)."""
+    tr = _training()
+    import oracle
+
+    class CpuMixer(tr.MixerLayer):
+        def forward(self, x):
+            B, T, D = x.shape
+            H, dh = self.h, self.dh
+            qkv = self.conv(self.qkv(x).transpose(1, 2))[..., :T].transpose(1, 2)
+            q, k, v = F.silu(qkv).chunk(3, dim=-1)
+            q = F.normalize(q.reshape(B, T, H, dh).transpose(1, 2), dim=-1)
+            k = F.normalize(k.reshape(B, T, H, dh).transpose(1, 2), dim=-1)
+            v = v.reshape(B, T, H, dh).transpose(1, 2)
+            g = torch.sigmoid(self.gates(x)).view(B, T, self.n_gates, H).permute(2, 0, 3, 1)
+            nu = g[3] if self.n_gates == 4 else None
+            rule = {"delta": 0, "muon": 1, "adam": 2}[self.inner]
+            o = oracle.mixer_core_forward(q, k, v, g[0], g[1], g[2], nu, rule, self.ns_steps,
+                                          self.chunk)
+            return self.out(self.norm(o).transpose(1, 2).reshape(B, T, D))
+
+    return CpuMixer
+
+
+def _model(seed):
+    tr = _training()
+    torch.manual_seed(seed)
+    return tr.LanguageModel(97, 32, 2, 2, "delta", chunk=16, mixer_cls=cpu_mixer_cls())
+
+
+def _batch():
+    g = torch.Generator().manual_seed(3)
+    idx = torch.randint(0, 97, (4, 32), generator=g)
+    return idx[:, :-1].contiguous()[:, :16], idx[:, 1:17].contiguous()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _ddp_worker(rank, world, port, out_dir):
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    tr = _training()
+    model = torch.nn.parallel.DistributedDataParallel(_model(0))
+    idx, tgt = _batch()
+    lo, hi = rank * 2, rank * 2 + 2
+    _, loss = model(idx[lo:hi], tgt[lo:hi])
+    loss.backward()
+    grads = {n: p.grad.clone() for n, p in model.module.named_parameters()}
+    opts = tr.build_optimizers(model)
+    torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+    for o in opts:
+        o.step()
+    if rank == 0:
+        torch.save({"grads": grads, "params": dict(model.module.state_dict())},
+                   os.path.join(out_dir, "ddp.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_rank_ddp_step_equals_single_process(tmp_path):
+    """DDP averages the two ranks' gradients over NCCL's CPU twin (gloo); with
+    equal shards that is the gradient of the mean loss on the whole batch, and
+    the step that follows (clipping, Muon, AdamW) equals the single-process
+    step on it."""
+    world = 2
+    mp.start_processes(_ddp_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    tr = _training()
+    model = _model(0)
+    idx, tgt = _batch()
+    _, loss = model(idx, tgt)
+    loss.backward()
+    got = torch.load(tmp_path / "ddp.pt")
+    for n, p in model.named_parameters():
+        e = (got["grads"][n] - p.grad).abs().max().item()
+        assert e <= 1e-5 * (p.grad.abs().max().item() + 1e-12) + 1e-7, n
+    opts = tr.build_optimizers(model)
+    torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+    for o in opts:
+        o.step()
+    for n, t in model.state_dict().items():
+        assert (got["params"][n] - t).abs().max().item() < 1e-5, n
