@@ -336,44 +336,17 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       if (threadIdx.x == 0) bulk_wait_read0();
       named_sync(2, 256);
       uint8_t* panel = sm + B1_SS + half * P128;
-      // The histories are read-only here (non-coherent loads) and the moment
-      // slabs are only touched through their own restrict pointers, so the
-      // loads of group g8 + 1 are issued before group g8 is computed and its
-      // slabs written back: one L2 round trip per group is hidden behind the
-      // previous group instead of eight in a dependent row.
-      const uint4* __restrict__ gh = slab_bf16(const_cast<uint16_t*>(args.G_hist), mm, half, 0, c);
-      const uint4* __restrict__ mh = slab_bf16(const_cast<uint16_t*>(args.Mp_hist), mm, half, 0, c);
-      const uint4* __restrict__ vh = slab_bf16(const_cast<uint16_t*>(args.Vp_hist), mm, half, 0, c);
-      float4* __restrict__ mbs = slab_f32(args.M_ws, bh, half, 0, c);
-      float4* __restrict__ vbs = slab_f32(args.V_ws, bh, half, 0, c);
-      uint4 ng = __ldg(gh), nm = __ldg(mh), nv = __ldg(vh), ns_ = __ldg(srow);
-      float4 nmb0 = make_float4(0.f, 0.f, 0.f, 0.f), nmb1 = nmb0, nvb0 = nmb0, nvb1 = nmb0;
-      if (have_bar) {
-        nmb0 = mbs[0]; nmb1 = mbs[128]; nvb0 = vbs[0]; nvb1 = vbs[128];
-      }
 #pragma unroll
       for (int g8 = 0; g8 < 8; ++g8) {
         float g[8], mp[8], vp[8], sv[8], mb[8], vb[8], gb[8];
-        unpack8(ng, g);
-        unpack8(nm, mp);
-        unpack8(nv, vp);
-        unpack8(ns_, sv);
-        const float4 m0 = nmb0, m1 = nmb1, v0 = nvb0, v1 = nvb1;
-        if (g8 + 1 < 8) {   // slab stride: 128 uint4 per column group (bf16), 256 float4 per 8 fp32
-          ng = __ldg(gh + (g8 + 1) * 128);
-          nm = __ldg(mh + (g8 + 1) * 128);
-          nv = __ldg(vh + (g8 + 1) * 128);
-          ns_ = __ldg(srow + g8 + 1);
-          if (have_bar) {
-            nmb0 = mbs[(g8 + 1) * 256];
-            nmb1 = mbs[(g8 + 1) * 256 + 128];
-            nvb0 = vbs[(g8 + 1) * 256];
-            nvb1 = vbs[(g8 + 1) * 256 + 128];
-          }
-        }
-        float4* mbp = mbs + g8 * 256;
-        float4* vbp = vbs + g8 * 256;
+        unpack8(*slab_bf16(const_cast<uint16_t*>(args.G_hist), mm, half, g8, c), g);
+        unpack8(*slab_bf16(const_cast<uint16_t*>(args.Mp_hist), mm, half, g8, c), mp);
+        unpack8(*slab_bf16(const_cast<uint16_t*>(args.Vp_hist), mm, half, g8, c), vp);
+        unpack8(srow[g8], sv);
+        float4* mbp = slab_f32(args.M_ws, bh, half, 2 * g8, c);
+        float4* vbp = slab_f32(args.V_ws, bh, half, 2 * g8, c);
         if (have_bar) {
+          const float4 m0 = mbp[0], m1 = mbp[128], v0 = vbp[0], v1 = vbp[128];
           mb[0] = m0.x; mb[1] = m0.y; mb[2] = m0.z; mb[3] = m0.w;
           mb[4] = m1.x; mb[5] = m1.y; mb[6] = m1.z; mb[7] = m1.w;
           vb[0] = v0.x; vb[1] = v0.y; vb[2] = v0.z; vb[3] = v0.w;

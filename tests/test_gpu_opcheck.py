@@ -98,5 +98,9 @@ def test_compiled_mixer_core_matches_eager(rule):
     # the cotangent dO = 2 o it feeds the op differs in the last bits
     assert torch.allclose(out, eager, rtol=1e-5)
     for a, b in zip(cl, dO_seed):
-        e = ((a.grad.float() - b.grad.float()).abs().max() / b.grad.float().abs().max()).item()
+        ref = b.grad.float().abs().max().item()
+        if ref == 0.0:       # a gate the rule never reads: zeros both ways
+            assert a.grad.abs().max().item() == 0.0
+            continue
+        e = (a.grad.float() - b.grad.float()).abs().max().item() / ref
         assert e < 1e-3, e
