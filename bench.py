@@ -614,11 +614,13 @@ def run_train(args) -> None:
         net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local],
                                                         gradient_as_bucket_view=True)
     opts = tr.build_optimizers(net)
+    sched = tr.LrSchedule(opts)   # the trainer's defaults: warm-up 500 of 9600 steps
     g = torch.Generator().manual_seed(1234 + rank)
     n_batches = max(args.warmup, 3) + args.steps
     data = torch.randint(0, vocab, (n_batches, mb, T + 1), generator=g).to(device)
 
     def step(i):
+        sched.set_step(i)
         return tr.train_step(net, opts, data[i, :, :-1], data[i, :, 1:])
 
     for i in range(max(args.warmup, 3)):
@@ -652,6 +654,8 @@ def run_train(args) -> None:
                    "parallelism": f"dp{world}" + (" (DDP, NCCL all-reduce)" if world > 1 else ""),
                    "params_M": sum(p.numel() for p in model.parameters()) / 1e6},
         "loss_first_last": [float(losses[0]), float(losses[-1])],
+        "lr_schedule": "train_ablation.py's: linear warm-up over 500 steps, these are steps "
+                       f"0-{max(args.warmup, 3) + args.steps - 1}",
         "kernel_times": {k: {"avg_ms": v[0] / max(v[1], 1), "launches": v[1]} for k, v in kt.items()},
     }
     if rank == 0:

@@ -430,9 +430,9 @@ int gmdn_scan_fwd(const float* U, const float* K, const float* a, const float* b
   uint32_t* status = static_cast<uint32_t*>(workspace);
   cudaError_t e = cudaMemsetAsync(status, 0, sizeof(uint32_t), st);
   if (e != cudaSuccess) return cuda_fail(e, "status reset");
-  // GMDN_PREC_FAST, delta / adam at dh 128: the tensor-core scan (its bounded
-  // waits report through the status word); everything else runs the
-  // exact-fp32 kernels.
+  // GMDN_PREC_FAST, delta at dh 128 with 16-byte aligned tensors: the
+  // tensor-core scan (its bounded waits report through the status word);
+  // everything else runs the exact-fp32 kernels.
   if (precision == GMDN_PREC_FAST && gmdn::scan_fwd_tc_supported(p)) {
     GMDN_LAUNCH(gmdn::scan_fwd_tc(p, status, st), "scan_fwd_tc");
     return GMDN_OK;

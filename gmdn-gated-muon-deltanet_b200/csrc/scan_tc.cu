@@ -1,18 +1,13 @@
 // Tensor-core state scan at the fast_state_scan boundary (fp32 U, K in HBM),
 // dh = 128: the GMDN_PREC_FAST path of gmdn_scan_fwd / gmdn_scan_bwd for the
 // delta rule (the reference's default tf32 `tl.dot`, fast_scan.py:196-199, run
-// on tcgen05 with more precision than tf32: it meets the 1e-4 fp32 bar).  The
-// forward kernel is also written for adam (RULE 2) but not dispatched (see
-// scan_fwd_tc_supported).
+// on tcgen05 with more precision than tf32: it meets the 1e-4 fp32 bar).
 //
 // One CTA per (batch, head) walks the N chunks in order (fast_scan.py:72-95):
 //
 //   S_out[i] = S_i                        (pre-update state)
 //   G_i      = U_i - S_i K_i
-//   delta:  S_{i+1} = a_i S_i + G_i
-//   adam:   M' = mu_i M + (1 - mu_i) G_i,  V' = nu_i V + (1 - nu_i) G_i^2,
-//           S_{i+1} = a_i S_i + b_i M' / (sqrt(V') + 1e-6)
-//           (M_hist[i] = M_i, V_hist[i] = V_i, pre-update)
+//   S_{i+1}  = a_i S_i + G_i
 //
 // The product S_i K_i is a split-bf16 GEMM on the tensor cores: S = S_hi +
 // S_lo and K = K_hi + K_lo (each part bf16, ~16 significant bits together),
@@ -21,20 +16,23 @@
 //   * S (fp32) lives in the registers of the eight state warps: thread (row c
 //     = TMEM lane, half h) owns S[c][64h .. 64h+63].  They write S_hi / S_lo
 //     as packed bf16 pairs into TMEM, the A operand (128 x 128, K = dk).
-//   * K_i arrives by TMA as fp32 in four 128-byte-swizzled boxes of 32
-//     columns x 128 rows; two converter warps turn it into bf16 hi / lo tiles
-//     (two 64-column SW128 panels each, rows = dk), the MN-major B operand.
-//     The tiles are double-buffered, so K_{i+1} is converted while the
+//   * K_i is read from global memory by two converter warps in row order (a
+//     half warp reads one 512-byte row: coalesced) and written as bf16 hi / lo
+//     tiles (two 64-column SW128 panels each, rows = dk), the MN-major B
+//     operand.  The tiles are double-buffered and the converters hold half of
+//     the next K in registers, so K_{i+1} is loaded and converted while the
 //     products of chunk i run.
-//   * U_i is read by the state threads straight from global memory into
-//     registers at the start of chunk i (its loads overlap the products);
-//     S_out and the moment histories are written from registers.
-//   * adam: M and V (fp32) stay in TMEM (columns 256-383 and 384-511).
+//   * U_i arrives by TMA as fp32 in four 128-byte-swizzled boxes of 32
+//     columns x 128 rows; a state thread reads its row's 16-byte chunks, which
+//     the swizzle spreads over all banks (a row per thread from global memory
+//     costs a wavefront per row and made the step L1-bound).  The TMA for
+//     U_{i+1} is issued as soon as every state warp has read U_i.
+//   * S_out is written from registers (16-byte stores).
 //
 // Warp roles (384 threads): warps 0-7 state, 8-9 K conversion, 10 TMA,
 // 11 TMEM allocation and MMA issue.  Every wait is bounded (tc.cuh).
 //
-// HBM per chunk-head: U, K in (128 KB), S out (64 KB); adam + M, V out (128 KB).
+// HBM per chunk-head: U, K in (128 KB), S out (64 KB).
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -54,16 +52,16 @@ constexpr int kConvThreads = 64;
 constexpr uint32_t P128 = 16384;   // panel stride of a 128-row bf16 tile
 
 // shared memory (bytes from a 1024-aligned base)
-constexpr uint32_t SC_RAW = 0;         // K_i fp32: 4 SW128 boxes of 32 cols x 128 rows (64 KB)
-constexpr uint32_t SC_KT = 65536;      // bf16 tiles, 2 buffers x (hi 32 KB, lo 32 KB)
+constexpr uint32_t SC_KT = 0;          // K_i bf16 tiles, 2 buffers x (hi 32 KB, lo 32 KB)
+constexpr uint32_t SC_U = 131072;      // U_i fp32: 4 SW128 boxes of 32 cols x 128 rows (64 KB)
 constexpr uint32_t SC_BAR = 196608;
 constexpr uint32_t SC_SMEM = SC_BAR + 256 + 1024;
 
-// TMEM columns
-constexpr uint32_t TS_SH = 0, TS_SL = 64, TS_G = 128, TS_M = 256, TS_V = 384;
+// TMEM columns: S hi / lo (packed bf16 pairs, the A operand), the product
+constexpr uint32_t TS_SH = 0, TS_SL = 64, TS_G = 128;
 
 struct BarsS {
-  uint64_t raw_full, raw_empty;
+  uint64_t u_full, u_empty;
   uint64_t kt_full[2], kt_empty[2];
   uint64_t s_full, g_full;
   uint64_t final_mma;
@@ -73,8 +71,8 @@ struct BarsS {
 static_assert(sizeof(BarsS) <= 256, "barrier block");
 
 struct ScanTcArgs {
-  const float *U, *a, *b, *m, *n;
-  float *S, *M_hist, *V_hist;
+  const float *U, *K, *a;
+  float* S;
   uint32_t* status;
   int N;
 };
@@ -83,22 +81,22 @@ __device__ __forceinline__ uint8_t* ktile(uint8_t* sm, int buf) {
   return sm + SC_KT + buf * 65536u;
 }
 
-// fp32 element (r, c) of the raw K tile: box c / 32, 16-byte chunk (c % 32) / 4
-// swizzled with the row.
-__device__ __forceinline__ const float4* raw_chunk(const uint8_t* raw, int r, int c) {
-  const int box = c >> 5;
+// 16-byte chunk holding fp32 columns [c, c+4) of row r of a tile stored as
+// four 128-byte-swizzled boxes of 32 columns (what a TMA load with
+// CU_TENSOR_MAP_SWIZZLE_128B and a 32 x 128 box writes).
+__device__ __forceinline__ const float4* box_chunk(const uint8_t* t, int r, int c) {
   const int j = (c & 31) >> 2;
-  return reinterpret_cast<const float4*>(raw + box * 16384 + r * 128 + ((j ^ (r & 7)) << 4));
+  return reinterpret_cast<const float4*>(t + (c >> 5) * 16384 + r * 128 + ((j ^ (r & 7)) << 4));
 }
 
-// RULE 0 / 2: the forward (chunks in order, B = K MN-major: G' = S K).
-// REV (rule 0 only): the delta backward's reverse chain, the same kernel with
+// Forward (REV false): chunks in order, B = K MN-major, G' = S K.
+// Reverse (REV true): the delta backward's reverse chain, the same kernel with
 // the chunks in reverse order, S := Sbar, U := gS, S_out := dU and B = K
 // K-major (C = Sbar K^T): Sbar_i = a_i Sbar_{i+1} + (gS_i - Sbar_{i+1} K_i^T),
 // dU_i = Sbar_{i+1} (fast_scan.py:182-186 for delta, where Gbar = Sbar).
-template <int RULE, bool REV>
+template <bool REV>
 __global__ void __launch_bounds__(kThreadsScan, 1)
-scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k, ScanTcArgs args) {
+scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_u, ScanTcArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
@@ -108,11 +106,11 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k, ScanTcArgs args) {
   const int bh = blockIdx.x;
   const int N = args.N;
   uint32_t* status = args.status;
-  constexpr uint32_t kTmemCols = RULE == 2 ? 512 : 256;
+  constexpr uint32_t kTmemCols = 256;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars->raw_full, 1);
-    mbar_init(&bars->raw_empty, kConvThreads / 32);
+    mbar_init(&bars->u_full, 1);
+    mbar_init(&bars->u_empty, 8);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->kt_full[b], kConvThreads / 32);
       mbar_init(&bars->kt_empty[b], 1);
@@ -132,22 +130,23 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k, ScanTcArgs args) {
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   const size_t mat0 = static_cast<size_t>(bh) * N;   // matrix index of chunk 0
+  auto chunk = [&](int i) { return REV ? N - 1 - i : i; };
 
   if (warp == 10) {
-    // ------------------------------------------------------------ TMA: raw K_i
+    // ------------------------------------------------------------ TMA: U_i
     if (lane == 0) {
       int issued = 0;
       for (int i = 0; i < N; ++i) {
-        if (!wait_free(&bars->raw_empty, i, status, ab)) break;
-        mbar_expect_tx(&bars->raw_full, 65536);
-        const int row = static_cast<int>((mat0 + (REV ? N - 1 - i : i)) * kD);
+        if (!wait_free(&bars->u_empty, i, status, ab)) break;   // U_{i-1} read by the drain
+        mbar_expect_tx(&bars->u_full, 65536);
+        const int row = static_cast<int>((mat0 + chunk(i)) * kD);
 #pragma unroll
         for (int bx = 0; bx < 4; ++bx)
-          tma_load_2d(sm + SC_RAW + bx * 16384, &tm_k, bx * 32, row, &bars->raw_full);
+          tma_load_2d(sm + SC_U + bx * 16384, &tm_u, bx * 32, row, &bars->u_full);
         issued = i + 1;
       }
       int dummy = 0;
-      if (issued >= 1) mbar_wait(&bars->raw_full, (issued - 1) & 1, status, &dummy);
+      if (issued >= 1) mbar_wait(&bars->u_full, (issued - 1) & 1, status, &dummy);
     }
   } else if (warp == 11) {
     // ------------------------------------------------------------ MMA issue
@@ -180,22 +179,31 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k, ScanTcArgs args) {
       mbar_wait(&bars->final_mma, 0, status, &dummy);
     }
   } else if (warp >= 8) {
-    // ------------------------------------------------------------ K_i fp32 -> bf16 hi / lo tiles
+    // ------------------------------------------------------------ K_i fp32 (global) -> bf16 hi / lo tiles
+    // Unit (row r, 8-column group g); thread t takes units t + 64 b, so the 16
+    // lanes of a half warp read one contiguous 512-byte row: coalesced.  Half
+    // a matrix (16 units, 32 float4) is held in registers at a time; the
+    // first half of the next K is loaded while this K's second half converts.
     const int t = threadIdx.x - 256;   // 0..63
-    for (int i = 0; i < N; ++i) {
-      const int buf = i & 1;
-      if (!wait_use_w(&bars->raw_full, i, status, ab)) break;
-      // tile `buf` was read by the products of chunk i - 2 (a barrier per
-      // buffer: a parity wait must never trail its barrier by two phases)
-      if (!wait_free_w(&bars->kt_empty[buf], i >> 1, status, ab)) break;
-      uint8_t* th = ktile(sm, buf);
-      uint8_t* tl = th + 32768;
-      // 2048 units of (row r, 8-column group g)
-      for (int u = t; u < 2048; u += kConvThreads) {
+    float4 x[32];
+    auto load_half = [&](int jj, int hf) {
+      const float4* src = reinterpret_cast<const float4*>(
+          args.K + (mat0 + jj) * static_cast<size_t>(kD) * kD);
+#pragma unroll
+      for (int b = 0; b < 16; ++b) {
+        const int u = t + 64 * (16 * hf + b);
         const int r = u >> 4, g = u & 15;
-        const float4 x0 = *raw_chunk(sm + SC_RAW, r, 8 * g);
-        const float4 x1 = *raw_chunk(sm + SC_RAW, r, 8 * g + 4);
-        const float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        x[2 * b] = __ldg(src + r * 32 + 2 * g);
+        x[2 * b + 1] = __ldg(src + r * 32 + 2 * g + 1);
+      }
+    };
+    auto convert_half = [&](uint8_t* th, int hf) {
+#pragma unroll
+      for (int b = 0; b < 16; ++b) {
+        const int u = t + 64 * (16 * hf + b);
+        const int r = u >> 4, g = u & 15;
+        const float v[8] = {x[2 * b].x, x[2 * b].y, x[2 * b].z, x[2 * b].w,
+                            x[2 * b + 1].x, x[2 * b + 1].y, x[2 * b + 1].z, x[2 * b + 1].w};
         float hi[8], lo[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -203,11 +211,22 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k, ScanTcArgs args) {
           lo[e] = v[e] - hi[e];
         }
         st_row8(th, P128, r, g, hi);
-        st_row8(tl, P128, r, g, lo);
+        st_row8(th + 32768, P128, r, g, lo);
       }
+    };
+    if (N > 0) load_half(chunk(0), 0);
+    for (int i = 0; i < N; ++i) {
+      const int buf = i & 1;
+      // tile `buf` was read by the products of chunk i - 2 (a barrier per
+      // buffer: a parity wait must never trail its barrier by two phases)
+      if (!wait_free_w(&bars->kt_empty[buf], i >> 1, status, ab)) break;
+      uint8_t* th = ktile(sm, buf);
+      convert_half(th, 0);
+      load_half(chunk(i), 1);
+      convert_half(th, 1);
       fence_async_smem();
-      mbar_arrive_warp(&bars->raw_empty);
       mbar_arrive_warp(&bars->kt_full[buf]);
+      if (i + 1 < N) load_half(chunk(i + 1), 0);
     }
   } else {
     // ------------------------------------------------------------ state rows
@@ -227,104 +246,43 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_k, ScanTcArgs args) {
         tmem_st16(tmem + lb + TS_SH + h * 32 + q * 16, zr);
         tmem_st16(tmem + lb + TS_SL + h * 32 + q * 16, zr);
       }
-      if (RULE == 2) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          tmem_st16(tmem + lb + TS_M + h * 64 + q * 16, zr);
-          tmem_st16(tmem + lb + TS_V + h * 64 + q * 16, zr);
-        }
-      }
       tmem_st_wait();
     }
     tc_fence_before();
     mbar_arrive_warp(&bars->s_full);
-    // U of a chunk is loaded a whole chunk step ahead: the loads of U_{i+1} go
-    // out right after the drain of chunk i has consumed U_i, so their latency
-    // (at the chip's load) is off the chain
-    float u[64];
-    auto load_u = [&](int jj) {
-      const float4* up = reinterpret_cast<const float4*>(
-          args.U + (mat0 + jj) * static_cast<size_t>(kD) * kD + rowoff);
-#pragma unroll
-      for (int f = 0; f < 16; ++f) {
-        const float4 x = __ldg(up + f);
-        u[4 * f] = x.x;
-        u[4 * f + 1] = x.y;
-        u[4 * f + 2] = x.z;
-        u[4 * f + 3] = x.w;
-      }
-    };
-    load_u(REV ? N - 1 : 0);
     for (int i = 0; i < N; ++i) {
-      const int j = REV ? N - 1 - i : i;   // chunk
+      const int j = chunk(i);
       const size_t mo = (mat0 + j) * static_cast<size_t>(kD) * kD + rowoff;
-      // pre-update state (and moments at chunk 0) out while the products run
+      // pre-update state out while the products run
       float4* so = reinterpret_cast<float4*>(args.S + mo);
 #pragma unroll
       for (int f = 0; f < 16; ++f)
         so[f] = make_float4(st[4 * f], st[4 * f + 1], st[4 * f + 2], st[4 * f + 3]);
-      if (RULE == 2 && i == 0) {
-        float4* mh = reinterpret_cast<float4*>(args.M_hist + mo);
-        float4* vh = reinterpret_cast<float4*>(args.V_hist + mo);
-#pragma unroll
-        for (int f = 0; f < 16; ++f) mh[f] = vh[f] = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      const size_t gi = mat0 + j;
-      const float a = __ldg(args.a + gi);
-      float bb = 0.f, mu = 0.f, nu = 0.f;
-      if (RULE == 2) {
-        bb = __ldg(args.b + gi);
-        mu = __ldg(args.m + gi);
-        nu = __ldg(args.n + gi);
-      }
+      const float a = __ldg(args.a + mat0 + j);
+      if (!wait_use_w(&bars->u_full, i, status, ab)) break;
       if (!wait_use_w(&bars->g_full, i, status, ab)) break;
       tc_fence_after();
       const bool last = i + 1 == N;
-      const size_t mo1 = mo + static_cast<size_t>(kD) * kD;   // chunk i + 1
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         float g[16];
         tmem_ld16(tmem + lb + TS_G + h * 64 + 16 * q, g);
-        tmem_ld_wait();
-        if (RULE == 0) {
+        // U_i from the swizzled boxes (row c, columns 64 h + 16 q ..)
+        float u[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) st[16 * q + e] = fmaf(a, st[16 * q + e], u[16 * q + e] - g[e]);
-        } else {
-          float mv[16], vv[16];
-          tmem_ld16(tmem + lb + TS_M + h * 64 + 16 * q, mv);
-          tmem_ld16(tmem + lb + TS_V + h * 64 + 16 * q, vv);
-          tmem_ld_wait();
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float gg = u[16 * q + e] - g[e];
-            mv[e] = fmaf(mu, mv[e], (1.f - mu) * gg);
-            vv[e] = fmaf(nu, vv[e], (1.f - nu) * (gg * gg));
-            st[16 * q + e] = fmaf(a, st[16 * q + e], bb * mv[e] / (sqrtf(vv[e]) + kEpsAdam));
-          }
-          uint32_t rm[16], rv[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            rm[e] = __float_as_uint(mv[e]);
-            rv[e] = __float_as_uint(vv[e]);
-          }
-          tmem_st16(tmem + lb + TS_M + h * 64 + 16 * q, rm);
-          tmem_st16(tmem + lb + TS_V + h * 64 + 16 * q, rv);
-          if (!last) {
-            float4* mh = reinterpret_cast<float4*>(args.M_hist + mo1) + 4 * q;
-            float4* vh = reinterpret_cast<float4*>(args.V_hist + mo1) + 4 * q;
-#pragma unroll
-            for (int f = 0; f < 4; ++f) {
-              mh[f] = make_float4(mv[4 * f], mv[4 * f + 1], mv[4 * f + 2], mv[4 * f + 3]);
-              vh[f] = make_float4(vv[4 * f], vv[4 * f + 1], vv[4 * f + 2], vv[4 * f + 3]);
-            }
-          }
+        for (int f = 0; f < 4; ++f) {
+          const float4 x = *box_chunk(sm + SC_U, c, h * 64 + 16 * q + 4 * f);
+          u[4 * f] = x.x;
+          u[4 * f + 1] = x.y;
+          u[4 * f + 2] = x.z;
+          u[4 * f + 3] = x.w;
         }
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) st[16 * q + e] = fmaf(a, st[16 * q + e], u[e] - g[e]);
       }
-      if (last) {
-        tmem_st_wait();
-        break;
-      }
-      load_u(REV ? j - 1 : j + 1);
+      mbar_arrive_warp(&bars->u_empty);   // U_i read: the next U may load
+      if (last) break;
       // S_{i+1} as packed bf16 hi / lo into TMEM (A operand of the next products)
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
@@ -564,63 +522,65 @@ cudaError_t make_tmap_f32_rows128(CUtensorMap* map, const void* base, uint64_t r
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-template <int RULE, bool REV>
-cudaError_t launch_scan_fwd_tc(const CUtensorMap& mk, const ScanTcArgs& a, int grid,
+template <bool REV>
+cudaError_t launch_scan_fwd_tc(const CUtensorMap& mu, const ScanTcArgs& a, int grid,
                                cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(scan_fwd_tc_kernel<RULE, REV>,
+  cudaError_t e = cudaFuncSetAttribute(scan_fwd_tc_kernel<REV>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, SC_SMEM);
   if (e != cudaSuccess) return e;
-  scan_fwd_tc_kernel<RULE, REV><<<grid, kThreadsScan, SC_SMEM, st>>>(mk, a);
+  scan_fwd_tc_kernel<REV><<<grid, kThreadsScan, SC_SMEM, st>>>(mu, a);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-// Delta only.  The kernel also runs adam (RULE 2), but adam's update
-// M / (sqrt(V) + 1e-6) turns sign-like where V ~ 0 (chunk 0, small nu), so
-// product errors of ~2^-17 move its states by ~1e-3 and its K cotangent by
-// ~1e-1: adam stays on the exact-fp32 kernels at both precisions.
+// Delta only.  Adam's update M / (sqrt(V) + 1e-6) turns sign-like where
+// V ~ 0 (chunk 0, small nu), so product errors of ~2^-17 move its states by
+// ~1e-3 and its K cotangent by ~1e-1: adam stays on the exact-fp32 kernels at
+// both precisions.  The kernels move U, K, S, gS, dU and dK as 16-byte
+// vectors (TMA or float4), so every such pointer must be 16-byte aligned;
+// others take the exact kernels.
+static bool al16(const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; }
+
 bool scan_fwd_tc_supported(const ScanArgs& p) {
-  return p.rule == 0 && p.dh == kD && p.N >= 1 && tma_encode_available();
+  return p.rule == 0 && p.dh == kD && p.N >= 1 && tma_encode_available() && al16(p.U) &&
+         al16(p.K) && al16(p.S);
 }
 
 cudaError_t scan_fwd_tc(const ScanArgs& p, uint32_t* status, cudaStream_t st) {
-  if (p.rule == 2 && (!p.M_hist || !p.V_hist)) return cudaErrorInvalidValue;
-  CUtensorMap mk;
-  cudaError_t e = make_tmap_f32_rows128(&mk, p.K, static_cast<uint64_t>(p.BH) * p.N * kD);
+  if (p.rule != 0) return cudaErrorInvalidValue;
+  CUtensorMap mu;
+  cudaError_t e = make_tmap_f32_rows128(&mu, p.U, static_cast<uint64_t>(p.BH) * p.N * kD);
   if (e != cudaSuccess) return e;
   ScanTcArgs a{};
   a.U = p.U;
+  a.K = p.K;
   a.a = p.a;
-  a.b = p.b;
-  a.m = p.m;
-  a.n = p.n;
   a.S = p.S;
-  a.M_hist = p.M_hist;
-  a.V_hist = p.V_hist;
   a.status = status;
   a.N = p.N;
-  if (p.rule == 2) return launch_scan_fwd_tc<2, false>(mk, a, p.BH, st);
-  return launch_scan_fwd_tc<0, false>(mk, a, p.BH, st);
+  return launch_scan_fwd_tc<false>(mu, a, p.BH, st);
 }
 
 bool scan_bwd_tc_supported(const ScanArgs& p) {
-  return p.rule == 0 && p.dh == kD && p.N >= 1 && tma_encode_available();
+  return p.rule == 0 && p.dh == kD && p.N >= 1 && tma_encode_available() && al16(p.K) &&
+         al16(p.S) && al16(p.gS) && al16(p.dU) && al16(p.dK);
 }
 
 cudaError_t scan_bwd_chain_tc(const ScanArgs& p, uint32_t* status, cudaStream_t st) {
   if (p.rule != 0) return cudaErrorInvalidValue;
-  // reverse chain: dU_i = Sbar_{i+1}
-  CUtensorMap mk;
-  cudaError_t e = make_tmap_f32_rows128(&mk, p.K, static_cast<uint64_t>(p.BH) * p.N * kD);
+  // reverse chain: U := gS, dU_i = Sbar_{i+1}
+  CUtensorMap mu;
+  cudaError_t e = make_tmap_f32_rows128(&mu, p.gS, static_cast<uint64_t>(p.BH) * p.N * kD);
   if (e != cudaSuccess) return e;
   ScanTcArgs a{};
   a.U = p.gS;
+  a.K = p.K;
   a.a = p.a;
   a.S = p.dU;
   a.status = status;
   a.N = p.N;
-  return launch_scan_fwd_tc<0, true>(mk, a, p.BH, st);
+  return launch_scan_fwd_tc<true>(mu, a, p.BH, st);
 }
 
 cudaError_t scan_bwd_dk_tc(const ScanArgs& p, uint32_t* status, cudaStream_t st) {

@@ -189,6 +189,32 @@ def build_optimizers(model: nn.Module, muon_lr=0.02, adam_lr=4e-4, weight_decay=
             torch.optim.AdamW(other, lr=adam_lr, betas=(0.9, 0.95), weight_decay=weight_decay)]
 
 
+def lr_factor(step: int, warmup: int, total: int) -> float:
+    """Linear warm-up to 1 over ``warmup`` steps, then a cosine from 1 to 0.1
+    at ``total`` (train_ablation.py:310-314)."""
+    if step < warmup:
+        return (step + 1) / warmup
+    prog = (step - warmup) / max(1, total - warmup)
+    return 0.1 + 0.9 * 0.5 * (1 + math.cos(math.pi * min(prog, 1.0)))
+
+
+class LrSchedule:
+    """Scales every parameter group's learning rate by ``lr_factor`` of the
+    step, from the rates the groups had when it was built, as the reference's
+    loop does before each step (train_ablation.py:453-457)."""
+
+    def __init__(self, optimizers, warmup: int = 500, total: int = 9600):
+        self.optimizers, self.warmup, self.total = optimizers, warmup, total
+        self.base = [[g["lr"] for g in o.param_groups] for o in optimizers]
+
+    def set_step(self, step: int) -> float:
+        fac = lr_factor(step, self.warmup, self.total)
+        for opt, bases in zip(self.optimizers, self.base):
+            for g, b in zip(opt.param_groups, bases):
+                g["lr"] = b * fac
+        return fac
+
+
 def train_step(model: nn.Module, optimizers, idx: torch.Tensor, targets: torch.Tensor,
                amp: bool = True) -> torch.Tensor:
     """One optimisation step (train_ablation.py:458-474 with accum = 1): bf16

@@ -53,6 +53,7 @@ def _cpu_forward(m, x):
 @pytest.mark.parametrize("inner", ["delta", "adam"])
 def test_patched_mixer_forward_matches_cpu(inner):
     load_pkg()
+    assert not torch.backends.cuda.matmul.allow_tf32   # fp32 projections, as on the CPU
     integ = importlib.import_module(PKG_NAME + ".integration")
     torch.manual_seed(11)
     m = _MixerLayout(256, 2, inner, 64, 3)

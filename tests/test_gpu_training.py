@@ -32,12 +32,21 @@ def test_model_forward_and_gradient_match_cpu_oracle():
         assert e < 1e-3, n
 
 
+@pytest.fixture
+def tf32_matmul():
+    """TF32 GEMMs as the reference's trainer enables them, restored afterwards
+    (other tests compare fp32 GEMMs against the CPU)."""
+    old = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    yield
+    torch.backends.cuda.matmul.allow_tf32 = old
+
+
 @pytest.mark.parametrize("inner", ["delta", "muon", "adam"])
-def test_training_steps_lower_the_loss(inner):
+def test_training_steps_lower_the_loss(inner, tf32_matmul):
     pkg = load_pkg()
     tr = _training()
     torch.manual_seed(7)
-    torch.backends.cuda.matmul.allow_tf32 = True
     model = tr.LanguageModel(1000, 256, 2, 4, inner, chunk=64).cuda()   # dh 64
     opts = tr.build_optimizers(model, muon_lr=0.02, adam_lr=3e-3)
     g = torch.Generator().manual_seed(8)

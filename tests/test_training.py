@@ -173,3 +173,21 @@ def test_two_rank_ddp_step_equals_single_process(tmp_path):
         o.step()
     for n, t in model.state_dict().items():
         assert (got["params"][n] - t).abs().max().item() < 1e-5, n
+
+
+def test_lr_schedule_matches_reference_factor():
+    """lr_factor restates train_ablation.py:310-314; LrSchedule scales the
+    groups' rates from their values at construction."""
+    import math
+    tr = _training()
+    assert tr.lr_factor(0, 500, 9600) == 1 / 500
+    assert tr.lr_factor(499, 500, 9600) == 1.0
+    assert abs(tr.lr_factor(500 + 9100 // 2, 500, 9600) - (0.1 + 0.45)) < 1e-12
+    assert abs(tr.lr_factor(20000, 500, 9600) - 0.1) < 1e-12
+    m = tr.LanguageModel(50, 32, 1, 2, "delta")
+    opts = tr.build_optimizers(m, muon_lr=0.02, adam_lr=4e-4)
+    sched = tr.LrSchedule(opts, warmup=10, total=100)
+    for step in (0, 4, 9, 55, 99):
+        fac = sched.set_step(step)
+        assert math.isclose(opts[0].param_groups[0]["lr"], 0.02 * fac)
+        assert math.isclose(opts[1].param_groups[0]["lr"], 4e-4 * fac)
