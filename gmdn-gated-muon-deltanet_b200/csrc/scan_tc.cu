@@ -16,21 +16,21 @@
 //   * S (fp32) lives in the registers of the eight state warps: thread (row c
 //     = TMEM lane, half h) owns S[c][64h .. 64h+63].  They write S_hi / S_lo
 //     as packed bf16 pairs into TMEM, the A operand (128 x 128, K = dk).
-//   * K_i is read from global memory by two converter warps in row order (a
-//     half warp reads one 512-byte row: coalesced) and written as bf16 hi / lo
+//   * K_i and U_i arrive by TMA as fp32 in four 128-byte-swizzled boxes of 32
+//     columns x 128 rows each, issued a chunk ahead by one thread.  After the
+//     products of chunk i the state warps turn K_{i+1} into the bf16 hi / lo
 //     tiles (two 64-column SW128 panels each, rows = dk), the MN-major B
-//     operand.  The tiles are double-buffered and the converters hold half of
-//     the next K in registers, so K_{i+1} is loaded and converted while the
-//     products of chunk i run.
-//   * U_i arrives by TMA as fp32 in four 128-byte-swizzled boxes of 32
-//     columns x 128 rows; a state thread reads its row's 16-byte chunks, which
-//     the swizzle spreads over all banks (a row per thread from global memory
-//     costs a wavefront per row and made the step L1-bound).  The TMA for
-//     U_{i+1} is issued as soon as every state warp has read U_i.
-//   * S_out is written from registers (16-byte stores).
+//     operand, next to their own update of S: the raw box and the tiles are
+//     read and written in orders where 32 threads hit every bank group once
+//     per 8 rows (four wavefronts per 512 bytes).
+//   * S_out[i] = S_i goes out through a 32 KB staging area and TMA stores, one
+//     half of the columns after the other, while the products of chunk i run.
+//     Storing rows straight from the registers (one row per thread) sends a
+//     16-byte partial line per thread and instruction to L2 and cost as much
+//     as the whole chain.
 //
-// Warp roles (384 threads): warps 0-7 state, 8-9 K conversion, 10 TMA,
-// 11 TMEM allocation and MMA issue.  Every wait is bounded (tc.cuh).
+// Warp roles (352 threads): warps 0-7 state, 8 TMA loads, 9 TMA stores,
+// 10 TMEM allocation and MMA issue.  Every wait is bounded (tc.cuh).
 //
 // HBM per chunk-head: U, K in (128 KB), S out (64 KB).
 
@@ -47,46 +47,45 @@ namespace {
 using namespace tc;
 
 constexpr int kD = 128;
-constexpr int kThreadsScan = 384;
-constexpr int kConvThreads = 64;
-constexpr uint32_t P128 = 16384;   // panel stride of a 128-row bf16 tile
+constexpr int kThreadsScan = 352;   // warps 0-7 state, 8 TMA loads, 9 TMA stores, 10 MMA
+constexpr uint32_t P128 = 16384;    // panel stride of a 128-row bf16 tile
 
-// shared memory (bytes from a 1024-aligned base)
-constexpr uint32_t SC_KT = 0;          // K_i bf16 tiles, 2 buffers x (hi 32 KB, lo 32 KB)
-constexpr uint32_t SC_U = 131072;      // U_i fp32: 4 SW128 boxes of 32 cols x 128 rows (64 KB)
-constexpr uint32_t SC_BAR = 196608;
+// shared memory (bytes from a 1024-aligned base); an fp32 matrix is four
+// 128-byte-swizzled TMA boxes of 32 columns x 128 rows (16 KB each)
+constexpr uint32_t SC_KR = 0;          // K_i fp32 (64 KB)
+constexpr uint32_t SC_KT = 65536;      // K_i bf16 hi (32 KB) + lo (32 KB): the MMA's B operand
+constexpr uint32_t SC_U = 131072;      // U_i fp32 (64 KB)
+constexpr uint32_t SC_SO = 196608;     // S_i staging for the TMA store: two boxes (32 KB)
+constexpr uint32_t SC_BAR = 229376;
 constexpr uint32_t SC_SMEM = SC_BAR + 256 + 1024;
+static_assert(SC_SMEM <= 232448, "shared memory per block");
 
 // TMEM columns: S hi / lo (packed bf16 pairs, the A operand), the product
 constexpr uint32_t TS_SH = 0, TS_SL = 64, TS_G = 128;
 
 struct BarsS {
-  uint64_t u_full, u_empty;
-  uint64_t kt_full[2], kt_empty[2];
-  uint64_t s_full, g_full;
-  uint64_t final_mma;
+  uint64_t u_full, u_empty, k_full, k_empty;
+  uint64_t so_full[2], so_free[2];   // S staging, [h]: columns 64h .. 64h + 63
+  uint64_t s_full, g_full, final_mma;
   uint32_t tmem_base;
   int abort_flag;
 };
 static_assert(sizeof(BarsS) <= 256, "barrier block");
 
 struct ScanTcArgs {
-  const float *U, *K, *a;
-  float* S;
+  const float* a;
   uint32_t* status;
   int N;
 };
 
-__device__ __forceinline__ uint8_t* ktile(uint8_t* sm, int buf) {
-  return sm + SC_KT + buf * 65536u;
-}
-
-// 16-byte chunk holding fp32 columns [c, c+4) of row r of a tile stored as
+// 16-byte chunk holding fp32 columns [c, c+4) of row r of a matrix stored as
 // four 128-byte-swizzled boxes of 32 columns (what a TMA load with
-// CU_TENSOR_MAP_SWIZZLE_128B and a 32 x 128 box writes).
-__device__ __forceinline__ const float4* box_chunk(const uint8_t* t, int r, int c) {
+// CU_TENSOR_MAP_SWIZZLE_128B and a 32 x 128 box writes).  Thirty-two threads
+// on consecutive rows reading the same columns hit every bank group once per
+// eight rows: four wavefronts for 512 bytes, no conflict.
+__device__ __forceinline__ uint32_t box_off(int r, int c) {
   const int j = (c & 31) >> 2;
-  return reinterpret_cast<const float4*>(t + (c >> 5) * 16384 + r * 128 + ((j ^ (r & 7)) << 4));
+  return (c >> 5) * 16384 + r * 128 + ((j ^ (r & 7)) << 4);
 }
 
 // Forward (REV false): chunks in order, B = K MN-major, G' = S K.
@@ -96,7 +95,8 @@ __device__ __forceinline__ const float4* box_chunk(const uint8_t* t, int r, int 
 // dU_i = Sbar_{i+1} (fast_scan.py:182-186 for delta, where Gbar = Sbar).
 template <bool REV>
 __global__ void __launch_bounds__(kThreadsScan, 1)
-scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_u, ScanTcArgs args) {
+scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_s, ScanTcArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
@@ -111,9 +111,11 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_u, ScanTcArgs args) {
   if (threadIdx.x == 0) {
     mbar_init(&bars->u_full, 1);
     mbar_init(&bars->u_empty, 8);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&bars->kt_full[b], kConvThreads / 32);
-      mbar_init(&bars->kt_empty[b], 1);
+    mbar_init(&bars->k_full, 1);
+    mbar_init(&bars->k_empty, 8);
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&bars->so_full[h], 4);
+      mbar_init(&bars->so_free[h], 1);
     }
     mbar_init(&bars->s_full, 8);
     mbar_init(&bars->g_full, 1);
@@ -121,7 +123,7 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_u, ScanTcArgs args) {
     bars->abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 11) {
+  if (warp == 10) {
     tmem_alloc(&bars->tmem_base, kTmemCols);
     tmem_relinquish();
   }
@@ -131,24 +133,51 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_u, ScanTcArgs args) {
   const uint32_t tmem = bars->tmem_base;
   const size_t mat0 = static_cast<size_t>(bh) * N;   // matrix index of chunk 0
   auto chunk = [&](int i) { return REV ? N - 1 - i : i; };
+  auto row0 = [&](int i) { return static_cast<int>((mat0 + chunk(i)) * kD); };
 
-  if (warp == 10) {
-    // ------------------------------------------------------------ TMA: U_i
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA loads: K_j, U_j
     if (lane == 0) {
       int issued = 0;
-      for (int i = 0; i < N; ++i) {
-        if (!wait_free(&bars->u_empty, i, status, ab)) break;   // U_{i-1} read by the drain
-        mbar_expect_tx(&bars->u_full, 65536);
-        const int row = static_cast<int>((mat0 + chunk(i)) * kD);
+      for (int j = 0; j < N; ++j) {
+        if (!wait_free(&bars->k_empty, j, status, ab)) break;   // K_{j-1} converted
+        mbar_expect_tx(&bars->k_full, 65536);
 #pragma unroll
         for (int bx = 0; bx < 4; ++bx)
-          tma_load_2d(sm + SC_U + bx * 16384, &tm_u, bx * 32, row, &bars->u_full);
-        issued = i + 1;
+          tma_load_2d(sm + SC_KR + bx * 16384, &tm_k, bx * 32, row0(j), &bars->k_full);
+        if (!wait_free(&bars->u_empty, j, status, ab)) { issued = -(j + 1); break; }
+        mbar_expect_tx(&bars->u_full, 65536);
+#pragma unroll
+        for (int bx = 0; bx < 4; ++bx)
+          tma_load_2d(sm + SC_U + bx * 16384, &tm_u, bx * 32, row0(j), &bars->u_full);
+        issued = j + 1;
       }
+      // no load may still be in flight when the block exits
       int dummy = 0;
-      if (issued >= 1) mbar_wait(&bars->u_full, (issued - 1) & 1, status, &dummy);
+      const int nk = issued < 0 ? -issued : issued, nu = issued < 0 ? -issued - 1 : issued;
+      if (nk >= 1) mbar_wait(&bars->k_full, (nk - 1) & 1, status, &dummy);
+      if (nu >= 1) mbar_wait(&bars->u_full, (nu - 1) & 1, status, &dummy);
     }
-  } else if (warp == 11) {
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ TMA stores: S_out[i] = S_i
+    // Both halves of S_i go through the same two staging boxes, one half
+    // after the other: columns 0-63 (state warps 0-3), then 64-127 (4-7).
+    if (lane == 0) {
+      for (int i = 0; i < N; ++i) {
+        bool ok = true;
+        for (int h = 0; h < 2 && ok; ++h) {
+          if (!wait_use(&bars->so_full[h], i, status, ab)) { ok = false; break; }
+          tma_store_2d(&tm_s, 64 * h, row0(i), sm + SC_SO);
+          tma_store_2d(&tm_s, 64 * h + 32, row0(i), sm + SC_SO + 16384);
+          bulk_commit();
+          bulk_wait_read0();
+          mbar_arrive(&bars->so_free[h]);
+        }
+        if (!ok) break;
+      }
+      bulk_wait0();
+    }
+  } else if (warp == 10) {
     // ------------------------------------------------------------ MMA issue
     if (lane == 0) {
       // forward: S (TMEM) x K (MN-major); reverse: Sbar (TMEM) x K^T (K-major)
@@ -156,12 +185,10 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_u, ScanTcArgs args) {
       auto bdesc = [](uint32_t t, int k) {
         return REV ? desc_kmajor(t, P128, k) : desc_mnmajor(t, P128, k);
       };
+      const uint32_t kh = smem_u32(sm + SC_KT), kl = kh + 32768u;
       for (int i = 0; i < N; ++i) {
-        const int buf = i & 1;
-        if (!wait_use(&bars->s_full, i, status, ab)) break;
-        if (!wait_use(&bars->kt_full[buf], i >> 1, status, ab)) break;
+        if (!wait_use(&bars->s_full, i, status, ab)) break;   // S_i and K_i tiles ready
         tc_fence_after();
-        const uint32_t kh = smem_u32(ktile(sm, buf)), kl = kh + 32768u;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           mma_bf16_ts(tmem + TS_G, tmem + TS_SH + k * 8, bdesc(kh, k), ID, k > 0);
@@ -172,71 +199,46 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_u, ScanTcArgs args) {
         for (int k = 0; k < 8; ++k)
           mma_bf16_ts(tmem + TS_G, tmem + TS_SL + k * 8, bdesc(kh, k), ID, 1);
         mma_commit(&bars->g_full);
-        mma_commit(&bars->kt_empty[buf]);
       }
       mma_commit(&bars->final_mma);
       int dummy = 0;
       mbar_wait(&bars->final_mma, 0, status, &dummy);
-    }
-  } else if (warp >= 8) {
-    // ------------------------------------------------------------ K_i fp32 (global) -> bf16 hi / lo tiles
-    // Unit (row r, 8-column group g); thread t takes units t + 64 b, so the 16
-    // lanes of a half warp read one contiguous 512-byte row: coalesced.  Half
-    // a matrix (16 units, 32 float4) is held in registers at a time; the
-    // first half of the next K is loaded while this K's second half converts.
-    const int t = threadIdx.x - 256;   // 0..63
-    float4 x[32];
-    auto load_half = [&](int jj, int hf) {
-      const float4* src = reinterpret_cast<const float4*>(
-          args.K + (mat0 + jj) * static_cast<size_t>(kD) * kD);
-#pragma unroll
-      for (int b = 0; b < 16; ++b) {
-        const int u = t + 64 * (16 * hf + b);
-        const int r = u >> 4, g = u & 15;
-        x[2 * b] = __ldg(src + r * 32 + 2 * g);
-        x[2 * b + 1] = __ldg(src + r * 32 + 2 * g + 1);
-      }
-    };
-    auto convert_half = [&](uint8_t* th, int hf) {
-#pragma unroll
-      for (int b = 0; b < 16; ++b) {
-        const int u = t + 64 * (16 * hf + b);
-        const int r = u >> 4, g = u & 15;
-        const float v[8] = {x[2 * b].x, x[2 * b].y, x[2 * b].z, x[2 * b].w,
-                            x[2 * b + 1].x, x[2 * b + 1].y, x[2 * b + 1].z, x[2 * b + 1].w};
-        float hi[8], lo[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          hi[e] = __bfloat162float(__float2bfloat16_rn(v[e]));
-          lo[e] = v[e] - hi[e];
-        }
-        st_row8(th, P128, r, g, hi);
-        st_row8(th + 32768, P128, r, g, lo);
-      }
-    };
-    if (N > 0) load_half(chunk(0), 0);
-    for (int i = 0; i < N; ++i) {
-      const int buf = i & 1;
-      // tile `buf` was read by the products of chunk i - 2 (a barrier per
-      // buffer: a parity wait must never trail its barrier by two phases)
-      if (!wait_free_w(&bars->kt_empty[buf], i >> 1, status, ab)) break;
-      uint8_t* th = ktile(sm, buf);
-      convert_half(th, 0);
-      load_half(chunk(i), 1);
-      convert_half(th, 1);
-      fence_async_smem();
-      mbar_arrive_warp(&bars->kt_full[buf]);
-      if (i + 1 < N) load_half(chunk(i + 1), 0);
     }
   } else {
     // ------------------------------------------------------------ state rows
     const int c = (warp & 3) * 32 + lane;   // row of S = TMEM lane
     const int h = warp >> 2;                // columns [64 h, 64 h + 64)
     const uint32_t lb = tmem_lane_base(warp);
-    const size_t rowoff = static_cast<size_t>(c) * kD + h * 64;
     float st[64];
 #pragma unroll
     for (int e = 0; e < 64; ++e) st[e] = 0.f;
+
+    // K_m fp32 (raw boxes) -> bf16 hi / lo tiles, the MMA's MN-major B
+    // operand; unit (row r, 8-column group g), thread t takes units t + 256 b
+    // (both sides conflict-free: four wavefronts per 512 bytes)
+    auto convert_k = [&]() {
+      uint8_t* kt = sm + SC_KT;
+      const int t = threadIdx.x;
+#pragma unroll 4
+      for (int b = 0; b < 8; ++b) {
+        const int u = t + 256 * b;
+        const int r = u >> 4, g = u & 15;
+        const float4 x0 = *reinterpret_cast<const float4*>(sm + SC_KR + box_off(r, 8 * g));
+        const float4 x1 = *reinterpret_cast<const float4*>(sm + SC_KR + box_off(r, 8 * g + 4));
+        const float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        float hi[8], lo[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          hi[e] = __bfloat162float(__float2bfloat16_rn(v[e]));
+          lo[e] = v[e] - hi[e];
+        }
+        st_row8(kt, P128, r, g, hi);
+        st_row8(kt + 32768, P128, r, g, lo);
+      }
+      fence_async_smem();                   // tiles -> the MMA (async proxy)
+      mbar_arrive_warp(&bars->k_empty);     // raw K read: the next K may load
+    };
+
     {
       uint32_t zr[16];
 #pragma unroll
@@ -248,17 +250,23 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_u, ScanTcArgs args) {
       }
       tmem_st_wait();
     }
+    bool ok = wait_use_w(&bars->k_full, 0, status, ab);
+    if (ok) convert_k();
     tc_fence_before();
     mbar_arrive_warp(&bars->s_full);
-    for (int i = 0; i < N; ++i) {
-      const int j = chunk(i);
-      const size_t mo = (mat0 + j) * static_cast<size_t>(kD) * kD + rowoff;
-      // pre-update state out while the products run
-      float4* so = reinterpret_cast<float4*>(args.S + mo);
+    for (int i = 0; ok && i < N; ++i) {
+      // pre-update state out: this half's 64 columns into the staging boxes
+      // (after the other half of S_{i-1}, or this half's, has been read out)
+      if (!(h == 0 ? wait_free_w(&bars->so_free[1], i, status, ab)
+                   : wait_use_w(&bars->so_free[0], i, status, ab)))
+        break;
 #pragma unroll
       for (int f = 0; f < 16; ++f)
-        so[f] = make_float4(st[4 * f], st[4 * f + 1], st[4 * f + 2], st[4 * f + 3]);
-      const float a = __ldg(args.a + mat0 + j);
+        *reinterpret_cast<float4*>(sm + SC_SO + box_off(c, 4 * f)) =
+            make_float4(st[4 * f], st[4 * f + 1], st[4 * f + 2], st[4 * f + 3]);
+      fence_async_smem();
+      mbar_arrive_warp(&bars->so_full[h]);
+      const float a = __ldg(args.a + mat0 + chunk(i));
       if (!wait_use_w(&bars->u_full, i, status, ab)) break;
       if (!wait_use_w(&bars->g_full, i, status, ab)) break;
       tc_fence_after();
@@ -267,11 +275,12 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_u, ScanTcArgs args) {
       for (int q = 0; q < 4; ++q) {
         float g[16];
         tmem_ld16(tmem + lb + TS_G + h * 64 + 16 * q, g);
-        // U_i from the swizzled boxes (row c, columns 64 h + 16 q ..)
+        // U_i (row c, columns 64 h + 16 q ..)
         float u[16];
 #pragma unroll
         for (int f = 0; f < 4; ++f) {
-          const float4 x = *box_chunk(sm + SC_U, c, h * 64 + 16 * q + 4 * f);
+          const float4 x =
+              *reinterpret_cast<const float4*>(sm + SC_U + box_off(c, h * 64 + 16 * q + 4 * f));
           u[4 * f] = x.x;
           u[4 * f + 1] = x.y;
           u[4 * f + 2] = x.z;
@@ -283,6 +292,9 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_u, ScanTcArgs args) {
       }
       mbar_arrive_warp(&bars->u_empty);   // U_i read: the next U may load
       if (last) break;
+      // K_{i+1} into the tiles (the products of chunk i are done: g_full)
+      if (!wait_use_w(&bars->k_full, i + 1, status, ab)) break;
+      convert_k();
       // S_{i+1} as packed bf16 hi / lo into TMEM (A operand of the next products)
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
@@ -304,7 +316,7 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_u, ScanTcArgs args) {
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 11) {
+  if (warp == 10) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -315,36 +327,43 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_u, ScanTcArgs args) {
 //   dK_i = -S_i^T dU_i          (fast_scan.py:185, dU_i = Gbar_i)
 //   da_i = <dU_i, S_i>          (fast_scan.py:150; for delta Gbar = Sbar)
 // Persistent: one CTA per SM walks the matrices.  Sixteen converter warps
-// read S_i and dU_i (fp32) from global memory, add the row dot products for
-// da_i, and write both as split bf16 hi / lo tiles (rows = v, the contracted
-// index); one thread issues D = S_hi^T dU_hi + S_hi^T dU_lo + S_lo^T dU_hi
-// (both operands MN-major) into one of two TMEM accumulators, which the same
-// warps drain into dK while the next matrix's tiles are built.
+// read S_i and dU_i (fp32) from global memory in row order (a warp reads one
+// 512-byte row per load), add the dot products for da_i, and write both as
+// split bf16 hi / lo tiles (rows = v, the contracted index); one thread
+// issues D = S_hi^T dU_hi + S_hi^T dU_lo + S_lo^T dU_hi (both operands
+// MN-major) into one of two TMEM accumulators, which the same warps drain
+// into a staging area for the TMA store of dK_i while the next matrix's
+// products run.  The next matrix's loads are in flight meanwhile.
 // ---------------------------------------------------------------------------
 
 constexpr int kConvWarpsDk = 16;                 // convert and drain, 4 per TMEM lane group
-constexpr int kThreadsDk = (kConvWarpsDk + 1) * 32;   // + warp 16: TMEM allocation, MMA issue
+constexpr int kMmaWarpDk = kConvWarpsDk;         // TMEM allocation, MMA issue
+constexpr int kStoreWarpDk = kConvWarpsDk + 1;   // TMA stores of dK
+constexpr int kThreadsDk = (kConvWarpsDk + 2) * 32;
 constexpr uint32_t DK_S = 0;            // S_i hi (32 KB), lo (32 KB)
 constexpr uint32_t DK_U = 65536;        // dU_i hi, lo
-constexpr uint32_t DK_BAR = 131072;
+constexpr uint32_t DK_O = 131072;       // dK_i fp32 staging: four SW128 boxes (64 KB)
+constexpr uint32_t DK_BAR = 196608;
 constexpr uint32_t DK_SMEM = DK_BAR + 256 + 1024;
 
 struct BarsDk {
-  uint64_t tiles_full, done[2], d_free[2], final_mma;
+  uint64_t tiles_full, done[2], d_free[2], o_full, o_free, final_mma;
   uint32_t tmem_base;
   int abort_flag;
-  float red[kConvWarpsDk];
+  int red_count[2];
+  float red[2][kConvWarpsDk];
 };
 static_assert(sizeof(BarsDk) <= 256, "barrier block");
 
 struct DkArgs {
   const float *S, *dU;
-  float *dK, *da;
+  float* da;
   uint32_t* status;
   int mats;
 };
 
-__global__ void __launch_bounds__(kThreadsDk, 1) scan_bwd_dk_tc_kernel(DkArgs args) {
+__global__ void __launch_bounds__(kThreadsDk, 1)
+scan_bwd_dk_tc_kernel(const __grid_constant__ CUtensorMap tm_dk, DkArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
@@ -359,12 +378,15 @@ __global__ void __launch_bounds__(kThreadsDk, 1) scan_bwd_dk_tc_kernel(DkArgs ar
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->done[b], 1);
       mbar_init(&bars->d_free[b], kConvWarpsDk);
+      bars->red_count[b] = 0;
     }
+    mbar_init(&bars->o_full, kConvWarpsDk);
+    mbar_init(&bars->o_free, 1);
     mbar_init(&bars->final_mma, 1);
     bars->abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == kConvWarpsDk) {
+  if (warp == kMmaWarpDk) {
     tmem_alloc(&bars->tmem_base, 256);
     tmem_relinquish();
   }
@@ -373,7 +395,7 @@ __global__ void __launch_bounds__(kThreadsDk, 1) scan_bwd_dk_tc_kernel(DkArgs ar
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
 
-  if (warp == kConvWarpsDk) {
+  if (warp == kMmaWarpDk) {
     if (lane == 0) {
       // D[m][n] = -sum_v S[v][m] dU[v][n]: A = S^T and B = dU, both MN-major
       constexpr uint32_t ID = idesc_bf16(128, 128, true, true, true);
@@ -401,16 +423,32 @@ __global__ void __launch_bounds__(kThreadsDk, 1) scan_bwd_dk_tc_kernel(DkArgs ar
       int dummy = 0;
       mbar_wait(&bars->final_mma, 0, status, &dummy);
     }
+  } else if (warp == kStoreWarpDk) {
+    if (lane == 0) {
+      int it = 0;
+      for (int m = blockIdx.x; m < args.mats; m += G, ++it) {
+        if (!wait_use(&bars->o_full, it, status, ab)) break;
+#pragma unroll
+        for (int bx = 0; bx < 4; ++bx)
+          tma_store_2d(&tm_dk, bx * 32, m * kD, sm + DK_O + bx * 16384);
+        bulk_commit();
+        bulk_wait_read0();
+        mbar_arrive(&bars->o_free);
+      }
+      bulk_wait0();
+    }
   } else {
-    const int r = (warp & 3) * 32 + lane;   // tile row v / TMEM lane m
-    const int qc = warp >> 2;               // columns [32 qc, 32 qc + 32)
+    const int t = threadIdx.x;              // 0 .. 511
+    const int r = (warp & 3) * 32 + lane;   // TMEM lane m (drain)
+    const int qc = warp >> 2;               // drain columns [32 qc, 32 qc + 32)
     const uint32_t lb = tmem_lane_base(warp);
-    auto drain = [&](int mm, int itp) -> bool {
+    // dK_i: TMEM -> the staging boxes (box qc, row r: conflict-free) -> TMA store
+    auto drain = [&](int itp) -> bool {
       const int b = itp & 1;
       if (!wait_use_w(&bars->done[b], itp >> 1, status, ab)) return false;
+      if (!wait_free_w(&bars->o_free, itp, status, ab)) return false;   // last store read out
       tc_fence_after();
-      float4* dk = reinterpret_cast<float4*>(args.dK + static_cast<size_t>(mm) * kD * kD +
-                                             static_cast<size_t>(r) * kD + qc * 32);
+      uint8_t* ob = sm + DK_O + qc * 16384 + r * 128;
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
         float x[16];
@@ -418,82 +456,96 @@ __global__ void __launch_bounds__(kThreadsDk, 1) scan_bwd_dk_tc_kernel(DkArgs ar
         tmem_ld_wait();
 #pragma unroll
         for (int f = 0; f < 4; ++f)
-          dk[4 * q + f] = make_float4(x[4 * f], x[4 * f + 1], x[4 * f + 2], x[4 * f + 3]);
+          *reinterpret_cast<float4*>(ob + (((4 * q + f) ^ (r & 7)) << 4)) =
+              make_float4(x[4 * f], x[4 * f + 1], x[4 * f + 2], x[4 * f + 3]);
       }
       tc_fence_before();
       mbar_arrive_warp(&bars->d_free[b]);
+      fence_async_smem();
+      mbar_arrive_warp(&bars->o_full);
       return true;
     };
-    // a row quarter of S_i and dU_i (32 + 32 floats) is loaded in one batch,
-    // and the next matrix's batch goes out as soon as the previous drain is
-    // done, so it is in flight while this matrix's products run
+    // S_i and dU_i in coalesced order: float4 j = t + 512 f is row j >> 5,
+    // columns 4 (j & 31) .. + 3, so a warp reads one 512-byte row per load.
+    // The next matrix's loads go out as soon as this one's tiles are written,
+    // so they are in flight while its products run and the previous dK drains.
     float4 sv4[8], uv4[8];
     auto load_mat = [&](int mm) {
-      const size_t off = static_cast<size_t>(mm) * kD * kD + static_cast<size_t>(r) * kD + qc * 32;
-      const float4* sp = reinterpret_cast<const float4*>(args.S + off);
-      const float4* up = reinterpret_cast<const float4*>(args.dU + off);
+      const float4* sp = reinterpret_cast<const float4*>(args.S + static_cast<size_t>(mm) * kD * kD);
+      const float4* up = reinterpret_cast<const float4*>(args.dU + static_cast<size_t>(mm) * kD * kD);
 #pragma unroll
       for (int f = 0; f < 8; ++f) {
-        sv4[f] = __ldg(sp + f);
-        uv4[f] = __ldg(up + f);
+        sv4[f] = __ldg(sp + t + 512 * f);
+        uv4[f] = __ldg(up + t + 512 * f);
       }
+    };
+    // four fp32 -> bf16 hi / lo at (row, columns 4 c4 ..): 8 bytes into the
+    // MN-major SW128 tile (panel c4 / 16, 16-byte chunk (c4 % 16) / 2, half c4 % 2)
+    auto put4 = [&](uint8_t* tile, int row, int c4, float4 x) {
+      const float v[4] = {x.x, x.y, x.z, x.w};
+      float hi[4], lo[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        hi[e] = __bfloat162float(__float2bfloat16_rn(v[e]));
+        lo[e] = v[e] - hi[e];
+      }
+      const uint32_t off = (c4 >> 4) * P128 + sw128_chunk(row, (c4 & 15) >> 1) + (c4 & 1) * 8;
+      *reinterpret_cast<uint2*>(tile + off) = make_uint2(pack_bf16(hi[0], hi[1]), pack_bf16(hi[2], hi[3]));
+      *reinterpret_cast<uint2*>(tile + 32768 + off) =
+          make_uint2(pack_bf16(lo[0], lo[1]), pack_bf16(lo[2], lo[3]));
     };
     if (static_cast<int>(blockIdx.x) < args.mats) load_mat(blockIdx.x);
     int it = 0;
-    int prev = -1;
+    bool ok = true;
     for (int m = blockIdx.x; m < args.mats; m += G, ++it) {
       // the tiles are free once the products of the previous matrix are done
-      if (it >= 1 && !wait_use_w(&bars->done[(it - 1) & 1], (it - 1) >> 1, status, ab)) break;
+      if (it >= 1 && !wait_use_w(&bars->done[(it - 1) & 1], (it - 1) >> 1, status, ab)) {
+        ok = false;
+        break;
+      }
       float part = 0.f;
 #pragma unroll
-      for (int g = 0; g < 4; ++g) {   // 8-column group g of this thread's quarter
-        const float sv[8] = {sv4[2 * g].x, sv4[2 * g].y, sv4[2 * g].z, sv4[2 * g].w,
-                             sv4[2 * g + 1].x, sv4[2 * g + 1].y, sv4[2 * g + 1].z, sv4[2 * g + 1].w};
-        const float uv[8] = {uv4[2 * g].x, uv4[2 * g].y, uv4[2 * g].z, uv4[2 * g].w,
-                             uv4[2 * g + 1].x, uv4[2 * g + 1].y, uv4[2 * g + 1].z, uv4[2 * g + 1].w};
-        float hi[8], lo[8];
-        const int col8 = qc * 4 + g;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          part = fmaf(sv[e], uv[e], part);
-          hi[e] = __bfloat162float(__float2bfloat16_rn(sv[e]));
-          lo[e] = sv[e] - hi[e];
-        }
-        st_row8(sm + DK_S, P128, r, col8, hi);
-        st_row8(sm + DK_S + 32768, P128, r, col8, lo);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          hi[e] = __bfloat162float(__float2bfloat16_rn(uv[e]));
-          lo[e] = uv[e] - hi[e];
-        }
-        st_row8(sm + DK_U, P128, r, col8, hi);
-        st_row8(sm + DK_U + 32768, P128, r, col8, lo);
+      for (int f = 0; f < 8; ++f) {
+        const int j = t + 512 * f;
+        const int row = j >> 5, c4 = j & 31;
+        part = fmaf(sv4[f].x, uv4[f].x, part);
+        part = fmaf(sv4[f].y, uv4[f].y, part);
+        part = fmaf(sv4[f].z, uv4[f].z, part);
+        part = fmaf(sv4[f].w, uv4[f].w, part);
+        put4(sm + DK_S, row, c4, sv4[f]);
+        put4(sm + DK_U, row, c4, uv4[f]);
       }
       fence_async_smem();
       mbar_arrive_warp(&bars->tiles_full);
-      // da_i: sum over the CTA's converter threads
-      part = warp_sum(part);
-      named_sync(1, kConvWarpsDk * 32);
-      if (lane == 0) bars->red[warp] = part;
-      named_sync(1, kConvWarpsDk * 32);
-      if (threadIdx.x == 0) {
-        float t = 0.f;
-#pragma unroll
-        for (int w = 0; w < kConvWarpsDk; ++w) t += bars->red[w];
-        args.da[m] = t;
-      }
-      // the previous matrix's dK while this one's products run, then the next
-      // matrix's loads (in flight until this one's products are done)
-      if (prev >= 0 && !drain(prev, it - 1)) break;
-      prev = m;
       if (m + G < args.mats) load_mat(m + G);
+      // da_i = <S_i, dU_i>: per-warp partials, summed in warp order by the
+      // last warp to arrive (no block-wide barrier, so no unbounded wait)
+      part = warp_sum(part);
+      if (lane == 0) {
+        const int slot = it & 1;
+        bars->red[slot][warp] = part;
+        __threadfence_block();
+        if (atomicAdd(&bars->red_count[slot], 1) == kConvWarpsDk - 1) {
+          __threadfence_block();
+          float tot = 0.f;
+#pragma unroll
+          for (int w = 0; w < kConvWarpsDk; ++w) tot += bars->red[slot][w];
+          args.da[m] = tot;
+          bars->red_count[slot] = 0;
+        }
+      }
+      // the previous matrix's dK while this one's products run
+      if (it >= 1 && !drain(it - 1)) {
+        ok = false;
+        break;
+      }
     }
-    if (prev >= 0 && !*ab) drain(prev, it - 1);
+    if (ok && it >= 1 && !*ab) drain(it - 1);
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kConvWarpsDk) {
+  if (warp == kMmaWarpDk) {
     tc_fence_after();
     tmem_dealloc(tmem, 256);
   }
@@ -523,12 +575,18 @@ cudaError_t make_tmap_f32_rows128(CUtensorMap* map, const void* base, uint64_t r
 }
 
 template <bool REV>
-cudaError_t launch_scan_fwd_tc(const CUtensorMap& mu, const ScanTcArgs& a, int grid,
-                               cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(scan_fwd_tc_kernel<REV>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, SC_SMEM);
+cudaError_t launch_scan_fwd_tc(const float* U, const float* K, float* S, const ScanTcArgs& a,
+                               int BH, cudaStream_t st) {
+  const uint64_t rows = static_cast<uint64_t>(BH) * a.N * kD;
+  CUtensorMap mu, mk, ms;
+  cudaError_t e;
+  if ((e = make_tmap_f32_rows128(&mu, U, rows)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32_rows128(&mk, K, rows)) != cudaSuccess) return e;
+  if ((e = make_tmap_f32_rows128(&ms, S, rows)) != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(scan_fwd_tc_kernel<REV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           SC_SMEM);
   if (e != cudaSuccess) return e;
-  scan_fwd_tc_kernel<REV><<<grid, kThreadsScan, SC_SMEM, st>>>(mu, a);
+  scan_fwd_tc_kernel<REV><<<BH, kThreadsScan, SC_SMEM, st>>>(mu, mk, ms, a);
   return cudaGetLastError();
 }
 
@@ -549,17 +607,11 @@ bool scan_fwd_tc_supported(const ScanArgs& p) {
 
 cudaError_t scan_fwd_tc(const ScanArgs& p, uint32_t* status, cudaStream_t st) {
   if (p.rule != 0) return cudaErrorInvalidValue;
-  CUtensorMap mu;
-  cudaError_t e = make_tmap_f32_rows128(&mu, p.U, static_cast<uint64_t>(p.BH) * p.N * kD);
-  if (e != cudaSuccess) return e;
   ScanTcArgs a{};
-  a.U = p.U;
-  a.K = p.K;
   a.a = p.a;
-  a.S = p.S;
   a.status = status;
   a.N = p.N;
-  return launch_scan_fwd_tc<false>(mu, a, p.BH, st);
+  return launch_scan_fwd_tc<false>(p.U, p.K, p.S, a, p.BH, st);
 }
 
 bool scan_bwd_tc_supported(const ScanArgs& p) {
@@ -570,17 +622,11 @@ bool scan_bwd_tc_supported(const ScanArgs& p) {
 cudaError_t scan_bwd_chain_tc(const ScanArgs& p, uint32_t* status, cudaStream_t st) {
   if (p.rule != 0) return cudaErrorInvalidValue;
   // reverse chain: U := gS, dU_i = Sbar_{i+1}
-  CUtensorMap mu;
-  cudaError_t e = make_tmap_f32_rows128(&mu, p.gS, static_cast<uint64_t>(p.BH) * p.N * kD);
-  if (e != cudaSuccess) return e;
   ScanTcArgs a{};
-  a.U = p.gS;
-  a.K = p.K;
   a.a = p.a;
-  a.S = p.dU;
   a.status = status;
   a.N = p.N;
-  return launch_scan_fwd_tc<true>(mu, a, p.BH, st);
+  return launch_scan_fwd_tc<true>(p.gS, p.K, p.dU, a, p.BH, st);
 }
 
 cudaError_t scan_bwd_dk_tc(const ScanArgs& p, uint32_t* status, cudaStream_t st) {
@@ -601,12 +647,14 @@ cudaError_t scan_bwd_dk_tc(const ScanArgs& p, uint32_t* status, cudaStream_t st)
   DkArgs d{};
   d.S = p.S;
   d.dU = p.dU;
-  d.dK = p.dK;
   d.da = p.da;
   d.status = status;
   d.mats = p.BH * p.N;
+  CUtensorMap mdk;
+  if ((e = make_tmap_f32_rows128(&mdk, p.dK, static_cast<uint64_t>(d.mats) * kD)) != cudaSuccess)
+    return e;
   const int grid = sms < d.mats ? sms : d.mats;
-  scan_bwd_dk_tc_kernel<<<grid, kThreadsDk, DK_SMEM, st>>>(d);
+  scan_bwd_dk_tc_kernel<<<grid, kThreadsDk, DK_SMEM, st>>>(mdk, d);
   return cudaGetLastError();
 }
 

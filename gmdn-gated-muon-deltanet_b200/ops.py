@@ -55,7 +55,14 @@ def _require_cuda(name: str, *tensors: Optional[Tensor]) -> None:
 
 
 def _scratch(nbytes: int, like: Tensor) -> Tensor:
-    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=like.device)
+    """An opaque byte buffer (the op's `saved` output).  The kernels fill its
+    pieces but never the alignment padding between them, nor the one-byte
+    placeholder of a rule that saves nothing; small buffers are zeroed so that
+    two calls on the same inputs return equal bytes (torch.library.opcheck
+    compares every output), large ones are left as allocated."""
+    n = max(int(nbytes), 1)
+    alloc = torch.zeros if n <= (1 << 20) else torch.empty
+    return alloc(n, dtype=torch.uint8, device=like.device)
 
 
 # GMDN_CHECK_STATUS=1: after every mixer-core call, synchronise and read the
