@@ -601,6 +601,7 @@ chunk_bwd1_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
         args.dnc[mj] = 0.f;
       }
       tc_fence_before();
+      fence_async_smem();   // tile and gate reads before the next loads (async proxy)
       mbar_arrive(&bars->gb_ready);
       // ================= phase A: Sb_j = a_c Sb_{j+1} + C
       if (!wait_use(&bars->c_full, i, status, ab)) break;

@@ -459,6 +459,7 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive_warp(&bars->de_smem);
+        fence_async_smem();   // gate reads before the stage's reload (async proxy)
         mbar_arrive_warp(&bars->ld_empty[i % kStages1]);   // done with this stage
       }
       if constexpr (RULE == 0) {
@@ -604,6 +605,7 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       }
       tc_fence_before();
       mbar_arrive_warp(&bars->de_smem);
+      fence_async_smem();   // gate reads before the stage's reload (async proxy)
       mbar_arrive_warp(&bars->ld_empty[i % kStages1]);   // done with this stage's gates
       }
       if (i + 1 < N && !build_as(i + 1)) break;
@@ -1213,6 +1215,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         part = warp_sum(part);
         if (lane == 0) atomicAdd(&bars->da[i & 1], part);
       }
+      fence_async_smem();   // Gb_j, gate reads before the group's reload (async proxy)
       mbar_arrive_warp(&bars->da_done);
       // ---- epilogue 2: dE -> bf16 (also dv), then dP = tril(dA) beta; dbeta pieces; dw
       if (!wait_use_w(&bars->ph2, i, status, ab)) break;
@@ -1349,6 +1352,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         }
         if (hi) gdw[half * 64 + r16] = dw;
       }
+      fence_async_smem();   // k reads before the buffer's reload (async proxy)
       mbar_arrive_warp(&bars->k_free);
       // ---- epilogue 3: dq (staged in the E^T tile), dk (A and dP tiles), gate gradients
       if (!wait_use_w(&bars->ph3, i, status, ab)) break;
@@ -1390,6 +1394,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       }
       if constexpr (RULE == 1) {
         // the dE tile (read by the dv store) is free for the next Gb lo
+        fence_async_smem();
         named_sync(1, 256);
         if (tid == 0) {
           bulk_wait_read0();

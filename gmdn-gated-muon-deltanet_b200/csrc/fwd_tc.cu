@@ -325,6 +325,7 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive_warp(&bars->e_smem);
+        fence_async_smem();   // gate reads before the stage's reload (async proxy)
         mbar_arrive_warp(&bars->ld_empty[j & 1]);   // done with this stage's gates
       }
       if constexpr (RULE == 2) {
@@ -336,6 +337,7 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                                        logf(fmaxf(mu[lane + 32], kGateFloor))));
         const float nc = expf(warp_sum(logf(fmaxf(nu[lane], kGateFloor)) +
                                        logf(fmaxf(nu[lane + 32], kGateFloor))));
+        fence_async_smem();   // gate reads before the stage's reload (async proxy)
         mbar_arrive_warp(&bars->ld_empty[j & 1]);   // done with this stage's gates
         if (!wait_use_w(&bars->g_full, j, status, ab)) break;
         tc_fence_after();
@@ -512,6 +514,7 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       }
       tc_fence_before();
       mbar_arrive_warp(&bars->e_smem);
+      fence_async_smem();   // gate reads before the stage's reload (async proxy)
       mbar_arrive_warp(&bars->ld_empty[j & 1]);   // done with this stage's gates
       }
       if (j + 1 < N && !build_as(j + 1)) break;

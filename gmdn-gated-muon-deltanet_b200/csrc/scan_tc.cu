@@ -290,7 +290,10 @@ scan_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_u, const __grid_consta
 #pragma unroll
         for (int e = 0; e < 16; ++e) st[16 * q + e] = fmaf(a, st[16 * q + e], u[e] - g[e]);
       }
-      mbar_arrive_warp(&bars->u_empty);   // U_i read: the next U may load
+      // U_i read: the next U may load (the proxy fence orders these generic
+      // reads before the TMA's async-proxy writes into the same boxes)
+      fence_async_smem();
+      mbar_arrive_warp(&bars->u_empty);
       if (last) break;
       // K_{i+1} into the tiles (the products of chunk i are done: g_full)
       if (!wait_use_w(&bars->k_full, i + 1, status, ab)) break;
