@@ -14,7 +14,12 @@ What it reproduces from the reference (train_ablation.py):
 * the optimisers: Nesterov Muon with Newton-Schulz msign on every 2-D hidden
   matrix and AdamW(0.9, 0.95) on the rest (train_ablation.py:60-73, 264-314);
 * one step: bf16 autocast forward, cross-entropy on fp32 logits, backward,
-  gradient clipping at 1.0, both optimiser steps (train_ablation.py:453-474).
+  gradient clipping at 1.0, both optimiser steps (train_ablation.py:453-474),
+  the learning-rate schedule and the evaluation pass (:310-314, 386-399);
+* the run's records: the per-interval CSV and the incrementally rewritten
+  JSON metrics file, and the final checkpoint, in the reference's formats
+  (:426-444, 476-529), so its analysis scripts read them unchanged and its
+  ``LM`` loads the checkpoint (same state-dict names).
 
 B200 choices: the mixer's scan runs on the tcgen05 kernels (dh 64 at
 d_model 768 / 12 heads); the msign of the outer Muon stacks every matrix of
@@ -26,7 +31,9 @@ backend, whose bucketed gradient all-reduce overlaps the backward.
 
 from __future__ import annotations
 
+import json
 import math
+import os
 from collections import defaultdict
 
 import torch
@@ -95,8 +102,8 @@ class LanguageModel(nn.Module):
         self.blocks = nn.ModuleList(Block(d_model, n_heads, inner, chunk, ns_steps, mixer_cls)
                                     for _ in range(n_layers))
         self.norm_f = nn.RMSNorm(d_model)
-        self.head = nn.Linear(d_model, vocab, bias=False)
-        self.head.weight = self.emb.weight
+        self.lm_head = nn.Linear(d_model, vocab, bias=False)   # the reference's name
+        self.lm_head.weight = self.emb.weight
         for m in self.modules():
             if isinstance(m, (nn.Linear, nn.Embedding)):
                 nn.init.normal_(m.weight, std=0.02)
@@ -112,11 +119,23 @@ class LanguageModel(nn.Module):
         x = self.emb(idx)
         for blk in self.blocks:
             x = blk(x)
-        logits = self.head(self.norm_f(x))
+        logits = self.lm_head(self.norm_f(x))
         if targets is None:
             return logits, None
         loss = F.cross_entropy(logits.reshape(-1, logits.shape[-1]).float(), targets.reshape(-1))
         return logits, loss
+
+    def gate_means(self) -> dict:
+        """Mean gate value per gate over the layers' last forward
+        (train_ablation.py:248-257); NaN for a gate no layer reported."""
+        vals = {k: [] for k in ("alpha", "beta", "mu", "nu")}
+        for blk in self.blocks:
+            for k in vals:
+                v = blk.mixer.last_gate_means.get(k, float("nan"))
+                v = v.item() if torch.is_tensor(v) else v
+                if v == v:
+                    vals[k].append(v)
+        return {k: (sum(v) / len(v) if v else float("nan")) for k, v in vals.items()}
 
 
 def msign(mats: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.Tensor:
@@ -176,17 +195,27 @@ class OuterMuon(torch.optim.Optimizer):
                     p.add_(ui, alpha=-lr * scale)
 
 
-def build_optimizers(model: nn.Module, muon_lr=0.02, adam_lr=4e-4, weight_decay=0.1):
-    """Muon on every 2-D parameter but the (tied) embedding, AdamW(0.9, 0.95)
-    on the rest (train_ablation.py:291-306)."""
+Muon = OuterMuon   # the reference's name
+
+
+def build_optimizers(model: nn.Module, muon_lr=0.02, adam_lr=4e-4, weight_decay=0.1,
+                     outer: str = "muon"):
+    """Every 2-D parameter but the (tied) embedding is a hidden matrix: outer
+    "muon" puts them on Muon and the rest on AdamW(0.9, 0.95); outer "adam"
+    puts both groups on AdamW (train_ablation.py:291-307)."""
+    if outer not in ("muon", "adam"):
+        raise ValueError(f"outer optimiser must be 'muon' or 'adam', got {outer!r}")
     base = model.module if hasattr(model, "module") else model
     emb = {id(base.emb.weight)}
     hidden, other = [], []
     for p in model.parameters():
         if p.requires_grad:
             (hidden if p.ndim == 2 and id(p) not in emb else other).append(p)
-    return [OuterMuon(hidden, lr=muon_lr, weight_decay=weight_decay),
-            torch.optim.AdamW(other, lr=adam_lr, betas=(0.9, 0.95), weight_decay=weight_decay)]
+    adamw = dict(lr=adam_lr, betas=(0.9, 0.95), weight_decay=weight_decay)
+    if outer == "muon":
+        return [OuterMuon(hidden, lr=muon_lr, weight_decay=weight_decay),
+                torch.optim.AdamW(other, **adamw)]
+    return [torch.optim.AdamW(hidden, **adamw), torch.optim.AdamW(other, **adamw)]
 
 
 def lr_factor(step: int, warmup: int, total: int) -> float:
@@ -230,3 +259,106 @@ def train_step(model: nn.Module, optimizers, idx: torch.Tensor, targets: torch.T
     for opt in optimizers:
         opt.step()
     return loss.detach()
+
+
+@torch.no_grad()
+def evaluate(model: nn.Module, val_batches, amp: bool = True):
+    """Mean loss over fixed validation batches and its perplexity
+    exp(min(loss, 20)) (train_ablation.py:386-399); the model is left in
+    training mode."""
+    model.eval()
+    total, n = 0.0, 0
+    for x, y in val_batches:
+        with torch.autocast(device_type="cuda", dtype=torch.bfloat16,
+                            enabled=amp and x.is_cuda):
+            _, loss = model(x, y)
+        total += loss.item()
+        n += 1
+    model.train()
+    loss = total / max(n, 1)
+    return loss, math.exp(min(loss, 20))
+
+
+# Column order and number formats of the per-interval CSV (train_ablation.py:
+# 426-428, 497-501): its readers parse these exact columns.
+CSV_COLUMNS = ("step", "train_loss", "val_loss", "val_ppl", "lr_hidden", "grad_norm", "tok_s",
+               "alpha", "beta", "mu", "nu", "elapsed_s")
+
+
+class RunLog:
+    """The records of one training condition, in the reference's formats:
+
+    * ``<cond>.csv``: a header line, then one row per logging interval;
+    * ``<cond>_metrics.json``: ``{"meta": ..., "log": [rows]}``, rewritten in
+      full after every row through a temporary file and ``os.replace`` (a
+      crash leaves the previous complete file), and once more with
+      ``meta["final"]`` at the end (train_ablation.py:429-444, 502-519).
+    """
+
+    def __init__(self, results_dir: str, condition: str, meta: dict):
+        os.makedirs(results_dir, exist_ok=True)
+        self.csv_path = os.path.join(results_dir, f"{condition}.csv")
+        self.json_path = os.path.join(results_dir, f"{condition}_metrics.json")
+        self.meta = dict(meta)
+        self.rows: list = []
+        with open(self.csv_path, "w") as f:
+            f.write(",".join(CSV_COLUMNS) + "\n")
+
+    def row(self, step: int, train_loss: float, val_loss: float, val_ppl: float,
+            lr_hidden: float, grad_norm: float, tok_s: float, gates: dict, elapsed_s: float,
+            tokens_seen: int) -> None:
+        g = {k: gates.get(k, float("nan")) for k in ("alpha", "beta", "mu", "nu")}
+        with open(self.csv_path, "a") as f:
+            f.write(f"{step},{train_loss:.6f},{val_loss:.6f},{val_ppl:.4f},"
+                    f"{lr_hidden:.6e},{grad_norm:.4f},{tok_s:.1f},"
+                    f"{g['alpha']:.4f},{g['beta']:.4f},{g['mu']:.4f},"
+                    f"{g['nu']:.4f},{elapsed_s:.1f}\n")
+        self.rows.append(dict(
+            step=step, train_loss=round(train_loss, 6), val_loss=round(val_loss, 6),
+            val_ppl=round(val_ppl, 4), lr_hidden=lr_hidden, grad_norm=round(grad_norm, 4),
+            tok_s=round(tok_s, 1), tokens_seen=tokens_seen,
+            alpha=round(g["alpha"], 4), beta=round(g["beta"], 4), mu=round(g["mu"], 4),
+            nu=round(g["nu"], 4), elapsed_s=round(elapsed_s, 1)))
+        self.flush()
+
+    def finish(self, result: dict) -> None:
+        self.meta["final"] = dict(result)
+        self.flush()
+
+    def flush(self) -> None:
+        tmp = self.json_path + ".tmp"
+        with open(tmp, "w") as f:
+            json.dump(dict(meta=self.meta, log=self.rows), f, indent=1)
+        os.replace(tmp, self.json_path)
+
+
+def save_checkpoint(path: str, model: nn.Module, *, vocab: int, d_model: int, n_layers: int,
+                    n_heads: int, inner: str, chunk: int, outer: str, step: int, seed: int,
+                    data_seed: int, args: dict, final_val_loss: float,
+                    final_val_ppl: float) -> None:
+    """``torch.save`` of the reference's checkpoint dictionary (train_ablation.py:
+    516-528): the model's state dict under the reference's parameter names
+    (``LM`` loads it), the model configuration, the condition and the run's
+    arguments and final validation figures."""
+    base = model.module if hasattr(model, "module") else model
+    torch.save(dict(
+        model_state=base.state_dict(),
+        model_config=dict(vocab=vocab, d_model=d_model, n_layers=n_layers, n_heads=n_heads,
+                          inner=inner, chunk=chunk),
+        condition=f"outer-{outer}_inner-{inner}", outer=outer, inner=inner,
+        step=step, seed=seed, data_seed=data_seed, args=dict(args),
+        torch_version=torch.__version__,
+        final_val_loss=final_val_loss, final_val_ppl=final_val_ppl,
+    ), path)
+
+
+def load_checkpoint(path: str, ns_steps: int = 3, map_location="cpu", mixer_cls=MixerLayer):
+    """Rebuilds the model of a checkpoint written by ``save_checkpoint`` or by
+    the reference's trainer and loads its weights; returns (model, checkpoint
+    dictionary)."""
+    ck = torch.load(path, map_location=map_location, weights_only=False)
+    cfg = ck["model_config"]
+    model = LanguageModel(cfg["vocab"], cfg["d_model"], cfg["n_layers"], cfg["n_heads"],
+                          cfg["inner"], chunk=cfg["chunk"], ns_steps=ns_steps, mixer_cls=mixer_cls)
+    model.load_state_dict(ck["model_state"])
+    return model, ck

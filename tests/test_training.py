@@ -191,3 +191,97 @@ def test_lr_schedule_matches_reference_factor():
         fac = sched.set_step(step)
         assert math.isclose(opts[0].param_groups[0]["lr"], 0.02 * fac)
         assert math.isclose(opts[1].param_groups[0]["lr"], 4e-4 * fac)
+
+
+def _lm_golden():
+    return torch.load(os.path.join(ROOT, "tests", "golden", "lm.pt"), weights_only=False)
+
+
+def test_model_matches_reference_lm_weights_and_logits():
+    """The fixture holds the reference trainer's own LM (train_ablation.py:
+    197-246) per inner rule: its seeded initialisation, and its logits on a
+    token batch.  The same seed gives this package's LanguageModel the same
+    weights under the same names, and with the mixer core on the oracle the
+    same logits."""
+    tr = _training()
+    gold = _lm_golden()
+    for inner, g in gold.items():
+        torch.manual_seed(0)
+        m = tr.LanguageModel(61, 32, 2, 2, inner, chunk=16, ns_steps=3, mixer_cls=cpu_mixer_cls())
+        sd = m.state_dict()
+        assert set(sd) == set(g["state"]), inner
+        for k, v in g["state"].items():
+            assert torch.equal(sd[k], v), (inner, k)
+        with torch.no_grad():
+            logits, loss = m(g["idx"][:, :-1], g["idx"][:, 1:])
+        err = (logits - g["logits"]).abs().max().item() / g["logits"].abs().max().item()
+        assert err < 1e-4, (inner, err)
+        assert abs(loss.item() - g["loss"].item()) < 1e-5 * abs(g["loss"].item()), inner
+
+
+def test_run_log_and_checkpoint_formats(tmp_path):
+    """RunLog writes the reference's CSV header and row formats and its
+    crash-safe {meta, log} JSON (train_ablation.py:426-444, 497-519);
+    save_checkpoint writes its checkpoint dictionary (:516-528), which
+    load_checkpoint turns back into the same model, and a checkpoint holding
+    the reference LM's own state dict loads the same way."""
+    import json
+    tr = _training()
+    m = _model(4)
+    opts = tr.build_optimizers(m)
+    sched = tr.LrSchedule(opts, warmup=2, total=4)
+    idx, tgt = _batch()
+    log = tr.RunLog(str(tmp_path), "outer-muon_inner-delta", dict(condition="outer-muon_inner-delta"))
+    for step in range(1, 4):
+        sched.set_step(step - 1)
+        for o in opts:
+            o.zero_grad(set_to_none=True)
+        _, loss = m(idx, tgt)
+        loss.backward()
+        gn = torch.nn.utils.clip_grad_norm_(m.parameters(), 1.0).item()
+        for o in opts:
+            o.step()
+        vl, vp = tr.evaluate(m, [(idx, tgt)], amp=False)
+        log.row(step, loss.item(), vl, vp, opts[0].param_groups[0]["lr"], gn, 123.4,
+                dict(alpha=0.9, beta=0.3, mu=0.7), 1.5 * step, tokens_seen=step * idx.numel())
+    log.finish(dict(final_val_loss=vl, final_val_ppl=vp))
+    lines = open(tmp_path / "outer-muon_inner-delta.csv").read().splitlines()
+    assert lines[0] == ("step,train_loss,val_loss,val_ppl,lr_hidden,grad_norm,tok_s,"
+                        "alpha,beta,mu,nu,elapsed_s")
+    assert len(lines) == 4
+    cells = lines[3].split(",")
+    assert cells[0] == "3" and cells[-1] == "4.5" and cells[-2] == "nan" and cells[6] == "123.4"
+    assert len(cells[1].split(".")[1]) == 6 and "e" in cells[4]
+    meta = json.load(open(tmp_path / "outer-muon_inner-delta_metrics.json"))
+    assert set(meta) == {"meta", "log"} and len(meta["log"]) == 3
+    assert meta["meta"]["final"]["final_val_loss"] == vl
+    assert meta["log"][2]["tokens_seen"] == 3 * idx.numel()
+    assert not os.path.exists(tmp_path / "outer-muon_inner-delta_metrics.json.tmp")
+    ck = tmp_path / "c.pt"
+    tr.save_checkpoint(str(ck), m, vocab=97, d_model=32, n_layers=2, n_heads=2, inner="delta",
+                       chunk=16, outer="muon", step=3, seed=0, data_seed=1, args={"lr": 1},
+                       final_val_loss=vl, final_val_ppl=vp)
+    m2, d = tr.load_checkpoint(str(ck), mixer_cls=cpu_mixer_cls())
+    assert d["condition"] == "outer-muon_inner-delta" and d["step"] == 3
+    assert set(d) >= {"model_state", "model_config", "outer", "inner", "seed", "data_seed",
+                      "args", "torch_version", "final_val_loss", "final_val_ppl"}
+    for k, v in m.state_dict().items():
+        assert torch.equal(m2.state_dict()[k], v), k
+    g = _lm_golden()["muon"]
+    ref_ck = tmp_path / "ref.pt"
+    torch.save(dict(model_state=g["state"], model_config=dict(
+        vocab=61, d_model=32, n_layers=2, n_heads=2, inner="muon", chunk=16)), ref_ck)
+    m3, _ = tr.load_checkpoint(str(ref_ck), mixer_cls=cpu_mixer_cls())
+    with torch.no_grad():
+        logits, _ = m3(g["idx"][:, :-1])
+    assert (logits - g["logits"]).abs().max().item() < 1e-4 * g["logits"].abs().max().item()
+
+
+def test_outer_adam_condition():
+    """outer 'adam' puts the hidden matrices on AdamW too
+    (train_ablation.py:303-307)."""
+    tr = _training()
+    m = tr.LanguageModel(50, 32, 1, 2, "delta")
+    opts = tr.build_optimizers(m, outer="adam")
+    assert all(isinstance(o, torch.optim.AdamW) for o in opts)
+    assert opts[0].param_groups[0]["betas"] == (0.9, 0.95)
