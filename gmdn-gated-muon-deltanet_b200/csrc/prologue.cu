@@ -82,6 +82,26 @@ __device__ __forceinline__ float wsum(float v) {
   return v;
 }
 
+// Per-thread prefetch rings: each lane copies its own VEC elements of a row
+// (4-16 bytes) into shared memory with cp.async and reads them back itself, so
+// a warp keeps that many rows in flight without holding them in registers.
+constexpr int kRingP = 8;    // forward: 8 warps a block, one array
+constexpr int kRingB = 8;    // backward: 2 warps a block, u and the cotangent (16 measured the same)
+template <int BYTES>
+__device__ __forceinline__ void cp_async(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+               "l"(gmem), "n"(BYTES)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // fast exp and divide: ~1e-6 relative, and these kernels are issue-bound
 __device__ __forceinline__ float sigm(float z) { return __fdividef(1.f, 1.f + __expf(-z)); }
 
@@ -316,6 +336,212 @@ prologue_bwd_kernel(const TT* __restrict__ u, const float* __restrict__ cw,
   }
 }
 
+// The same strip walks with the rows of u (and of the output cotangent) coming
+// through a per-lane cp.async ring (kRingP / kRingB rows deep) instead of
+// loads kPF / kPB rows ahead into registers: a warp keeps 8 rows in flight at
+// the register cost of none (the backward dropped from ~141 registers and 12
+// warps an SM to 124 and 16, and from 1.03 to 0.60 ms at config-1 size; the
+// forward from 0.36 to 0.29 ms).  Used where a lane holds at least 4 bytes of
+// a row (VEC * sizeof(TT) >= 4: every head dim but bf16 dh 32).
+template <int VEC, typename TT>
+__global__ void __launch_bounds__(kWarpsP * 32, 4)
+prologue_fwd_ring_kernel(const TT* __restrict__ u, const float* __restrict__ cw,
+                         const float* __restrict__ cb, TT* __restrict__ q, TT* __restrict__ k,
+                         TT* __restrict__ v, int B, int T, int H, int strips) {
+  constexpr int DH = VEC * 32;
+  constexpr int VB = VEC * static_cast<int>(sizeof(TT));
+  static_assert(VB == 4 || VB == 8 || VB == 16, "cp.async size");
+  __shared__ __align__(16) uint8_t ring[kWarpsP][kRingP][32 * VB];
+  const int wl = threadIdx.x >> 5;
+  const int w = blockIdx.x * kWarpsP + wl;
+  if (w >= strips) return;
+  const int lane = threadIdx.x & 31;
+  const Strip s = strip_of(w, H, T);
+  const int D = H * DH;
+  const int c0 = s.part * D + s.h * DH + lane * VEC;
+  const size_t row = static_cast<size_t>(3) * D;
+  const TT* ub = u + static_cast<size_t>(s.b) * T * row + c0;
+  TT* out = (s.part == 0 ? q : s.part == 1 ? k : v) +
+            (static_cast<size_t>(s.b) * H + s.h) * static_cast<size_t>(T) * DH + lane * VEC;
+  float wt[4][VEC], bias[VEC], win[3][VEC];
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) wt[j][e] = cw[(c0 + e) * 4 + j];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) win[j][e] = 0.f;
+    bias[e] = cb[c0 + e];
+  }
+  // steps t0 - 3 .. t1 - 1 through the ring: the first three fill the window
+  const int first = s.t0 - 3, n = s.t1 - first;
+  auto slot = [&](int i) { return &ring[wl][i % kRingP][lane * VB]; };
+  auto issue = [&](int i) {
+    const int t = first + i;
+    if (i < n && t >= 0) cp_async<VB>(slot(i), ub + static_cast<size_t>(t) * row);
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int i = 0; i < kRingP - 1; ++i) issue(i);
+  for (int i = 0; i < n; ++i) {
+    issue(i + kRingP - 1);   // refills the slot read in step i - 1
+    cp_async_wait<kRingP - 1>();
+    const int t = first + i;
+    float x[VEC];
+    if (t >= 0) {
+      VecP<VEC, TT>::load(reinterpret_cast<const TT*>(slot(i)), x);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) x[e] = 0.f;
+    }
+    if (i < 3) {   // fill the window (shifted, so that no index is dynamic)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        win[0][e] = win[1][e];
+        win[1][e] = win[2][e];
+        win[2][e] = x[e];
+      }
+      continue;
+    }
+    float o[VEC];
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const float z = bias[e] + wt[0][e] * win[0][e] + wt[1][e] * win[1][e] +
+                      wt[2][e] * win[2][e] + wt[3][e] * x[e];
+      o[e] = z * sigm(z);
+      ss = fmaf(o[e], o[e], ss);
+      win[0][e] = win[1][e];
+      win[1][e] = win[2][e];
+      win[2][e] = x[e];
+    }
+    if (s.part < 2) {
+      const float inv = 1.f / fmaxf(sqrtf(wsum(ss)), kNormEps);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] *= inv;
+    }
+    VecP<VEC, TT>::store(out + static_cast<size_t>(t) * DH, o);
+  }
+  cp_async_wait<0>();
+}
+
+template <int VEC, typename TT>
+__global__ void __launch_bounds__(kWarpsB * 32)
+prologue_bwd_ring_kernel(const TT* __restrict__ u, const float* __restrict__ cw,
+                         const float* __restrict__ cb, const TT* __restrict__ dq,
+                         const TT* __restrict__ dk, const TT* __restrict__ dv, TT* __restrict__ du,
+                         float* __restrict__ dcw, float* __restrict__ dcb, int B, int T, int H,
+                         int strips) {
+  constexpr int DH = VEC * 32;
+  constexpr int VB = VEC * static_cast<int>(sizeof(TT));
+  static_assert(VB == 4 || VB == 8 || VB == 16, "cp.async size");
+  __shared__ __align__(16) uint8_t ring[kWarpsB][kRingB][2][32 * VB];
+  const int wl = threadIdx.x >> 5;
+  const int w = blockIdx.x * kWarpsB + wl;
+  if (w >= strips) return;
+  const int lane = threadIdx.x & 31;
+  const Strip s = strip_of(w, H, T);
+  const int D = H * DH;
+  const int c0 = s.part * D + s.h * DH + lane * VEC;
+  const size_t row = static_cast<size_t>(3) * D;
+  const TT* ub = u + static_cast<size_t>(s.b) * T * row + c0;
+  TT* dub = du + static_cast<size_t>(s.b) * T * row + c0;
+  const TT* dout = (s.part == 0 ? dq : s.part == 1 ? dk : dv) +
+                   (static_cast<size_t>(s.b) * H + s.h) * static_cast<size_t>(T) * DH + lane * VEC;
+  float wt[4][VEC], bias[VEC], win[3][VEC], dzw[3][VEC];   // dzw: dz[t-3], dz[t-2], dz[t-1]
+  float aw[4][VEC], ab[VEC];
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      wt[j][e] = cw[(c0 + e) * 4 + j];
+      aw[j][e] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 3; ++j) dzw[j][e] = win[j][e] = 0.f;   // dz before t0 is never read
+    bias[e] = cb[c0 + e];
+    ab[e] = 0.f;
+  }
+  // steps t0 - 3 .. t1 + 2: u through the ring from t0 - 3 (the window), the
+  // cotangent from t0; dz[t] for t >= t0, du[t-3] once dz[t-3 .. t] are known
+  const int first = s.t0 - 3, n = s.t1 + 3 - first;
+  const int tend = min(s.t1 + 3, T);   // steps whose dz this strip needs
+  auto slot = [&](int i, int a) { return &ring[wl][i % kRingB][a][lane * VB]; };
+  auto issue = [&](int i) {
+    const int t = first + i;
+    if (i < n && t >= 0 && t < tend) {
+      cp_async<VB>(slot(i, 0), ub + static_cast<size_t>(t) * row);
+      if (t >= s.t0) cp_async<VB>(slot(i, 1), dout + static_cast<size_t>(t) * DH);
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int i = 0; i < kRingB - 1; ++i) issue(i);
+  for (int i = 0; i < n; ++i) {
+    issue(i + kRingB - 1);   // refills the slot read in step i - 1
+    cp_async_wait<kRingB - 1>();
+    const int t = first + i;
+    float x[VEC], gs[VEC];
+    if (t >= 0 && t < tend) {
+      VecP<VEC, TT>::load(reinterpret_cast<const TT*>(slot(i, 0)), x);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) x[e] = 0.f;
+    }
+    if (i < 3) {   // fill the window (shifted, so that no index is dynamic)
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        win[0][e] = win[1][e];
+        win[1][e] = win[2][e];
+        win[2][e] = x[e];
+      }
+      continue;
+    }
+    if (t < tend) {
+      VecP<VEC, TT>::load(reinterpret_cast<const TT*>(slot(i, 1)), gs);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) gs[e] = 0.f;
+    }
+    float dz[VEC];
+    dz_at<VEC>(t, T, s.part, win, x, wt, bias, gs, dz);
+    if (t < s.t1) {   // this strip's own steps: weight and bias gradients
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) {
+        aw[0][e] = fmaf(dz[e], win[0][e], aw[0][e]);
+        aw[1][e] = fmaf(dz[e], win[1][e], aw[1][e]);
+        aw[2][e] = fmaf(dz[e], win[2][e], aw[2][e]);
+        aw[3][e] = fmaf(dz[e], x[e], aw[3][e]);
+        ab[e] += dz[e];
+      }
+    }
+    const int tp = t - 3;   // du[tp] = w0 dz[tp+3] + w1 dz[tp+2] + w2 dz[tp+1] + w3 dz[tp]
+    if (tp >= s.t0) {
+      float g[VEC];
+#pragma unroll
+      for (int e = 0; e < VEC; ++e)
+        g[e] = wt[0][e] * dz[e] + wt[1][e] * dzw[2][e] + wt[2][e] * dzw[1][e] +
+               wt[3][e] * dzw[0][e];
+      VecP<VEC, TT>::store(dub + static_cast<size_t>(tp) * row, g);
+    }
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      win[0][e] = win[1][e];
+      win[1][e] = win[2][e];
+      win[2][e] = x[e];
+      dzw[0][e] = dzw[1][e];
+      dzw[1][e] = dzw[2][e];
+      dzw[2][e] = dz[e];
+    }
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) atomicAdd(dcw + (c0 + e) * 4 + j, aw[j][e]);
+    atomicAdd(dcb + c0 + e, ab[e]);
+  }
+}
+
 // gates: gl (B, T, nG*H) -> g (nG, B, H, T) = sigmoid; backward dgl = dg s (1 - s)
 template <typename TT>
 __global__ void gates_fwd_kernel(const TT* __restrict__ gl, TT* __restrict__ g, int B, int T,
@@ -359,9 +585,15 @@ template <int VEC, typename TT>
 cudaError_t fwd_t(const void* u, const float* cw, const float* cb, const void* gl, void* q,
                   void* k, void* v, void* g, int B, int T, int H, int nG, cudaStream_t st) {
   const int strips = B * 3 * H * ((T + kTB - 1) / kTB);
-  prologue_fwd_kernel<VEC, TT><<<(strips + kWarpsP - 1) / kWarpsP, kWarpsP * 32, 0, st>>>(
-      static_cast<const TT*>(u), cw, cb, static_cast<TT*>(q), static_cast<TT*>(k),
-      static_cast<TT*>(v), B, T, H, strips);
+  const int blocks = (strips + kWarpsP - 1) / kWarpsP;
+  if constexpr (VEC * sizeof(TT) >= 4)
+    prologue_fwd_ring_kernel<VEC, TT><<<blocks, kWarpsP * 32, 0, st>>>(
+        static_cast<const TT*>(u), cw, cb, static_cast<TT*>(q), static_cast<TT*>(k),
+        static_cast<TT*>(v), B, T, H, strips);
+  else
+    prologue_fwd_kernel<VEC, TT><<<blocks, kWarpsP * 32, 0, st>>>(
+        static_cast<const TT*>(u), cw, cb, static_cast<TT*>(q), static_cast<TT*>(k),
+        static_cast<TT*>(v), B, T, H, strips);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const long long n = static_cast<long long>(B) * T * nG * H;
@@ -380,9 +612,15 @@ cudaError_t bwd_t(const void* u, const float* cw, const float* cb, const void* g
   if (e == cudaSuccess) e = cudaMemsetAsync(dcb, 0, sizeof(float) * 3 * D, st);
   if (e != cudaSuccess) return e;
   const int strips = B * 3 * H * ((T + kTB - 1) / kTB);
-  prologue_bwd_kernel<VEC, TT><<<(strips + kWarpsB - 1) / kWarpsB, kWarpsB * 32, 0, st>>>(
-      static_cast<const TT*>(u), cw, cb, static_cast<const TT*>(dq), static_cast<const TT*>(dk),
-      static_cast<const TT*>(dv), static_cast<TT*>(du), dcw, dcb, B, T, H, strips);
+  const int blocks = (strips + kWarpsB - 1) / kWarpsB;
+  if constexpr (VEC * sizeof(TT) >= 4)
+    prologue_bwd_ring_kernel<VEC, TT><<<blocks, kWarpsB * 32, 0, st>>>(
+        static_cast<const TT*>(u), cw, cb, static_cast<const TT*>(dq), static_cast<const TT*>(dk),
+        static_cast<const TT*>(dv), static_cast<TT*>(du), dcw, dcb, B, T, H, strips);
+  else
+    prologue_bwd_kernel<VEC, TT><<<blocks, kWarpsB * 32, 0, st>>>(
+        static_cast<const TT*>(u), cw, cb, static_cast<const TT*>(dq), static_cast<const TT*>(dk),
+        static_cast<const TT*>(dv), static_cast<TT*>(du), dcw, dcb, B, T, H, strips);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   const long long n = static_cast<long long>(B) * T * nG * H;
