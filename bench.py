@@ -608,7 +608,8 @@ def run_train(args) -> None:
     vocab, d, layers, heads, T, mb = 32000, 768, 12, 12, 2048, args.batch or 8
     inner = {0: "delta", 1: "muon", 2: "adam"}[CONFIGS[args.config]["rule"]]
     torch.manual_seed(0)
-    model = tr.LanguageModel(vocab, d, layers, heads, inner, chunk=64, ns_steps=3).to(device)
+    model = tr.LanguageModel(vocab, d, layers, heads, inner, chunk=64, ns_steps=3,
+                             mlp=args.mlp).to(device)
     net = model
     if dist is not None:
         net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[local],
@@ -648,7 +649,8 @@ def run_train(args) -> None:
         "value": tokens / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "config4_train", "inner": inner, "micro_batch_per_gpu": mb,
+        "config": {"workload": "config4_train", "inner": inner, "mlp": args.mlp,
+                   "micro_batch_per_gpu": mb,
                    "global_batch": world * mb, "seq_len": T, "layers": layers, "d_model": d,
                    "heads": heads, "vocab": vocab,
                    "parallelism": f"dp{world}" + (" (DDP, NCCL all-reduce)" if world > 1 else ""),
@@ -723,6 +725,9 @@ def main():
                     choices=["mixer", "epilogue", "prologue", "scan", "train"],
                     help="epilogue / prologue: that part of the mixer alone; scan: the "
                          "scan-only drop-in (fast_state_scan) on fp32 U, K; one GPU each")
+    ap.add_argument("--mlp", default="gelu", choices=["gelu", "swiglu"],
+                    help="train workload: the reference trainer's GELU MLP, or the SwiGLU MLP "
+                         "that the config-4 benchmark description names")
     ap.add_argument("--scaling", default="strong", choices=["weak", "strong"],
                     help="strong (default): the one global batch the metric names split into "
                          "(b, h) shards over the ranks; weak: a full batch per rank.  At N > 1 "

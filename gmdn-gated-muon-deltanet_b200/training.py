@@ -76,15 +76,39 @@ class MixerLayer(nn.Module):
         return integration.mixer_forward(self, x)
 
 
+class SwiGLU(nn.Module):
+    """out(silu(gate(x)) * up(x)) with a 4x hidden width: the MLP that the
+    benchmark description of config 4 names.  The reference's trainer uses a
+    GELU MLP (train_ablation.py:202-205), which stays the default; indexing
+    [2] gives the residual output projection like the GELU Sequential."""
+
+    def __init__(self, d_model: int):
+        super().__init__()
+        self.gate = nn.Linear(d_model, 4 * d_model, bias=False)
+        self.up = nn.Linear(d_model, 4 * d_model, bias=False)
+        self.out = nn.Linear(4 * d_model, d_model, bias=False)
+
+    def __getitem__(self, i: int) -> nn.Module:
+        return {0: self.gate, 2: self.out}[i]
+
+    def forward(self, x):
+        return self.out(F.silu(self.gate(x)) * self.up(x))
+
+
 class Block(nn.Module):
     def __init__(self, d_model: int, n_heads: int, inner: str, chunk: int, ns_steps: int,
-                 mixer_cls=MixerLayer):
+                 mixer_cls=MixerLayer, mlp: str = "gelu"):
         super().__init__()
         self.n1 = nn.RMSNorm(d_model)
         self.mixer = mixer_cls(d_model, n_heads, inner, chunk, ns_steps)
         self.n2 = nn.RMSNorm(d_model)
-        self.mlp = nn.Sequential(nn.Linear(d_model, 4 * d_model, bias=False), nn.GELU(),
-                                 nn.Linear(4 * d_model, d_model, bias=False))
+        if mlp == "gelu":
+            self.mlp = nn.Sequential(nn.Linear(d_model, 4 * d_model, bias=False), nn.GELU(),
+                                     nn.Linear(4 * d_model, d_model, bias=False))
+        elif mlp == "swiglu":
+            self.mlp = SwiGLU(d_model)
+        else:
+            raise ValueError(f"mlp must be 'gelu' or 'swiglu', got {mlp!r}")
 
     def forward(self, x):
         x = x + self.mixer(self.n1(x))
@@ -96,10 +120,10 @@ class LanguageModel(nn.Module):
     targets)`` returns (logits, mean cross-entropy or None)."""
 
     def __init__(self, vocab: int, d_model: int, n_layers: int, n_heads: int, inner: str,
-                 chunk: int = 64, ns_steps: int = 3, mixer_cls=MixerLayer):
+                 chunk: int = 64, ns_steps: int = 3, mixer_cls=MixerLayer, mlp: str = "gelu"):
         super().__init__()
         self.emb = nn.Embedding(vocab, d_model)
-        self.blocks = nn.ModuleList(Block(d_model, n_heads, inner, chunk, ns_steps, mixer_cls)
+        self.blocks = nn.ModuleList(Block(d_model, n_heads, inner, chunk, ns_steps, mixer_cls, mlp)
                                     for _ in range(n_layers))
         self.norm_f = nn.RMSNorm(d_model)
         self.lm_head = nn.Linear(d_model, vocab, bias=False)   # the reference's name

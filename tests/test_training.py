@@ -285,3 +285,24 @@ def test_outer_adam_condition():
     opts = tr.build_optimizers(m, outer="adam")
     assert all(isinstance(o, torch.optim.AdamW) for o in opts)
     assert opts[0].param_groups[0]["betas"] == (0.9, 0.95)
+
+
+def test_swiglu_variant():
+    """The SwiGLU MLP (the config-4 benchmark description's variant): all
+    three of its matrices are hidden matrices for Muon, the residual output
+    projection gets the scaled init, and a step runs."""
+    import math
+    tr = _training()
+    torch.manual_seed(2)
+    m = tr.LanguageModel(97, 32, 2, 2, "delta", chunk=16, mixer_cls=cpu_mixer_cls(), mlp="swiglu")
+    muon, _ = tr.build_optimizers(m)
+    hidden = {id(p) for g in muon.param_groups for p in g["params"]}
+    for blk in m.blocks:
+        for lin in (blk.mlp.gate, blk.mlp.up, blk.mlp.out):
+            assert id(lin.weight) in hidden
+        assert blk.mlp[2] is blk.mlp.out
+        assert blk.mlp.out.weight.std().item() < 0.02 / math.sqrt(2 * 2) * 1.5
+    idx, tgt = _batch()
+    _, loss = m(idx, tgt)
+    loss.backward()
+    assert torch.isfinite(loss) and all(p.grad is not None for p in m.parameters())
