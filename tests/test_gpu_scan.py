@@ -194,3 +194,37 @@ def test_tensor_core_scan_config1_slices(rule, ns):
         got = dict(zip(["S"] + NAMES, [S[b:b + 1, h:h + 1]] + [a[b:b + 1, h:h + 1] for a in g]))
         check_outputs(got, scan_ref_fn(sl, gS[b:b + 1, h:h + 1], rule, ns), TOL_FP32,
                       prefix=f"({b},{h}):", widen=rule != 0)
+
+
+def test_misaligned_tensors_take_the_exact_scan():
+    """The tensor-core scan moves U, K, S, gS, dU and dK as 16-byte vectors
+    (TMA boxes, float4); fp32 views that start 4 bytes into their storage are
+    routed to the exact-fp32 kernels instead, with the same results."""
+    pkg = load_pkg()
+    base = pkg.workloads.scan_inputs(1, 2, 3, 128, C=64, seed=41)
+    gS = torch.randn(base[0].shape, generator=torch.Generator().manual_seed(2))
+
+    def shifted(t):   # same values, data pointer 4 bytes past a 16-byte boundary
+        buf = torch.empty(t.numel() + 1, dtype=torch.float32, device="cuda")
+        v = buf[1:].view(t.shape)
+        v.copy_(t.float().cuda())
+        assert v.data_ptr() % 16 == 4
+        return v.requires_grad_(True)
+
+    ins = [shifted(base[0]), shifted(base[1])] + [t.float().cuda().requires_grad_(True)
+                                                  for t in base[2:]]
+
+    def run():
+        S = pkg.state_scan(*ins, 0, 3, pkg.GMDN_PREC_FAST)
+        S.backward(gS.float().cuda())
+        torch.cuda.synchronize()
+        return S
+    names = _launched(pkg, run)
+    assert "scan_fwd_ieee" in names and "scan_fwd_tc" not in names, names
+    for t in ins:
+        t.grad = None
+    S = run()
+    S_ref, g_ref = run_kernel(pkg, base, gS, 0, 3, pkg.GMDN_PREC_FAST)
+    assert (S.detach().cpu() - S_ref).abs().max().item() <= 1e-4 * S_ref.abs().max().item()
+    for t, r in zip(ins, g_ref):
+        assert (t.grad.cpu() - r).abs().max().item() <= 1e-4 * (r.abs().max().item() + 1e-30)
