@@ -24,6 +24,7 @@
 
 #include <type_traits>
 
+#include "cp_async.cuh"
 #include "fast_path.h"
 
 namespace gmdn {
@@ -82,26 +83,10 @@ __device__ __forceinline__ float wsum(float v) {
   return v;
 }
 
-// Per-thread prefetch rings: each lane copies its own VEC elements of a row
-// (4-16 bytes) into shared memory with cp.async and reads them back itself, so
-// a warp keeps that many rows in flight without holding them in registers.
+// Per-thread prefetch rings (cp_async.cuh): each lane copies its own VEC
+// elements of a row (4-16 bytes) into shared memory and reads them back itself.
 constexpr int kRingP = 8;    // forward: 8 warps a block, one array
 constexpr int kRingB = 8;    // backward: 2 warps a block, u and the cotangent (16 measured the same)
-template <int BYTES>
-__device__ __forceinline__ void cp_async(void* smem, const void* gmem) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(
-                   static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
-               "l"(gmem), "n"(BYTES)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // fast exp and divide: ~1e-6 relative, and these kernels are issue-bound
 __device__ __forceinline__ float sigm(float z) { return __fdividef(1.f, 1.f + __expf(-z)); }
 

@@ -7,7 +7,7 @@ Run in the development container, where the reference checkout is readable:
 
 It imports the reference's ``train_ablation.py`` unmodified and records, on
 CPU in float32, for each inner rule (delta, muon, adam): the state dict of a
-small seeded ``LM`` (vocab 61, d_model 32, 2 layers, 2 heads, chunk 16; the
+small seeded ``LM`` (vocab 61, d_model 64, 2 layers, 2 heads of 32, chunk 32; the
 reference's own initialisation and gate priors), a token batch, the logits and
 loss of ``LM.forward`` on it (the eager fast_scan path), and the layers' gate
 means.  tests/test_training.py loads these weights into this package's
@@ -36,8 +36,8 @@ def main() -> None:
     out = {}
     for inner in ("delta", "muon", "adam"):
         torch.manual_seed(0)
-        model = ta.LM(61, 32, 2, 2, inner, chunk=16, ns_steps=3)
-        idx = torch.randint(0, 61, (2, 33), generator=torch.Generator().manual_seed(1))
+        model = ta.LM(61, 64, 2, 2, inner, chunk=32, ns_steps=3)
+        idx = torch.randint(0, 61, (2, 65), generator=torch.Generator().manual_seed(1))
         with torch.no_grad():
             logits, loss = model(idx[:, :-1], idx[:, 1:])
         out[inner] = dict(

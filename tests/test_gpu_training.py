@@ -62,3 +62,27 @@ def test_training_steps_lower_the_loss(inner, tf32_matmul):
     assert {fwd, "chunk_bwd2_tc", "mixer_prologue_fwd", "head_rmsnorm_bwd"} <= names, names
     assert all(l == l for l in losses)            # finite
     assert losses[-1] < losses[0] - 0.05, losses
+
+
+def test_b200_model_matches_reference_lm_logits():
+    """The reference trainer's own LM (weights and logits recorded in
+    tests/golden/lm.pt, d_model 64, 2 heads of 32, chunk 32) loaded into this
+    package's LanguageModel on the GPU: the mixer runs the B200 prologue,
+    chunk and epilogue ops (fp32, head dim 32: the exact chunk kernels) and gives
+    the reference's logits."""
+    import os
+    from conftest import ROOT
+    tr = _training()
+    gold = torch.load(os.path.join(ROOT, "tests", "golden", "lm.pt"), weights_only=False)
+    for inner, g in gold.items():
+        m = tr.LanguageModel(61, 64, 2, 2, inner, chunk=32, ns_steps=3)
+        m.load_state_dict(g["state"])
+        m = m.cuda()
+        with torch.no_grad():
+            logits, loss = m(g["idx"][:, :-1].cuda(), g["idx"][:, 1:].cuda())
+        err = (logits.cpu() - g["logits"]).abs().max().item() / g["logits"].abs().max().item()
+        assert err < 1e-4, (inner, err)
+        assert abs(loss.item() - g["loss"].item()) < 1e-4 * abs(g["loss"].item()), inner
+        gm = m.gate_means()
+        for k in ("alpha", "beta", "mu"):
+            assert abs(gm[k] - g["gate_means"][k]) < 1e-5, (inner, k)

@@ -207,7 +207,7 @@ def test_model_matches_reference_lm_weights_and_logits():
     gold = _lm_golden()
     for inner, g in gold.items():
         torch.manual_seed(0)
-        m = tr.LanguageModel(61, 32, 2, 2, inner, chunk=16, ns_steps=3, mixer_cls=cpu_mixer_cls())
+        m = tr.LanguageModel(61, 64, 2, 2, inner, chunk=32, ns_steps=3, mixer_cls=cpu_mixer_cls())
         sd = m.state_dict()
         assert set(sd) == set(g["state"]), inner
         for k, v in g["state"].items():
@@ -270,7 +270,7 @@ def test_run_log_and_checkpoint_formats(tmp_path):
     g = _lm_golden()["muon"]
     ref_ck = tmp_path / "ref.pt"
     torch.save(dict(model_state=g["state"], model_config=dict(
-        vocab=61, d_model=32, n_layers=2, n_heads=2, inner="muon", chunk=16)), ref_ck)
+        vocab=61, d_model=64, n_layers=2, n_heads=2, inner="muon", chunk=32)), ref_ck)
     m3, _ = tr.load_checkpoint(str(ref_ck), mixer_cls=cpu_mixer_cls())
     with torch.no_grad():
         logits, _ = m3(g["idx"][:, :-1])
