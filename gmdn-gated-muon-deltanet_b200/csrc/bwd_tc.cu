@@ -75,16 +75,38 @@ struct BwArgs {
 // ===========================================================================
 
 constexpr int kThreads1 = 448;  // warps 0-7 state, 8-11 chunk-local, 12 TMA + P, Z, 13 chain MMAs
-constexpr int kStages1 = 3;           // q, k, dO ring: the load of step i+3 goes in after step i
-constexpr uint32_t B1_Q = 0;          // q: 3 stages x 16 KB
-constexpr uint32_t B1_K = 49152;      // k: 3 stages
-constexpr uint32_t B1_G = 98304;      // dO: 3 stages
-constexpr uint32_t B1_AS = 147456;    // A' (bf16), 1 panel x 64 rows
-constexpr uint32_t B1_SS = 155648;    // Gb hi staging for the TMA store, 2 panels x 128 rows
-constexpr uint32_t B1_GATE = 188416;  // beta, alpha, mu, nu: 3 stages x 64 floats each
-constexpr uint32_t B1_RED = 191488;   // adam: per-warp partial chunk-scalar cotangents [8][4]
-constexpr uint32_t B1_BAR = 191616;
-constexpr uint32_t B1_SMEM = B1_BAR + 256 + 1024;
+// adam adds warp 14, which streams the forward's G, M, V history into a ring,
+// and warp 15, which loads the S_j history tile of each adam pass
+template <int RULE>
+constexpr int kThreads1R = RULE == 2 ? kThreads1 + 64 : kThreads1;
+constexpr int kStagesMax = 3;
+
+// Shared-memory map of the reverse chain (bytes from a 1024-aligned base).
+// q, k, dO come through a ring of kSt stages: delta's ~2.5 us step wants the
+// load of step i+3 issued after step i (three stages).  Adam's step is ~10x
+// longer, so two stages hide that load, and the space goes to what its adam
+// pass reads per element: the S_j history tile (32 KB, SW128 panels like the
+// Gb staging, loaded by TMA for each pass) and a ring of four 12 KB slots for
+// the G, M, V history (one slot = one 8-column group: 3 arrays x 2 halves x
+// 128 rows x 16 bytes).
+template <int RULE>
+struct L1 {
+  static constexpr int kSt = RULE == 2 ? 2 : 3;
+  static constexpr uint32_t Q = 0;                        // q: kSt stages x 16 KB
+  static constexpr uint32_t K = Q + kSt * 16384;          // k
+  static constexpr uint32_t G = K + kSt * 16384;          // dO
+  static constexpr uint32_t AS = G + kSt * 16384;         // A' (bf16), 1 panel x 64 rows
+  static constexpr uint32_t SS = AS + 8192;               // Gb hi staging, 2 panels x 128 rows
+  static constexpr uint32_t GATE = SS + 32768;            // beta, alpha, mu, nu: kSt x 64 floats
+  static constexpr uint32_t RED = GATE + kSt * 4 * 256;   // adam: per-warp partials [8][4]
+  static constexpr uint32_t SH = (RED + 128 + 1023) / 1024 * 1024;   // adam: S_j tile
+  static constexpr uint32_t HIST = SH + (RULE == 2 ? 32768 : 0);     // adam: the history ring
+  static constexpr int kHist = RULE == 2 ? 4 : 0;
+  static constexpr uint32_t HSLOT = 12288;
+  static constexpr uint32_t BAR = HIST + kHist * HSLOT;
+  static constexpr uint32_t SMEM = BAR + 512 + 1024;   // barrier block, alignment slack
+  static_assert(SMEM <= 232448, "shared memory per block");
+};
 
 // TMEM: chain accumulator C, dE^T hi / lo (packed bf16 pairs, the A operand of
 // C -= dE^T k), D = Gb k^T + dO^T A' (dE^T = D diag(w)), P (lanes 0-15), Gb hi
@@ -102,28 +124,34 @@ template <int RULE>
 constexpr int kDeWarps1 = 8;
 
 struct Bars1 {
-  uint64_t ld_full[kStages1], ld_empty[kStages1];
+  uint64_t ld_full[kStagesMax], ld_empty[kStagesMax];
   uint64_t wk_full, p_full, as_full, de_full, de_smem;
   uint64_t c_full[2], c_empty[2];
   uint64_t s_full, final_mma, z_full, final_tma;
+  uint64_t hist_full[4], hist_empty[4];   // adam
+  uint64_t sh_full, sh_free;              // adam
   uint32_t tmem_base;
   int abort_flag;
 };
-static_assert(sizeof(Bars1) <= 256, "barrier block");
+static_assert(sizeof(Bars1) <= 512, "barrier block");
 
 template <int RULE>
-__global__ void __launch_bounds__(kThreads1, 1)
+__global__ void __launch_bounds__(kThreads1R<RULE>, 1)
 chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_sb,
-                    BwArgs args) {
+                    const __grid_constant__ CUtensorMap tm_sh, BwArgs args) {
+  using Lay = L1<RULE>;
+  constexpr int kStages1 = Lay::kSt;
+  constexpr uint32_t B1_Q = Lay::Q, B1_K = Lay::K, B1_G = Lay::G, B1_AS = Lay::AS, B1_SS = Lay::SS,
+                     B1_GATE = Lay::GATE, B1_RED = Lay::RED, B1_BAR = Lay::BAR;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
   Bars1* bars = reinterpret_cast<Bars1*>(sm + B1_BAR);
-  float* gate_beta = reinterpret_cast<float*>(sm + B1_GATE);   // [3][64] by ring stage
-  float* gate_alpha = gate_beta + 3 * 64;
-  float* gate_mu = gate_beta + 6 * 64;   // adam
-  float* gate_nu = gate_beta + 9 * 64;   // adam
+  float* gate_beta = reinterpret_cast<float*>(sm + B1_GATE);   // [kStages1][64] by ring stage
+  float* gate_alpha = gate_beta + kStages1 * 64;
+  float* gate_mu = gate_beta + 2 * kStages1 * 64;   // adam
+  float* gate_nu = gate_beta + 3 * kStages1 * 64;   // adam
   volatile int* ab = &bars->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.x;
@@ -148,6 +176,12 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     mbar_init(&bars->final_mma, 1);
     mbar_init(&bars->z_full, 1);
     mbar_init(&bars->final_tma, 1);
+    for (int s = 0; s < Lay::kHist; ++s) {
+      mbar_init(&bars->hist_full[s], 1);
+      mbar_init(&bars->hist_empty[s], 8);
+    }
+    mbar_init(&bars->sh_full, 1);
+    mbar_init(&bars->sh_free, 8);
     bars->abort_flag = 0;
     fence_mbar_init();
   }
@@ -280,6 +314,64 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       int dummy = 0;
       mbar_wait(&bars->final_mma, 0, status, &dummy);
     }
+  } else if (warp == 14) {
+    // ------------------------------------------------------------ adam: history ring
+    // The state warps' adam pass of step i reads, per 8-column group, the
+    // forward's G, M, V of chunk N - 2 - i; element loads from global memory
+    // there put a DRAM round trip per group on the chain (~0.7 ms of a 1.9 ms
+    // chain at config 3).  This thread bulk-copies the groups, in the order
+    // the passes read them, into a ring of four slots, running half a pass
+    // ahead while the chain does the rest of its step.
+    if constexpr (RULE == 2) {
+      if (lane == 0) {
+        constexpr int kH = Lay::kHist;
+        int n = 0;   // groups issued
+        bool ok = true;
+        for (int i = 0; ok && i + 1 < N; ++i) {
+          const size_t mm = static_cast<size_t>(bh) * N + (N - 2 - i);
+          for (int g = 0; g < 8; ++g, ++n) {
+            const int slot = n % kH;
+            if (!wait_free(&bars->hist_empty[slot], n / kH, status, ab)) {
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(&bars->hist_full[slot], Lay::HSLOT);
+            uint8_t* dst = sm + Lay::HIST + slot * Lay::HSLOT;
+            const uint16_t* src[3] = {args.G_hist, args.Mp_hist, args.Vp_hist};
+#pragma unroll
+            for (int arr = 0; arr < 3; ++arr)
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+                bulk_load(dst + arr * 4096 + h * 2048,
+                          slab_bf16(const_cast<uint16_t*>(src[arr]), mm, h, g, 0), 2048,
+                          &bars->hist_full[slot]);
+          }
+        }
+        // no copy may still be in flight when the block exits
+        int dummy = 0;
+        for (int k = n - kH; k < n; ++k)
+          if (k >= 0) mbar_wait(&bars->hist_full[k % kH], (k / kH) & 1, status, &dummy);
+      }
+    }
+  } else if (warp == 15) {
+    // ------------------------------------------------------------ adam: S_j history tile
+    // The pass of step i reads <Sb_{j+1}, S_j> for chunk jm = N - 2 - i; row-
+    // per-thread loads of S_j put a DRAM round trip per group on the chain.
+    // The tile of pass i goes in as soon as pass i - 1 is done with it.
+    if constexpr (RULE == 2) {
+      if (lane == 0) {
+        int n = 0;
+        for (int i = 0; i + 1 < N; ++i, ++n) {
+          if (!wait_free(&bars->sh_free, i, status, ab)) break;
+          const int row = static_cast<int>((static_cast<size_t>(bh) * N + (N - 2 - i)) * kD);
+          mbar_expect_tx(&bars->sh_full, 32768);
+          tma_load_2d(sm + Lay::SH, &tm_sh, 0, row, &bars->sh_full);
+          tma_load_2d(sm + Lay::SH + P128, &tm_sh, 64, row, &bars->sh_full);
+        }
+        int dummy = 0;
+        if (n >= 1) mbar_wait(&bars->sh_full, (n - 1) & 1, status, &dummy);
+      }
+    }
   } else if (warp < 8) {
     // ------------------------------------------------------------ state cotangent rows
     const int c = (warp & 3) * 32 + lane;   // row of Sb = TMEM lane
@@ -331,29 +423,56 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       const float nc = expf(warp_sum(logf(fmaxf(nu[lane], kGateFloor)) +
                                      logf(fmaxf(nu[lane + 32], kGateFloor))));
       const bool have_bar = jm + 2 < N;   // Mb, Vb of chunk jm + 1 exist (else zero)
-      const uint4* srow = reinterpret_cast<const uint4*>(args.S_hist + (mm * kD + c) * kD + half * 64);
+      const int pass = N - 2 - jm;
+      if (!wait_use_w(&bars->sh_full, pass, status, ab)) return false;
+      const uint8_t* stile = sm + Lay::SH + half * P128;   // S_j, row c, this half's panel
       float pda = 0.f, pdb = 0.f, pdm = 0.f, pdn = 0.f;
+      // Mb, Vb of the next group load while this one computes (L2 round trips
+      // one group ahead instead of on the chain)
+      float4 nm0 = make_float4(0.f, 0.f, 0.f, 0.f), nm1 = nm0, nv0 = nm0, nv1 = nm0;
+      if (have_bar) {
+        const float4* mp0 = slab_f32(args.M_ws, bh, half, 0, c);
+        const float4* vp0 = slab_f32(args.V_ws, bh, half, 0, c);
+        nm0 = mp0[0];
+        nm1 = mp0[128];
+        nv0 = vp0[0];
+        nv1 = vp0[128];
+      }
       if (threadIdx.x == 0) bulk_wait_read0();
       named_sync(2, 256);
       uint8_t* panel = sm + B1_SS + half * P128;
 #pragma unroll
       for (int g8 = 0; g8 < 8; ++g8) {
         float g[8], mp[8], vp[8], sv[8], mb[8], vb[8], gb[8];
-        unpack8(*slab_bf16(const_cast<uint16_t*>(args.G_hist), mm, half, g8, c), g);
-        unpack8(*slab_bf16(const_cast<uint16_t*>(args.Mp_hist), mm, half, g8, c), mp);
-        unpack8(*slab_bf16(const_cast<uint16_t*>(args.Vp_hist), mm, half, g8, c), vp);
-        unpack8(srow[g8], sv);
+        {
+          // G, M, V of this group from the history ring (pass N - 2 - jm)
+          constexpr int kH = Lay::kHist > 0 ? Lay::kHist : 1;
+          const int n = (N - 2 - jm) * 8 + g8, slot = n % kH;
+          if (!wait_use_w(&bars->hist_full[slot], n / kH, status, ab)) return false;
+          const uint8_t* hb = sm + Lay::HIST + slot * Lay::HSLOT + half * 2048 + c * 16;
+          unpack8(*reinterpret_cast<const uint4*>(hb), g);
+          unpack8(*reinterpret_cast<const uint4*>(hb + 4096), mp);
+          unpack8(*reinterpret_cast<const uint4*>(hb + 8192), vp);
+          // the slot's next bulk copy (async proxy) must not overtake these reads
+          fence_async_smem();
+          mbar_arrive_warp(&bars->hist_empty[slot]);
+        }
+        unpack8(*reinterpret_cast<const uint4*>(stile + sw128_chunk(c, g8)), sv);
+        if (g8 == 7) {   // S_j read out: the next pass's tile may load
+          fence_async_smem();
+          mbar_arrive_warp(&bars->sh_free);
+        }
         float4* mbp = slab_f32(args.M_ws, bh, half, 2 * g8, c);
         float4* vbp = slab_f32(args.V_ws, bh, half, 2 * g8, c);
-        if (have_bar) {
-          const float4 m0 = mbp[0], m1 = mbp[128], v0 = vbp[0], v1 = vbp[128];
-          mb[0] = m0.x; mb[1] = m0.y; mb[2] = m0.z; mb[3] = m0.w;
-          mb[4] = m1.x; mb[5] = m1.y; mb[6] = m1.z; mb[7] = m1.w;
-          vb[0] = v0.x; vb[1] = v0.y; vb[2] = v0.z; vb[3] = v0.w;
-          vb[4] = v1.x; vb[5] = v1.y; vb[6] = v1.z; vb[7] = v1.w;
-        } else {
-#pragma unroll
-          for (int t = 0; t < 8; ++t) mb[t] = vb[t] = 0.f;
+        mb[0] = nm0.x; mb[1] = nm0.y; mb[2] = nm0.z; mb[3] = nm0.w;
+        mb[4] = nm1.x; mb[5] = nm1.y; mb[6] = nm1.z; mb[7] = nm1.w;
+        vb[0] = nv0.x; vb[1] = nv0.y; vb[2] = nv0.z; vb[3] = nv0.w;
+        vb[4] = nv1.x; vb[5] = nv1.y; vb[6] = nv1.z; vb[7] = nv1.w;
+        if (have_bar && g8 + 1 < 8) {
+          nm0 = mbp[256];   // group g8 + 1: f = 2 g8 + 2 (two float4 rows on)
+          nm1 = mbp[384];
+          nv0 = vbp[256];
+          nv1 = vbp[384];
         }
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
@@ -361,12 +480,16 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           const float mi = fmaf(mc, mp[t], (1.f - mc) * g[t]);
           const float vi = fmaf(nc, vp[t], (1.f - nc) * (g[t] * g[t]));
           const float root = sqrtf(vi);
-          const float den = root + kEpsAdam;
+          // two correctly rounded reciprocals instead of four IEEE divisions:
+          // the pass is on the chain and issue-bound (2 warps per scheduler),
+          // and each division is a long dependent sequence
+          const float rden = __frcp_rn(root + kEpsAdam);
+          const float mr = mi * rden;   // Mi / den
           pda = fmaf(sbar, sv[t], pda);
-          pdb = fmaf(sbar, mi / den, pdb);
+          pdb = fmaf(sbar, mr, pdb);
           const float ub = b * sbar;
-          const float mt = mb[t] + ub / den;
-          const float vt = vb[t] - ub * mi / (den * den) / (2.f * fmaxf(root, 1e-12f));
+          const float mt = fmaf(ub, rden, mb[t]);
+          const float vt = vb[t] - ub * mr * rden * (0.5f * __frcp_rn(fmaxf(root, 1e-12f)));
           pdm = fmaf(mt, mp[t] - g[t], pdm);
           pdn = fmaf(vt, vp[t] - g[t] * g[t], pdn);
           mb[t] = mc * mt;
@@ -1460,11 +1583,13 @@ bool adam_bufs_ok(const ChunkArgs& p, const TcBufs& b) {
 
 template <int RULE>
 cudaError_t launch_bw1(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mg,
-                       const CUtensorMap& msb, const BwArgs& a, int grid, cudaStream_t st) {
+                       const CUtensorMap& msb, const CUtensorMap& msh, const BwArgs& a, int grid,
+                       cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(chunk_bwd1_tc_kernel<RULE>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, B1_SMEM);
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, L1<RULE>::SMEM);
   if (e != cudaSuccess) return e;
-  chunk_bwd1_tc_kernel<RULE><<<grid, kThreads1, B1_SMEM, st>>>(mq, mk, mg, msb, a);
+  chunk_bwd1_tc_kernel<RULE><<<grid, kThreads1R<RULE>, L1<RULE>::SMEM, st>>>(mq, mk, mg, msb, msh,
+                                                                               a);
   return cudaGetLastError();
 }
 
@@ -1489,22 +1614,22 @@ cudaError_t launch_bw2(const CUtensorMap* m, BwArgs a, int tiles, cudaStream_t s
 }  // namespace
 
 cudaError_t chunk_bwd1_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st) {
-  CUtensorMap mq, mk, mg, msb;
+  CUtensorMap mq, mk, mg, msb, msh;
   const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
+  const uint64_t srows = static_cast<uint64_t>(p.BH) * p.N * kD;
   cudaError_t e;
   const uint32_t w = static_cast<uint32_t>(p.dh);
   if ((e = make_tmap_rows128(&mq, p.q, rows, 64, w)) != cudaSuccess) return e;
   if ((e = make_tmap_rows128(&mk, p.k, rows, 64, w)) != cudaSuccess) return e;
   if ((e = make_tmap_rows128(&mg, p.dO, rows, 64, w)) != cudaSuccess) return e;
-  if ((e = make_tmap_rows128(&msb, b.Gbar_hist, static_cast<uint64_t>(p.BH) * p.N * kD, 128)) !=
-      cudaSuccess)
-    return e;
+  if ((e = make_tmap_rows128(&msb, b.Gbar_hist, srows, 128)) != cudaSuccess) return e;
+  if ((e = make_tmap_rows128(&msh, b.S_hist, srows, 128)) != cudaSuccess) return e;   // adam's pass
   const BwArgs a = bw_args(p, b);
   if (p.rule == 2) {
     if (!adam_bufs_ok(p, b)) return cudaErrorInvalidValue;
-    return launch_bw1<2>(mq, mk, mg, msb, a, p.BH, st);
+    return launch_bw1<2>(mq, mk, mg, msb, msh, a, p.BH, st);
   }
-  return launch_bw1<0>(mq, mk, mg, msb, a, p.BH, st);
+  return launch_bw1<0>(mq, mk, mg, msb, msh, a, p.BH, st);
 }
 
 cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st) {

@@ -339,42 +339,57 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
                                        logf(fmaxf(nu[lane + 32], kGateFloor))));
         fence_async_smem();   // gate reads before the stage's reload (async proxy)
         mbar_arrive_warp(&bars->ld_empty[j & 1]);   // done with this stage's gates
+        // M_j, V_j (fp32, L2-resident slabs) in 8-column groups, the next
+        // group's loaded while this one computes; group 0's go out before the
+        // wait for G, so no slab round trip sits between G and the update
+        const size_t mj = static_cast<size_t>(bh) * N + j;
+        float4 nm0 = make_float4(0.f, 0.f, 0.f, 0.f), nm1 = nm0, nv0 = nm0, nv1 = nm0;
+        if (j > 0) {
+          const float4* m0p = slab_f32(args.M_ws, bh, half, 0, c);
+          const float4* v0p = slab_f32(args.V_ws, bh, half, 0, c);
+          nm0 = m0p[0];
+          nm1 = m0p[128];
+          nv0 = v0p[0];
+          nv1 = v0p[128];
+        }
         if (!wait_use_w(&bars->g_full, j, status, ab)) break;
         tc_fence_after();
-        const size_t mj = static_cast<size_t>(bh) * N + j;
         const uint32_t rg = tmem + lb + TM_G + half * 64;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float mv[16], vv[16], g[16];
-          float* mp = reinterpret_cast<float*>(slab_f32(args.M_ws, bh, half, 4 * q, c));
-          float* vp = reinterpret_cast<float*>(slab_f32(args.V_ws, bh, half, 4 * q, c));
-          if (j > 0) {
-            ld_f16x4(mp, mv);
-            ld_f16x4(vp, vv);
-          } else {
-#pragma unroll
-            for (int t = 0; t < 16; ++t) mv[t] = vv[t] = 0.f;
+        for (int g8 = 0; g8 < 8; ++g8) {
+          float4* mp = slab_f32(args.M_ws, bh, half, 2 * g8, c);
+          float4* vp = slab_f32(args.V_ws, bh, half, 2 * g8, c);
+          float mv[8] = {nm0.x, nm0.y, nm0.z, nm0.w, nm1.x, nm1.y, nm1.z, nm1.w};
+          float vv[8] = {nv0.x, nv0.y, nv0.z, nv0.w, nv1.x, nv1.y, nv1.z, nv1.w};
+          if (j > 0 && g8 + 1 < 8) {
+            nm0 = mp[256];   // group g8 + 1: float4 rows 2 g8 + 2, 2 g8 + 3
+            nm1 = mp[384];
+            nv0 = vp[256];
+            nv1 = vp[384];
           }
-          tmem_ld16(rg + 16 * q, g);
+          float g[8];
+          tmem_ld8(rg + 8 * g8, g);
           tmem_ld_wait();
           // pre-update G_j, M_j, V_j for the backward
-          *slab_bf16(args.G_hist, mj, half, 2 * q, c) = pack8(g);
-          *slab_bf16(args.G_hist, mj, half, 2 * q + 1, c) = pack8(g + 8);
-          *slab_bf16(args.Mp_hist, mj, half, 2 * q, c) = pack8(mv);
-          *slab_bf16(args.Mp_hist, mj, half, 2 * q + 1, c) = pack8(mv + 8);
-          *slab_bf16(args.Vp_hist, mj, half, 2 * q, c) = pack8(vv);
-          *slab_bf16(args.Vp_hist, mj, half, 2 * q + 1, c) = pack8(vv + 8);
+          *slab_bf16(args.G_hist, mj, half, g8, c) = pack8(g);
+          *slab_bf16(args.Mp_hist, mj, half, g8, c) = pack8(mv);
+          *slab_bf16(args.Vp_hist, mj, half, g8, c) = pack8(vv);
 #pragma unroll
-          for (int t = 0; t < 16; ++t) {
+          for (int t = 0; t < 8; ++t) {
             const float m1 = fmaf(mc, mv[t], (1.f - mc) * g[t]);
             const float v1 = fmaf(nc, vv[t], (1.f - nc) * (g[t] * g[t]));
             mv[t] = m1;
             vv[t] = v1;
-            st[16 * q + t] = fmaf(a, st[16 * q + t], b * m1 / (sqrtf(v1) + kEpsAdam));
+            // a correctly rounded reciprocal for the IEEE division (the update
+            // is on the chain and the division is a long dependent sequence)
+            st[8 * g8 + t] =
+                fmaf(a, st[8 * g8 + t], b * m1 * __frcp_rn(sqrtf(v1) + kEpsAdam));
           }
           if (j + 1 < N) {
-            st_f16x4(mp, mv);
-            st_f16x4(vp, vv);
+            mp[0] = make_float4(mv[0], mv[1], mv[2], mv[3]);
+            mp[128] = make_float4(mv[4], mv[5], mv[6], mv[7]);
+            vp[0] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+            vp[128] = make_float4(vv[4], vv[5], vv[6], vv[7]);
           }
         }
       } else {
