@@ -115,6 +115,11 @@ struct L1 {
 // the chain's operands other than the TMA-loaded tiles stay in TMEM.
 constexpr uint32_t T1_C = 0, T1_DEH = 128, T1_DEL = 160, T1_E = 256, T1_P = 320, T1_SH = 384,
                    T1_SL = 448;
+// adam: Sb_{j+1} (fp32, 128 values a lane) parked in columns 128-255 during
+// the adam pass (dE^T hi / lo are dead from W's completion to the next dE
+// drain, 192-255 are unused), so its 64 registers a thread are free for the
+// pass's temporaries instead of spilling
+constexpr uint32_t T1_STASH = 128;
 
 // Who drains dE: the eight state warps (idle between packing Sb and W; two
 // warps per TMEM subpartition drain in about half the time of one).  Delta's
@@ -462,6 +467,9 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           fence_async_smem();
           mbar_arrive_warp(&bars->sh_free);
         }
+        float sbv[8];   // Sb_{j+1} of this group, from the TMEM stash
+        tmem_ld8(tmem + lb + T1_STASH + half * 64 + 8 * g8, sbv);
+        tmem_ld_wait();
         float4* mbp = slab_f32(args.M_ws, bh, half, 2 * g8, c);
         float4* vbp = slab_f32(args.V_ws, bh, half, 2 * g8, c);
         mb[0] = nm0.x; mb[1] = nm0.y; mb[2] = nm0.z; mb[3] = nm0.w;
@@ -476,20 +484,19 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         }
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
-          const float sbar = sb[8 * g8 + t];
+          const float sbar = sbv[t];
           const float mi = fmaf(mc, mp[t], (1.f - mc) * g[t]);
           const float vi = fmaf(nc, vp[t], (1.f - nc) * (g[t] * g[t]));
-          const float root = sqrtf(vi);
-          // two correctly rounded reciprocals instead of four IEEE divisions:
-          // the pass is on the chain and issue-bound (2 warps per scheduler),
-          // and each division is a long dependent sequence
-          const float rden = __frcp_rn(root + kEpsAdam);
+          // the pass is on the chain: SFU square root and two reciprocals
+          // instead of an IEEE square root and four IEEE divisions (tc.cuh)
+          const float root = sqrt_sfu(vi);
+          const float rden = rcp_sfu(root + kEpsAdam);
           const float mr = mi * rden;   // Mi / den
           pda = fmaf(sbar, sv[t], pda);
           pdb = fmaf(sbar, mr, pdb);
           const float ub = b * sbar;
           const float mt = fmaf(ub, rden, mb[t]);
-          const float vt = vb[t] - ub * mr * rden * (0.5f * __frcp_rn(fmaxf(root, 1e-12f)));
+          const float vt = vb[t] - ub * mr * rden * (0.5f * rcp_sfu(fmaxf(root, 1e-12f)));
           pdm = fmaf(mt, mp[t] - g[t], pdm);
           pdn = fmaf(vt, vp[t] - g[t] * g[t], pdn);
           mb[t] = mc * mt;
@@ -634,7 +641,26 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       tc_fence_before();
       mbar_arrive_warp(&bars->c_empty[0]);
       if constexpr (RULE == 2) {
-        if (j >= 1 && !adam_pass(j - 1)) break;
+        if (j >= 1) {
+          // park Sb_{j+1} in TMEM for the pass, take it back after
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t r[16];
+#pragma unroll
+            for (int t = 0; t < 16; ++t) r[t] = __float_as_uint(sb[16 * q + t]);
+            tmem_st16(tmem + lb + T1_STASH + half * 64 + 16 * q, r);
+          }
+          tmem_st_wait();
+          if (!adam_pass(j - 1)) break;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float x[16];
+            tmem_ld16(tmem + lb + T1_STASH + half * 64 + 16 * q, x);
+            tmem_ld_wait();
+#pragma unroll
+            for (int t = 0; t < 16; ++t) sb[16 * q + t] = x[t];
+          }
+        }
       } else {
       // Sb_j as packed bf16 hi / lo pairs into TMEM (A operand of the next
       // chain product)

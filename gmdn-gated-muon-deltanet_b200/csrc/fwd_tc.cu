@@ -380,10 +380,9 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             const float v1 = fmaf(nc, vv[t], (1.f - nc) * (g[t] * g[t]));
             mv[t] = m1;
             vv[t] = v1;
-            // a correctly rounded reciprocal for the IEEE division (the update
-            // is on the chain and the division is a long dependent sequence)
+            // SFU square root and reciprocal (the update is on the chain; tc.cuh)
             st[8 * g8 + t] =
-                fmaf(a, st[8 * g8 + t], b * m1 * __frcp_rn(sqrtf(v1) + kEpsAdam));
+                fmaf(a, st[8 * g8 + t], b * m1 * rcp_sfu(sqrt_sfu(v1) + kEpsAdam));
           }
           if (j + 1 < N) {
             mp[0] = make_float4(mv[0], mv[1], mv[2], mv[3]);
