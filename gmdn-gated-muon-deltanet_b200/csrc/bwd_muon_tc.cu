@@ -665,8 +665,11 @@ chunk_bwd1_tc_muon(const __grid_constant__ CUtensorMap tm_q, const __grid_consta
 #pragma unroll
             for (int x = 0; x < 8; ++x) {
               const int sc = cc * 16 + h * 8 + x;
-              v8[x] = (sc <= t16) ? src[x] * gate_beta[sc] / fmaxf(gate_w[sc], kMuonWFloor)
-                                  : 0.f;
+              // SFU reciprocal: A' goes to bf16, and IEEE divisions here held
+              // up the chain's X product (tc.cuh)
+              v8[x] = (sc <= t16)
+                          ? src[x] * gate_beta[sc] * rcp_sfu(fmaxf(gate_w[sc], kMuonWFloor))
+                          : 0.f;
             }
             st_row8(sm + A_AS, P64, t16, cc * 2 + h, v8);
           }

@@ -1315,8 +1315,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
               // A' = tril(P) beta / w: delta (w = beta) tril(P); muon tril(P) beta / w
               // (w floored, see kMuonWFloor); adam (w = 1) tril(P) beta
               v8[x] = (sc <= r16) ? (RULE == 0   ? p[h * 8 + x]
-                                     : RULE == 1 ? p[h * 8 + x] * gbeta[sc] /
-                                                       fmaxf(gw[sc], kMuonWFloor)
+                                     : RULE == 1 ? p[h * 8 + x] * gbeta[sc] *
+                                                       rcp_sfu(fmaxf(gw[sc], kMuonWFloor))
                                                  : p[h * 8 + x] * gbeta[sc])
                                   : 0.f;
             }
