@@ -667,6 +667,49 @@ def run_train(args) -> None:
         dist.destroy_process_group()
 
 
+def graph_of(step, device):
+    """The step captured into a CUDA graph (warm-up on a side stream, then one
+    capture), so that the timed loop replays the same launches without the
+    host's per-launch work (the ctypes calls, tensor-map encoding and autograd
+    bookkeeping of the custom ops): the replay runs the step's every kernel,
+    and at strong-scaling sizes the host was otherwise slower than the GPU.
+    Returns (replay, outputs of the captured step, None) or (step, None,
+    reason) when capture is not possible."""
+    try:
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                step()
+        torch.cuda.current_stream(device).wait_stream(side)
+        torch.cuda.synchronize(device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out = step()
+        torch.cuda.synchronize(device)
+        return g.replay, out, None
+    except Exception as e:   # capture not available: time the plain step
+        torch.cuda.synchronize(device)
+        return step, None, f"{type(e).__name__}: {str(e)[:120]}"
+
+
+def graph_matches(replay, out, step) -> bool:
+    """One replay's gradients equal a plain step's: dq, dk, dv bit for bit (the
+    kernels are deterministic; a difference means the capture missed work),
+    the gate gradients to 1e-5 (their per-chunk partials are summed with float
+    atomics across CTAs, in no fixed order)."""
+    replay()
+    ref = step()
+    torch.cuda.synchronize()
+    for i, (a, b) in enumerate(zip(out, ref)):
+        if i < 3:
+            if not torch.equal(a, b):
+                return False
+        elif (a.float() - b.float()).abs().max().item() > 1e-5 * (b.float().abs().max().item() + 1e-30):
+            return False
+    return True
+
+
 def time_config(pkg, L, name: str, prec: int, steps: int, warmup: int, peaks: dict,
                 peak_kind: str) -> dict:
     """One GPU, another configuration of the baseline on the same box and
@@ -688,20 +731,29 @@ def time_config(pkg, L, name: str, prec: int, steps: int, warmup: int, peaks: di
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
+    run, gout, gerr = graph_of(step, torch.device("cuda"))
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    L.prof_report()
-    L.prof_enable(True)
+    for _ in range(2):
+        run()
+    torch.cuda.synchronize()
     e0.record(stream)
     for _ in range(steps):
-        step()
+        run()
     e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    # per-kernel times from the library's per-launch events, on plain steps
+    L.prof_report()
+    L.prof_enable(True)
+    for _ in range(min(steps, 5)):
+        step()
     torch.cuda.synchronize()
     L.prof_enable(False)
     kt = L.prof_report()
-    ms = e0.elapsed_time(e1) / steps
     return {"config": name, "rule": RULE_NAMES[rule], "B": B, "H": H, "T": T, "ns": ns,
             "ms_per_step": ms, "value": B * T / (ms / 1e3), "unit": "tokens/s", "steps": steps,
+            "launch": "cuda_graph" if gerr is None else f"plain ({gerr})",
             "step_roofline": step_roofline(cfg, ms, peaks, peak_kind),
             "kernel_times": {k: {"avg_ms": v[0] / max(v[1], 1), "launches": v[1]}
                              for k, v in kt.items()}}
@@ -725,6 +777,8 @@ def main():
                     choices=["mixer", "epilogue", "prologue", "scan", "train"],
                     help="epilogue / prologue: that part of the mixer alone; scan: the "
                          "scan-only drop-in (fast_state_scan) on fp32 U, K; one GPU each")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="time plain steps instead of CUDA-graph replays of the step")
     ap.add_argument("--mlp", default="gelu", choices=["gelu", "swiglu"],
                     help="train workload: the reference trainer's GELU MLP, or the SwiGLU MLP "
                          "that the config-4 benchmark description names")
@@ -798,25 +852,44 @@ def main():
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
+    # the timed loop replays the step as one CUDA graph (graph_of); the graph
+    # is checked against a plain step first
+    run, gout, gerr = (step, None, "disabled") if args.no_graph else graph_of(step, device)
+    graph_ok = None if gerr is not None else graph_matches(run, gout, step)
+    if graph_ok is False:
+        run, gerr = step, "replay differed from a plain step"
+    for _ in range(max(args.warmup, 3)):
+        run()
+    torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
 
     stream = torch.cuda.current_stream(device)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = L.kernel_launches()
-    L.prof_report()  # drop anything recorded so far
-    L.prof_enable(True)
+    step()   # one plain step: the library's launch counter per step
+    torch.cuda.synchronize()
+    launches_per_step = L.kernel_launches() - launches0
+    barrier()
+    torch.cuda.synchronize()
     clocks.mark(True)
     ev0.record(stream)
     for _ in range(args.steps):
-        step()
+        run()
     ev1.record(stream)
     torch.cuda.synchronize()
     clocks.mark(False)
+    launches = launches_per_step * args.steps
+    elapsed = ev0.elapsed_time(ev1)  # ms
+    # per-kernel times from the library's per-launch CUDA events, on plain
+    # steps right after the timed loop (events cannot sit inside the graph)
+    L.prof_report()  # drop anything recorded so far
+    L.prof_enable(True)
+    for _ in range(min(args.steps, 5)):
+        step()
+    torch.cuda.synchronize()
     L.prof_enable(False)
     kt = L.prof_report()
-    launches = L.kernel_launches() - launches0
-    elapsed = ev0.elapsed_time(ev1)  # ms
     own_ms = elapsed
     barrier()
     elapsed = pkg.sharding.max_over_ranks(elapsed, device)
@@ -857,6 +930,10 @@ def main():
 
         for _ in range(3):
             ostep()
+        torch.cuda.synchronize()
+        orun = ostep if args.no_graph else graph_of(ostep, device)[0]
+        for _ in range(2):
+            orun()
         osteps = max(3, min(args.steps, 10))
         torch.cuda.synchronize()
         barrier()
@@ -864,7 +941,7 @@ def main():
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(osteps):
-            ostep()
+            orun()
         e1.record(stream)
         torch.cuda.synchronize()
         oms = pkg.sharding.max_over_ranks(e0.elapsed_time(e1), device)
@@ -1017,6 +1094,8 @@ def main():
             "step_roofline": step_roofline(cfg, elapsed / args.steps, peaks, peak_kind),
             "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": launches, "clocks": clock_info,
+            "launch": ("cuda_graph (each timed step replays the captured fwd+bwd; checked "
+                       "against a plain step)") if gerr is None else f"plain steps ({gerr})",
             "kernel_times": kernel_times, "per_rank": per_rank, "other_scaling": other,
             "other_configs": other_configs,
         }
