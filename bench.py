@@ -390,6 +390,30 @@ def run_reference_arm(args, cfg: dict) -> None:
 # GPU arm
 # ---------------------------------------------------------------------------
 
+def timed_steps(step, L, steps: int, stream, device, no_graph: bool):
+    """Total ms of `steps` steps on `stream` (CUDA events; CUDA-graph replays
+    of the step unless no_graph, see graph_of), and the library's per-kernel
+    times from as many plain steps (at most five) right after."""
+    run, _, gerr = (step, None, "disabled") if no_graph else graph_of(step, device)
+    for _ in range(2):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        run()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    L.prof_report()
+    L.prof_enable(True)
+    for _ in range(min(steps, 5)):
+        step()
+    torch.cuda.synchronize()
+    L.prof_enable(False)
+    return ms, L.prof_report(), "cuda_graph" if gerr is None else f"plain steps ({gerr})"
+
+
 def run_epilogue(args) -> None:
     """The mixer epilogue alone (train_ablation.py:188-189 up to the output
     projection): per-head RMSNorm of o (B8 H16 T4096 d128, bf16) into the
@@ -416,16 +440,7 @@ def run_epilogue(args) -> None:
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    L.prof_report()
-    L.prof_enable(True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    L.prof_enable(False)
-    kt = L.prof_report()
-    ms = e0.elapsed_time(e1)
+    ms, kt, launch = timed_steps(step, L, args.steps, stream, device, args.no_graph)
     row_bytes = B * H * T * dh * 2
     work = {"head_rmsnorm_fwd": 2 * row_bytes, "head_rmsnorm_bwd": 3 * row_bytes}
     peaks, kind = load_peaks()
@@ -445,7 +460,7 @@ def run_epilogue(args) -> None:
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps,
         "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "epilogue_config1", "l2": "inputs larger than L2 (o 134 MB)"},
-        "roofline": roof, "kernel_times": kernel_times}), flush=True)
+        "roofline": roof, "kernel_times": kernel_times, "launch": launch}), flush=True)
 
 
 def run_prologue(args) -> None:
@@ -478,16 +493,7 @@ def run_prologue(args) -> None:
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    L.prof_report()
-    L.prof_enable(True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    L.prof_enable(False)
-    kt = L.prof_report()
-    ms = e0.elapsed_time(e1)
+    ms, kt, launch = timed_steps(step, L, args.steps, stream, device, args.no_graph)
     ub = B * T * D3 * 2
     work = {"mixer_prologue_fwd": 2 * ub, "mixer_prologue_bwd": 3 * ub}
     peaks, kind = load_peaks()
@@ -507,7 +513,7 @@ def run_prologue(args) -> None:
         "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms / args.steps,
         "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "prologue_config1", "l2": "inputs larger than L2 (u 403 MB)"},
-        "roofline": roof, "kernel_times": kernel_times}), flush=True)
+        "roofline": roof, "kernel_times": kernel_times, "launch": launch}), flush=True)
 
 
 def run_scan(args) -> None:
@@ -544,16 +550,7 @@ def run_scan(args) -> None:
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream(device)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    L.prof_report()
-    L.prof_enable(True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    L.prof_enable(False)
-    kt = L.prof_report()
-    ms = e0.elapsed_time(e1)
+    ms, kt, launch = timed_steps(step, L, args.steps, stream, device, args.no_graph)
     mat = B * H * N * dh * dh * 4
     # algorithmic HBM bytes per launch: forward U, K in and S out; exact
     # backward U, K, S, gS in and dU, dK out; tensor-core backward: the chain
@@ -578,7 +575,7 @@ def run_scan(args) -> None:
         "higher_is_better": True, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "scan_config1", "precision": args.precision,
                    "l2": "inputs larger than L2 (U, K 537 MB each)"},
-        "roofline": roof, "kernel_times": kernel_times}), flush=True)
+        "roofline": roof, "kernel_times": kernel_times, "launch": launch}), flush=True)
 
 
 def run_train(args) -> None:
