@@ -1003,8 +1003,8 @@ def main():
         torch.cuda.synchronize()
         barrier()
         # the copies of one step fill the pipeline before the first and drain it
-        # after the last: time as many steps as the device-timed run (4..20)
-        e2e_steps = max(4, min(args.steps, 20))
+        # after the last: time twice the device-timed steps (8..30) to amortise that
+        e2e_steps = max(8, min(2 * args.steps, 30))
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(s_h2d)
