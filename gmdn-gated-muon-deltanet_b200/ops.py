@@ -71,7 +71,9 @@ _CHECK_STATUS = os.environ.get("GMDN_CHECK_STATUS", "0") == "1"
 
 
 def _check_status(ws: Tensor, what: str) -> None:
-    if _CHECK_STATUS:
+    # reading the word synchronises the stream: not while it is being
+    # captured into a CUDA graph (the replays are checked by their caller)
+    if _CHECK_STATUS and not torch.cuda.is_current_stream_capturing():
         check(lib.gmdn_chunk_status(_ptr(ws), _stream(ws)), what)
 
 
