@@ -16,6 +16,13 @@ __device__ __forceinline__ void cp_async(void* smem, const void* gmem) {
                "l"(gmem), "n"(BYTES)
                : "memory");
 }
+// 16 bytes, cached in L2 only (streamed rows are read once)
+__device__ __forceinline__ void cp_async_cg16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+               "l"(gmem)
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");
 }

@@ -37,10 +37,16 @@ def _check(pkg, u, w, b, gl, H, cot, tol, gtol):
 
 
 @pytest.mark.parametrize("B,T,H,dh,nG,dt", [
+    # wide strips (16-byte lanes, several heads a warp) where H allows, else one head a warp
     (2, 150, 2, 128, 3, torch.float32),    # T not a multiple of the 64-step strips
-    (1, 64, 3, 64, 4, torch.float32),
-    (2, 96, 2, 32, 3, torch.float32),
+    (1, 64, 3, 64, 4, torch.float32),      # H 3: one head a warp
+    (2, 96, 2, 32, 3, torch.float32),      # H 2 < 4 heads a warp: one head a warp
     (2, 256, 4, 128, 4, torch.bfloat16),
+    (1, 130, 4, 64, 4, torch.bfloat16),    # four heads a warp, ragged last strip
+    (2, 70, 8, 32, 3, torch.bfloat16),     # eight heads a warp
+    (1, 67, 2, 64, 4, torch.float32),      # two heads a warp, fp32
+    (1, 200, 4, 32, 3, torch.float32),
+    (1, 128, 3, 128, 4, torch.bfloat16),   # H 3 at bf16 dh 128: one head a warp
 ])
 def test_mixer_prologue_matches_oracle(B, T, H, dh, nG, dt):
     pkg = load_pkg()
