@@ -431,7 +431,7 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       const int pass = N - 2 - jm;
       if (!wait_use_w(&bars->sh_full, pass, status, ab)) return false;
       const uint8_t* stile = sm + Lay::SH + half * P128;   // S_j, row c, this half's panel
-      float pda = 0.f, pdb = 0.f, pdm = 0.f, pdn = 0.f;
+      float2 pda2 = p2(0.f), pdb2 = p2(0.f), pdm2 = p2(0.f), pdn2 = p2(0.f);
       // Mb, Vb of the next group load while this one computes (L2 round trips
       // one group ahead instead of on the chain)
       float4 nm0 = make_float4(0.f, 0.f, 0.f, 0.f), nm1 = nm0, nv0 = nm0, nv1 = nm0;
@@ -482,26 +482,37 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
           nv0 = vbp[256];
           nv1 = vbp[384];
         }
+        // element pairs (tc.cuh p2 / fma2 / mul2): the pass is on the chain.
+        // One reciprocal square root serves both sqrt(Vi) and 1 / max(sqrt(Vi),
+        // 1e-12), one reciprocal 1 / (sqrt(Vi) + eps): two special-function ops
+        // an element instead of an IEEE square root and four IEEE divisions.
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const float sbar = sbv[t];
-          const float mi = fmaf(mc, mp[t], (1.f - mc) * g[t]);
-          const float vi = fmaf(nc, vp[t], (1.f - nc) * (g[t] * g[t]));
-          // the pass is on the chain: SFU square root and two reciprocals
-          // instead of an IEEE square root and four IEEE divisions (tc.cuh)
-          const float root = sqrt_sfu(vi);
-          const float rden = rcp_sfu(root + kEpsAdam);
-          const float mr = mi * rden;   // Mi / den
-          pda = fmaf(sbar, sv[t], pda);
-          pdb = fmaf(sbar, mr, pdb);
-          const float ub = b * sbar;
-          const float mt = fmaf(ub, rden, mb[t]);
-          const float vt = vb[t] - ub * mr * rden * (0.5f * rcp_sfu(fmaxf(root, 1e-12f)));
-          pdm = fmaf(mt, mp[t] - g[t], pdm);
-          pdn = fmaf(vt, vp[t] - g[t] * g[t], pdn);
-          mb[t] = mc * mt;
-          vb[t] = nc * vt;
-          gb[t] = fmaf(1.f - mc, mt, 2.f * (1.f - nc) * g[t] * vt);
+        for (int t = 0; t < 8; t += 2) {
+          const float2 sbar = p2(sbv[t], sbv[t + 1]);
+          const float2 G = p2(g[t], g[t + 1]), Mp = p2(mp[t], mp[t + 1]), Vp = p2(vp[t], vp[t + 1]);
+          const float2 GG = mul2(G, G);
+          const float2 mi = fma2(p2(mc), Mp, mul2(p2(1.f - mc), G));
+          const float2 vi = fma2(p2(nc), Vp, mul2(p2(1.f - nc), GG));
+          const float rs0 = rsqrtf(vi.x), rs1 = rsqrtf(vi.y);   // +inf at 0
+          const float2 root = p2(vi.x > 0.f ? vi.x * rs0 : 0.f, vi.y > 0.f ? vi.y * rs1 : 0.f);
+          const float2 rden = p2(rcp_sfu(root.x + kEpsAdam), rcp_sfu(root.y + kEpsAdam));
+          const float2 hr = mul2(p2(0.5f), p2(fminf(rs0, 1e12f), fminf(rs1, 1e12f)));
+          const float2 mr = mul2(mi, rden);   // Mi / den
+          pda2 = fma2(sbar, p2(sv[t], sv[t + 1]), pda2);
+          pdb2 = fma2(sbar, mr, pdb2);
+          const float2 ub = mul2(p2(b), sbar);
+          const float2 mt = fma2(ub, rden, p2(mb[t], mb[t + 1]));
+          const float2 vt = sub2(p2(vb[t], vb[t + 1]), mul2(mul2(mul2(ub, mr), rden), hr));
+          pdm2 = fma2(mt, sub2(Mp, G), pdm2);
+          pdn2 = fma2(vt, sub2(Vp, GG), pdn2);
+          const float2 mbn = mul2(p2(mc), mt), vbn = mul2(p2(nc), vt);
+          const float2 gbn = fma2(p2(1.f - mc), mt, mul2(mul2(p2(2.f * (1.f - nc)), G), vt));
+          mb[t] = mbn.x;
+          mb[t + 1] = mbn.y;
+          vb[t] = vbn.x;
+          vb[t + 1] = vbn.y;
+          gb[t] = gbn.x;
+          gb[t + 1] = gbn.y;
         }
         if (jm >= 1) {
           mbp[0] = make_float4(mb[0], mb[1], mb[2], mb[3]);
@@ -523,10 +534,10 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       tc_fence_before();
       mbar_arrive_warp(&bars->s_full);
       float* red = reinterpret_cast<float*>(sm + B1_RED);
-      pda = warp_sum(pda);
-      pdb = warp_sum(pdb);
-      pdm = warp_sum(pdm);
-      pdn = warp_sum(pdn);
+      const float pda = warp_sum(pda2.x + pda2.y);
+      const float pdb = warp_sum(pdb2.x + pdb2.y);
+      const float pdm = warp_sum(pdm2.x + pdm2.y);
+      const float pdn = warp_sum(pdn2.x + pdn2.y);
       if (lane == 0) {
         red[warp * 4 + 0] = pda;
         red[warp * 4 + 1] = pdb;

@@ -374,15 +374,23 @@ chunk_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           *slab_bf16(args.G_hist, mj, half, g8, c) = pack8(g);
           *slab_bf16(args.Mp_hist, mj, half, g8, c) = pack8(mv);
           *slab_bf16(args.Vp_hist, mj, half, g8, c) = pack8(vv);
+          // element pairs on the packed fp32x2 instructions, SFU square root
+          // and reciprocal (the update is on the chain; tc.cuh)
 #pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            const float m1 = fmaf(mc, mv[t], (1.f - mc) * g[t]);
-            const float v1 = fmaf(nc, vv[t], (1.f - nc) * (g[t] * g[t]));
-            mv[t] = m1;
-            vv[t] = v1;
-            // SFU square root and reciprocal (the update is on the chain; tc.cuh)
-            st[8 * g8 + t] =
-                fmaf(a, st[8 * g8 + t], b * m1 * rcp_sfu(sqrt_sfu(v1) + kEpsAdam));
+          for (int t = 0; t < 8; t += 2) {
+            const float2 G = p2(g[t], g[t + 1]);
+            const float2 m1 = fma2(p2(mc), p2(mv[t], mv[t + 1]), mul2(p2(1.f - mc), G));
+            const float2 v1 = fma2(p2(nc), p2(vv[t], vv[t + 1]), mul2(p2(1.f - nc), mul2(G, G)));
+            mv[t] = m1.x;
+            mv[t + 1] = m1.y;
+            vv[t] = v1.x;
+            vv[t + 1] = v1.y;
+            const float2 rden = p2(rcp_sfu(sqrt_sfu(v1.x) + kEpsAdam),
+                                   rcp_sfu(sqrt_sfu(v1.y) + kEpsAdam));
+            const float2 sn = fma2(p2(a), p2(st[8 * g8 + t], st[8 * g8 + t + 1]),
+                                   mul2(mul2(p2(b), m1), rden));
+            st[8 * g8 + t] = sn.x;
+            st[8 * g8 + t + 1] = sn.y;
           }
           if (j + 1 < N) {
             mp[0] = make_float4(mv[0], mv[1], mv[2], mv[3]);

@@ -442,6 +442,17 @@ __device__ __forceinline__ uint32_t sw128_elem(int row, int col) {
 __device__ __forceinline__ float sqrt_sfu(float x) { return x > 0.f ? x * rsqrtf(x) : 0.f; }
 __device__ __forceinline__ float rcp_sfu(float x) { return __fdividef(1.f, x); }
 
+// Element pairs on sm_100's packed fp32x2 FMA / multiply / add: one
+// instruction for two elements, each rounded exactly as the scalar one.
+__device__ __forceinline__ float2 p2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 p2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {   // a - b, exact as a subtraction
+  return __ffma2_rn(b, make_float2(-1.f, -1.f), a);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
