@@ -11,8 +11,11 @@
 //   x_hat = x rstd,  g = dy w,  dx = (g - x_hat <x_hat, g> / dh) rstd,
 //   dw = sum over rows of dy x_hat.
 //
-// Both kernels stream HBM once: one warp per (b, h, t) row, dh / 32 elements
-// per lane, the input row read contiguously from o (B, H, T, dh) and the
+// Both kernels stream HBM once.  The wide kernels (below) give a lane 16
+// bytes of a row and a warp several consecutive rows a step; the kernels
+// described next (one warp per (b, h, t) row, dh / 32 elements per lane) take
+// a bf16-in, fp32-out backward.  The input row is read contiguously from
+// o (B, H, T, dh) and the
 // output row written contiguously at (b, t, h * dh) of y (B, T, H * dh), so
 // the head transpose costs nothing.  dw is reduced per block in shared memory
 // and added with one atomic per column per block.  A warp walks rows r, r +
@@ -313,6 +316,225 @@ head_rmsnorm_bwd_ring_kernel(const TI* __restrict__ o, const float* __restrict__
   }
 }
 
+// Wide rows: a lane holds 16 bytes of a row of o (VEC = 8 bf16 or 4 fp32
+// elements), so a warp step covers RPW = 32 * VEC / dh consecutive rows (2 at
+// bf16 dh 128, 4 at dh 64) and the per-row work that does not grow with dh
+// (the ring's copy issue and wait, the loop, the shuffle reduction over the
+// LPR lanes of a row) is shared by RPW rows.  Each warp walks one contiguous
+// run of rows (b, h, t), t advancing by RPW a step, so the output row's
+// (b, t, h) place comes from a cursor instead of two divisions a row.  The
+// channel arithmetic runs on element pairs (packed fp32x2 instructions).
+template <int D, typename TI>
+struct WideE {
+  static constexpr int VEC = 16 / static_cast<int>(sizeof(TI));
+  static constexpr int NP = VEC / 2;
+  static constexpr int LPR = D / VEC;   // lanes a row
+  static constexpr int RPW = 32 / LPR;  // rows a warp step
+  static_assert(LPR >= 1 && LPR <= 32 && 32 % LPR == 0, "row width");
+};
+
+template <int LPR>
+__device__ __forceinline__ float row_sum(float v) {
+#pragma unroll
+  for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+
+// VEC elements of T at p, in one or two 16-byte accesses
+template <int VEC, typename T>
+__device__ __forceinline__ void store_n(T* p, const float* x) {
+  if constexpr (VEC * sizeof(T) <= 16) {
+    Vec<VEC, T>::store(p, x);
+  } else {
+    Vec<VEC / 2, T>::store(p, x);
+    Vec<VEC / 2, T>::store(p + VEC / 2, x + VEC / 2);
+  }
+}
+// the lane's row of step m: (bh, t) cursor, advanced by RPW rows a step
+struct RowCursor {
+  int bh, t, b, h;
+  __device__ __forceinline__ void init(int r, int T, int H) {
+    bh = r / T;
+    t = r - bh * T;
+    b = bh / H;
+    h = bh - b * H;
+  }
+  __device__ __forceinline__ void advance(int by, int T, int H) {
+    t += by;
+    while (t >= T) {   // rare: the run crosses into the next (b, h)
+      t -= T;
+      if (++h == H) {
+        h = 0;
+        ++b;
+      }
+    }
+  }
+};
+
+template <int D, typename TI, typename TO>
+__global__ void __launch_bounds__(kWarps * 32)
+head_rmsnorm_fwd_wide_kernel(const TI* __restrict__ o, const float* __restrict__ w,
+                             TO* __restrict__ y, int H, int T, float eps, int rows, int per) {
+  using W = WideE<D, TI>;
+  constexpr int VEC = W::VEC, NP = W::NP, LPR = W::LPR, RPW = W::RPW;
+  __shared__ __align__(16) uint8_t ring[kWarps][kRingF][32 * 16];
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
+  const int gw = blockIdx.x * kWarps + wl;
+  const int r0 = gw * per;   // this warp's rows: r0 .. r1 - 1 (per is a multiple of RPW)
+  if (r0 >= rows) return;
+  const int r1 = min(r0 + per, rows);
+  const int sub = lane / LPR, col = (lane % LPR) * VEC;
+  float2 wr[NP];
+#pragma unroll
+  for (int c = 0; c < NP; ++c) wr[c] = f2(w[col + 2 * c], w[col + 2 * c + 1]);
+  const int n = (r1 - r0 + RPW - 1) / RPW;
+  auto slot = [&](int m) { return &ring[wl][m % kRingF][lane * 16]; };
+  auto issue = [&](int m) {
+    const int r = r0 + m * RPW + sub;
+    if (m < n && r < r1) cp_async_cg16(slot(m), o + static_cast<size_t>(r) * D + col);
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int m = 0; m < kRingF - 1; ++m) issue(m);
+  RowCursor cur;
+  cur.init(r0 + sub, T, H);
+  for (int m = 0; m < n; ++m) {
+    issue(m + kRingF - 1);
+    cp_async_wait<kRingF - 1>();
+    float x[VEC];
+    Vec<VEC, TI>::load(reinterpret_cast<const TI*>(slot(m)), x);
+    float2 ss2 = f2(0.f);
+#pragma unroll
+    for (int c = 0; c < NP; ++c) {
+      const float2 xc = f2(x[2 * c], x[2 * c + 1]);
+      ss2 = fma2(xc, xc, ss2);
+    }
+    const float2 rs = f2(rsqrtf(row_sum<LPR>(ss2.x + ss2.y) * (1.f / D) + eps));
+    float out[VEC];
+#pragma unroll
+    for (int c = 0; c < NP; ++c) {
+      const float2 v = mul2(mul2(f2(x[2 * c], x[2 * c + 1]), rs), wr[c]);
+      out[2 * c] = to_f(from_f<TI>(v.x));   // input dtype
+      out[2 * c + 1] = to_f(from_f<TI>(v.y));
+    }
+    if (r0 + m * RPW + sub < r1)
+      store_n<VEC, TO>(y + ((static_cast<size_t>(cur.b) * T + cur.t) * H + cur.h) * D + col, out);
+    cur.advance(RPW, T, H);
+  }
+  cp_async_wait<0>();
+}
+
+template <int D, typename TI, typename TO>
+__global__ void __launch_bounds__(kWarps * 32)
+head_rmsnorm_bwd_wide_kernel(const TI* __restrict__ o, const float* __restrict__ w,
+                             const TO* __restrict__ dy, TI* __restrict__ d_o,
+                             float* __restrict__ dw, int H, int T, float eps, int rows, int per) {
+  using W = WideE<D, TI>;
+  constexpr int VEC = W::VEC, NP = W::NP, LPR = W::LPR, RPW = W::RPW;
+  constexpr int VBO = VEC * static_cast<int>(sizeof(TO));
+  static_assert(VBO == 4 || VBO == 8 || VBO == 16, "cotangent slice");
+  __shared__ __align__(16) uint8_t ring_o[kWarps][kRingB][32 * 16];
+  __shared__ __align__(16) uint8_t ring_g[kWarps][kRingB][32 * VBO];
+  __shared__ float red[kWarps][D];
+  const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
+  const int gw = blockIdx.x * kWarps + wl;
+  const int r0 = gw * per;
+  const int r1 = min(r0 + per, rows);
+  const int sub = lane / LPR, col = (lane % LPR) * VEC;
+  float2 wr[NP], acc[NP];
+#pragma unroll
+  for (int c = 0; c < NP; ++c) {
+    wr[c] = f2(w[col + 2 * c], w[col + 2 * c + 1]);
+    acc[c] = f2(0.f);
+  }
+  if (r0 < rows) {
+    const int n = (r1 - r0 + RPW - 1) / RPW;
+    RowCursor ic;   // the cursor of the row being issued (kRingB - 1 steps ahead)
+    ic.init(r0 + sub, T, H);
+    auto issue = [&](int m) {
+      const int r = r0 + m * RPW + sub;
+      if (m < n && r < r1) {
+        cp_async_cg16(&ring_o[wl][m % kRingB][lane * 16], o + static_cast<size_t>(r) * D + col);
+        cp_async<VBO>(&ring_g[wl][m % kRingB][lane * VBO],
+                      dy + ((static_cast<size_t>(ic.b) * T + ic.t) * H + ic.h) * D + col);
+      }
+      cp_async_commit();
+      ic.advance(RPW, T, H);
+    };
+#pragma unroll
+    for (int m = 0; m < kRingB - 1; ++m) issue(m);
+    for (int m = 0; m < n; ++m) {
+      issue(m + kRingB - 1);
+      cp_async_wait<kRingB - 1>();
+      float x[VEC], g[VEC];
+      Vec<VEC, TI>::load(reinterpret_cast<const TI*>(&ring_o[wl][m % kRingB][lane * 16]), x);
+      Vec<VEC, TO>::load(reinterpret_cast<const TO*>(&ring_g[wl][m % kRingB][lane * VBO]), g);
+      const bool valid = r0 + m * RPW + sub < r1;
+      if (!valid) {   // a row past the run: its slots were never filled
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) x[v] = g[v] = 0.f;
+      }
+      float2 ss2 = f2(0.f);
+#pragma unroll
+      for (int c = 0; c < NP; ++c) {
+        const float2 xc = f2(x[2 * c], x[2 * c + 1]);
+        ss2 = fma2(xc, xc, ss2);
+      }
+      const float rs1 = rsqrtf(row_sum<LPR>(ss2.x + ss2.y) * (1.f / D) + eps);
+      const float2 rs = f2(rs1);
+      float2 xh[NP], gw2[NP], dot2 = f2(0.f);
+#pragma unroll
+      for (int c = 0; c < NP; ++c) {
+        // the cotangent in the input dtype
+        const float2 gc = f2(to_f(from_f<TI>(g[2 * c])), to_f(from_f<TI>(g[2 * c + 1])));
+        xh[c] = mul2(f2(x[2 * c], x[2 * c + 1]), rs);   // x_hat
+        acc[c] = fma2(gc, xh[c], acc[c]);
+        gw2[c] = mul2(gc, wr[c]);                      // dL/dx_hat
+        dot2 = fma2(xh[c], gw2[c], dot2);
+      }
+      const float2 dt = f2(row_sum<LPR>(dot2.x + dot2.y) * (1.f / D));
+      float dx[VEC];
+#pragma unroll
+      for (int c = 0; c < NP; ++c) {
+        const float2 d = mul2(fma2(xh[c], f2(-dt.x), gw2[c]), rs);
+        dx[2 * c] = d.x;
+        dx[2 * c + 1] = d.y;
+      }
+      if (valid) Vec<VEC, TI>::store(d_o + static_cast<size_t>(r0 + m * RPW + sub) * D + col, dx);
+    }
+    cp_async_wait<0>();
+  }
+  // dw: the RPW lanes of a column first, then the block's warps
+#pragma unroll
+  for (int c = 0; c < NP; ++c) {
+#pragma unroll
+    for (int off = LPR; off < 32; off <<= 1) {
+      acc[c].x += __shfl_xor_sync(0xffffffffu, acc[c].x, off);
+      acc[c].y += __shfl_xor_sync(0xffffffffu, acc[c].y, off);
+    }
+  }
+  if (sub == 0) {
+#pragma unroll
+    for (int c = 0; c < NP; ++c) {
+      red[wl][col + 2 * c] = acc[c].x;
+      red[wl][col + 2 * c + 1] = acc[c].y;
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += kWarps * 32) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < kWarps; ++k) s += red[k][c];
+    atomicAdd(dw + c, s);
+  }
+}
+
+int wide_grid(int sms) { return sms * 8; }   // 64 warps an SM
+
 int grid_for(long long rows) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess)
@@ -322,10 +544,34 @@ int grid_for(long long rows) {
   return static_cast<int>(want < cap ? (want > 0 ? want : 1) : cap);
 }
 
+int sm_count() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+// rows a warp of the wide kernels walks: all rows over the grid's warps, a
+// multiple of RPW
+int wide_per(long long rows, int grid, int rpw) {
+  const long long warps = static_cast<long long>(grid) * kWarps;
+  long long per = (rows + warps - 1) / warps;
+  per = (per + rpw - 1) / rpw * rpw;
+  return static_cast<int>(per > 0 ? per : rpw);
+}
+
 template <int VEC, typename TI, typename TO>
 cudaError_t fwd_typed(const void* o, const float* w, void* y, int B, int H, int T, float eps,
                       cudaStream_t st) {
   const long long rows = static_cast<long long>(B) * H * T;
+  constexpr int D = VEC * 32;
+  if constexpr (D / (16 / sizeof(TI)) <= 32) {
+    const int grid = wide_grid(sm_count());
+    head_rmsnorm_fwd_wide_kernel<D, TI, TO><<<grid, kWarps * 32, 0, st>>>(
+        static_cast<const TI*>(o), w, static_cast<TO*>(y), H, T, eps, static_cast<int>(rows),
+        wide_per(rows, grid, WideE<D, TI>::RPW));
+    return cudaGetLastError();
+  }
   if constexpr (VEC * sizeof(TI) >= 4)
     head_rmsnorm_fwd_ring_kernel<VEC, TI, TO><<<grid_for(rows), kWarps * 32, 0, st>>>(
         static_cast<const TI*>(o), w, static_cast<TO*>(y), H, T, eps, rows);
@@ -339,6 +585,14 @@ template <int VEC, typename TI, typename TO>
 cudaError_t bwd_typed(const void* o, const float* w, const void* dy, void* d_o, float* dw, int B,
                       int H, int T, float eps, cudaStream_t st) {
   const long long rows = static_cast<long long>(B) * H * T;
+  constexpr int D = VEC * 32;
+  if constexpr (D / (16 / sizeof(TI)) <= 32 && sizeof(TO) <= sizeof(TI)) {
+    const int grid = wide_grid(sm_count());
+    head_rmsnorm_bwd_wide_kernel<D, TI, TO><<<grid, kWarps * 32, 0, st>>>(
+        static_cast<const TI*>(o), w, static_cast<const TO*>(dy), static_cast<TI*>(d_o), dw, H,
+        T, eps, static_cast<int>(rows), wide_per(rows, grid, WideE<D, TI>::RPW));
+    return cudaGetLastError();
+  }
   if constexpr (VEC * sizeof(TI) >= 4 && VEC * sizeof(TO) >= 4)
     head_rmsnorm_bwd_ring_kernel<VEC, TI, TO><<<grid_for(rows), kWarps * 32, 0, st>>>(
         static_cast<const TI*>(o), w, static_cast<const TO*>(dy), static_cast<TI*>(d_o), dw, H,

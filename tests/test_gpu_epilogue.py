@@ -48,6 +48,12 @@ def _oracle(o, w, dy, out_dtype):
     (1, 2, 33, 64, torch.float32, torch.float32),
     (1, 2, 17, 32, torch.bfloat16, torch.bfloat16),
     (1, 4, 4096, 128, torch.bfloat16, torch.bfloat16),   # many blocks, grid-stride rows
+    # wide rows (several rows a warp step): runs crossing (b, h), odd row counts, T < rows a step
+    (3, 5, 1, 32, torch.bfloat16, torch.bfloat16),        # T 1: every step crosses heads
+    (2, 3, 7, 64, torch.bfloat16, torch.bfloat16),
+    (1, 3, 3001, 64, torch.float32, torch.bfloat16),
+    (2, 2, 999, 128, torch.bfloat16, torch.float32),
+    (8, 16, 512, 128, torch.bfloat16, torch.bfloat16),    # 65,536 rows over the whole grid
 ])
 def test_head_rmsnorm_matches_oracle(B, H, T, dh, in_dt, out_dt):
     pkg = load_pkg()
@@ -61,7 +67,8 @@ def test_head_rmsnorm_matches_oracle(B, H, T, dh, in_dt, out_dt):
     assert y.dtype == ry.dtype and y.shape == ry.shape
     assert d_o.dtype == in_dt and dw.dtype == torch.float32
     tol = _tol(in_dt)
-    assert _rel(y, ry) <= tol, f"y {_rel(y, ry):.3e}"
+    # y is rounded to the output dtype last: a bf16 output is held to the bf16 bound
+    assert _rel(y, ry) <= max(tol, _tol(out_dt)), f"y {_rel(y, ry):.3e}"
     assert _rel(d_o, rdo) <= tol, f"d_o {_rel(d_o, rdo):.3e}"
     assert _rel(dw, rdw) <= max(tol, 1e-4), f"dweight {_rel(dw, rdw):.3e}"
 
