@@ -85,7 +85,11 @@ def kernel_work(name: str, cfg: dict) -> tuple[str, float, float]:
                           (3 C d 2), every gate of the rule in and its cotangent out
                           (2 n_g C 4; n_g = 2 delta, 3 muon, 4 adam) = 115,712 B for delta.
                           The S_j and Gb_j histories it also reads by design (2 d^2 2, muon
-                          + Gb_j lo d^2 2) are reported apart as design bytes.
+                          + Gb_j lo d^2 2) are reported apart as design bytes.  Where the
+                          delta backward is fused (cfg["n_fused"] > 0 tiles done beside the
+                          chains), this launch does the other tiles only.
+      chunk_bwd_fused_tc  bytes: the chains' inputs (q, k, dO 3 C d 2 and the gates n_g C 4
+                          per chunk-head) and the token bytes of its n_fused tiles.
     Newton-Schulz counts the algorithmic products once (the kernels spend three
     split-bf16 MMAs on each).  The exact-fp32 kernels count their products.
     """
@@ -110,9 +114,11 @@ def kernel_work(name: str, cfg: dict) -> tuple[str, float, float]:
     }
     n_g = {0: 2, 1: 3, 2: 4}[cfg["rule"]]
     bw2 = 7 * C * d * 2 + 2 * n_g * C * 4
-    nbytes = {"chunk_bwd2_tc": bw2}
-    if name in nbytes:
-        return "hbm", float(nbytes[name] * units), 0.0
+    nf = int(cfg.get("n_fused", 0) or 0)
+    if name == "chunk_bwd2_tc":
+        return "hbm", float(bw2 * (units - nf)), 0.0
+    if name == "chunk_bwd_fused_tc":
+        return "hbm", float(bw2 * nf + (3 * C * d * 2 + n_g * C * 4) * units), 0.0
     if name in flops:
         f16, f32 = flops[name]
         return "tensor", float(f16 * units), float(f32 * units)
@@ -127,7 +133,8 @@ def design_bytes(name: str, cfg: dict) -> float | None:
         return None
     B, H, T, d, C = cfg["B"], cfg["H"], cfg["T"], cfg["dh"], cfg["chunk"]
     per = 2 * d * d * 2 + (d * d * 2 if cfg["rule"] == 1 else 0)
-    return float(kernel_work(name, cfg)[1] + per * B * H * (T // C))
+    nf = int(cfg.get("n_fused", 0) or 0)
+    return float(kernel_work(name, cfg)[1] + per * (B * H * (T // C) - nf))
 
 
 def step_work(cfg: dict) -> tuple[float, float, float]:
@@ -715,6 +722,7 @@ def time_config(pkg, L, name: str, prec: int, steps: int, warmup: int, peaks: di
     against the survey's roofline."""
     cfg = dict(CONFIGS[name])
     B, H, T, dh, C, rule, ns = (cfg[k] for k in ("B", "H", "T", "dh", "chunk", "rule", "ns"))
+    cfg["n_fused"] = L.chunk_bwd_fused_tiles(B, H, T, dh, C, rule, prec)
     dev = pkg.workloads.mixer_inputs(B, H, T, dh, rule, C, seed=0).to("cuda", torch.bfloat16)
     leaves = [dev.q, dev.k, dev.v, dev.alpha, dev.beta, dev.mu] + ([dev.nu] if rule == 2 else [])
     for t in leaves:
@@ -829,6 +837,8 @@ def main():
         start, end = pkg.sharding.shard_bh(B * H, rank, world)
         B, H = 1, end - start
         cfg["B"], cfg["H"] = B, H
+    # delta with fewer sequences than SMs: tiles the fused backward does beside its chains
+    cfg["n_fused"] = L.chunk_bwd_fused_tiles(B, H, T, dh, C, rule, prec)
     host = pkg.workloads.mixer_inputs(B, H, T, dh, rule, C, seed=rank)
     dev = host.to(device, torch.bfloat16)
     leaves = [dev.q, dev.k, dev.v, dev.alpha, dev.beta, dev.mu] + ([dev.nu] if rule == 2 else [])
@@ -1095,6 +1105,9 @@ def main():
                        "against a plain step)") if gerr is None else f"plain steps ({gerr})",
             "kernel_times": kernel_times, "per_rank": per_rank, "other_scaling": other,
             "other_configs": other_configs,
+            # rank 0's backward: token-gradient tiles done beside the chains in the fused
+            # launch (chunk_bwd_fused_tc), of all its chunk-heads
+            "backward_split": {"fused_tiles": cfg["n_fused"], "tiles": B * H * (T // C)},
         }
         print(json.dumps(line), flush=True)
     if dist is not None:

@@ -39,6 +39,8 @@ lib.gmdn_last_error_string.restype = ctypes.c_char_p
 lib.gmdn_last_error_string.argtypes = []
 lib.gmdn_kernel_launches.restype = ctypes.c_uint64
 lib.gmdn_kernel_launches.argtypes = []
+lib.gmdn_chunk_bwd_fused_tiles.restype = _i
+lib.gmdn_chunk_bwd_fused_tiles.argtypes = [_i] * 8
 lib.gmdn_selftest_wait_timeout.restype = _i
 lib.gmdn_selftest_wait_timeout.argtypes = [_p, ctypes.c_uint64, _p]
 lib.gmdn_prof_enable.restype = None
@@ -95,6 +97,14 @@ def check(rc: int, what: str) -> None:
 
 def kernel_launches() -> int:
     return int(lib.gmdn_kernel_launches())
+
+
+def chunk_bwd_fused_tiles(B: int, H: int, T: int, dh: int, chunk: int, rule: int,
+                          precision: int, io_f32: bool = False) -> int:
+    """Tiles (chunk-heads) whose token gradients the fused delta backward
+    computes beside its reverse chains; 0 where the backward is the two plain
+    launches."""
+    return int(lib.gmdn_chunk_bwd_fused_tiles(B, H, T, dh, chunk, rule, precision, int(io_f32)))
 
 
 def prof_enable(on: bool) -> None:

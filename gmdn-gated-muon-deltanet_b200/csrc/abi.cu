@@ -133,6 +133,7 @@ ChunkBufs carve_chunk(void* saved, void* ws, int BH, int N, int dh, int rule, in
     b.saved_bytes = cs.used;
     b.tc.Gbar_hist = half_mats(cw);
     if (rule == 1) b.tc.Gbar_lo_hist = half_mats(cw);
+    if (rule == 0) b.tc.progress = reinterpret_cast<uint32_t*>(cw.take(BH));
     if (rule != 0) {
       b.tc.M_ws = cw.take(mats(BH, dh));
       if (rule == 2) b.tc.V_ws = cw.take(mats(BH, dh));
@@ -248,6 +249,23 @@ int gmdn_abi_version(void) { return 1; }
 const char* gmdn_last_error_string(void) { return g_last_error.c_str(); }
 
 uint64_t gmdn_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int gmdn_chunk_bwd_fused_tiles(int B, int H, int T, int dh, int chunk, int rule, int precision,
+                               int io_f32) {
+  g_last_error.clear();
+  if (B <= 0 || H <= 0 || chunk <= 0 || T <= 0 || T % chunk) return 0;
+  const int N = T / chunk;
+  if (!chunk_fast(dh, chunk, rule, precision, io_f32, N)) return 0;
+  gmdn::ChunkArgs p{};
+  p.BH = B * H;
+  p.T = T;
+  p.N = N;
+  p.C = chunk;
+  p.dh = dh;
+  p.rule = rule;
+  p.io_f32 = io_f32 != 0;
+  return gmdn::chunk_bwd_fused_tiles(p);
+}
 
 int gmdn_selftest_wait_timeout(uint32_t* status, uint64_t limit_ns, void* stream) {
   g_last_error.clear();
@@ -611,6 +629,13 @@ int gmdn_chunk_bwd_ex(const void* q, const void* k, const void* v, const float* 
   cudaError_t e = cudaMemsetAsync(bufs.status, 0, sizeof(uint32_t), st);
   if (e != cudaSuccess) return cuda_fail(e, "status reset");
   if (fast) {
+    const int n_fused = rule == 0 ? gmdn::chunk_bwd_fused_tiles(p) : 0;
+    if (n_fused > 0) {
+      GMDN_LAUNCH(gmdn::chunk_bwd_fused_tc(p, bufs.tc, n_fused, st), "chunk_bwd_fused_tc");
+      if (n_fused < p.BH * p.N)
+        GMDN_LAUNCH(gmdn::chunk_bwd2_tc(p, bufs.tc, st, n_fused), "chunk_bwd2_tc");
+      return GMDN_OK;
+    }
     if (rule == 1)
       GMDN_LAUNCH(gmdn::chunk_bwd1_muon_tc(p, bufs.tc, ns, st), "chunk_bwd1_muon_tc");
     else

@@ -65,6 +65,7 @@ struct BwArgs {
   uint16_t *dq, *dk, *dv;
   float *dalpha, *dbeta, *dmu, *dnu;
   uint32_t* status;
+  uint32_t* progress;   // fused backward: per (b, h), chunks (from the last) whose Gb_j is stored
   int N, T;
   int tiles;      // bw2: B * H * N
   int store_hi;   // dh 128: store the upper 64 columns of dq, dk, dv (dh 64: zero padding)
@@ -73,6 +74,15 @@ struct BwArgs {
 // ===========================================================================
 // bw1: reverse chain
 // ===========================================================================
+
+// Fused backward: the chain publishes the Gb_j it has stored kPubLag steps
+// after the store (waiting on the store's completion) and every kPubEvery
+// steps: each publication is a proxy fence and a gpu-scope release on the
+// chain's storing thread, ~0.6 us of the chain's time (publishing every step
+// took the chains of 64 sequences from 0.18 to 0.22 ms; every 4 or 8 steps
+// measured best).
+constexpr int kPubLag = 1;
+constexpr int kPubEvery = 8;
 
 constexpr int kThreads1 = 448;  // warps 0-7 state, 8-11 chunk-local, 12 TMA + P, Z, 13 chain MMAs
 // adam adds warp 14, which streams the forward's G, M, V history into a ring,
@@ -140,11 +150,14 @@ struct Bars1 {
 };
 static_assert(sizeof(Bars1) <= 512, "barrier block");
 
-template <int RULE>
-__global__ void __launch_bounds__(kThreads1R<RULE>, 1)
-chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_sb,
-                    const __grid_constant__ CUtensorMap tm_sh, BwArgs args) {
+// The reverse chain of sequence bh.  kPub (the fused backward, below): after
+// each Gb_j store has completed, publish in args.progress[bh] how many chunks,
+// counted from the last, have their Gb_j in memory (one step behind the
+// stores, so the storing thread never waits on the one it just issued).
+template <int RULE, bool kPub>
+__device__ __forceinline__ void bw1_body(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                                         const CUtensorMap& tm_g, const CUtensorMap& tm_sb,
+                                         const CUtensorMap& tm_sh, const BwArgs& args, int bh) {
   using Lay = L1<RULE>;
   constexpr int kStages1 = Lay::kSt;
   constexpr uint32_t B1_Q = Lay::Q, B1_K = Lay::K, B1_G = Lay::G, B1_AS = Lay::AS, B1_SS = Lay::SS,
@@ -159,7 +172,6 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   float* gate_nu = gate_beta + 3 * kStages1 * 64;   // adam
   volatile int* ab = &bars->abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.x;
   const int N = args.N;
   uint32_t* status = args.status;
 
@@ -628,6 +640,16 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
             tma_store_2d(&tm_sb, 0, srow, sm + B1_SS);
             tma_store_2d(&tm_sb, 64, srow, sm + B1_SS + P128);
             bulk_commit();
+            if constexpr (kPub) {
+              // kPubLag steps behind: the stores of steps 1 .. i-kPubLag (chunks
+              // N-2 .. N-1-i+kPubLag) are complete, and row N-1 was written before
+              // the state warps' barriers above
+              if (i >= kPubLag && i % kPubEvery == 0) {
+                bulk_wait_n<kPubLag>();
+                fence_proxy_async_global();
+                st_release_gpu(args.progress + bh, static_cast<uint32_t>(i + 1 - kPubLag));
+              }
+            }
           }
         }
       }
@@ -694,7 +716,18 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     }
     // shared memory must outlive the reads of the bulk stores; grid completion
     // makes their global writes visible to the next kernel
-    if (threadIdx.x == 0) bulk_wait_read0();
+    if (threadIdx.x == 0) {
+      if constexpr (kPub) {
+        bulk_wait0();
+        if (!*ab) {   // every Gb_j stored (an aborted chain publishes nothing more, so
+                      // its readers give up on their bounded waits)
+          fence_proxy_async_global();
+          st_release_gpu(args.progress + bh, static_cast<uint32_t>(N));
+        }
+      } else {
+        bulk_wait_read0();
+      }
+    }
   } else {
     // ------------------------------------------------------------ chunk-local (warps 8-11)
     const int sp = warp - 8;
@@ -780,6 +813,14 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   }
 }
 
+template <int RULE>
+__global__ void __launch_bounds__(kThreads1R<RULE>, 1)
+chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_sb,
+                    const __grid_constant__ CUtensorMap tm_sh, BwArgs args) {
+  bw1_body<RULE, false>(tm_q, tm_k, tm_g, tm_sb, tm_sh, args, static_cast<int>(blockIdx.x));
+}
+
 // ===========================================================================
 // bw2: token and gate gradients of one chunk
 // ===========================================================================
@@ -791,6 +832,15 @@ chunk_bwd1_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
 // paired two per TMEM column range (lanes 0-15 / 16-31).
 
 constexpr int kThreads2 = 320;
+// The fused backward runs where at least this many SMs are left beside the
+// chains.  Measured (delta, T 4096, steps of one B200): 16, 32 and 64
+// sequences 0.358 / 0.371 / 0.462 ms against 0.394 / 0.438 / 0.516 ms with
+// the two plain launches; at 128 sequences (20 spare SMs) the fused launch
+// was 3 % slower (the chains' publications cost more than 20 SMs return).
+constexpr int kFusedMinWorkers = 32;
+// a worker's share: kFusedNum / kFusedDen tiles per chain step (the best of
+// 0.3 ... 0.6 at 64 sequences; larger shares outlast the chains)
+constexpr int kFusedNum = 3, kFusedDen = 10;
 // Muon token weights w_s = prod_{t>s} mu_t can underflow; A' = A / w uses
 // max(w, kMuonWFloor), and the drain multiplies by the same value, so dE is
 // exact up to (w_eff - w) k Gb^T, below 1e-28 |k Gb^T|.
@@ -846,14 +896,29 @@ static_assert(sizeof(Bars2) <= 256, "barrier block");
 // w * k (w_s = prod_{t>s} mu_t can underflow, so beta / w is no option).
 // dbeta: delta takes it whole as the row product <E_s, dE_s / beta_s>; muon
 // and adam reduce the column sums of tril(dA) * P across lanes with shuffles.
+// Which tiles a bw2 CTA takes: entries e0 + w, e0 + w + W, ... below e1, w
+// the CTA's index among the W workers (CTAs from worker0 on).  order 0: entry
+// = tile (bh * N + j); order 1: the order in which the reverse chains finish
+// Gb_j (chunk N-1 of every sequence, then N-2, ...).  progress (fused
+// backward): a worker waits until the chain of a tile's sequence has
+// published its Gb_j before loading it.
+struct Sched2 {
+  int e0, e1, worker0, BH, N, order;
+  const uint32_t* progress;
+  __device__ __forceinline__ int tile(int e) const {
+    if (!order) return e;
+    const int r = e / BH;   // r-th chunk from the last
+    return (e - r * BH) * N + (N - 1 - r);
+  }
+};
+
 template <int RULE>
-__global__ void __launch_bounds__(kThreads2, 1)
-chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
-                    const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_sb,
-                    const __grid_constant__ CUtensorMap tm_sbl,
-                    const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dk,
-                    const __grid_constant__ CUtensorMap tm_dv, BwArgs args) {
+__device__ __forceinline__ void bw2_body(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
+                                         const CUtensorMap& tm_v, const CUtensorMap& tm_g,
+                                         const CUtensorMap& tm_s, const CUtensorMap& tm_sb,
+                                         const CUtensorMap& tm_sbl, const CUtensorMap& tm_dq,
+                                         const CUtensorMap& tm_dk, const CUtensorMap& tm_dv,
+                                         const BwArgs& args, const Sched2& sc) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                            ~static_cast<uintptr_t>(1023));
@@ -876,8 +941,11 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
   auto d_tm = [&](int i) { return T2_D0 + static_cast<uint32_t>(i & 1) * 128u; };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int N = args.N;
-  const int tiles = args.tiles;
-  const int G = gridDim.x;
+  // this CTA's entries: ew, ew + G, ... below `tiles` (tile_at maps them to tiles)
+  const int tiles = sc.e1;
+  const int G = static_cast<int>(gridDim.x) - sc.worker0;
+  const int ew = sc.e0 + static_cast<int>(blockIdx.x) - sc.worker0;
+  auto tile_at = [&](int e) { return sc.tile(e); };
   uint32_t* status = args.status;
   // gate buffer of local tile i: beta, alpha, mu, w
   auto gates = [&](int i) { return gate0 + (i & 1) * 256; };
@@ -909,7 +977,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     bars->da[0] = bars->da[1] = 0.f;
     fence_mbar_init();
   }
-  build_identity64(sm + B2_I, threadIdx.x, kThreads2);
+  build_identity64(sm + B2_I, threadIdx.x, blockDim.x);
   if (warp == 8) {
     tmem_alloc(&bars->tmem_base, 512);
     tmem_relinquish();
@@ -985,51 +1053,78 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       };
       // local tile of a load group in flight, not yet waited on
       int pa = -1, ps = -1, pl = -1, pv = -1, pb[2] = {-1, -1};
-      if (static_cast<int>(blockIdx.x) < tiles) {
+      // fused backward: Gb_j of a tile is loaded only once its chain has published it
+      auto ready = [&](int tile) -> bool {
+        if (!sc.progress) return true;
+        const uint32_t* pr = sc.progress + tile / N;
+        const uint32_t need = static_cast<uint32_t>(N - tile % N);
+        if (ld_acquire_gpu(pr) < need) {
+          const uint64_t t0 = global_ns();
+          while (ld_acquire_gpu(pr) < need) {
+            if (*ab) return false;
+            if (global_ns() - t0 > kWaitLimitNs) {
+              *ab = 1;
+              atomicOr(status, kStatusWaitTimeout);
+              return false;
+            }
+            __nanosleep(200);
+          }
+        }
+        fence_proxy_async_global();   // the TMA loads that follow read what was published
+        return true;
+      };
+      bool started = false;
+      if (ew < tiles) {
+        const int t0 = tile_at(ew);
         if (RULE != 1) {
-          issue_v(blockIdx.x);
+          issue_v(t0);
           pv = 0;
         }
-        issue_a(0, blockIdx.x);
-        issue_b(0, blockIdx.x);
-        issue_sb(0, blockIdx.x);
-        pa = ps = pb[0] = 0;
-        if (kQK == 2 && static_cast<int>(blockIdx.x) + G < tiles) {
-          issue_b(1, blockIdx.x + G);
+        issue_a(0, t0);
+        issue_b(0, t0);
+        pa = pb[0] = 0;
+        if (kQK == 2 && ew + G < tiles) {
+          issue_b(1, tile_at(ew + G));
           pb[1] = 1;
         }
+        if (ready(t0)) {
+          issue_sb(0, t0);
+          ps = 0;
+          started = true;
+        }
         if (RULE == 1) {
-          issue_lo(blockIdx.x);
+          issue_lo(t0);
           pl = 0;
         }
       }
       int i = 0;
-      for (int tile = blockIdx.x; tile < tiles; tile += G, ++i) {
-        const int next = tile + G;
-        if (RULE != 1 && next < tiles) {   // phase 1a has read v: the next tile's
+      for (int e = ew; started && e < tiles; e += G, ++i) {
+        const int ne = e + G;
+        const int next = ne < tiles ? tile_at(ne) : 0;
+        if (RULE != 1 && ne < tiles) {   // phase 1a has read v: the next tile's
           if (!wait_use(&bars->ph1a, i, status, ab)) break;
           issue_v(next);
           pv = i + 1;
         }
-        if (next < tiles) {
+        if (ne < tiles) {
           // dO and Gb_j have been read (Gb_j also by da): the next tile's dO and S_j
           if (!wait_use(&bars->ph2, i, status, ab) || !wait_use(&bars->da_done, i, status, ab)) break;
           issue_a(i + 1, next);
           pa = i + 1;
           // S_j has been read by -dE S: the next tile's Gb_j into its tile
-          if (!wait_use(&bars->s_free, i, status, ab)) break;
+          if (!wait_use(&bars->s_free, i, status, ab) || !ready(next)) break;
           issue_sb(i + 1, next);
           ps = i + 1;
         }
         // q and k have been read (k also by epilogue 2): the q, k of the tile that
         // uses this buffer next
-        const int nb = tile + kQK * G;
-        if (nb < tiles) {
+        const int nbe = e + kQK * G;
+        if (nbe < tiles) {
           if (!wait_use(&bars->ph3, i, status, ab) || !wait_use(&bars->k_free, i, status, ab)) break;
-          issue_b(i + kQK, nb);
+          issue_b(i + kQK, tile_at(nbe));
           pb[qk_buf(i)] = i + kQK;
         }
-        if (RULE == 1 && next < tiles) {
+        if (RULE == 1 && ne < tiles) {
           if (!wait_use(&bars->tail_done, i, status, ab)) break;
           issue_lo(next);
           pl = i + 1;
@@ -1060,7 +1155,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       constexpr uint32_t ID_EK = idesc_bf16(128, 64, false, false, true); // E^T: -S k^T
       constexpr uint32_t ID_DA = idesc_bf16(64, 64, false, true);         // dO E^T
       int i = 0;
-      for (int tile = blockIdx.x; tile < tiles; tile += G, ++i) {
+      for (int e = ew; e < tiles; e += G, ++i) {
         const uint32_t q_s = smem_u32(sm + q_off(i)), k_s = smem_u32(sm + k_off(i));
         const uint32_t s_s = smem_u32(sm + s_off(i)), sb_s = smem_u32(sm + sb_off(i));
         if (RULE == 1 && !wait_use(&bars->ld_a, i, status, ab)) break;
@@ -1172,7 +1267,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       int dummy = 0;
       mbar_wait(&bars->final_mma, 0, status, &dummy);
     }
-  } else {
+  } else if (warp < 8) {
     // ------------------------------------------------------------ epilogue warps 0-7
     const int tid = threadIdx.x;               // 0..255
     const int sp = warp & 3, half = warp >> 2; // subpartition, column half
@@ -1252,7 +1347,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       }
     };
     int i = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += G, ++i) {
+    for (int e = ew; e < tiles; e += G, ++i) {
+      const int tile = tile_at(e);
       const int bh = tile / N, j = tile % N;
       const size_t tok = static_cast<size_t>(bh) * args.T + static_cast<size_t>(j) * kC;
       float* gbeta = gates(i);
@@ -1358,7 +1454,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
       fence_async_smem();
       tc_fence_before();
       mbar_arrive_warp(&bars->ep1);
-      if (i >= 1) gate_stage(i - 1, tile - G);
+      if (i >= 1) gate_stage(i - 1, tile_at(e - G));
       if constexpr (RULE == 0) {
         if (!wait_use_w(&bars->ld_sb, i, status, ab)) break;
         // da = <Sb_{j+1}, S_j> while phase 2 runs (phase 1 is bound by shared-memory
@@ -1562,7 +1658,7 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
         }
       }
     }
-    if (i >= 1 && !*ab) gate_stage(i - 1, static_cast<int>(blockIdx.x) + (i - 1) * G);
+    if (i >= 1 && !*ab) gate_stage(i - 1, tile_at(ew + (i - 1) * G));
     // shared memory must outlive the reads of the bulk stores; grid completion
     // makes their global writes visible to the next kernel
     if (tid == 0) bulk_wait_read0();
@@ -1574,6 +1670,44 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+}
+
+template <int RULE>
+__global__ void __launch_bounds__(kThreads2, 1)
+chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
+                    const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_sb,
+                    const __grid_constant__ CUtensorMap tm_sbl,
+                    const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dk,
+                    const __grid_constant__ CUtensorMap tm_dv, BwArgs args, Sched2 sc) {
+  bw2_body<RULE>(tm_q, tm_k, tm_v, tm_g, tm_s, tm_sb, tm_sbl, tm_dq, tm_dk, tm_dv, args, sc);
+}
+
+// Fused backward (delta): CTAs 0 .. BH-1 run the reverse chains, publishing
+// how far each has stored Gb_j; the other CTAs compute the token gradients of
+// the chunks the chains have finished, in the order they finish, each waiting
+// (bounded) for its tile's Gb_j.  With fewer sequences than SMs the chains
+// leave SMs idle, and this puts the token gradients there while the chains
+// run; a plain bw2 launch takes the tiles left after it.  A cooperative
+// launch: all CTAs are resident at once, so no worker waits on a chain that
+// has not been scheduled.  The chain's maps are the token kernel's q, k, dO,
+// Gb and S maps.
+template <int RULE>
+__global__ void __launch_bounds__(kThreads1R<RULE>, 1)
+chunk_bwd_fused_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
+                          const __grid_constant__ CUtensorMap tm_k,
+                          const __grid_constant__ CUtensorMap tm_v,
+                          const __grid_constant__ CUtensorMap tm_g,
+                          const __grid_constant__ CUtensorMap tm_s,
+                          const __grid_constant__ CUtensorMap tm_sb,
+                          const __grid_constant__ CUtensorMap tm_sbl,
+                          const __grid_constant__ CUtensorMap tm_dq,
+                          const __grid_constant__ CUtensorMap tm_dk,
+                          const __grid_constant__ CUtensorMap tm_dv, BwArgs args, Sched2 sc) {
+  if (static_cast<int>(blockIdx.x) < sc.worker0)
+    bw1_body<RULE, true>(tm_q, tm_k, tm_g, tm_sb, tm_s, args, static_cast<int>(blockIdx.x));
+  else
+    bw2_body<RULE>(tm_q, tm_k, tm_v, tm_g, tm_s, tm_sb, tm_sbl, tm_dq, tm_dk, tm_dv, args, sc);
 }
 
 }  // namespace
@@ -1607,6 +1741,7 @@ BwArgs bw_args(const ChunkArgs& p, const TcBufs& b) {
   a.dmu = p.dmu;
   a.dnu = p.dnu;
   a.status = b.status;
+  a.progress = b.progress;
   a.N = p.N;
   a.T = p.T;
   a.store_hi = p.dh == kD;
@@ -1630,22 +1765,48 @@ cudaError_t launch_bw1(const CUtensorMap& mq, const CUtensorMap& mk, const CUten
   return cudaGetLastError();
 }
 
+cudaError_t sm_count(int* sms) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev);
+  return e;
+}
+
 // bw2 is persistent: one CTA per SM (it needs all of the SM's shared memory)
-// walks the tiles with a stride of the grid size.
+// walks its entries with a stride of the grid size.  first > 0: the entries
+// left by the fused backward (readiness order from `first` on).
 template <int RULE>
-cudaError_t launch_bw2(const CUtensorMap* m, BwArgs a, int tiles, cudaStream_t st) {
+cudaError_t launch_bw2(const CUtensorMap* m, BwArgs a, int BH, int N, int first, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(chunk_bwd2_tc_kernel<RULE>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, B2_SMEM);
   if (e != cudaSuccess) return e;
-  int dev = 0, sms = 0;
-  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
-    return e;
+  int sms = 0;
+  if ((e = sm_count(&sms)) != cudaSuccess) return e;
+  const int tiles = BH * N;
   a.tiles = tiles;
-  const int grid = sms < tiles ? sms : tiles;
+  const Sched2 sc{first, tiles, 0, BH, N, first > 0 ? 1 : 0, nullptr};
+  const int left = tiles - first;
+  if (left <= 0) return cudaSuccess;
+  const int grid = sms < left ? sms : left;
   chunk_bwd2_tc_kernel<RULE><<<grid, kThreads2, B2_SMEM, st>>>(m[0], m[1], m[2], m[3], m[4],
-                                                              m[5], m[6], m[7], m[8], m[9], a);
+                                                              m[5], m[6], m[7], m[8], m[9], a, sc);
   return cudaGetLastError();
+}
+
+// The token maps of bw2 (and the fused backward): q, k, v, dO, S_j, Gb_j,
+// Gb_j lo (muon; else Gb_j again), dq, dk, dv
+cudaError_t bw2_maps(const ChunkArgs& p, const TcBufs& b, CUtensorMap* m) {
+  const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
+  const uint64_t srows = static_cast<uint64_t>(p.BH) * p.N * kD;
+  const void* lo = (p.rule == 1 && b.Gbar_lo_hist) ? b.Gbar_lo_hist : b.Gbar_hist;
+  const void* base[10] = {p.q, p.k, p.v, p.dO, b.S_hist, b.Gbar_hist, lo, p.dq, p.dk, p.dv};
+  for (int i = 0; i < 10; ++i) {
+    const bool hist = i >= 4 && i <= 6;
+    cudaError_t e = make_tmap_rows128(&m[i], base[i], hist ? srows : rows, hist ? 128 : 64,
+                                      hist ? 128u : static_cast<uint32_t>(p.dh));
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace
@@ -1669,29 +1830,63 @@ cudaError_t chunk_bwd1_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st) 
   return launch_bw1<0>(mq, mk, mg, msb, msh, a, p.BH, st);
 }
 
-cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st) {
-  // q, k, v, dO, S_j, Gb_j, Gb_j lo (muon; else Gb_j again), dq, dk, dv
+cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st, int first) {
   CUtensorMap m[10];
-  const uint64_t rows = static_cast<uint64_t>(p.BH) * p.T;
-  const uint64_t srows = static_cast<uint64_t>(p.BH) * p.N * kD;
-  const void* lo = (p.rule == 1 && b.Gbar_lo_hist) ? b.Gbar_lo_hist : b.Gbar_hist;
-  const void* base[10] = {p.q, p.k, p.v, p.dO, b.S_hist, b.Gbar_hist, lo, p.dq, p.dk, p.dv};
-  for (int i = 0; i < 10; ++i) {
-    const bool hist = i >= 4 && i <= 6;
-    cudaError_t e = make_tmap_rows128(&m[i], base[i], hist ? srows : rows, hist ? 128 : 64,
-                                      hist ? 128u : static_cast<uint32_t>(p.dh));
-    if (e != cudaSuccess) return e;
-  }
+  cudaError_t e = bw2_maps(p, b, m);
+  if (e != cudaSuccess) return e;
   const BwArgs a = bw_args(p, b);
   if (p.rule == 2) {
     if (!adam_bufs_ok(p, b) || !p.dnu) return cudaErrorInvalidValue;
-    return launch_bw2<2>(m, a, p.BH * p.N, st);
+    return launch_bw2<2>(m, a, p.BH, p.N, first, st);
   }
   if (p.rule == 1) {
     if (!b.dac || !b.dbc || !b.dmc || !b.Gbar_lo_hist) return cudaErrorInvalidValue;
-    return launch_bw2<1>(m, a, p.BH * p.N, st);
+    return launch_bw2<1>(m, a, p.BH, p.N, first, st);
   }
-  return launch_bw2<0>(m, a, p.BH * p.N, st);
+  return launch_bw2<0>(m, a, p.BH, p.N, first, st);
+}
+
+int chunk_bwd_fused_tiles(const ChunkArgs& p) {
+  int sms = 0;
+  if (p.rule != 0 || p.N <= 0 || sm_count(&sms) != cudaSuccess) return 0;
+  const int workers = sms - p.BH;
+  if (workers < kFusedMinWorkers) return 0;
+  const int per_worker = (p.N * kFusedNum + kFusedDen - 1) / kFusedDen;
+  const long long n = static_cast<long long>(workers) * per_worker;
+  const long long tiles = static_cast<long long>(p.BH) * p.N;
+  return static_cast<int>(n < tiles ? n : tiles);
+}
+
+cudaError_t chunk_bwd_fused_tc(const ChunkArgs& p, const TcBufs& b, int n_fused,
+                               cudaStream_t st) {
+  if (p.rule != 0 || !b.progress || n_fused <= 0) return cudaErrorInvalidValue;
+  CUtensorMap m[10];
+  cudaError_t e = bw2_maps(p, b, m);
+  if (e != cudaSuccess) return e;
+  int sms = 0;
+  if ((e = sm_count(&sms)) != cudaSuccess) return e;
+  const uint32_t smem = L1<0>::SMEM > B2_SMEM ? L1<0>::SMEM : B2_SMEM;
+  e = cudaFuncSetAttribute(chunk_bwd_fused_tc_kernel<0>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  if ((e = cudaMemsetAsync(b.progress, 0, sizeof(uint32_t) * p.BH, st)) != cudaSuccess) return e;
+  BwArgs a = bw_args(p, b);
+  a.tiles = p.BH * p.N;
+  const Sched2 sc{0, n_fused, p.BH, p.BH, p.N, 1, b.progress};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(sms));
+  cfg.blockDim = dim3(kThreads1R<0>);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, chunk_bwd_fused_tc_kernel<0>, m[0], m[1], m[2], m[3], m[4], m[5],
+                         m[6], m[7], m[8], m[9], a, sc);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
 }
 
 }  // namespace gmdn

@@ -32,6 +32,8 @@ struct TcBufs {
   float* M_ws;            // workspace, adam: fp32 slab of M (forward) / Mbar (backward)
   float* V_ws;            // workspace, adam: fp32 slab of V (forward) / Vbar (backward)
   float *dac, *dbc, *dmc, *dnc;  // workspace, adam: cotangents of a_c, b_c, mu_c, nu_c
+  uint32_t* progress;     // workspace, delta: per (b, h), chunks whose Gb_j the fused
+                          //   backward's chain has stored (counted from the last)
 };
 
 // True when the driver's cuTensorMapEncodeTiled could be resolved (every
@@ -57,7 +59,15 @@ cudaError_t chunk_bwd1_muon_tc(const ChunkArgs& p, const TcBufs& b, int ns, cuda
 // gradient per (b, h, chunk).
 bool chunk_bwd_tc_supported(const ChunkArgs& p);
 cudaError_t chunk_bwd1_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st);
-cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st);
+// first > 0: only the tiles the fused backward left (its n_fused on)
+cudaError_t chunk_bwd2_tc(const ChunkArgs& p, const TcBufs& b, cudaStream_t st, int first = 0);
+// Delta with fewer sequences than SMs: one cooperative launch runs the chains
+// and, on the SMs they leave, the token gradients of the first n_fused tiles
+// in the order the chains finish them; chunk_bwd2_tc(..., n_fused) does the
+// rest.  chunk_bwd_fused_tiles is n_fused (0: use bw1 + bw2).
+int chunk_bwd_fused_tiles(const ChunkArgs& p);
+cudaError_t chunk_bwd_fused_tc(const ChunkArgs& p, const TcBufs& b, int n_fused,
+                               cudaStream_t st);
 
 // Phase-2 state scan on the tensor cores (scan_tc.cu): gmdn_scan_fwd with
 // GMDN_PREC_FAST, delta and adam, dh 128; split-bf16 products.  `status` is

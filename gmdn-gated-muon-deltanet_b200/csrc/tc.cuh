@@ -400,6 +400,28 @@ __device__ __forceinline__ void bulk_wait_read0() {
 __device__ __forceinline__ void bulk_wait0() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
+// ... all but the N most recently committed groups.
+template <int N>
+__device__ __forceinline__ void bulk_wait_n() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Cross-CTA hand-off of data written by bulk stores and read by TMA loads
+// (both async proxy) through a counter in global memory (generic proxy):
+// the writer waits for its stores to complete, orders them before the
+// counter's release with a proxy fence; the reader acquires the counter and
+// orders its later TMA loads after it with the same fence.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 // Plain 1-D bulk copy global -> shared (16-byte aligned, size multiple of 16).
 // shared -> global bulk copy (16-byte aligned, size a multiple of 16), bulk group

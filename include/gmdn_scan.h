@@ -238,6 +238,16 @@ int gmdn_selftest_wait_timeout(uint32_t* status, uint64_t limit_ns, void* stream
  * no reference counterpart). */
 uint64_t gmdn_kernel_launches(void);
 
+/* How gmdn_chunk_bwd(_ex) splits the delta backward on the tensor-core path
+ * (diagnostic for benchmarks; no reference counterpart): with fewer
+ * (b, h) sequences than SMs, one cooperative launch runs the reverse chains
+ * and, on the SMs they leave, the token gradients of the first n tiles
+ * (chunk-heads) in the order the chains finish them; a second launch does
+ * the other B*H*(T/chunk) - n.  Returns n, or 0 where the backward is the
+ * two plain launches. */
+int gmdn_chunk_bwd_fused_tiles(int B, int H, int T, int dh, int chunk, int rule, int precision,
+                               int io_f32);
+
 /* Per-launch timing for benchmarks (diagnostic; no reference counterpart).
  * gmdn_prof_enable(1) brackets every subsequent kernel launch with two CUDA
  * events on its stream; gmdn_prof_report() waits for the recorded events and

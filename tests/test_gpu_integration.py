@@ -118,7 +118,8 @@ def test_patched_mixer_reference_benchmark_shape(inner, ns):
         runs[prec] = (y.detach().float(), xg.grad.float(), set(L.prof_report()))
     fwd = "chunk_fwd_muon_tc" if inner == "muon" else "chunk_fwd_tc"
     names = runs[pkg.GMDN_PREC_FAST][2]
-    assert {fwd, "chunk_bwd2_tc", "mixer_prologue_fwd", "head_rmsnorm_fwd"} <= names, names
+    assert {fwd, "mixer_prologue_fwd", "head_rmsnorm_fwd"} <= names, names
+    assert names & {"chunk_bwd2_tc", "chunk_bwd_fused_tc"}, names   # token gradients
     assert "chunk_prep" in runs[pkg.GMDN_PREC_IEEE][2]
     (yf, gf, _), (ye, ge, _) = runs[pkg.GMDN_PREC_FAST], runs[pkg.GMDN_PREC_IEEE]
     # adam's first chunk updates with M / (sqrt(V) + 1e-6) from V = 0, i.e.
