@@ -905,14 +905,17 @@ static_assert(sizeof(Bars2) <= 256, "barrier block");
 struct Sched2 {
   int e0, e1, worker0, BH, N, order;
   const uint32_t* progress;
-  __device__ __forceinline__ int tile(int e) const {
-    if (!order) return e;
+  __device__ __forceinline__ int list_tile(int e) const {
     const int r = e / BH;   // r-th chunk from the last
     return (e - r * BH) * N + (N - 1 - r);
   }
 };
 
-template <int RULE>
+// kMode (compile time, so the plain kernel carries none of the schedule):
+// 0 every tile, entry = tile, CTA b takes b, b + grid, ...; 1 the entries
+// sc.e0 .. sc.e1 - 1 in the chains' order (what the fused backward left);
+// 2 a worker of the fused backward (waits for each tile's Gb_j).
+template <int RULE, int kMode>
 __device__ __forceinline__ void bw2_body(const CUtensorMap& tm_q, const CUtensorMap& tm_k,
                                          const CUtensorMap& tm_v, const CUtensorMap& tm_g,
                                          const CUtensorMap& tm_s, const CUtensorMap& tm_sb,
@@ -942,10 +945,17 @@ __device__ __forceinline__ void bw2_body(const CUtensorMap& tm_q, const CUtensor
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int N = args.N;
   // this CTA's entries: ew, ew + G, ... below `tiles` (tile_at maps them to tiles)
-  const int tiles = sc.e1;
-  const int G = static_cast<int>(gridDim.x) - sc.worker0;
-  const int ew = sc.e0 + static_cast<int>(blockIdx.x) - sc.worker0;
-  auto tile_at = [&](int e) { return sc.tile(e); };
+  const int tiles = kMode == 0 ? args.tiles : sc.e1;
+  const int G = kMode == 2 ? static_cast<int>(gridDim.x) - sc.worker0 : static_cast<int>(gridDim.x);
+  const int ew = kMode == 0 ? static_cast<int>(blockIdx.x)
+                            : sc.e0 + static_cast<int>(blockIdx.x) - (kMode == 2 ? sc.worker0 : 0);
+  auto tile_at = [&](int e) {
+    if constexpr (kMode == 0) {
+      return e;
+    } else {
+      return sc.list_tile(e);
+    }
+  };
   uint32_t* status = args.status;
   // gate buffer of local tile i: beta, alpha, mu, w
   auto gates = [&](int i) { return gate0 + (i & 1) * 256; };
@@ -1055,7 +1065,7 @@ __device__ __forceinline__ void bw2_body(const CUtensorMap& tm_q, const CUtensor
       int pa = -1, ps = -1, pl = -1, pv = -1, pb[2] = {-1, -1};
       // fused backward: Gb_j of a tile is loaded only once its chain has published it
       auto ready = [&](int tile) -> bool {
-        if (!sc.progress) return true;
+        if constexpr (kMode != 2) return true;
         const uint32_t* pr = sc.progress + tile / N;
         const uint32_t need = static_cast<uint32_t>(N - tile % N);
         if (ld_acquire_gpu(pr) < need) {
@@ -1672,7 +1682,7 @@ __device__ __forceinline__ void bw2_body(const CUtensorMap& tm_q, const CUtensor
   }
 }
 
-template <int RULE>
+template <int RULE, int kMode>
 __global__ void __launch_bounds__(kThreads2, 1)
 chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
@@ -1680,7 +1690,8 @@ chunk_bwd2_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_cons
                     const __grid_constant__ CUtensorMap tm_sbl,
                     const __grid_constant__ CUtensorMap tm_dq, const __grid_constant__ CUtensorMap tm_dk,
                     const __grid_constant__ CUtensorMap tm_dv, BwArgs args, Sched2 sc) {
-  bw2_body<RULE>(tm_q, tm_k, tm_v, tm_g, tm_s, tm_sb, tm_sbl, tm_dq, tm_dk, tm_dv, args, sc);
+  bw2_body<RULE, kMode>(tm_q, tm_k, tm_v, tm_g, tm_s, tm_sb, tm_sbl, tm_dq, tm_dk, tm_dv, args,
+                        sc);
 }
 
 // Fused backward (delta): CTAs 0 .. BH-1 run the reverse chains, publishing
@@ -1707,7 +1718,7 @@ chunk_bwd_fused_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
   if (static_cast<int>(blockIdx.x) < sc.worker0)
     bw1_body<RULE, true>(tm_q, tm_k, tm_g, tm_sb, tm_s, args, static_cast<int>(blockIdx.x));
   else
-    bw2_body<RULE>(tm_q, tm_k, tm_v, tm_g, tm_s, tm_sb, tm_sbl, tm_dq, tm_dk, tm_dv, args, sc);
+    bw2_body<RULE, 2>(tm_q, tm_k, tm_v, tm_g, tm_s, tm_sb, tm_sbl, tm_dq, tm_dk, tm_dv, args, sc);
 }
 
 }  // namespace
@@ -1775,9 +1786,10 @@ cudaError_t sm_count(int* sms) {
 // bw2 is persistent: one CTA per SM (it needs all of the SM's shared memory)
 // walks its entries with a stride of the grid size.  first > 0: the entries
 // left by the fused backward (readiness order from `first` on).
-template <int RULE>
-cudaError_t launch_bw2(const CUtensorMap* m, BwArgs a, int BH, int N, int first, cudaStream_t st) {
-  cudaError_t e = cudaFuncSetAttribute(chunk_bwd2_tc_kernel<RULE>,
+template <int RULE, int kMode>
+cudaError_t launch_bw2_mode(const CUtensorMap* m, BwArgs a, int BH, int N, int first,
+                            cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(chunk_bwd2_tc_kernel<RULE, kMode>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, B2_SMEM);
   if (e != cudaSuccess) return e;
   int sms = 0;
@@ -1788,9 +1800,15 @@ cudaError_t launch_bw2(const CUtensorMap* m, BwArgs a, int BH, int N, int first,
   const int left = tiles - first;
   if (left <= 0) return cudaSuccess;
   const int grid = sms < left ? sms : left;
-  chunk_bwd2_tc_kernel<RULE><<<grid, kThreads2, B2_SMEM, st>>>(m[0], m[1], m[2], m[3], m[4],
-                                                              m[5], m[6], m[7], m[8], m[9], a, sc);
+  chunk_bwd2_tc_kernel<RULE, kMode><<<grid, kThreads2, B2_SMEM, st>>>(
+      m[0], m[1], m[2], m[3], m[4], m[5], m[6], m[7], m[8], m[9], a, sc);
   return cudaGetLastError();
+}
+
+template <int RULE>
+cudaError_t launch_bw2(const CUtensorMap* m, BwArgs a, int BH, int N, int first, cudaStream_t st) {
+  return first > 0 ? launch_bw2_mode<RULE, 1>(m, a, BH, N, first, st)
+                   : launch_bw2_mode<RULE, 0>(m, a, BH, N, first, st);
 }
 
 // The token maps of bw2 (and the fused backward): q, k, v, dO, S_j, Gb_j,
